@@ -1,0 +1,197 @@
+// C ABI entry points (include/dwdp_b200.h): argument validation, the
+// thread-local error message, and dispatch to the kernel launchers.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+
+extern "C" int dwdp_router_launch(const void*, int, const void*, int, const float*, const void*,
+                                  int64_t, int, int, int, float, int, float, float*, float*,
+                                  int64_t*, float*, float*, cudaStream_t);
+extern "C" int dwdp_dispatch_launch(const int64_t*, const void*, int, int64_t, int, int, int64_t*,
+                                    int64_t*, int64_t*, int64_t*, int64_t*, int64_t*, void*,
+                                    const void*, int, void*, void*, int*, cudaStream_t);
+extern "C" int dwdp_schedule_launch(const int64_t*, const int64_t*, int, int, int64_t*, int64_t*,
+                                    int64_t*, int64_t*, int64_t*, int64_t*, int64_t*, cudaStream_t);
+extern "C" int dwdp_pack_launch(const void* const*, int, int, int, int, int, int, void*, float*,
+                                cudaStream_t);
+extern "C" int dwdp_unpack_launch(const void*, const float*, int, int, int, int, int, float*,
+                                  cudaStream_t);
+extern "C" size_t dwdp_moe_workspace_bytes_impl(int64_t, int, int, int, int, int);
+extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group*, const dwdp_expert_group*,
+                                       const void*, const void*, int64_t, int, const int64_t*,
+                                       const int64_t*, const float*, const float*, void*, void*,
+                                       void*, size_t, int*, cudaStream_t);
+extern "C" int dwdp_merge_launch(const void*, const int64_t*, const void*, int64_t, int, int, void*,
+                                 int, int*, cudaStream_t);
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int check(int rc, const char* what) {
+  if (rc == DWDP_OK) return rc;
+  if (rc == DWDP_ERR_CUDA) {
+    cudaError_t e = cudaGetLastError();
+    return fail(rc, "%s: CUDA error %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+  }
+  if (g_last_error.empty()) return fail(rc, "%s failed with status %d", what, rc);
+  return rc;
+}
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+}  // namespace
+
+extern "C" int dwdp_version(void) { return 100; }
+
+extern "C" const char* dwdp_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" int dwdp_router_topk(const void* hidden, int hidden_dtype, const void* weight,
+                                int weight_dtype, const float* bias, const void* shared_gate_weight,
+                                int64_t num_tokens, int hidden_size, int num_experts, int top_k,
+                                float score_scale, int renormalize, float eps, float* logits,
+                                float* probs, int64_t* topk_idx, float* topk_weights,
+                                float* shared_gate, int* status, void* stream) {
+  g_last_error.clear();
+  (void)status;
+  if (num_tokens < 0 || hidden_size <= 0) return fail(DWDP_ERR_INVALID_ARGUMENT, "router: bad sizes");
+  if (num_experts <= 0 || num_experts > 256)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "router: num_experts must be in [1, 256], got %d", num_experts);
+  if (top_k <= 0 || top_k > 16 || top_k > num_experts)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "router: top_k must be in [1, min(16, E)], got %d", top_k);
+  if (!(score_scale > 0.f) || !(eps > 0.f))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "router: score_scale and eps must be > 0");
+  if (num_tokens > 0 && (hidden == nullptr || weight == nullptr || topk_idx == nullptr || topk_weights == nullptr))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "router: null pointer");
+  if (shared_gate_weight != nullptr && shared_gate == nullptr)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "router: shared_gate output required with a gate weight");
+  return check(dwdp_router_launch(hidden, hidden_dtype, weight, weight_dtype, bias, shared_gate_weight,
+                                  num_tokens, hidden_size, num_experts, top_k, score_scale, renormalize,
+                                  eps, logits, probs, topk_idx, topk_weights, shared_gate,
+                                  as_stream(stream)),
+               "router");
+}
+
+extern "C" int dwdp_dispatch(const int64_t* topk_idx, const void* topk_weights, int weight_dtype,
+                             int64_t num_tokens, int top_k, int num_experts, int64_t* counts,
+                             int64_t* offsets, int64_t* perm, int64_t* inv, int64_t* ids, int64_t* tok,
+                             void* packed_weights, const void* hidden, int hidden_size,
+                             void* packed_hidden, void* scratch, int* status, void* stream) {
+  g_last_error.clear();
+  if (num_experts <= 0 || num_experts > 1024)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "dispatch: num_experts must be in [1, 1024], got %d", num_experts);
+  if (top_k <= 0 || num_tokens < 0) return fail(DWDP_ERR_INVALID_ARGUMENT, "dispatch: bad top_k/num_tokens");
+  if (num_tokens * top_k > ((int64_t)1 << 31) - 1)
+    return fail(DWDP_ERR_CAPACITY, "dispatch: more than 2^31 assignments");
+  if (counts == nullptr || offsets == nullptr)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "dispatch: null counts/offsets");
+  if (num_tokens > 0 && (topk_idx == nullptr || topk_weights == nullptr || perm == nullptr || inv == nullptr ||
+                         ids == nullptr || tok == nullptr || packed_weights == nullptr || scratch == nullptr))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "dispatch: null pointer");
+  if (packed_hidden != nullptr && (hidden == nullptr || hidden_size <= 0))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "dispatch: packed_hidden needs hidden and hidden_size");
+  return check(dwdp_dispatch_launch(topk_idx, topk_weights, weight_dtype, num_tokens, top_k, num_experts,
+                                    counts, offsets, perm, inv, ids, tok, packed_weights, hidden,
+                                    hidden_size, packed_hidden, scratch, status, as_stream(stream)),
+               "dispatch");
+}
+
+extern "C" int dwdp_schedule(const int64_t* counts, const int64_t* offsets, int num_experts,
+                             int stream_count, int64_t* expert_queue, int64_t* starts, int64_t* ends,
+                             int64_t* active_counts, int64_t* priority, int64_t* stream_ids,
+                             int64_t* num_active, void* stream) {
+  g_last_error.clear();
+  if (num_experts <= 0 || stream_count <= 0)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "schedule: num_experts and stream_count must be > 0");
+  return check(dwdp_schedule_launch(counts, offsets, num_experts, stream_count, expert_queue, starts, ends,
+                                    active_counts, priority, stream_ids, num_active, as_stream(stream)),
+               "schedule");
+}
+
+extern "C" int dwdp_pack_weights(const void* const* src_mats, int src_dtype, int rows, int cols,
+                                 int num_mats, int dst_dtype, int scale_mode, void* dst_tiles,
+                                 float* dst_scales, void* stream) {
+  g_last_error.clear();
+  if (rows <= 0 || cols <= 0 || rows % 128 || cols % 128)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "pack_weights: rows (%d) and cols (%d) must be positive multiples of 128",
+                rows, cols);
+  return check(dwdp_pack_launch(src_mats, src_dtype, rows, cols, num_mats, dst_dtype, scale_mode, dst_tiles,
+                                dst_scales, as_stream(stream)),
+               "pack_weights");
+}
+
+extern "C" int dwdp_unpack_weights(const void* tiles, const float* scales, int rows, int cols, int num_mats,
+                                   int dst_dtype, int scale_mode, float* out, void* stream) {
+  g_last_error.clear();
+  return check(dwdp_unpack_launch(tiles, scales, rows, cols, num_mats, dst_dtype, scale_mode, out,
+                                  as_stream(stream)),
+               "unpack_weights");
+}
+
+extern "C" size_t dwdp_moe_workspace_bytes(int64_t num_tokens, int top_k, int num_experts,
+                                           int intermediate_size, int shared_intermediate_size) {
+  // The hidden size enters only through the tile count of the down projection;
+  // size for the largest supported hidden size (8192) to stay an upper bound.
+  return dwdp_moe_workspace_bytes_impl(num_tokens, top_k, num_experts, 8192, intermediate_size,
+                                       shared_intermediate_size);
+}
+
+extern "C" int dwdp_moe_experts(const dwdp_expert_group* routed, const dwdp_expert_group* shared,
+                                const void* packed_hidden, const void* hidden, int64_t num_tokens, int top_k,
+                                const int64_t* counts, const int64_t* offsets, const float* packed_weights,
+                                const float* shared_gate, void* weighted_out, void* shared_out, void* workspace,
+                                size_t workspace_bytes, int* status, void* stream) {
+  g_last_error.clear();
+  if (routed == nullptr) return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_experts: routed group is required");
+  if (routed->hidden_size <= 0 || routed->hidden_size > 8192)
+    return fail(DWDP_ERR_UNSUPPORTED, "moe_experts: hidden_size must be in (0, 8192]");
+  if (routed->hidden_size % 128 || routed->intermediate_size <= 0 || routed->intermediate_size % 128 ||
+      (shared && (shared->intermediate_size <= 0 || shared->intermediate_size % 128)))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_experts: hidden/intermediate sizes must be multiples of 128");
+  if (routed->weight_dtype == DWDP_DTYPE_FP8_E4M3 && routed->scale_mode != DWDP_SCALE_CHANNEL &&
+      routed->scale_mode != DWDP_SCALE_BLOCK128)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_experts: fp8 weights need a CHANNEL or BLOCK128 scale mode");
+  if (shared != nullptr && (shared->num_experts != 1 || shared->hidden_size != routed->hidden_size ||
+                            shared->weight_dtype != routed->weight_dtype))
+    return fail(DWDP_ERR_INVALID_ARGUMENT,
+                "moe_experts: shared group must hold one expert of the routed hidden size and weight dtype");
+  if (top_k <= 0 || num_tokens < 0) return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_experts: bad top_k/num_tokens");
+  if (num_tokens > 0 && (counts == nullptr || offsets == nullptr || weighted_out == nullptr ||
+                         packed_weights == nullptr || packed_hidden == nullptr))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_experts: null pointer");
+  if (shared != nullptr && (hidden == nullptr || shared_out == nullptr))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_experts: shared group needs hidden and shared_out");
+  const size_t need = dwdp_moe_workspace_bytes(num_tokens, top_k, routed->num_experts,
+                                               routed->intermediate_size,
+                                               shared ? shared->intermediate_size : 0);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(DWDP_ERR_CAPACITY, "moe_experts: workspace of %zu bytes < required %zu", workspace_bytes, need);
+  return check(dwdp_moe_experts_launch(routed, shared, packed_hidden, hidden, num_tokens, top_k, counts, offsets,
+                                       packed_weights, shared_gate, weighted_out, shared_out, workspace,
+                                       workspace_bytes, status, as_stream(stream)),
+               "moe_experts");
+}
+
+extern "C" int dwdp_merge(const void* weighted, const int64_t* inv, const void* shared_out, int64_t num_tokens,
+                          int top_k, int hidden_size, void* out, int out_dtype, void* stream) {
+  g_last_error.clear();
+  if (top_k <= 0 || top_k > 16) return fail(DWDP_ERR_INVALID_ARGUMENT, "merge: top_k must be in [1, 16]");
+  if (hidden_size <= 0 || hidden_size % 8)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "merge: hidden_size must be a positive multiple of 8");
+  return check(dwdp_merge_launch(weighted, inv, shared_out, num_tokens, top_k, hidden_size, out, out_dtype,
+                                 nullptr, as_stream(stream)),
+               "merge");
+}

@@ -1,0 +1,92 @@
+// Merger: deterministic token-major reduction of the expert-major weighted
+// rows (replaces reference_merge, DWDP/merger/kernels/reference.py:6-27, which
+// is zeros[T,H].index_add_(0, packed_token_indices, weighted) — atomics on a
+// GPU, hence run-to-run nondeterministic there).
+//
+// Each token's K rows are found through inv[t*K + k] (the destination of
+// assignment (t, k)) and summed in ascending row order, which is the order the
+// CPU index_add_ visits them. The optional shared-expert row is added last
+// (DWDP/adapters/qwen15_moe.py:302-319 adds it after the merger). fp32
+// accumulation, 16-byte vector loads; one CTA per token, HBM-bound.
+#include "common.cuh"
+
+namespace dwdp {
+
+template <typename TOut>
+__global__ void __launch_bounds__(256)
+merge_kernel(const __nv_bfloat16* __restrict__ weighted, const int64_t* __restrict__ inv,
+             const __nv_bfloat16* __restrict__ shared_out, int64_t T, int K, int H, int64_t nrows,
+             TOut* __restrict__ out, DeviceStatus* st) {
+  const int64_t t = blockIdx.x;
+  int64_t rows[16];
+  int nk = 0;
+  for (int k = 0; k < K; ++k) {
+    const int64_t r = inv[t * K + k];
+    if (r < 0 || r >= nrows) {
+      if (threadIdx.x == 0) record_error(st, DWDP_ERR_DEVICE_BOUNDS, 300, (int)t);
+      continue;
+    }
+    int p = nk++;  // insertion into ascending order
+    while (p > 0 && rows[p - 1] > r) { rows[p] = rows[p - 1]; --p; }
+    rows[p] = r;
+  }
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < nk; ++j) {
+      const uint4 v = *reinterpret_cast<const uint4*>(weighted + rows[j] * H + c);
+      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(b[q]);
+        acc[2 * q] += f.x;
+        acc[2 * q + 1] += f.y;
+      }
+    }
+    if (shared_out != nullptr) {
+      const uint4 v = *reinterpret_cast<const uint4*>(shared_out + t * H + c);
+      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(b[q]);
+        acc[2 * q] += f.x;
+        acc[2 * q + 1] += f.y;
+      }
+    }
+    if constexpr (sizeof(TOut) == 2) {
+      uint4 o;
+      __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) ob[q] = __floats2bfloat162_rn(acc[2 * q], acc[2 * q + 1]);
+      *reinterpret_cast<uint4*>(out + t * H + c) = o;
+    } else {
+      float4* o = reinterpret_cast<float4*>(out + t * H + c);
+      o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+  }
+}
+
+}  // namespace dwdp
+
+using namespace dwdp;
+
+extern "C" int dwdp_merge_launch(const void* weighted, const int64_t* inv, const void* shared_out,
+                                 int64_t T, int K, int H, void* out, int out_dtype, int* status,
+                                 cudaStream_t stream) {
+  if (K <= 0 || K > 16 || (H & 7) != 0 || T < 0) return DWDP_ERR_INVALID_ARGUMENT;
+  if (T == 0) return DWDP_OK;
+  DeviceStatus* st = reinterpret_cast<DeviceStatus*>(status);
+  const int threads = H / 8 >= 256 ? 256 : ((H / 8 + 31) / 32) * 32;
+  if (out_dtype == DWDP_DTYPE_BF16) {
+    merge_kernel<__nv_bfloat16><<<(unsigned)T, threads, 0, stream>>>(
+        (const __nv_bfloat16*)weighted, inv, (const __nv_bfloat16*)shared_out, T, K, H, T * K,
+        (__nv_bfloat16*)out, st);
+  } else if (out_dtype == DWDP_DTYPE_F32) {
+    merge_kernel<float><<<(unsigned)T, threads, 0, stream>>>(
+        (const __nv_bfloat16*)weighted, inv, (const __nv_bfloat16*)shared_out, T, K, H, T * K,
+        (float*)out, st);
+  } else {
+    return DWDP_ERR_UNSUPPORTED;
+  }
+  return cudaGetLastError() == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;
+}

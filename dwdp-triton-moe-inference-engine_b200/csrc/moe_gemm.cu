@@ -1,0 +1,568 @@
+// Grouped expert GEMMs on tcgen05 (sm_100a): the executor hot path.
+//
+// Replaces the per-expert loop of DWDP/executor/pytorch.py:66-160 (gather,
+// down(silu(gate(x)) * up(x)), times routing weight) and the Triton persistent
+// kernels of DWDP/executor/kernels/persistent.py:241-401 / fp8.py:147-318.
+//
+// Orientation ("swap AB"): the weight rows of one 128-row block are the MMA M
+// dimension (TMEM lanes), the tokens of one expert tile are the MMA N dimension
+// (16..128 columns, chosen per expert so a 273-row expert runs as 3 x 96, not
+// 3 x 128). A per-output-channel or per-block weight scale therefore becomes a
+// per-thread constant, and a decode step with one token per expert still fills
+// the 128-row MMA with weights.
+//
+// Two launches per layer:
+//   MODE 0  gate/up: acc_g, acc_u [128 feat x N tok] in TMEM (two MMAs sharing
+//           the activation tile), epilogue h = silu(g) * u -> bf16 h[row, feat]
+//   MODE 1  down   : acc [128 out x N tok], epilogue y * row_scale -> bf16 out
+//
+// Warp roles (one CTA per SM, persistent over a device-built work list):
+//   warp 0      producer: one cp.async.bulk for the pre-tiled weight block(s)
+//               + one TMA tile load of the activations per 64-wide K step
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2-5   epilogue (TMEM lane quadrant = warp % 4), double-buffered acc
+//   warps 6-13  (FP8 weights only) converter: e4m3 x scale -> bf16 into the
+//               128B-swizzled operand image, then fence.proxy.async
+// FP8 weights are multiplied as bf16 (e4m3 is exact in bf16; the fp32 scale is
+// folded in with one rounding), so activations stay bf16: quantising them to
+// e4m3 costs ~4.5% relative error, over the 2e-2 parity bar.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace dwdp {
+
+constexpr int BM = 128;                    // weight rows per tile (MMA M)
+constexpr int BK = 64;                     // K elements per pipeline stage (128 bytes of bf16)
+constexpr int BN_MAX = 128;                // max tokens per tile (MMA N)
+constexpr int kBTileBytes = BN_MAX * 128;  // activation tile: BN_MAX rows x 128 B
+constexpr int kConvTileBytes = BM * 128;   // bf16 weight tile 128 x 64
+constexpr int kFp8TileBytes = BM * BK;     // fp8 weight tile 128 x 64
+
+struct WorkItem {
+  int group;   // 0 routed, 1 shared
+  int expert;  // expert index inside the group
+  int rb;      // 128-row weight block
+  int row0;    // first activation row of the tile
+  int nrows;   // rows in this tile (<= BN_MAX)
+  int pad0, pad1, pad2;
+};
+
+struct GroupParams {
+  CUtensorMap tmap_b;      // activations [rows, K] bf16, box {64, BN_MAX}, 128B swizzle
+  const void* const* w;    // [E] packed weight tiles
+  const float* const* s;   // [E] scales (fp8) or nullptr
+  void* out;               // bf16 [rows, R]
+  const float* row_scale;  // MODE 1: per-row multiplier (routing weight / shared gate) or null
+  int K;                   // reduction size
+  int R;                   // output rows of the projection (= out leading dim)
+  int scale_mode;
+  int enabled;
+};
+
+struct GemmParams {
+  GroupParams g[2];
+  const WorkItem* items;
+  const int* n_items;
+  DeviceStatus* st;
+};
+
+template <int MODE, bool WFP8>
+struct Cfg {
+  static constexpr int NMAT = MODE == 0 ? 2 : 1;
+  static constexpr int S = MODE == 0 ? 4 : 6;  // load stages
+  static constexpr int SC = WFP8 ? 2 : 0;      // converted-weight stages
+  static constexpr int W_STAGE_BYTES = NMAT * (WFP8 ? kFp8TileBytes : kConvTileBytes);
+  static constexpr int CONV_STAGE_BYTES = NMAT * kConvTileBytes;
+  static constexpr int NUM_WARPS = WFP8 ? 14 : 6;
+  static constexpr int THREADS = NUM_WARPS * 32;
+  static constexpr int CONV_THREADS = 256;
+  static constexpr int TMEM_COLS = NMAT * BN_MAX * 2 <= 256 ? 256 : 512;
+  static constexpr int ACC_STRIDE = NMAT * BN_MAX;  // TMEM columns per accumulator buffer
+  static constexpr int SMEM_B = S * kBTileBytes;
+  static constexpr int SMEM_W = S * W_STAGE_BYTES;
+  static constexpr int SMEM_C = SC * CONV_STAGE_BYTES;
+  static constexpr int SMEM_BYTES = SMEM_B + SMEM_W + SMEM_C + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+// 16 e4m3 values of row r, elements [sub*16, sub*16+16) -> 32 bytes of bf16
+// written to their 128B-swizzled positions.
+__device__ __forceinline__ void convert_chunk(const uint8_t* src16, uint8_t* conv_tile, int r, int sub,
+                                              float s) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(src16);
+  const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+  uint32_t outw[8];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+#pragma unroll
+    for (int hlf = 0; hlf < 2; ++hlf) {
+      const __nv_fp8x2_storage_t pair = (__nv_fp8x2_storage_t)((wv[q] >> (16 * hlf)) & 0xFFFFu);
+      const __half2_raw h2 = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+      const __nv_bfloat162 b = __floats2bfloat162_rn(f.x * s, f.y * s);
+      outw[q * 2 + hlf] = *reinterpret_cast<const uint32_t*>(&b);
+    }
+  }
+  const int c0 = sub * 2;  // 16-byte chunk index of the first 8 elements
+  uint8_t* row = conv_tile + r * 128;
+  *reinterpret_cast<uint4*>(row + ((c0 ^ (r & 7)) << 4)) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
+  *reinterpret_cast<uint4*>(row + (((c0 + 1) ^ (r & 7)) << 4)) = make_uint4(outw[4], outw[5], outw[6], outw[7]);
+}
+
+template <int MODE, bool WFP8>
+__global__ void __launch_bounds__(Cfg<MODE, WFP8>::THREADS, 1)
+moe_gemm_kernel(const __grid_constant__ GemmParams p) {
+  using C = Cfg<MODE, WFP8>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sB = smem;
+  uint8_t* sW = sB + C::SMEM_B;
+  uint8_t* sC = sW + C::SMEM_W;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sC + C::SMEM_C);
+  uint64_t* ld_full = bars;
+  uint64_t* ld_empty = ld_full + C::S;
+  uint64_t* cv_full = ld_empty + C::S;
+  uint64_t* cv_empty = cv_full + 2;
+  uint64_t* acc_full = cv_empty + 2;
+  uint64_t* acc_empty = acc_full + 2;
+  __shared__ uint32_t s_tmem_base;
+  __shared__ volatile int s_abort;
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  DeviceStatus* st = p.st;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int i = 0; i < C::S; ++i) {
+      mbar_init(&ld_full[i], 1);
+      mbar_init(&ld_empty[i], WFP8 ? 2 : 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&cv_full[i], 1);
+      mbar_init(&cv_empty[i], 1);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&s_tmem_base, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    if (p.g[0].enabled) prefetch_tmap(&p.g[0].tmap_b);
+    if (p.g[1].enabled) prefetch_tmap(&p.g[1].tmap_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s_tmem_base;
+  const int n_items = *p.n_items;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
+        const WorkItem wi = p.items[item];
+        const GroupParams& g = p.g[wi.group];
+        const int KB = g.K / BK;
+        const uint8_t* wbase = reinterpret_cast<const uint8_t*>(g.w[wi.expert]);
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % C::S;
+          if (!mbar_wait(&ld_empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 1)) break;
+          mbar_arrive_expect_tx(&ld_full[s], C::W_STAGE_BYTES + kBTileBytes);
+          const size_t woff = ((size_t)wi.rb * KB + kb) * C::W_STAGE_BYTES;
+          bulk_g2s(sW + s * C::W_STAGE_BYTES, wbase + woff, C::W_STAGE_BYTES, &ld_full[s]);
+          tma_load_2d(sB + s * kBTileBytes, &g.tmap_b, kb * BK, wi.row0, &ld_full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0, cit = 0;
+      int li = 0;
+      for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++li) {
+        const WorkItem wi = p.items[item];
+        const GroupParams& g = p.g[wi.group];
+        const int KB = g.K / BK;
+        const int a = li & 1;
+        if (!mbar_wait(&acc_empty[a], ((li >> 1) & 1) ^ 1, &s_abort, st, 2)) break;
+        tc_fence_after();
+        const int n_mma = max(16, (wi.nrows + 15) & ~15);
+        const uint32_t idesc = idesc_bf16(BM, n_mma);
+        const uint32_t d_base = tmem_base + a * C::ACC_STRIDE;
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % C::S;
+          if (!mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 3)) { ok = false; break; }
+          const uint8_t* wtile;
+          int c = 0;
+          if constexpr (WFP8) {
+            c = cit % 2;
+            if (!mbar_wait(&cv_full[c], (cit / 2) & 1, &s_abort, st, 4)) { ok = false; break; }
+            wtile = sC + c * C::CONV_STAGE_BYTES;
+          } else {
+            wtile = sW + s * C::W_STAGE_BYTES;
+          }
+          tc_fence_after();
+          const uint32_t b_addr = smem_u32(sB + s * kBTileBytes);
+#pragma unroll
+          for (int m = 0; m < C::NMAT; ++m) {
+            const uint32_t a_addr = smem_u32(wtile + m * kConvTileBytes);
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              mma_bf16_ss(d_base + m * BN_MAX, smem_desc_sw128(a_addr + kk * 32),
+                          smem_desc_sw128(b_addr + kk * 32), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          mma_commit(&ld_empty[s]);
+          if constexpr (WFP8) {
+            mma_commit(&cv_empty[c]);
+            ++cit;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[a]);
+      }
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;
+    const int lrow = quad * 32 + lane;  // weight row inside the 128-row block
+    int li = 0;
+    for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++li) {
+      const WorkItem wi = p.items[item];
+      const GroupParams& g = p.g[wi.group];
+      const int a = li & 1;
+      if (!mbar_wait(&acc_full[a], (li >> 1) & 1, &s_abort, st, 5)) break;
+      tc_fence_after();
+      const uint32_t t_acc = tmem_base + a * C::ACC_STRIDE + ((uint32_t)(quad * 32) << 16);
+      const int feat = wi.rb * BM + lrow;
+      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out);
+      for (int c0 = 0; c0 < wi.nrows; c0 += 16) {
+        if constexpr (MODE == 0) {
+          float gv[16], uv[16];
+          tmem_ld16(t_acc + c0, gv);
+          tmem_ld16(t_acc + BN_MAX + c0, uv);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int col = c0 + j;
+            if (col < wi.nrows) {
+              const float h = silu(gv[j]) * uv[j];
+              out[(size_t)(wi.row0 + col) * g.R + feat] = __float2bfloat16_rn(h);
+            }
+          }
+        } else {
+          float yv[16];
+          tmem_ld16(t_acc + c0, yv);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int col = c0 + j;
+            if (col < wi.nrows) {
+              const int row = wi.row0 + col;
+              const float sc = g.row_scale != nullptr ? g.row_scale[row] : 1.0f;
+              out[(size_t)row * g.R + feat] = __float2bfloat16_rn(yv[j] * sc);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[a]);
+    }
+  } else if constexpr (WFP8) {
+    // ------------------------------------------------------------ converter (fp8 -> bf16)
+    const int ct = threadIdx.x - 6 * 32;  // 0..255
+    uint32_t it = 0, cit = 0;
+    for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
+      const WorkItem wi = p.items[item];
+      const GroupParams& g = p.g[wi.group];
+      const int KB = g.K / BK;
+      const float* sc = g.s[wi.expert];
+      bool ok = true;
+      for (int kb = 0; kb < KB; ++kb, ++it, ++cit) {
+        const int s = it % C::S;
+        const int c = cit % 2;
+        if (!mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 6)) { ok = false; break; }
+        if (!mbar_wait(&cv_empty[c], ((cit / 2) & 1) ^ 1, &s_abort, st, 7)) { ok = false; break; }
+        const uint8_t* raw = sW + s * C::W_STAGE_BYTES;
+        uint8_t* conv = sC + c * C::CONV_STAGE_BYTES;
+        constexpr int kChunks = C::NMAT * kFp8TileBytes / 16;  // 16-byte chunks per stage
+#pragma unroll
+        for (int q = ct; q < kChunks; q += C::CONV_THREADS) {
+          const int m = q / (kFp8TileBytes / 16);
+          const int rem = q % (kFp8TileBytes / 16);
+          const int r = rem >> 2, sub = rem & 3;
+          float s_val;
+          if (g.scale_mode == DWDP_SCALE_CHANNEL) {
+            s_val = sc[(size_t)m * g.R + wi.rb * BM + r];
+          } else {
+            s_val = sc[((size_t)m * (g.R / 128) + wi.rb) * (g.K / 128) + (kb >> 1)];
+          }
+          convert_chunk(raw + m * kFp8TileBytes + r * BK + sub * 16, conv + m * kConvTileBytes, r, sub, s_val);
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(1, C::CONV_THREADS);
+        if (ct == 0) {
+          mbar_arrive(&cv_full[c]);
+          mbar_arrive(&ld_empty[s]);
+        }
+      }
+      if (!ok) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Device tile planner (the scheduler's job, DWDP/scheduler/ops/round_robin.py:
+// active experts in ascending id), run on device so no counts reach the host.
+// Shared-expert tiles go first (longest-running work first); routed tiles are
+// ordered (expert, weight block, token tile) so CTAs running at the same time
+// stream the same weight blocks through L2.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024)
+plan_kernel(const int64_t* __restrict__ counts, const int64_t* __restrict__ offsets, int E,
+            int T, int has_shared, int rb_gu_r, int rb_dn_r, int rb_gu_s, int rb_dn_s,
+            WorkItem* __restrict__ items_gu, WorkItem* __restrict__ items_dn,
+            int* __restrict__ n_items, int cap_gu, int cap_dn, DeviceStatus* st) {
+  __shared__ int s_scan[1024];
+  __shared__ int s_total;
+  const int tid = threadIdx.x;
+  int n_sh_tiles = 0, bn_s = 0;
+  if (has_shared && T > 0) {
+    n_sh_tiles = (T + BN_MAX - 1) / BN_MAX;
+    bn_s = (((T + n_sh_tiles - 1) / n_sh_tiles) + 15) & ~15;
+  }
+  const int base_gu = n_sh_tiles * rb_gu_s;
+  const int base_dn = n_sh_tiles * rb_dn_s;
+  for (int i = tid; i < base_gu; i += blockDim.x) {
+    const int rb = i / n_sh_tiles, j = i % n_sh_tiles;
+    const int row0 = j * bn_s;
+    if (i < cap_gu) items_gu[i] = WorkItem{1, 0, rb, row0, min(bn_s, T - row0), 0, 0, 0};
+  }
+  for (int i = tid; i < base_dn; i += blockDim.x) {
+    const int rb = i / n_sh_tiles, j = i % n_sh_tiles;
+    const int row0 = j * bn_s;
+    if (i < cap_dn) items_dn[i] = WorkItem{1, 0, rb, row0, min(bn_s, T - row0), 0, 0, 0};
+  }
+  int carry = 0;
+  for (int e0 = 0; e0 < E; e0 += 1024) {
+    const int e = e0 + tid;
+    int nt = 0, cnt = 0, bn = 0;
+    int64_t off = 0;
+    if (e < E) {
+      cnt = (int)counts[e];
+      off = offsets[e];
+      if (cnt > 0) {
+        nt = (cnt + BN_MAX - 1) / BN_MAX;
+        bn = (((cnt + nt - 1) / nt) + 15) & ~15;
+      }
+    }
+    s_scan[tid] = nt;
+    __syncthreads();
+    for (int o = 1; o < 1024; o <<= 1) {
+      const int add = tid >= o ? s_scan[tid - o] : 0;
+      __syncthreads();
+      s_scan[tid] += add;
+      __syncthreads();
+    }
+    const int excl = carry + s_scan[tid] - nt;
+    if (e < E && nt > 0) {
+      for (int rb = 0; rb < rb_gu_r; ++rb)
+        for (int j = 0; j < nt; ++j) {
+          const int idx = base_gu + excl * rb_gu_r + rb * nt + j;
+          const int row0 = (int)off + j * bn;
+          if (idx < cap_gu) items_gu[idx] = WorkItem{0, e, rb, row0, min(bn, cnt - j * bn), 0, 0, 0};
+        }
+      for (int rb = 0; rb < rb_dn_r; ++rb)
+        for (int j = 0; j < nt; ++j) {
+          const int idx = base_dn + excl * rb_dn_r + rb * nt + j;
+          const int row0 = (int)off + j * bn;
+          if (idx < cap_dn) items_dn[idx] = WorkItem{0, e, rb, row0, min(bn, cnt - j * bn), 0, 0, 0};
+        }
+    }
+    if (tid == 1023) s_total = carry + s_scan[1023];
+    __syncthreads();
+    carry = s_total;
+    __syncthreads();
+  }
+  if (tid == 0) {
+    const int ngu = base_gu + carry * rb_gu_r;
+    const int ndn = base_dn + carry * rb_dn_r;
+    if (ngu > cap_gu || ndn > cap_dn) {
+      record_error(st, DWDP_ERR_CAPACITY, 200, ngu);
+      n_items[0] = 0;
+      n_items[1] = 0;
+    } else {
+      n_items[0] = ngu;
+      n_items[1] = ndn;
+    }
+  }
+}
+
+}  // namespace dwdp
+
+using namespace dwdp;
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix, box {64, BN_MAX}, 128B swizzle.
+bool make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols) {
+  auto enc = get_encode_fn();
+  if (enc == nullptr || rows <= 0) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BN_MAX};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct WsLayout {
+  size_t h_routed, h_shared, items_gu, items_dn, n_items, total;
+  int cap_gu, cap_dn;
+};
+
+WsLayout ws_layout(int64_t T, int K, int E, int I, int H, int Is) {
+  const int64_t N = T * K;
+  const int64_t tiles_r = N / BN_MAX + std::min<int64_t>(E, N) + 1;
+  const int64_t tiles_s = Is > 0 ? (T + BN_MAX - 1) / BN_MAX : 0;
+  WsLayout w{};
+  w.cap_gu = (int)(tiles_r * (I / BM) + tiles_s * (Is / BM));
+  w.cap_dn = (int)((tiles_r + tiles_s) * (H / BM));
+  size_t o = 0;
+  w.h_routed = o; o = align256(o + (size_t)N * I * 2);
+  w.h_shared = o; o = align256(o + (size_t)T * (Is > 0 ? Is : 0) * 2);
+  w.items_gu = o; o = align256(o + (size_t)w.cap_gu * sizeof(WorkItem));
+  w.items_dn = o; o = align256(o + (size_t)w.cap_dn * sizeof(WorkItem));
+  w.n_items = o; o = align256(o + 16);
+  w.total = o;
+  return w;
+}
+
+int g_num_sms = 0;
+
+template <int MODE, bool WFP8>
+int launch_gemm(const GemmParams& prm, int grid, cudaStream_t stream) {
+  using C = Cfg<MODE, WFP8>;
+  auto kfn = moe_gemm_kernel<MODE, WFP8>;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
+    return DWDP_ERR_CUDA;
+  kfn<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(prm);
+  return cudaGetLastError() == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" int dwdp_device_sm_count(void) {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  }
+  return g_num_sms;
+}
+
+extern "C" size_t dwdp_moe_workspace_bytes_impl(int64_t T, int K, int E, int H, int I, int Is) {
+  return ws_layout(T, K, E, I, H, Is).total;
+}
+
+extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dwdp_expert_group* shared,
+                                       const void* packed_hidden, const void* hidden, int64_t T,
+                                       int K, const int64_t* counts, const int64_t* offsets,
+                                       const float* packed_weights, const float* shared_gate,
+                                       void* weighted_out, void* shared_out, void* workspace,
+                                       size_t workspace_bytes, int* status, cudaStream_t stream) {
+  if (routed == nullptr || T < 0 || K <= 0) return DWDP_ERR_INVALID_ARGUMENT;
+  const int H = routed->hidden_size, I = routed->intermediate_size, E = routed->num_experts;
+  const int Is = shared ? shared->intermediate_size : 0;
+  if (H % 128 || I % 128 || Is % 128 || E <= 0 || E > 1024) return DWDP_ERR_INVALID_ARGUMENT;
+  const bool fp8 = routed->weight_dtype == DWDP_DTYPE_FP8_E4M3;
+  if (!fp8 && routed->weight_dtype != DWDP_DTYPE_BF16) return DWDP_ERR_UNSUPPORTED;
+  const int64_t N = T * K;
+  const WsLayout L = ws_layout(T, K, E, I, H, Is);
+  if (workspace == nullptr || workspace_bytes < L.total) return DWDP_ERR_CAPACITY;
+  if (T == 0) return DWDP_OK;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  __nv_bfloat16* h_r = reinterpret_cast<__nv_bfloat16*>(ws + L.h_routed);
+  __nv_bfloat16* h_s = reinterpret_cast<__nv_bfloat16*>(ws + L.h_shared);
+  WorkItem* items_gu = reinterpret_cast<WorkItem*>(ws + L.items_gu);
+  WorkItem* items_dn = reinterpret_cast<WorkItem*>(ws + L.items_dn);
+  int* n_items = reinterpret_cast<int*>(ws + L.n_items);
+  DeviceStatus* st = reinterpret_cast<DeviceStatus*>(status);
+  const int has_shared = shared != nullptr ? 1 : 0;
+
+  plan_kernel<<<1, 1024, 0, stream>>>(counts, offsets, E, (int)T, has_shared, I / BM, H / BM,
+                                      has_shared ? Is / BM : 0, has_shared ? H / BM : 0, items_gu,
+                                      items_dn, n_items, L.cap_gu, L.cap_dn, st);
+  if (cudaGetLastError() != cudaSuccess) return DWDP_ERR_CUDA;
+
+  GemmParams gu{}, dn{};
+  gu.g[0].enabled = N > 0;
+  if (N > 0 && !make_tmap(&gu.g[0].tmap_b, packed_hidden, N, H)) return DWDP_ERR_CUDA;
+  gu.g[0].w = routed->w13; gu.g[0].s = routed->s13; gu.g[0].out = h_r; gu.g[0].row_scale = nullptr;
+  gu.g[0].K = H; gu.g[0].R = I; gu.g[0].scale_mode = routed->scale_mode;
+  gu.g[1].enabled = has_shared;
+  if (has_shared) {
+    if (!make_tmap(&gu.g[1].tmap_b, hidden, T, H)) return DWDP_ERR_CUDA;
+    gu.g[1].w = shared->w13; gu.g[1].s = shared->s13; gu.g[1].out = h_s; gu.g[1].row_scale = nullptr;
+    gu.g[1].K = H; gu.g[1].R = Is; gu.g[1].scale_mode = shared->scale_mode;
+  }
+  gu.items = items_gu; gu.n_items = n_items; gu.st = st;
+
+  dn.g[0].enabled = N > 0;
+  if (N > 0 && !make_tmap(&dn.g[0].tmap_b, h_r, N, I)) return DWDP_ERR_CUDA;
+  dn.g[0].w = routed->w2; dn.g[0].s = routed->s2; dn.g[0].out = weighted_out;
+  dn.g[0].row_scale = packed_weights; dn.g[0].K = I; dn.g[0].R = H; dn.g[0].scale_mode = routed->scale_mode;
+  dn.g[1].enabled = has_shared;
+  if (has_shared) {
+    if (!make_tmap(&dn.g[1].tmap_b, h_s, T, Is)) return DWDP_ERR_CUDA;
+    dn.g[1].w = shared->w2; dn.g[1].s = shared->s2; dn.g[1].out = shared_out;
+    dn.g[1].row_scale = shared_gate; dn.g[1].K = Is; dn.g[1].R = H; dn.g[1].scale_mode = shared->scale_mode;
+  }
+  dn.items = items_dn; dn.n_items = n_items + 1; dn.st = st;
+
+  const int sms = dwdp_device_sm_count();
+  if (sms <= 0) return DWDP_ERR_CUDA;
+  const int grid_gu = std::max(1, std::min(sms, L.cap_gu));
+  const int grid_dn = std::max(1, std::min(sms, L.cap_dn));
+  int rc;
+  if (fp8) {
+    rc = launch_gemm<0, true>(gu, grid_gu, stream);
+    if (rc == DWDP_OK) rc = launch_gemm<1, true>(dn, grid_dn, stream);
+  } else {
+    rc = launch_gemm<0, false>(gu, grid_gu, stream);
+    if (rc == DWDP_OK) rc = launch_gemm<1, false>(dn, grid_dn, stream);
+  }
+  return rc;
+}

@@ -1,0 +1,187 @@
+/*
+ * dwdp_b200.h — C ABI of the B200-native DWDP MoE-layer hot path.
+ *
+ * Plain C: raw device pointers, sizes, dtype codes and an opaque CUDA stream
+ * (`void*` holding a cudaStream_t; NULL = legacy default stream). Every entry
+ * point returns an int status (DWDP_OK = 0, negative on error) and never
+ * throws; dwdp_last_error() returns a thread-local message for the last
+ * failure on the calling thread.
+ *
+ * Reference interfaces each group replaces (paths inside the DWDP project):
+ *   router    DWDP/router/kernels/fused.py:8-42 reference_topk_routing,
+ *             DWDP/router/linear.py:38-44 compute_router_logits
+ *   dispatch  DWDP/dispatcher/kernels/reference.py:163-257
+ *             counting_scatter_expert_major_dispatch (+ ops/scatter.py:6-96)
+ *   schedule  DWDP/scheduler/ops/round_robin.py:8-80 build_round_robin_schedule
+ *   experts   DWDP/executor/pytorch.py:32-224 PyTorchExecutor.forward,
+ *             DWDP/executor/kernels/persistent.py:160-226 / fp8.py:82-143,
+ *             DWDP/executor/tensor_list.py:29-67 (pointer-array expert handles)
+ *   weights   DWDP/executor/fp8.py:17-51, 118-146 (one-shot FP8 conversion)
+ *   merge     DWDP/merger/kernels/reference.py:6-27 reference_merge
+ *   shared    DWDP/adapters/qwen15_moe.py:302-319 _add_shared_expert
+ */
+#ifndef DWDP_B200_H_
+#define DWDP_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define DWDP_OK 0
+#define DWDP_ERR_INVALID_ARGUMENT (-1)
+#define DWDP_ERR_CAPACITY (-2)
+#define DWDP_ERR_CUDA (-3)
+#define DWDP_ERR_DEVICE_TIMEOUT (-4)
+#define DWDP_ERR_DEVICE_BOUNDS (-5)
+#define DWDP_ERR_UNSUPPORTED (-6)
+#define DWDP_ERR_STATE (-7)
+#define DWDP_ERR_NOT_FOUND (-8)
+
+/* ---- dtype codes (1..3 follow DWDP/executor/tensor_list.py:237-246) ---- */
+#define DWDP_DTYPE_F16 1
+#define DWDP_DTYPE_BF16 2
+#define DWDP_DTYPE_FP8_E4M3 3
+#define DWDP_DTYPE_F32 4
+
+/* ---- weight scale modes ------------------------------------------------ */
+#define DWDP_SCALE_NONE 0     /* bf16 weights, no scale                     */
+#define DWDP_SCALE_CHANNEL 1  /* fp8, one fp32 scale per output row         */
+#define DWDP_SCALE_BLOCK128 2 /* fp8, one fp32 scale per 128x128 block      */
+
+/* Device status word: int[4] {code, where, detail, count} in device memory,
+ * zeroed by the caller. Kernels record bounded-wait timeouts and failed bounds
+ * checks there instead of trapping. May be NULL. */
+
+int dwdp_version(void);
+const char* dwdp_last_error(void);
+/* Number of SMs of the current device (the persistent grid size). */
+int dwdp_device_sm_count(void);
+
+/* ======================================================================== *
+ * Router: logits = x . W^T (+bias) (*score_scale) in fp32; top-k over logits
+ * (ties -> lower expert id, slots in descending logit order); softmax over the
+ * k selected; optional renormalisation by sum.clamp_min(eps); k == 1 gives
+ * weight 1. Optionally the sigmoid shared-expert gate sigmoid(x . g).
+ * Replaces reference_topk_routing + compute_router_logits (fused.py:8-42,
+ * linear.py:38-44). E <= 256, K <= 16.
+ *   hidden [T,H] (hidden_dtype bf16|f32), weight [E,H] (weight_dtype bf16|f32)
+ *   bias [E] f32 or NULL, shared_gate_weight [H] (weight_dtype) or NULL
+ *   logits [T,E] f32 (may be NULL), probs/topk_weights [T,K] f32,
+ *   topk_idx [T,K] int64, shared_gate [T] f32 (NULL when no gate weight)
+ * ======================================================================== */
+int dwdp_router_topk(const void* hidden, int hidden_dtype, const void* weight, int weight_dtype,
+                     const float* bias, const void* shared_gate_weight, int64_t num_tokens,
+                     int hidden_size, int num_experts, int top_k, float score_scale,
+                     int renormalize, float eps, float* logits, float* probs, int64_t* topk_idx,
+                     float* topk_weights, float* shared_gate, int* status, void* stream);
+
+/* ======================================================================== *
+ * Dispatch: stable counting sort of the T*K token-major assignments into
+ * expert-major order, bit-exact with counting_scatter_expert_major_dispatch
+ * (reference.py:163-257): dest[i] = offsets[e_i] + #{j < i : e_j == e_i}.
+ *   counts [E], offsets [E+1], perm/inv/ids/tok [T*K]  (all int64)
+ *   packed_weights [T*K] in weight_dtype (f32|bf16|f16), bit-copied
+ *   hidden/packed_hidden: optional bf16 row gather packed_hidden[d] = hidden[tok[d]]
+ *   (hidden_size columns); pass NULL to skip.
+ *   scratch: dwdp_dispatch_scratch_bytes() bytes of device memory.
+ * ======================================================================== */
+size_t dwdp_dispatch_scratch_bytes(int64_t num_tokens, int top_k, int num_experts);
+int dwdp_dispatch(const int64_t* topk_idx, const void* topk_weights, int weight_dtype,
+                  int64_t num_tokens, int top_k, int num_experts, int64_t* counts,
+                  int64_t* offsets, int64_t* perm, int64_t* inv, int64_t* ids, int64_t* tok,
+                  void* packed_weights, const void* hidden, int hidden_size, void* packed_hidden,
+                  void* scratch, int* status, void* stream);
+
+/* ======================================================================== *
+ * Round-robin schedule over active experts in ascending id
+ * (build_round_robin_schedule, round_robin.py:8-80), padded to E entries:
+ * rows [0, num_active) hold the reference values, the rest are -1.
+ *   out arrays [E] int64: expert_queue, starts, ends, active_counts,
+ *   priority (= order), stream_ids (= order % stream_count); num_active [1].
+ * ======================================================================== */
+int dwdp_schedule(const int64_t* counts, const int64_t* offsets, int num_experts,
+                  int stream_count, int64_t* expert_queue, int64_t* starts, int64_t* ends,
+                  int64_t* active_counts, int64_t* priority, int64_t* stream_ids,
+                  int64_t* num_active, void* stream);
+
+/* ======================================================================== *
+ * Expert weight store. Weights are kept pre-tiled in the layout the grouped
+ * GEMM streams: for an [R, Kd] projection (R output rows, Kd inputs, both
+ * multiples of 128) tiles of 128 rows x 64 inputs, tile (rb, kb) of matrix p
+ * of a P-matrix pack at tile index (rb * (Kd/64) + kb) * P + p.
+ *   FP8: 8192-byte tiles, rows of 64 bytes, scales fp32
+ *        (CHANNEL: [P][R]; BLOCK128: [P][R/128][Kd/128]).
+ *   BF16: 16384-byte tiles stored in the 128-byte-swizzled smem image.
+ * Quantisation follows DWDP/executor/fp8.py:118-146: scale = max(amax, 1e-5)
+ * / 448, q = e4m3(w / scale) (round to nearest even, IEEE division).
+ * Gate/up are packed together (P = 2, gate then up) so one tile fetch brings
+ * both halves of a SwiGLU feature block.
+ *   src_mats: host array of P device pointers to row-major [R, Kd] matrices
+ *   (src_dtype bf16|f32).
+ * ======================================================================== */
+size_t dwdp_packed_weight_bytes(int rows, int cols, int num_mats, int dst_dtype);
+size_t dwdp_packed_scale_floats(int rows, int cols, int num_mats, int scale_mode);
+int dwdp_pack_weights(const void* const* src_mats, int src_dtype, int rows, int cols,
+                      int num_mats, int dst_dtype, int scale_mode, void* dst_tiles,
+                      float* dst_scales, void* stream);
+/* Inverse of dwdp_pack_weights: dequantised fp32 [P][R][Kd]. */
+int dwdp_unpack_weights(const void* tiles, const float* scales, int rows, int cols,
+                        int num_mats, int dst_dtype, int scale_mode, float* out,
+                        void* stream);
+
+/* ======================================================================== *
+ * Expert group: the device-resident handle set one grouped GEMM launch reads
+ * (the TensorList pointer arrays of tensor_list.py:29-67, reduced to what the
+ * kernel needs). Pointer arrays live in device memory, one entry per expert.
+ * ======================================================================== */
+typedef struct dwdp_expert_group {
+  int num_experts;
+  int hidden_size;         /* H: K of gate/up, output width of down       */
+  int intermediate_size;   /* I: output width of gate/up, K of down       */
+  int weight_dtype;        /* DWDP_DTYPE_BF16 | DWDP_DTYPE_FP8_E4M3       */
+  int scale_mode;          /* DWDP_SCALE_*                                */
+  const void* const* w13;  /* [E] packed gate/up tiles (num_mats = 2)     */
+  const void* const* w2;   /* [E] packed down tiles (num_mats = 1)        */
+  const float* const* s13; /* [E] gate/up scales                          */
+  const float* const* s2;  /* [E] down scales                             */
+} dwdp_expert_group;
+
+/* ======================================================================== *
+ * Grouped expert execution (replaces PyTorchExecutor.forward's per-expert
+ * loop, pytorch.py:66-160): for every routed assignment row d
+ *   weighted_out[d] = w[d] * down(silu(gate(xd)) * up(xd)),  xd = packed_hidden[d]
+ * and, when `shared` is given, for every token t
+ *   shared_out[t] = shared_gate[t] * down_s(silu(gate_s(x_t)) * up_s(x_t))
+ * (shared_gate NULL = 1). bf16 activations, fp32 accumulation in TMEM,
+ * bf16 outputs. Two persistent tcgen05 launches (gate/up+SwiGLU, down+scale).
+ * Expert row ranges come from device offsets; no host synchronisation.
+ * hidden_size <= 8192.
+ * ======================================================================== */
+size_t dwdp_moe_workspace_bytes(int64_t num_tokens, int top_k, int num_experts,
+                                int intermediate_size, int shared_intermediate_size);
+int dwdp_moe_experts(const dwdp_expert_group* routed, const dwdp_expert_group* shared,
+                     const void* packed_hidden, const void* hidden, int64_t num_tokens,
+                     int top_k, const int64_t* counts, const int64_t* offsets,
+                     const float* packed_weights, const float* shared_gate, void* weighted_out,
+                     void* shared_out, void* workspace, size_t workspace_bytes, int* status,
+                     void* stream);
+
+/* ======================================================================== *
+ * Merge (reference_merge, merger/kernels/reference.py:6-27): deterministic
+ * token-major reduction. out[t] = sum over the K rows inv[t*K+k] of
+ * weighted[row] taken in ascending row order, plus shared_out[t] if given.
+ * fp32 accumulation; out_dtype bf16|f32; weighted/shared bf16. K <= 16.
+ * ======================================================================== */
+int dwdp_merge(const void* weighted, const int64_t* inv, const void* shared_out,
+               int64_t num_tokens, int top_k, int hidden_size, void* out, int out_dtype,
+               void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DWDP_B200_H_ */
