@@ -1,0 +1,143 @@
+"""ctypes binding of the C-ABI library ``libdwdp_b200.so`` (include/dwdp_b200.h).
+
+The library is loaded from this package directory. There is no fallback: if the
+library is missing or fails to load, every op raises ``RuntimeError`` instead of
+computing anything on the CPU.
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import threading
+
+HERE = pathlib.Path(__file__).resolve().parent
+LIB_PATH = HERE / "libdwdp_b200.so"
+
+DWDP_OK = 0
+DWDP_ERR_INVALID_ARGUMENT = -1
+DWDP_ERR_CAPACITY = -2
+DWDP_ERR_CUDA = -3
+DWDP_ERR_DEVICE_TIMEOUT = -4
+DWDP_ERR_DEVICE_BOUNDS = -5
+DWDP_ERR_UNSUPPORTED = -6
+DWDP_ERR_STATE = -7
+DWDP_ERR_NOT_FOUND = -8
+
+DTYPE_F16 = 1
+DTYPE_BF16 = 2
+DTYPE_FP8_E4M3 = 3
+DTYPE_F32 = 4
+
+SCALE_NONE = 0
+SCALE_CHANNEL = 1
+SCALE_BLOCK128 = 2
+
+c_void_p = ctypes.c_void_p
+c_int = ctypes.c_int
+c_int64 = ctypes.c_int64
+c_float = ctypes.c_float
+c_size_t = ctypes.c_size_t
+
+
+class ExpertGroup(ctypes.Structure):
+    """Mirror of ``dwdp_expert_group`` (device pointer arrays per expert)."""
+
+    _fields_ = [
+        ("num_experts", c_int),
+        ("hidden_size", c_int),
+        ("intermediate_size", c_int),
+        ("weight_dtype", c_int),
+        ("scale_mode", c_int),
+        ("w13", c_void_p),
+        ("w2", c_void_p),
+        ("s13", c_void_p),
+        ("s2", c_void_p),
+    ]
+
+
+# name -> (restype, argtypes)
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "dwdp_version": (c_int, []),
+    "dwdp_last_error": (ctypes.c_char_p, []),
+    "dwdp_device_sm_count": (c_int, []),
+    "dwdp_router_topk": (
+        c_int,
+        [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int, c_int, c_int,
+         c_float, c_int, c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_void_p],
+    ),
+    "dwdp_dispatch_scratch_bytes": (c_size_t, [c_int64, c_int, c_int]),
+    "dwdp_dispatch": (
+        c_int,
+        [c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p,
+         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
+         c_void_p],
+    ),
+    "dwdp_schedule": (
+        c_int,
+        [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_void_p, c_void_p, c_void_p],
+    ),
+    "dwdp_packed_weight_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "dwdp_packed_scale_floats": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "dwdp_pack_weights": (
+        c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]
+    ),
+    "dwdp_unpack_weights": (
+        c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p]
+    ),
+    "dwdp_moe_workspace_bytes": (c_size_t, [c_int64, c_int, c_int, c_int, c_int]),
+    "dwdp_moe_experts": (
+        c_int,
+        [ctypes.POINTER(ExpertGroup), ctypes.POINTER(ExpertGroup), c_void_p, c_void_p, c_int64,
+         c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+         c_void_p, c_void_p],
+    ),
+    "dwdp_merge": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p, c_int, c_void_p]
+    ),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load(path: pathlib.Path | str | None = None) -> ctypes.CDLL:
+    """Load (once) and return the library with argument types set."""
+    global _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = pathlib.Path(path) if path is not None else LIB_PATH
+        if not p.exists():
+            raise RuntimeError(
+                f"DWDP B200 extension not built: {p} is missing (run build.py); "
+                "there is no CPU fallback"
+            )
+        lib = ctypes.CDLL(str(p))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    msg = load().dwdp_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int, what: str) -> None:
+    """Translate a C status code into the reference's exception types."""
+    if rc == DWDP_OK:
+        return
+    msg = last_error() or f"{what} failed with status {rc}"
+    if rc == DWDP_ERR_INVALID_ARGUMENT:
+        raise ValueError(msg)
+    if rc == DWDP_ERR_NOT_FOUND:
+        raise KeyError(msg)
+    if rc == DWDP_ERR_UNSUPPORTED:
+        raise NotImplementedError(msg)
+    raise RuntimeError(msg)

@@ -1,0 +1,330 @@
+"""Tensor-level wrappers over the C ABI: torch supplies device memory and the
+current CUDA stream; every computation runs in the hand-written sm_100a kernels.
+
+Each function validates like the reference op it replaces (``ValueError`` on a
+contract violation) and raises ``RuntimeError`` when the extension is missing or
+a tensor is not on a CUDA device. Nothing here computes on the CPU.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+_DTYPE_CODES = {
+    torch.float16: _lib.DTYPE_F16,
+    torch.bfloat16: _lib.DTYPE_BF16,
+    torch.float8_e4m3fn: _lib.DTYPE_FP8_E4M3,
+    torch.float32: _lib.DTYPE_F32,
+}
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODES[dtype]
+    except KeyError as exc:
+        raise ValueError(f"unsupported dtype {dtype}") from exc
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _require_cuda(*tensors: torch.Tensor | None) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("DWDP B200 ops need CUDA tensors; there is no CPU fallback")
+
+
+# --------------------------------------------------------------------------- router
+@dataclass
+class RouterResult:
+    router_logits: torch.Tensor  # [T, E] fp32
+    routing_probabilities: torch.Tensor  # [T, K] fp32
+    topk_indices: torch.Tensor  # [T, K] int64
+    topk_weights: torch.Tensor  # [T, K] fp32
+    shared_gate: torch.Tensor | None  # [T] fp32
+
+
+def router_topk(
+    hidden: torch.Tensor,
+    weight: torch.Tensor,
+    top_k: int,
+    *,
+    bias: torch.Tensor | None = None,
+    shared_gate_weight: torch.Tensor | None = None,
+    score_scale: float = 1.0,
+    renormalize: bool = True,
+    eps: float = 1e-9,
+    out: RouterResult | None = None,
+) -> RouterResult:
+    """Fused logits + top-k + softmax-over-k + renormalisation (fp32 math).
+
+    Mirrors ``LinearTopKRouter.compute_router_logits`` + ``reference_topk_routing``
+    (DWDP/router/linear.py:38-44, DWDP/router/kernels/fused.py:8-42). Slots come
+    out in descending logit order; ties go to the lower expert id.
+    """
+    _require_cuda(hidden, weight, bias, shared_gate_weight)
+    H = hidden.shape[-1]
+    x = hidden.reshape(-1, H).contiguous()
+    T = x.shape[0]
+    E = weight.shape[0]
+    if weight.ndim != 2 or weight.shape[1] != H:
+        raise ValueError("router weight must be [num_experts, hidden_size]")
+    w = weight.contiguous()
+    if shared_gate_weight is not None:
+        shared_gate_weight = shared_gate_weight.reshape(-1).to(w.dtype).contiguous()
+        if shared_gate_weight.numel() != H:
+            raise ValueError("shared gate weight must have hidden_size elements")
+    dev = x.device
+    if out is None:
+        out = RouterResult(
+            router_logits=torch.empty(T, E, dtype=torch.float32, device=dev),
+            routing_probabilities=torch.empty(T, top_k, dtype=torch.float32, device=dev),
+            topk_indices=torch.empty(T, top_k, dtype=torch.int64, device=dev),
+            topk_weights=torch.empty(T, top_k, dtype=torch.float32, device=dev),
+            shared_gate=(torch.empty(T, dtype=torch.float32, device=dev)
+                         if shared_gate_weight is not None else None),
+        )
+    b = None if bias is None else bias.float().contiguous()
+    rc = _lib.load().dwdp_router_topk(
+        x.data_ptr(), dtype_code(x.dtype), w.data_ptr(), dtype_code(w.dtype), _ptr(b),
+        _ptr(shared_gate_weight), T, H, E, top_k, float(score_scale), int(renormalize), float(eps),
+        _ptr(out.router_logits), _ptr(out.routing_probabilities), _ptr(out.topk_indices),
+        _ptr(out.topk_weights), _ptr(out.shared_gate), None, _stream(),
+    )
+    _lib.check(rc, "router_topk")
+    return out
+
+
+# --------------------------------------------------------------------------- dispatch
+@dataclass
+class DispatchResult:
+    expert_counts: torch.Tensor  # [E] int64
+    expert_offsets: torch.Tensor  # [E+1] int64
+    token_permutation: torch.Tensor  # [N] int64
+    inverse_permutation: torch.Tensor  # [N] int64
+    packed_expert_ids: torch.Tensor  # [N] int64
+    packed_token_indices: torch.Tensor  # [N] int64
+    packed_routing_weights: torch.Tensor  # [N] weight dtype
+    packed_hidden: torch.Tensor | None  # [N, H] bf16
+
+
+def dispatch_scratch_bytes(num_tokens: int, top_k: int, num_experts: int) -> int:
+    return int(_lib.load().dwdp_dispatch_scratch_bytes(num_tokens, top_k, num_experts))
+
+
+def dispatch(
+    topk_indices: torch.Tensor,
+    topk_weights: torch.Tensor,
+    num_experts: int,
+    *,
+    hidden: torch.Tensor | None = None,
+    scratch: torch.Tensor | None = None,
+    out: DispatchResult | None = None,
+    status: torch.Tensor | None = None,
+) -> DispatchResult:
+    """Stable counting-sort dispatch, bit-exact with the reference's
+    ``counting_scatter_expert_major_dispatch`` (DWDP/dispatcher/kernels/reference.py:163-257).
+    With ``hidden`` it also gathers the packed bf16 activation rows."""
+    _require_cuda(topk_indices, topk_weights, hidden)
+    if topk_indices.shape != topk_weights.shape:
+        raise ValueError("topk_indices and topk_weights must have identical shapes")
+    if topk_indices.ndim < 1 or topk_indices.shape[-1] <= 0:
+        raise ValueError("topk_indices must have a positive top-k dimension")
+    if topk_indices.dtype.is_floating_point:
+        raise ValueError("topk_indices must use an integer dtype")
+    if not topk_weights.dtype.is_floating_point:
+        raise ValueError("topk_weights must use a floating-point dtype")
+    K = topk_indices.shape[-1]
+    idx = topk_indices.reshape(-1).to(torch.int64).contiguous()
+    wts = topk_weights.reshape(-1).contiguous()
+    N = idx.numel()
+    T = N // K
+    dev = idx.device
+    if out is None:
+        out = DispatchResult(
+            expert_counts=torch.empty(num_experts, dtype=torch.int64, device=dev),
+            expert_offsets=torch.empty(num_experts + 1, dtype=torch.int64, device=dev),
+            token_permutation=torch.empty(N, dtype=torch.int64, device=dev),
+            inverse_permutation=torch.empty(N, dtype=torch.int64, device=dev),
+            packed_expert_ids=torch.empty(N, dtype=torch.int64, device=dev),
+            packed_token_indices=torch.empty(N, dtype=torch.int64, device=dev),
+            packed_routing_weights=torch.empty(N, dtype=wts.dtype, device=dev),
+            packed_hidden=None,
+        )
+    H = 0
+    if hidden is not None:
+        if hidden.dtype != torch.bfloat16:
+            raise ValueError("packed activation gather expects bf16 hidden states")
+        H = hidden.shape[-1]
+        hidden = hidden.reshape(-1, H).contiguous()
+        if out.packed_hidden is None:
+            out.packed_hidden = torch.empty(N, H, dtype=torch.bfloat16, device=dev)
+    if scratch is None:
+        scratch = torch.empty(dispatch_scratch_bytes(T, K, num_experts), dtype=torch.uint8, device=dev)
+    rc = _lib.load().dwdp_dispatch(
+        idx.data_ptr(), wts.data_ptr(), dtype_code(wts.dtype), T, K, num_experts,
+        _ptr(out.expert_counts), _ptr(out.expert_offsets), _ptr(out.token_permutation),
+        _ptr(out.inverse_permutation), _ptr(out.packed_expert_ids), _ptr(out.packed_token_indices),
+        _ptr(out.packed_routing_weights), _ptr(hidden), H,
+        _ptr(out.packed_hidden) if hidden is not None else None, scratch.data_ptr(), _ptr(status),
+        _stream(),
+    )
+    _lib.check(rc, "dispatch")
+    return out
+
+
+# --------------------------------------------------------------------------- schedule
+@dataclass
+class ScheduleResult:
+    expert_queue: torch.Tensor
+    expert_starts: torch.Tensor
+    expert_ends: torch.Tensor
+    expert_counts: torch.Tensor
+    execution_priority: torch.Tensor
+    stream_assignments: torch.Tensor
+    num_active: torch.Tensor  # [1] int64 on device
+
+
+def schedule(expert_counts: torch.Tensor, expert_offsets: torch.Tensor, stream_count: int = 1) -> ScheduleResult:
+    """Ascending-expert round-robin schedule (DWDP/scheduler/ops/round_robin.py:8-80),
+    padded to E rows with -1 so it needs no host synchronisation."""
+    _require_cuda(expert_counts, expert_offsets)
+    if stream_count <= 0:
+        raise ValueError("stream_count must be > 0")
+    E = expert_counts.numel()
+    dev = expert_counts.device
+    counts = expert_counts.to(torch.int64).contiguous()
+    offsets = expert_offsets.to(torch.int64).contiguous()
+
+    def mk() -> torch.Tensor:
+        return torch.empty(E, dtype=torch.int64, device=dev)
+
+    res = ScheduleResult(mk(), mk(), mk(), mk(), mk(), mk(), torch.empty(1, dtype=torch.int64, device=dev))
+    rc = _lib.load().dwdp_schedule(
+        counts.data_ptr(), offsets.data_ptr(), E, stream_count,
+        res.expert_queue.data_ptr(), res.expert_starts.data_ptr(), res.expert_ends.data_ptr(),
+        res.expert_counts.data_ptr(), res.execution_priority.data_ptr(),
+        res.stream_assignments.data_ptr(), res.num_active.data_ptr(), _stream(),
+    )
+    _lib.check(rc, "schedule")
+    return res
+
+
+# --------------------------------------------------------------------------- weights
+def packed_weight_bytes(rows: int, cols: int, num_mats: int, dtype: torch.dtype) -> int:
+    return int(_lib.load().dwdp_packed_weight_bytes(rows, cols, num_mats, dtype_code(dtype)))
+
+
+def packed_scale_floats(rows: int, cols: int, num_mats: int, scale_mode: int) -> int:
+    return int(_lib.load().dwdp_packed_scale_floats(rows, cols, num_mats, scale_mode))
+
+
+def pack_weights(
+    mats: list[torch.Tensor], dst_dtype: torch.dtype, scale_mode: int
+) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Quantise (fp8) or convert (bf16) one or two [R, C] projections into the
+    tiled store. Returns (tiles uint8, scales fp32 or None)."""
+    _require_cuda(*mats)
+    if not 1 <= len(mats) <= 2:
+        raise ValueError("pack_weights takes one or two matrices")
+    R, C = mats[0].shape
+    for m in mats:
+        if tuple(m.shape) != (R, C) or m.dtype != mats[0].dtype:
+            raise ValueError("packed matrices must share shape and dtype")
+    src = [m.contiguous() for m in mats]
+    dev = src[0].device
+    tiles = torch.empty(packed_weight_bytes(R, C, len(src), dst_dtype), dtype=torch.uint8, device=dev)
+    nsc = packed_scale_floats(R, C, len(src), scale_mode) if dst_dtype == torch.float8_e4m3fn else 0
+    scales = torch.empty(nsc, dtype=torch.float32, device=dev) if nsc else None
+    ptrs = (ctypes.c_void_p * 2)(*([m.data_ptr() for m in src] + [0] * (2 - len(src))))
+    rc = _lib.load().dwdp_pack_weights(
+        ctypes.cast(ptrs, ctypes.c_void_p), dtype_code(src[0].dtype), R, C, len(src),
+        dtype_code(dst_dtype), scale_mode, tiles.data_ptr(), _ptr(scales), _stream(),
+    )
+    _lib.check(rc, "pack_weights")
+    return tiles, scales
+
+
+def unpack_weights(
+    tiles: torch.Tensor, scales: torch.Tensor | None, rows: int, cols: int, num_mats: int,
+    dst_dtype: torch.dtype, scale_mode: int,
+) -> torch.Tensor:
+    """Dequantised fp32 view [num_mats, rows, cols] of a packed store (for checks)."""
+    _require_cuda(tiles, scales)
+    out = torch.empty(num_mats, rows, cols, dtype=torch.float32, device=tiles.device)
+    rc = _lib.load().dwdp_unpack_weights(
+        tiles.data_ptr(), _ptr(scales), rows, cols, num_mats, dtype_code(dst_dtype), scale_mode,
+        out.data_ptr(), _stream(),
+    )
+    _lib.check(rc, "unpack_weights")
+    return out
+
+
+# --------------------------------------------------------------------------- experts + merge
+def moe_workspace_bytes(num_tokens: int, top_k: int, num_experts: int, intermediate: int,
+                        shared_intermediate: int) -> int:
+    return int(_lib.load().dwdp_moe_workspace_bytes(num_tokens, top_k, num_experts, intermediate,
+                                                    shared_intermediate))
+
+
+def moe_experts(
+    routed: _lib.ExpertGroup,
+    shared: _lib.ExpertGroup | None,
+    packed_hidden: torch.Tensor,
+    hidden: torch.Tensor,
+    top_k: int,
+    counts: torch.Tensor,
+    offsets: torch.Tensor,
+    packed_weights: torch.Tensor,
+    shared_gate: torch.Tensor | None,
+    weighted_out: torch.Tensor,
+    shared_out: torch.Tensor | None,
+    workspace: torch.Tensor,
+    status: torch.Tensor | None = None,
+) -> None:
+    """Grouped tcgen05 expert GEMMs (gate/up + SwiGLU, down + routing weight)."""
+    _require_cuda(packed_hidden, hidden, counts, offsets, packed_weights, weighted_out, workspace)
+    if packed_weights.dtype != torch.float32:
+        raise ValueError("packed routing weights must be fp32 for the grouped GEMM")
+    T = hidden.shape[0]
+    rc = _lib.load().dwdp_moe_experts(
+        ctypes.byref(routed), ctypes.byref(shared) if shared is not None else None,
+        packed_hidden.data_ptr(), hidden.data_ptr(), T, top_k, counts.data_ptr(), offsets.data_ptr(),
+        packed_weights.data_ptr(), _ptr(shared_gate), weighted_out.data_ptr(), _ptr(shared_out),
+        workspace.data_ptr(), workspace.numel(), _ptr(status), _stream(),
+    )
+    _lib.check(rc, "moe_experts")
+
+
+def merge(
+    weighted: torch.Tensor,
+    inverse_permutation: torch.Tensor,
+    num_tokens: int,
+    top_k: int,
+    *,
+    shared_out: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+    out_dtype: torch.dtype = torch.bfloat16,
+) -> torch.Tensor:
+    """Deterministic token-major merge (DWDP/merger/kernels/reference.py:6-27)."""
+    _require_cuda(weighted, inverse_permutation, shared_out)
+    if weighted.dtype != torch.bfloat16:
+        raise ValueError("merge expects bf16 weighted rows")
+    H = weighted.shape[-1]
+    if out is None:
+        out = torch.empty(num_tokens, H, dtype=out_dtype, device=weighted.device)
+    rc = _lib.load().dwdp_merge(
+        weighted.data_ptr(), inverse_permutation.contiguous().data_ptr(), _ptr(shared_out), num_tokens,
+        top_k, H, out.data_ptr(), dtype_code(out.dtype), _stream(),
+    )
+    _lib.check(rc, "merge")
+    return out
