@@ -197,3 +197,14 @@ def rel_frobenius(a: torch.Tensor, b: torch.Tensor) -> float:
     a64, b64 = a.double(), b.double()
     den = b64.norm().item()
     return (a64 - b64).norm().item() / (den if den > 0 else 1.0)
+
+
+def quantize_activations_blockwise(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """[M, K] -> (e4m3 [M, K], fp32 scales [M, ceil(K/128)]), one scale per
+    (row, 128-column block) = max(amax, 1e-5) / 448 (DWDP/executor/fp8.py:86-115)."""
+    M, K = x.shape
+    kb = -(-K // 128)
+    work = torch.nn.functional.pad(x.float(), (0, kb * 128 - K)).view(M, kb, 128)
+    scales = work.abs().amax(dim=-1).clamp(min=1e-5) / FP8_E4M3_MAX
+    q = (work / scales.unsqueeze(-1)).view(M, kb * 128)[:, :K]
+    return q.to(torch.float8_e4m3fn), scales.contiguous()
