@@ -1,0 +1,376 @@
+"""MoE-layer throughput benchmark (Qwen1.5-MoE-A2.7B-shaped layer, synthetic inputs).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl ours|reference]
+
+One step = one full MoE-layer forward (router -> dispatch -> grouped expert
+GEMMs incl. the shared expert -> merge) over T tokens, replayed from a CUDA
+graph, with the weights (554 MB FP8) larger than L2 and L2 flushed before every
+timed step. Under torchrun each rank runs its own T tokens (weak scaling); the
+reported time is the max over ranks. Rank 0 prints one JSON line.
+
+``--impl reference`` times the reference algorithm's CPU path (the oracle
+restatement of the reference's PyTorch executor, all host threads) on the same
+workload and prints the same metric with ``"impl": "reference"``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-layer tokens/s (Qwen1.5-MoE-A2.7B shape)"
+QWEN = dict(H=2048, E=60, I=1408, K=4, Is=5632)
+DECODE_SWEEP = [1, 8, 32, 64]
+
+
+def _peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+# ----------------------------------------------------------------------------- setup
+def make_qwen_layer(pkg, device, seed: int = 1235):
+    """Random-init Qwen-shaped layer: router W ~ N(0, 1/H) (logits ~ N(0,1)),
+    experts ~ N(0, 0.02) quantised to FP8 E4M3 with per-output-channel scales,
+    shared expert Is=5632 with sigmoid gate g ~ N(0, 0.02)."""
+    H, E, I, K, Is = QWEN["H"], QWEN["E"], QWEN["I"], QWEN["K"], QWEN["Is"]
+    g = torch.Generator(device=device).manual_seed(seed)
+    wr = (torch.randn(E, H, generator=g, device=device) / H**0.5).bfloat16()
+    store = pkg.ExpertWeightStore(E, H, I, weight_dtype=torch.float8_e4m3fn,
+                                  scale_mode=pkg._lib.SCALE_CHANNEL, device=device)
+    for e in range(E):
+        gw = torch.randn(I, H, generator=g, device=device) * 0.02
+        uw = torch.randn(I, H, generator=g, device=device) * 0.02
+        dw = torch.randn(H, I, generator=g, device=device) * 0.02
+        store.load_expert(e, gw, uw, dw)
+    shared = pkg.ExpertWeightStore(1, H, Is, weight_dtype=torch.float8_e4m3fn,
+                                   scale_mode=pkg._lib.SCALE_CHANNEL, device=device)
+    shared.load_expert(0, torch.randn(Is, H, generator=g, device=device) * 0.02,
+                       torch.randn(Is, H, generator=g, device=device) * 0.02,
+                       torch.randn(H, Is, generator=g, device=device) * 0.02)
+    gate = (torch.randn(H, generator=g, device=device) * 0.02).bfloat16()
+    return pkg.MoELayer(wr, store, K, shared_expert=shared, shared_gate_weight=gate)
+
+
+def make_inputs(T: int, device, seed: int) -> torch.Tensor:
+    g = torch.Generator(device=device).manual_seed(seed)
+    return torch.randn(T, QWEN["H"], generator=g, device=device).bfloat16()
+
+
+class L2Flusher:
+    """Writes a buffer larger than L2 (126 MB) between timed steps."""
+
+    def __init__(self, device):
+        self.buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+
+    def __call__(self):
+        self.buf.fill_(1.0)
+
+
+def time_device(fn, steps: int, warmup: int, flush: L2Flusher) -> list[float]:
+    """Per-step CUDA-event times (ms) on the current stream, flush outside the events."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in evs:
+        flush()
+        a.record()
+        fn()
+        b.record()
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown," \
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
+             "clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+
+    def summary(self) -> dict:
+        rows = []
+        if self.path and os.path.exists(self.path):
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 8:
+                    rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        loaded = [s for s in sm if s > 0.5 * max(sm)] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[4:8]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": float(rows[0][2]),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------- our arm
+def expert_bytes(layer, counts: torch.Tensor, T: int) -> int:
+    """Algorithmic bytes of the grouped expert GEMMs: weights+scales of the active
+    experts and the shared expert, packed activations in, weighted rows out."""
+    active = int((counts > 0).sum().item())
+    H, K = layer.hidden_size, layer.top_k
+    b = active * layer.experts.nbytes_per_expert() + layer.shared_expert.nbytes_per_expert()
+    b += (T * K + T) * H * 2 * 2
+    return b
+
+
+def expert_flops(layer, T: int) -> int:
+    H, I, K, Is = layer.hidden_size, layer.experts.intermediate_size, layer.top_k, layer.shared_expert.intermediate_size
+    return 2 * T * K * 3 * H * I + 2 * T * 3 * H * Is
+
+
+def run_point(pkg, layer, T: int, steps: int, warmup: int, flush, device, rank: int, world: int):
+    from dwdp_b200 import ops
+
+    x = make_inputs(T, device, seed=4242 + 7919 * rank + T)
+    out = torch.empty(T, layer.hidden_size, dtype=torch.bfloat16, device=device)
+    ws = layer.workspace(T)
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            layer.run(x, ws, out)
+    torch.cuda.current_stream().wait_stream(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        layer.run(x, ws, out)
+    # expert GEMMs alone (plan + gate/up + down), inputs left in the workspace by the run above
+    g_exp = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_exp):
+        ops.moe_experts(layer._routed_group, layer._shared_group, ws.dispatch.packed_hidden, x, layer.top_k,
+                        ws.dispatch.expert_counts, ws.dispatch.expert_offsets,
+                        ws.dispatch.packed_routing_weights, ws.router.shared_gate, ws.weighted, ws.shared_out,
+                        ws.moe_ws, ws.status)
+    layer_ms = time_device(graph.replay, steps, warmup, flush)
+    exp_ms = time_device(g_exp.replay, steps, warmup, flush)
+    st = layer.read_status(T)
+    if st[0] != 0:
+        raise RuntimeError(f"device status {st}")
+    counts = ws.dispatch.expert_counts
+    return {
+        "T": T,
+        "layer_ms": layer_ms,
+        "experts_ms": exp_ms,
+        "bytes": expert_bytes(layer, counts, T),
+        "flops": expert_flops(layer, T),
+        "active_experts": int((counts > 0).sum().item()),
+        "graph": graph,
+        "x": x,
+        "out": out,
+    }
+
+
+def e2e_point(layer, T: int, steps: int, warmup: int, device, rank: int):
+    """Public-API forward with host buffers: pinned H2D of the inputs, forward,
+    D2H of the output, all inside the timed region of every step."""
+    x_host = make_inputs(T, device, seed=999 + rank).cpu().pin_memory()
+    y_host = torch.empty(T, layer.hidden_size, dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty(T, layer.hidden_size, dtype=torch.bfloat16, device=device)
+    out = torch.empty_like(x_dev)
+
+    def step():
+        x_dev.copy_(x_host, non_blocking=True)
+        layer.forward(x_dev, out=out)
+        y_host.copy_(out, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b), T * layer.hidden_size * 2, T * layer.hidden_size * 2
+
+
+# ----------------------------------------------------------------------------- CPU arm
+def cpu_layer_step(orc, x, router_w, gate_w, experts, shared, K):
+    logits = orc.router_logits(x, router_w)
+    _, idx, w = orc.topk_routing(logits, K)
+    sg = torch.sigmoid(x.float() @ gate_w.float())
+    return orc.moe_forward(x, idx, w, experts, shared=shared, shared_gate=sg)
+
+
+def cpu_baseline(pkg, layer, T_sample: int, iters: int, device) -> dict:
+    """The reference algorithm's CPU path (oracle port: PyTorch executor loop,
+    counting-scatter dispatch, index_add merge) timed on the host cores."""
+    from oracle import moe_oracle as orc
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    experts = [tuple(t.cpu() for t in layer.experts.dequantized(e)) for e in range(layer.num_experts)]
+    shared = tuple(t.cpu() for t in layer.shared_expert.dequantized(0))
+    x = make_inputs(T_sample, device, seed=31337).float().cpu()
+    rw, gw = layer.router_weight.cpu(), layer.shared_gate_weight.cpu()
+    cpu_layer_step(orc, x, rw, gw, experts, shared, layer.top_k)  # warm-up
+    times = []
+    for _ in range(iters):
+        t0 = time.perf_counter()
+        cpu_layer_step(orc, x, rw, gw, experts, shared, layer.top_k)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    try:
+        model = next(l.split(":", 1)[1].strip() for l in open("/proc/cpuinfo") if l.startswith("model name"))
+    except (OSError, StopIteration):
+        model = "unknown"
+    return {"value": T_sample / med, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{T_sample} tokens of the same Qwen-shaped layer, fp32 torch CPU, median of {iters}; "
+                      f"CPU {model}", "seconds_per_step": med}
+
+
+# ----------------------------------------------------------------------------- main
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--tokens", type=int, default=4096)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--cpu-sample", type=int, default=256)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import __graft_entry__
+
+    pkg = __graft_entry__.load_package()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=device)
+    T = args.tokens
+    config = {"workload": f"qwen1.5-moe-a2.7b MoE layer, prefill T={T} per GPU", "model": "Qwen1.5-MoE-A2.7B (shape)",
+              "tokens_per_gpu": T, "hidden": QWEN["H"], "experts": QWEN["E"], "top_k": QWEN["K"],
+              "moe_intermediate": QWEN["I"], "shared_intermediate": QWEN["Is"],
+              "weights": "fp8 e4m3, per-output-channel fp32 scales", "activations": "bf16",
+              "l2": "flushed (256 MB write) before every timed step; weights 554 MB > L2",
+              "parallelism": f"dp{world} (tokens per GPU fixed; experts replicated)"}
+
+    if args.impl == "reference":
+        if rank == 0:
+            layer = make_qwen_layer(pkg, device)
+            cb = cpu_baseline(pkg, layer, args.cpu_sample, max(args.steps // 5, 2), device)
+            print(json.dumps({
+                "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s",
+                "n_gpus": args.gpus, "steps": max(args.steps // 5, 2), "warmup": 1,
+                "ms_per_step": cb["seconds_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+                "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            }), flush=True)
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        return
+
+    layer = make_qwen_layer(pkg, device)
+    flush = L2Flusher(device)
+    peaks = _peaks()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        main_pt = run_point(pkg, layer, T, args.steps, args.warmup, flush, device, rank, world)
+    total_ms = sum(main_pt["layer_ms"])
+    if world > 1:
+        t = torch.tensor([total_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    value = world * T / (ms_per_step / 1e3)
+    exp_ms = statistics.mean(main_pt["experts_ms"])
+    tensor_bound = T >= 1024
+    if tensor_bound:
+        ach = main_pt["flops"] / (exp_ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": ach / peaks["bf16_tflops"], "traffic": None,
+                "kernel": "grouped expert GEMMs (plan + gate/up + down launches), bf16 MMA on fp8 weights",
+                "peak_source": peaks["source"] + " bf16 dense (burst)"}
+    else:
+        ach = main_pt["bytes"] / (exp_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": ach / peaks["hbm_gbs"], "traffic": None,
+                "kernel": "grouped expert GEMMs (plan + gate/up + down launches)",
+                "peak_source": peaks["source"] + " HBM copy"}
+
+    sweep = []
+    if not args.no_sweep:
+        for Ts in DECODE_SWEEP:
+            pt = run_point(pkg, layer, Ts, args.steps, args.warmup, flush, device, rank, world)
+            lm, em = statistics.mean(pt["layer_ms"]), statistics.mean(pt["experts_ms"])
+            gbs = pt["bytes"] / (em / 1e3) / 1e9
+            sweep.append({"T": Ts, "layer_us": lm * 1e3, "tokens_per_s": Ts / (lm / 1e3),
+                          "experts_us": em * 1e3, "active_experts": pt["active_experts"],
+                          "expert_bytes": pt["bytes"], "hbm_gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"]})
+        sweep.append({"T": T, "layer_us": ms_per_step * 1e3, "tokens_per_s": T / (ms_per_step / 1e3),
+                      "experts_us": exp_ms * 1e3, "tflops": main_pt["flops"] / (exp_ms / 1e3) / 1e12})
+
+    e2e_ms, h2d, d2h = e2e_point(layer, T, args.steps, args.warmup, device, rank)
+    e2e_val = world * T / (e2e_ms / args.steps / 1e3)
+    cb = None
+    if rank == 0 and world == 1:
+        cb = cpu_baseline(pkg, layer, args.cpu_sample, 3, device)
+        cb = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config,
+            "roofline": roof, "cpu_baseline": cb, "clocks": clocks.summary(),
+            "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": 8 * args.steps, "sweep": sweep,
+        }), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
