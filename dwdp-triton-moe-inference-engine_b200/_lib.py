@@ -94,8 +94,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          c_void_p, c_void_p],
     ),
     "dwdp_merge": (
-        c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p, c_int, c_void_p]
+        c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_void_p, c_int, c_void_p]
     ),
+    "dwdp_moe_shared_parts": (c_int, [c_int64, c_int]),
 }
 
 _lib = None

@@ -24,8 +24,8 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group*, const dwdp_expe
                                        const void*, const void*, int64_t, int, const int64_t*,
                                        const int64_t*, const float*, const float*, void*, void*,
                                        void*, size_t, int*, cudaStream_t);
-extern "C" int dwdp_merge_launch(const void*, const int64_t*, const void*, int64_t, int, int, void*,
-                                 int, int*, cudaStream_t);
+extern "C" int dwdp_merge_launch(const void*, const int64_t*, const void*, int, int64_t, int, int,
+                                 void*, int, int*, cudaStream_t);
 
 namespace {
 
@@ -185,13 +185,16 @@ extern "C" int dwdp_moe_experts(const dwdp_expert_group* routed, const dwdp_expe
                "moe_experts");
 }
 
-extern "C" int dwdp_merge(const void* weighted, const int64_t* inv, const void* shared_out, int64_t num_tokens,
-                          int top_k, int hidden_size, void* out, int out_dtype, void* stream) {
+extern "C" int dwdp_merge(const void* weighted, const int64_t* inv, const void* shared_out, int shared_parts,
+                          int64_t num_tokens, int top_k, int hidden_size, void* out, int out_dtype,
+                          void* stream) {
   g_last_error.clear();
   if (top_k <= 0 || top_k > 16) return fail(DWDP_ERR_INVALID_ARGUMENT, "merge: top_k must be in [1, 16]");
   if (hidden_size <= 0 || hidden_size % 8)
     return fail(DWDP_ERR_INVALID_ARGUMENT, "merge: hidden_size must be a positive multiple of 8");
-  return check(dwdp_merge_launch(weighted, inv, shared_out, num_tokens, top_k, hidden_size, out, out_dtype,
+  if (shared_out != nullptr && (shared_parts < 1 || shared_parts > 64))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "merge: shared_parts must be in [1, 64]");
+  return check(dwdp_merge_launch(weighted, inv, shared_out, shared_parts, num_tokens, top_k, hidden_size, out, out_dtype,
                                  nullptr, as_stream(stream)),
                "merge");
 }

@@ -5,7 +5,8 @@
 //
 // Each token's K rows are found through inv[t*K + k] (the destination of
 // assignment (t, k)) and summed in ascending row order, which is the order the
-// CPU index_add_ visits them. The optional shared-expert row is added last
+// CPU index_add_ visits them. The optional shared-expert rows (the K-split
+// partials of the shared down projection, summed in order) are added last
 // (DWDP/adapters/qwen15_moe.py:302-319 adds it after the merger). fp32
 // accumulation, 16-byte vector loads; one CTA per token, HBM-bound.
 #include "common.cuh"
@@ -15,7 +16,8 @@ namespace dwdp {
 template <typename TOut>
 __global__ void __launch_bounds__(256)
 merge_kernel(const __nv_bfloat16* __restrict__ weighted, const int64_t* __restrict__ inv,
-             const __nv_bfloat16* __restrict__ shared_out, int64_t T, int K, int H, int64_t nrows,
+             const __nv_bfloat16* __restrict__ shared_out, int shared_parts, int64_t T, int K, int H,
+             int64_t nrows,
              TOut* __restrict__ out, DeviceStatus* st) {
   const int64_t t = blockIdx.x;
   int64_t rows[16];
@@ -42,8 +44,8 @@ merge_kernel(const __nv_bfloat16* __restrict__ weighted, const int64_t* __restri
         acc[2 * q + 1] += f.y;
       }
     }
-    if (shared_out != nullptr) {
-      const uint4 v = *reinterpret_cast<const uint4*>(shared_out + t * H + c);
+    for (int sp = 0; sp < shared_parts; ++sp) {
+      const uint4 v = *reinterpret_cast<const uint4*>(shared_out + ((int64_t)sp * T + t) * H + c);
       const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -71,19 +73,21 @@ merge_kernel(const __nv_bfloat16* __restrict__ weighted, const int64_t* __restri
 using namespace dwdp;
 
 extern "C" int dwdp_merge_launch(const void* weighted, const int64_t* inv, const void* shared_out,
-                                 int64_t T, int K, int H, void* out, int out_dtype, int* status,
+                                 int shared_parts, int64_t T, int K, int H, void* out, int out_dtype,
+                                 int* status,
                                  cudaStream_t stream) {
   if (K <= 0 || K > 16 || (H & 7) != 0 || T < 0) return DWDP_ERR_INVALID_ARGUMENT;
   if (T == 0) return DWDP_OK;
+  if (shared_out == nullptr) shared_parts = 0;
   DeviceStatus* st = reinterpret_cast<DeviceStatus*>(status);
   const int threads = H / 8 >= 256 ? 256 : ((H / 8 + 31) / 32) * 32;
   if (out_dtype == DWDP_DTYPE_BF16) {
     merge_kernel<__nv_bfloat16><<<(unsigned)T, threads, 0, stream>>>(
-        (const __nv_bfloat16*)weighted, inv, (const __nv_bfloat16*)shared_out, T, K, H, T * K,
+        (const __nv_bfloat16*)weighted, inv, (const __nv_bfloat16*)shared_out, shared_parts, T, K, H, T * K,
         (__nv_bfloat16*)out, st);
   } else if (out_dtype == DWDP_DTYPE_F32) {
     merge_kernel<float><<<(unsigned)T, threads, 0, stream>>>(
-        (const __nv_bfloat16*)weighted, inv, (const __nv_bfloat16*)shared_out, T, K, H, T * K,
+        (const __nv_bfloat16*)weighted, inv, (const __nv_bfloat16*)shared_out, shared_parts, T, K, H, T * K,
         (float*)out, st);
   } else {
     return DWDP_ERR_UNSUPPORTED;

@@ -43,12 +43,14 @@ constexpr int kConvTileBytes = BM * 128;   // bf16 weight tile 128 x 64
 constexpr int kFp8TileBytes = BM * BK;     // fp8 weight tile 128 x 64
 
 struct WorkItem {
-  int group;   // 0 routed, 1 shared
-  int expert;  // expert index inside the group
-  int rb;      // 128-row weight block
-  int row0;    // first activation row of the tile
-  int nrows;   // rows in this tile (<= BN_MAX)
-  int pad0, pad1, pad2;
+  int group;     // 0 routed, 1 shared
+  int expert;    // expert index inside the group
+  int rb;        // 128-row weight block
+  int row0;      // first activation row of the tile
+  int nrows;     // rows in this tile (<= BN_MAX)
+  int kb_begin;  // first / one-past-last 64-wide K step of this item (split K)
+  int kb_end;
+  int part;      // K-split index: output goes to out + part * part_stride
 };
 
 struct GroupParams {
@@ -61,6 +63,8 @@ struct GroupParams {
   int R;                   // output rows of the projection (= out leading dim)
   int scale_mode;
   int enabled;
+  int box_rows;            // activation rows per TMA box (multiple of 16, <= BN_MAX)
+  long long part_stride;   // elements between K-split partial outputs
 };
 
 struct GemmParams {
@@ -90,6 +94,7 @@ struct Cfg {
 
 // 16 e4m3 values of row r, elements [sub*16, sub*16+16) -> 32 bytes of bf16
 // written to their 128B-swizzled positions.
+template <bool SCALED>
 __device__ __forceinline__ void convert_chunk(const uint8_t* src16, uint8_t* conv_tile, int r, int sub,
                                               float s) {
   const uint4 raw = *reinterpret_cast<const uint4*>(src16);
@@ -102,7 +107,7 @@ __device__ __forceinline__ void convert_chunk(const uint8_t* src16, uint8_t* con
       const __nv_fp8x2_storage_t pair = (__nv_fp8x2_storage_t)((wv[q] >> (16 * hlf)) & 0xFFFFu);
       const __half2_raw h2 = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
       const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
-      const __nv_bfloat162 b = __floats2bfloat162_rn(f.x * s, f.y * s);
+      const __nv_bfloat162 b = SCALED ? __floats2bfloat162_rn(f.x * s, f.y * s) : __floats2bfloat162_rn(f.x, f.y);
       outw[q * 2 + hlf] = *reinterpret_cast<const uint32_t*>(&b);
     }
   }
@@ -172,10 +177,11 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
         const GroupParams& g = p.g[wi.group];
         const int KB = g.K / BK;
         const uint8_t* wbase = reinterpret_cast<const uint8_t*>(g.w[wi.expert]);
-        for (int kb = 0; kb < KB; ++kb, ++it) {
+        const uint32_t b_bytes = (uint32_t)g.box_rows * 128u;
+        for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
           const int s = it % C::S;
           if (!mbar_wait(&ld_empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 1)) break;
-          mbar_arrive_expect_tx(&ld_full[s], C::W_STAGE_BYTES + kBTileBytes);
+          mbar_arrive_expect_tx(&ld_full[s], C::W_STAGE_BYTES + b_bytes);
           const size_t woff = ((size_t)wi.rb * KB + kb) * C::W_STAGE_BYTES;
           bulk_g2s(sW + s * C::W_STAGE_BYTES, wbase + woff, C::W_STAGE_BYTES, &ld_full[s]);
           tma_load_2d(sB + s * kBTileBytes, &g.tmap_b, kb * BK, wi.row0, &ld_full[s]);
@@ -189,8 +195,6 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
       int li = 0;
       for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++li) {
         const WorkItem wi = p.items[item];
-        const GroupParams& g = p.g[wi.group];
-        const int KB = g.K / BK;
         const int a = li & 1;
         if (!mbar_wait(&acc_empty[a], ((li >> 1) & 1) ^ 1, &s_abort, st, 2)) break;
         tc_fence_after();
@@ -198,7 +202,7 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
         const uint32_t idesc = idesc_bf16(BM, n_mma);
         const uint32_t d_base = tmem_base + a * C::ACC_STRIDE;
         bool ok = true;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
+        for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
           const int s = it % C::S;
           if (!mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 3)) { ok = false; break; }
           const uint8_t* wtile;
@@ -218,7 +222,8 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
 #pragma unroll
             for (int kk = 0; kk < BK / 16; ++kk) {
               mma_bf16_ss(d_base + m * BN_MAX, smem_desc_sw128(a_addr + kk * 32),
-                          smem_desc_sw128(b_addr + kk * 32), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                          smem_desc_sw128(b_addr + kk * 32), idesc,
+                          (kb > wi.kb_begin || kk > 0) ? 1u : 0u);
             }
           }
           mma_commit(&ld_empty[s]);
@@ -244,7 +249,14 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
       tc_fence_after();
       const uint32_t t_acc = tmem_base + a * C::ACC_STRIDE + ((uint32_t)(quad * 32) << 16);
       const int feat = wi.rb * BM + lrow;
-      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out);
+      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)wi.part * g.part_stride;
+      // per-output-channel weight scales are exact per-thread constants here
+      float s0 = 1.0f, s1 = 1.0f;
+      if (WFP8 && g.scale_mode == DWDP_SCALE_CHANNEL) {
+        const float* sc = g.s[wi.expert];
+        s0 = sc[feat];
+        if (MODE == 0) s1 = sc[g.R + feat];
+      }
       for (int c0 = 0; c0 < wi.nrows; c0 += 16) {
         if constexpr (MODE == 0) {
           float gv[16], uv[16];
@@ -255,7 +267,7 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
           for (int j = 0; j < 16; ++j) {
             const int col = c0 + j;
             if (col < wi.nrows) {
-              const float h = silu(gv[j]) * uv[j];
+              const float h = silu(gv[j] * s0) * (uv[j] * s1);
               out[(size_t)(wi.row0 + col) * g.R + feat] = __float2bfloat16_rn(h);
             }
           }
@@ -269,7 +281,7 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
             if (col < wi.nrows) {
               const int row = wi.row0 + col;
               const float sc = g.row_scale != nullptr ? g.row_scale[row] : 1.0f;
-              out[(size_t)row * g.R + feat] = __float2bfloat16_rn(yv[j] * sc);
+              out[(size_t)row * g.R + feat] = __float2bfloat16_rn(yv[j] * s0 * sc);
             }
           }
         }
@@ -279,17 +291,24 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
     }
   } else if constexpr (WFP8) {
     // ------------------------------------------------------------ converter (fp8 -> bf16)
+    // CHANNEL scales are applied in the epilogue, so the conversion is exact
+    // (e4m3 values are representable in bf16); BLOCK128 scales vary with K and
+    // are folded in here with one rounding.
     const int ct = threadIdx.x - 6 * 32;  // 0..255
     uint32_t it = 0, cit = 0;
     for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
       const WorkItem wi = p.items[item];
       const GroupParams& g = p.g[wi.group];
-      const int KB = g.K / BK;
+      const bool block_scaled = g.scale_mode == DWDP_SCALE_BLOCK128;
       const float* sc = g.s[wi.expert];
       bool ok = true;
-      for (int kb = 0; kb < KB; ++kb, ++it, ++cit) {
+      for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it, ++cit) {
         const int s = it % C::S;
         const int c = cit % 2;
+        float sblk[C::NMAT];
+#pragma unroll
+        for (int m = 0; m < C::NMAT; ++m)
+          sblk[m] = block_scaled ? sc[((size_t)m * (g.R / 128) + wi.rb) * (g.K / 128) + (kb >> 1)] : 1.0f;
         if (!mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 6)) { ok = false; break; }
         if (!mbar_wait(&cv_empty[c], ((cit / 2) & 1) ^ 1, &s_abort, st, 7)) { ok = false; break; }
         const uint8_t* raw = sW + s * C::W_STAGE_BYTES;
@@ -300,13 +319,10 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
           const int m = q / (kFp8TileBytes / 16);
           const int rem = q % (kFp8TileBytes / 16);
           const int r = rem >> 2, sub = rem & 3;
-          float s_val;
-          if (g.scale_mode == DWDP_SCALE_CHANNEL) {
-            s_val = sc[(size_t)m * g.R + wi.rb * BM + r];
-          } else {
-            s_val = sc[((size_t)m * (g.R / 128) + wi.rb) * (g.K / 128) + (kb >> 1)];
-          }
-          convert_chunk(raw + m * kFp8TileBytes + r * BK + sub * 16, conv + m * kConvTileBytes, r, sub, s_val);
+          if (block_scaled)
+            convert_chunk<true>(raw + m * kFp8TileBytes + r * BK + sub * 16, conv + m * kConvTileBytes, r, sub, sblk[m]);
+          else
+            convert_chunk<false>(raw + m * kFp8TileBytes + r * BK + sub * 16, conv + m * kConvTileBytes, r, sub, 1.0f);
         }
         fence_proxy_async_smem();
         named_bar_sync(1, C::CONV_THREADS);
@@ -334,39 +350,54 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
 // ordered (expert, weight block, token tile) so CTAs running at the same time
 // stream the same weight blocks through L2.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024)
-plan_kernel(const int64_t* __restrict__ counts, const int64_t* __restrict__ offsets, int E,
-            int T, int has_shared, int rb_gu_r, int rb_dn_r, int rb_gu_s, int rb_dn_s,
-            WorkItem* __restrict__ items_gu, WorkItem* __restrict__ items_dn,
-            int* __restrict__ n_items, int cap_gu, int cap_dn, DeviceStatus* st) {
+struct PlanParams {
+  const int64_t* counts;
+  const int64_t* offsets;
+  int E, T, has_shared;
+  int rb_gu_r, rb_dn_r, rb_gu_s, rb_dn_s;  // 128-row weight blocks per projection
+  int kb_gu, kb_dn_r, kb_dn_s;              // 64-wide K steps per projection
+  int sdn_parts;                            // K splits of the shared down projection
+  WorkItem* items_gu;
+  WorkItem* items_dn;
+  int* n_items;
+  int cap_gu, cap_dn;
+  DeviceStatus* st;
+};
+
+__global__ void __launch_bounds__(1024) plan_kernel(const PlanParams pp) {
   __shared__ int s_scan[1024];
   __shared__ int s_total;
   const int tid = threadIdx.x;
+  const int T = pp.T;
   int n_sh_tiles = 0, bn_s = 0;
-  if (has_shared && T > 0) {
+  if (pp.has_shared && T > 0) {
     n_sh_tiles = (T + BN_MAX - 1) / BN_MAX;
     bn_s = (((T + n_sh_tiles - 1) / n_sh_tiles) + 15) & ~15;
   }
-  const int base_gu = n_sh_tiles * rb_gu_s;
-  const int base_dn = n_sh_tiles * rb_dn_s;
+  const int base_gu = n_sh_tiles * pp.rb_gu_s;
+  const int base_dn = n_sh_tiles * pp.rb_dn_s * pp.sdn_parts;
   for (int i = tid; i < base_gu; i += blockDim.x) {
     const int rb = i / n_sh_tiles, j = i % n_sh_tiles;
     const int row0 = j * bn_s;
-    if (i < cap_gu) items_gu[i] = WorkItem{1, 0, rb, row0, min(bn_s, T - row0), 0, 0, 0};
+    if (i < pp.cap_gu) pp.items_gu[i] = WorkItem{1, 0, rb, row0, min(bn_s, T - row0), 0, pp.kb_gu, 0};
   }
+  const int kb_part = pp.sdn_parts > 0 ? pp.kb_dn_s / pp.sdn_parts : 0;
   for (int i = tid; i < base_dn; i += blockDim.x) {
-    const int rb = i / n_sh_tiles, j = i % n_sh_tiles;
+    const int part = i / (n_sh_tiles * pp.rb_dn_s);
+    const int rem = i % (n_sh_tiles * pp.rb_dn_s);
+    const int rb = rem / n_sh_tiles, j = rem % n_sh_tiles;
     const int row0 = j * bn_s;
-    if (i < cap_dn) items_dn[i] = WorkItem{1, 0, rb, row0, min(bn_s, T - row0), 0, 0, 0};
+    if (i < pp.cap_dn)
+      pp.items_dn[i] = WorkItem{1, 0, rb, row0, min(bn_s, T - row0), part * kb_part, (part + 1) * kb_part, part};
   }
   int carry = 0;
-  for (int e0 = 0; e0 < E; e0 += 1024) {
+  for (int e0 = 0; e0 < pp.E; e0 += 1024) {
     const int e = e0 + tid;
     int nt = 0, cnt = 0, bn = 0;
     int64_t off = 0;
-    if (e < E) {
-      cnt = (int)counts[e];
-      off = offsets[e];
+    if (e < pp.E) {
+      cnt = (int)pp.counts[e];
+      off = pp.offsets[e];
       if (cnt > 0) {
         nt = (cnt + BN_MAX - 1) / BN_MAX;
         bn = (((cnt + nt - 1) / nt) + 15) & ~15;
@@ -381,18 +412,18 @@ plan_kernel(const int64_t* __restrict__ counts, const int64_t* __restrict__ offs
       __syncthreads();
     }
     const int excl = carry + s_scan[tid] - nt;
-    if (e < E && nt > 0) {
-      for (int rb = 0; rb < rb_gu_r; ++rb)
+    if (e < pp.E && nt > 0) {
+      for (int rb = 0; rb < pp.rb_gu_r; ++rb)
         for (int j = 0; j < nt; ++j) {
-          const int idx = base_gu + excl * rb_gu_r + rb * nt + j;
+          const int idx = base_gu + excl * pp.rb_gu_r + rb * nt + j;
           const int row0 = (int)off + j * bn;
-          if (idx < cap_gu) items_gu[idx] = WorkItem{0, e, rb, row0, min(bn, cnt - j * bn), 0, 0, 0};
+          if (idx < pp.cap_gu) pp.items_gu[idx] = WorkItem{0, e, rb, row0, min(bn, cnt - j * bn), 0, pp.kb_gu, 0};
         }
-      for (int rb = 0; rb < rb_dn_r; ++rb)
+      for (int rb = 0; rb < pp.rb_dn_r; ++rb)
         for (int j = 0; j < nt; ++j) {
-          const int idx = base_dn + excl * rb_dn_r + rb * nt + j;
+          const int idx = base_dn + excl * pp.rb_dn_r + rb * nt + j;
           const int row0 = (int)off + j * bn;
-          if (idx < cap_dn) items_dn[idx] = WorkItem{0, e, rb, row0, min(bn, cnt - j * bn), 0, 0, 0};
+          if (idx < pp.cap_dn) pp.items_dn[idx] = WorkItem{0, e, rb, row0, min(bn, cnt - j * bn), 0, pp.kb_dn_r, 0};
         }
     }
     if (tid == 1023) s_total = carry + s_scan[1023];
@@ -401,15 +432,15 @@ plan_kernel(const int64_t* __restrict__ counts, const int64_t* __restrict__ offs
     __syncthreads();
   }
   if (tid == 0) {
-    const int ngu = base_gu + carry * rb_gu_r;
-    const int ndn = base_dn + carry * rb_dn_r;
-    if (ngu > cap_gu || ndn > cap_dn) {
-      record_error(st, DWDP_ERR_CAPACITY, 200, ngu);
-      n_items[0] = 0;
-      n_items[1] = 0;
+    const int ngu = base_gu + carry * pp.rb_gu_r;
+    const int ndn = base_dn + carry * pp.rb_dn_r;
+    if (ngu > pp.cap_gu || ndn > pp.cap_dn) {
+      record_error(pp.st, DWDP_ERR_CAPACITY, 200, ngu);
+      pp.n_items[0] = 0;
+      pp.n_items[1] = 0;
     } else {
-      n_items[0] = ngu;
-      n_items[1] = ndn;
+      pp.n_items[0] = ngu;
+      pp.n_items[1] = ndn;
     }
   }
 }
@@ -433,12 +464,12 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 }
 
 // 2-D bf16 tensor map over a row-major [rows, cols] matrix, box {64, BN_MAX}, 128B swizzle.
-bool make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols) {
+bool make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows) {
   auto enc = get_encode_fn();
   if (enc == nullptr || rows <= 0) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BN_MAX};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -447,6 +478,24 @@ bool make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols) {
 }
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// K splits of the shared expert's down projection. Its K (= shared intermediate
+// size) is several times the routed one, so at decode sizes its few long tiles
+// would be the critical path; splitting K yields partial rows that the merge
+// sums. Prefill has enough tiles to balance without it.
+int shared_down_parts(int64_t T, int Is) {
+  if (Is <= 0) return 0;
+  const int kb = Is / BK;
+  if (T > 256) return 1;
+  for (int parts = 8; parts > 1; --parts)
+    if (kb % parts == 0 && kb / parts >= 16) return parts;
+  return 1;
+}
+
+inline int box_rows_for(int64_t max_rows) {
+  const int64_t r = ((max_rows + 15) / 16) * 16;
+  return (int)std::min<int64_t>(BN_MAX, std::max<int64_t>(16, r));
+}
 
 struct WsLayout {
   size_t h_routed, h_shared, items_gu, items_dn, n_items, total;
@@ -459,7 +508,7 @@ WsLayout ws_layout(int64_t T, int K, int E, int I, int H, int Is) {
   const int64_t tiles_s = Is > 0 ? (T + BN_MAX - 1) / BN_MAX : 0;
   WsLayout w{};
   w.cap_gu = (int)(tiles_r * (I / BM) + tiles_s * (Is / BM));
-  w.cap_dn = (int)((tiles_r + tiles_s) * (H / BM));
+  w.cap_dn = (int)((tiles_r + tiles_s * shared_down_parts(T, Is)) * (H / BM));
   size_t o = 0;
   w.h_routed = o; o = align256(o + (size_t)N * I * 2);
   w.h_shared = o; o = align256(o + (size_t)T * (Is > 0 ? Is : 0) * 2);
@@ -493,6 +542,10 @@ extern "C" int dwdp_device_sm_count(void) {
   return g_num_sms;
 }
 
+extern "C" int dwdp_moe_shared_parts(int64_t num_tokens, int shared_intermediate_size) {
+  return shared_down_parts(num_tokens, shared_intermediate_size);
+}
+
 extern "C" size_t dwdp_moe_workspace_bytes_impl(int64_t T, int K, int E, int H, int I, int Is) {
   return ws_layout(T, K, E, I, H, Is).total;
 }
@@ -522,33 +575,43 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   DeviceStatus* st = reinterpret_cast<DeviceStatus*>(status);
   const int has_shared = shared != nullptr ? 1 : 0;
 
-  plan_kernel<<<1, 1024, 0, stream>>>(counts, offsets, E, (int)T, has_shared, I / BM, H / BM,
-                                      has_shared ? Is / BM : 0, has_shared ? H / BM : 0, items_gu,
-                                      items_dn, n_items, L.cap_gu, L.cap_dn, st);
+  const int parts = shared_down_parts(T, Is);
+  PlanParams pp{};
+  pp.counts = counts; pp.offsets = offsets; pp.E = E; pp.T = (int)T; pp.has_shared = has_shared;
+  pp.rb_gu_r = I / BM; pp.rb_dn_r = H / BM;
+  pp.rb_gu_s = has_shared ? Is / BM : 0; pp.rb_dn_s = has_shared ? H / BM : 0;
+  pp.kb_gu = H / BK; pp.kb_dn_r = I / BK; pp.kb_dn_s = has_shared ? Is / BK : 0;
+  pp.sdn_parts = has_shared ? parts : 0;
+  pp.items_gu = items_gu; pp.items_dn = items_dn; pp.n_items = n_items;
+  pp.cap_gu = L.cap_gu; pp.cap_dn = L.cap_dn; pp.st = st;
+  plan_kernel<<<1, 1024, 0, stream>>>(pp);
   if (cudaGetLastError() != cudaSuccess) return DWDP_ERR_CUDA;
 
+  // routed rows per expert tile <= min(T, BN_MAX); shared tiles <= min(T, BN_MAX)
+  const int box = box_rows_for(T);
   GemmParams gu{}, dn{};
   gu.g[0].enabled = N > 0;
-  if (N > 0 && !make_tmap(&gu.g[0].tmap_b, packed_hidden, N, H)) return DWDP_ERR_CUDA;
+  if (N > 0 && !make_tmap(&gu.g[0].tmap_b, packed_hidden, N, H, box)) return DWDP_ERR_CUDA;
   gu.g[0].w = routed->w13; gu.g[0].s = routed->s13; gu.g[0].out = h_r; gu.g[0].row_scale = nullptr;
-  gu.g[0].K = H; gu.g[0].R = I; gu.g[0].scale_mode = routed->scale_mode;
+  gu.g[0].K = H; gu.g[0].R = I; gu.g[0].scale_mode = routed->scale_mode; gu.g[0].box_rows = box;
   gu.g[1].enabled = has_shared;
   if (has_shared) {
-    if (!make_tmap(&gu.g[1].tmap_b, hidden, T, H)) return DWDP_ERR_CUDA;
+    if (!make_tmap(&gu.g[1].tmap_b, hidden, T, H, box)) return DWDP_ERR_CUDA;
     gu.g[1].w = shared->w13; gu.g[1].s = shared->s13; gu.g[1].out = h_s; gu.g[1].row_scale = nullptr;
-    gu.g[1].K = H; gu.g[1].R = Is; gu.g[1].scale_mode = shared->scale_mode;
+    gu.g[1].K = H; gu.g[1].R = Is; gu.g[1].scale_mode = shared->scale_mode; gu.g[1].box_rows = box;
   }
   gu.items = items_gu; gu.n_items = n_items; gu.st = st;
 
   dn.g[0].enabled = N > 0;
-  if (N > 0 && !make_tmap(&dn.g[0].tmap_b, h_r, N, I)) return DWDP_ERR_CUDA;
-  dn.g[0].w = routed->w2; dn.g[0].s = routed->s2; dn.g[0].out = weighted_out;
+  if (N > 0 && !make_tmap(&dn.g[0].tmap_b, h_r, N, I, box)) return DWDP_ERR_CUDA;
+  dn.g[0].w = routed->w2; dn.g[0].s = routed->s2; dn.g[0].out = weighted_out; dn.g[0].box_rows = box;
   dn.g[0].row_scale = packed_weights; dn.g[0].K = I; dn.g[0].R = H; dn.g[0].scale_mode = routed->scale_mode;
   dn.g[1].enabled = has_shared;
   if (has_shared) {
-    if (!make_tmap(&dn.g[1].tmap_b, h_s, T, Is)) return DWDP_ERR_CUDA;
-    dn.g[1].w = shared->w2; dn.g[1].s = shared->s2; dn.g[1].out = shared_out;
+    if (!make_tmap(&dn.g[1].tmap_b, h_s, T, Is, box)) return DWDP_ERR_CUDA;
+    dn.g[1].w = shared->w2; dn.g[1].s = shared->s2; dn.g[1].out = shared_out; dn.g[1].box_rows = box;
     dn.g[1].row_scale = shared_gate; dn.g[1].K = Is; dn.g[1].R = H; dn.g[1].scale_mode = shared->scale_mode;
+    dn.g[1].part_stride = (long long)T * H;
   }
   dn.items = items_dn; dn.n_items = n_items + 1; dn.st = st;
 

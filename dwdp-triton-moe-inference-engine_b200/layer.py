@@ -28,6 +28,7 @@ class LayerWorkspace:
     dispatch_scratch: torch.Tensor
     weighted: torch.Tensor
     shared_out: torch.Tensor | None
+    shared_parts: int
     moe_ws: torch.Tensor
     status: torch.Tensor
 
@@ -105,13 +106,15 @@ class MoELayer:
             packed_hidden=torch.empty(N, H, dtype=torch.bfloat16, device=dev),
         )
         Is = self.shared_expert.intermediate_size if has_shared else 0
+        parts = ops.moe_shared_parts(T, Is) if has_shared else 0
         ws = LayerWorkspace(
             num_tokens=T,
             router=router,
             dispatch=disp,
             dispatch_scratch=torch.empty(ops.dispatch_scratch_bytes(T, K, E), dtype=torch.uint8, device=dev),
             weighted=torch.empty(N, H, dtype=torch.bfloat16, device=dev),
-            shared_out=torch.empty(T, H, dtype=torch.bfloat16, device=dev) if has_shared else None,
+            shared_out=torch.empty(parts, T, H, dtype=torch.bfloat16, device=dev) if has_shared else None,
+            shared_parts=parts,
             moe_ws=torch.empty(
                 ops.moe_workspace_bytes(T, K, E, self.experts.intermediate_size, Is),
                 dtype=torch.uint8, device=dev,
@@ -160,7 +163,8 @@ class MoELayer:
             ws.dispatch.expert_counts, ws.dispatch.expert_offsets, ws.dispatch.packed_routing_weights,
             ws.router.shared_gate, ws.weighted, ws.shared_out, ws.moe_ws, ws.status,
         )
-        ops.merge(ws.weighted, ws.dispatch.inverse_permutation, T, K, shared_out=ws.shared_out, out=out)
+        ops.merge(ws.weighted, ws.dispatch.inverse_permutation, T, K, shared_out=ws.shared_out,
+                  shared_parts=ws.shared_parts, out=out)
 
     def read_status(self, num_tokens: int) -> tuple[int, ...]:
         """Device status word {code, where, detail, count} of the last forward."""

@@ -270,6 +270,11 @@ def unpack_weights(
 
 
 # --------------------------------------------------------------------------- experts + merge
+def moe_shared_parts(num_tokens: int, shared_intermediate: int) -> int:
+    """Partial [T, H] slabs the shared-expert output buffer must hold."""
+    return int(_lib.load().dwdp_moe_shared_parts(num_tokens, shared_intermediate))
+
+
 def moe_workspace_bytes(num_tokens: int, top_k: int, num_experts: int, intermediate: int,
                         shared_intermediate: int) -> int:
     return int(_lib.load().dwdp_moe_workspace_bytes(num_tokens, top_k, num_experts, intermediate,
@@ -312,6 +317,7 @@ def merge(
     top_k: int,
     *,
     shared_out: torch.Tensor | None = None,
+    shared_parts: int = 1,
     out: torch.Tensor | None = None,
     out_dtype: torch.dtype = torch.bfloat16,
 ) -> torch.Tensor:
@@ -323,7 +329,7 @@ def merge(
     if out is None:
         out = torch.empty(num_tokens, H, dtype=out_dtype, device=weighted.device)
     rc = _lib.load().dwdp_merge(
-        weighted.data_ptr(), inverse_permutation.contiguous().data_ptr(), _ptr(shared_out), num_tokens,
+        weighted.data_ptr(), inverse_permutation.contiguous().data_ptr(), _ptr(shared_out), shared_parts, num_tokens,
         top_k, H, out.data_ptr(), dtype_code(out.dtype), _stream(),
     )
     _lib.check(rc, "merge")

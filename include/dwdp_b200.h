@@ -155,12 +155,17 @@ typedef struct dwdp_expert_group {
  * loop, pytorch.py:66-160): for every routed assignment row d
  *   weighted_out[d] = w[d] * down(silu(gate(xd)) * up(xd)),  xd = packed_hidden[d]
  * and, when `shared` is given, for every token t
- *   shared_out[t] = shared_gate[t] * down_s(silu(gate_s(x_t)) * up_s(x_t))
- * (shared_gate NULL = 1). bf16 activations, fp32 accumulation in TMEM,
+ *   sum_p shared_out[p][t] = shared_gate[t] * down_s(silu(gate_s(x_t)) * up_s(x_t))
+ * (shared_gate NULL = 1; p < dwdp_moe_shared_parts(T, Is), shared_out is
+ * [parts][T][H] bf16). bf16 activations, fp32 accumulation in TMEM,
  * bf16 outputs. Two persistent tcgen05 launches (gate/up+SwiGLU, down+scale).
  * Expert row ranges come from device offsets; no host synchronisation.
  * hidden_size <= 8192.
  * ======================================================================== */
+/* Number of [T, H] partial slabs `shared_out` must hold: the shared expert's
+ * down projection is split along K at decode sizes (its K is several times the
+ * routed one) and the merge sums the partials. */
+int dwdp_moe_shared_parts(int64_t num_tokens, int shared_intermediate_size);
 size_t dwdp_moe_workspace_bytes(int64_t num_tokens, int top_k, int num_experts,
                                 int intermediate_size, int shared_intermediate_size);
 int dwdp_moe_experts(const dwdp_expert_group* routed, const dwdp_expert_group* shared,
@@ -173,10 +178,11 @@ int dwdp_moe_experts(const dwdp_expert_group* routed, const dwdp_expert_group* s
 /* ======================================================================== *
  * Merge (reference_merge, merger/kernels/reference.py:6-27): deterministic
  * token-major reduction. out[t] = sum over the K rows inv[t*K+k] of
- * weighted[row] taken in ascending row order, plus shared_out[t] if given.
- * fp32 accumulation; out_dtype bf16|f32; weighted/shared bf16. K <= 16.
+ * weighted[row] taken in ascending row order, plus shared_out[p][t] for
+ * p < shared_parts when shared_out is given. fp32 accumulation; out_dtype
+ * bf16|f32; weighted/shared bf16. K <= 16.
  * ======================================================================== */
-int dwdp_merge(const void* weighted, const int64_t* inv, const void* shared_out,
+int dwdp_merge(const void* weighted, const int64_t* inv, const void* shared_out, int shared_parts,
                int64_t num_tokens, int top_k, int hidden_size, void* out, int out_dtype,
                void* stream);
 

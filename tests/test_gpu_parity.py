@@ -250,3 +250,11 @@ def test_moe_layer_deterministic(pkg):
     a = layer(x)
     b = layer(x)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("T", [1, 5, 200])
+def test_moe_layer_shared_k_split(pkg, orc, T):
+    # shared intermediate 2048 -> 32 K steps: decode sizes split its down projection in parts
+    layer = _make_layer(pkg, 8, 256, 128, 2, 2048, torch.float8_e4m3fn, pkg._lib.SCALE_BLOCK128)
+    assert pkg.ops.moe_shared_parts(T, 2048) == 2
+    _check_layer(pkg, orc, layer, T, FP8_TOL)
