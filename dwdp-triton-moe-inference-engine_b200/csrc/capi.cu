@@ -74,7 +74,8 @@ extern "C" int dwdp_router_topk(const void* hidden, int hidden_dtype, const void
     return fail(DWDP_ERR_INVALID_ARGUMENT, "router: top_k must be in [1, min(16, E)], got %d", top_k);
   if (!(score_scale > 0.f) || !(eps > 0.f))
     return fail(DWDP_ERR_INVALID_ARGUMENT, "router: score_scale and eps must be > 0");
-  if (num_tokens > 0 && (hidden == nullptr || weight == nullptr || topk_idx == nullptr || topk_weights == nullptr))
+  if (num_tokens > 0 && (hidden == nullptr || weight == nullptr || topk_idx == nullptr || topk_weights == nullptr ||
+                         logits == nullptr))
     return fail(DWDP_ERR_INVALID_ARGUMENT, "router: null pointer");
   if (shared_gate_weight != nullptr && shared_gate == nullptr)
     return fail(DWDP_ERR_INVALID_ARGUMENT, "router: shared_gate output required with a gate weight");

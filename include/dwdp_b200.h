@@ -70,7 +70,7 @@ int dwdp_device_sm_count(void);
  * linear.py:38-44). E <= 256, K <= 16.
  *   hidden [T,H] (hidden_dtype bf16|f32), weight [E,H] (weight_dtype bf16|f32)
  *   bias [E] f32 or NULL, shared_gate_weight [H] (weight_dtype) or NULL
- *   logits [T,E] f32 (may be NULL), probs/topk_weights [T,K] f32,
+ *   logits [T,E] f32 (required), probs [T,K] f32 (may be NULL), topk_weights [T,K] f32,
  *   topk_idx [T,K] int64, shared_gate [T] f32 (NULL when no gate weight)
  * ======================================================================== */
 int dwdp_router_topk(const void* hidden, int hidden_dtype, const void* weight, int weight_dtype,
