@@ -13,6 +13,12 @@ extern "C" int dwdp_router_launch(const void*, int, const void*, int, const floa
 extern "C" int dwdp_dispatch_launch(const int64_t*, const void*, int, int64_t, int, int, int64_t*,
                                     int64_t*, int64_t*, int64_t*, int64_t*, int64_t*, void*,
                                     const void*, int, void*, void*, int*, cudaStream_t);
+extern "C" int dwdp_dispatch_noalloc_launch(const int64_t*, const void*, int, int64_t, int, int,
+                                            int64_t*, int64_t*, int64_t*, int64_t*, int64_t*,
+                                            int64_t*, void*, const void*, int, void*, int*,
+                                            cudaStream_t);
+extern "C" size_t dwdp_dispatch_noalloc_max_scratch_bytes(void);
+extern "C" size_t dwdp_dispatch_scratch_bytes(int64_t, int, int);
 extern "C" int dwdp_schedule_launch(const int64_t*, const int64_t*, int, int, int64_t*, int64_t*,
                                     int64_t*, int64_t*, int64_t*, int64_t*, int64_t*, cudaStream_t);
 extern "C" int dwdp_pack_launch(const void* const*, int, int, int, int, int, int, void*, float*,
@@ -108,6 +114,40 @@ extern "C" int dwdp_dispatch(const int64_t* topk_idx, const void* topk_weights, 
                                     counts, offsets, perm, inv, ids, tok, packed_weights, hidden,
                                     hidden_size, packed_hidden, scratch, status, as_stream(stream)),
                "dispatch");
+}
+
+extern "C" int dwdp_dispatch_noalloc(const int64_t* topk_idx, const void* topk_weights, int weight_dtype,
+                                     int64_t num_tokens, int top_k, int num_experts, int64_t* counts,
+                                     int64_t* offsets, int64_t* perm, int64_t* inv, int64_t* ids,
+                                     int64_t* tok, void* packed_weights, const void* hidden,
+                                     int hidden_size, void* packed_hidden, int* status, void* stream) {
+  g_last_error.clear();
+  if (num_experts <= 0 || num_experts > 1024)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "dispatch_noalloc: num_experts must be in [1, 1024], got %d",
+                num_experts);
+  if (top_k <= 0 || num_tokens < 0)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "dispatch_noalloc: bad top_k/num_tokens");
+  if (num_tokens * top_k > ((int64_t)1 << 31) - 1)
+    return fail(DWDP_ERR_CAPACITY, "dispatch_noalloc: more than 2^31 assignments");
+  const size_t need = dwdp_dispatch_scratch_bytes(num_tokens, top_k, num_experts) - 256;
+  const size_t have = dwdp_dispatch_noalloc_max_scratch_bytes();
+  if (need > have)
+    return fail(DWDP_ERR_CAPACITY,
+                "dispatch_noalloc: ceil(T*K/256)*E*4 = %zu bytes of histogram scratch exceed the fixed "
+                "%zu-byte buffer; use dwdp_dispatch with caller-provided scratch",
+                need, have);
+  if (counts == nullptr || offsets == nullptr)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "dispatch_noalloc: null counts/offsets");
+  if (num_tokens > 0 && (topk_idx == nullptr || topk_weights == nullptr || perm == nullptr || inv == nullptr ||
+                         ids == nullptr || tok == nullptr || packed_weights == nullptr))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "dispatch_noalloc: null pointer");
+  if (packed_hidden != nullptr && (hidden == nullptr || hidden_size <= 0))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "dispatch_noalloc: packed_hidden needs hidden and hidden_size");
+  return check(dwdp_dispatch_noalloc_launch(topk_idx, topk_weights, weight_dtype, num_tokens, top_k,
+                                            num_experts, counts, offsets, perm, inv, ids, tok,
+                                            packed_weights, hidden, hidden_size, packed_hidden, status,
+                                            as_stream(stream)),
+               "dispatch_noalloc");
 }
 
 extern "C" int dwdp_schedule(const int64_t* counts, const int64_t* offsets, int num_experts,

@@ -195,3 +195,61 @@ extern "C" int dwdp_dispatch_launch(const int64_t* idx, const void* wts, int wei
   }
   return cudaGetLastError() == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free dispatch. Some callers cannot allocate device memory at the
+// moment they dispatch: code running under an allocator that forbids new
+// allocations (a serving loop with a fixed memory budget), plugins that only
+// receive the tensors of one call, or hosts without a device allocator of their
+// own. For them the per-tile histogram scratch lives in this fixed array, which
+// every GPU that loads the library holds until the process exits.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace dwdp {
+
+// 1 MiB: enough for ceil(T*K / 256) * E <= 262144 (e.g. T*K = 65536 with E = 1024).
+constexpr size_t kNoAllocScratchInts = 262144;
+static __device__ __align__(256) int g_dispatch_scratch[kNoAllocScratchInts];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+int* g_scratch_ptr[kMaxDevices] = {};  // device address of g_dispatch_scratch, per device
+}  // namespace
+
+}  // namespace dwdp
+
+extern "C" size_t dwdp_dispatch_noalloc_max_scratch_bytes(void) {
+  return dwdp::kNoAllocScratchInts * sizeof(int);
+}
+
+// The host-side name g_dispatch_scratch is only a stand-in; the device address
+// comes from cudaGetSymbolAddress, looked up once per device with that device
+// current (the first call on a device does it, so make that call before any
+// stream capture). Nothing in the array has to start at zero: every call first
+// writes each histogram entry it later reads. Calls that overlap on the GPU
+// (on different streams) share the array and race.
+extern "C" int dwdp_dispatch_noalloc_launch(const int64_t* idx, const void* wts, int weight_dtype,
+                                            int64_t T, int K, int E, int64_t* counts,
+                                            int64_t* offsets, int64_t* perm, int64_t* inv,
+                                            int64_t* ids, int64_t* tok, void* packed_w,
+                                            const void* hidden, int H, void* packed_hidden,
+                                            int* status, cudaStream_t stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return DWDP_ERR_CUDA;
+  if (dev < 0 || dev >= dwdp::kMaxDevices) return DWDP_ERR_UNSUPPORTED;
+  int* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(dwdp::g_scratch_mu);
+    if (dwdp::g_scratch_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, dwdp::g_dispatch_scratch) != cudaSuccess || p == nullptr)
+        return DWDP_ERR_CUDA;
+      dwdp::g_scratch_ptr[dev] = static_cast<int*>(p);
+    }
+    scratch = dwdp::g_scratch_ptr[dev];
+  }
+  return dwdp_dispatch_launch(idx, wts, weight_dtype, T, K, E, counts, offsets, perm, inv, ids, tok,
+                              packed_w, hidden, H, packed_hidden, scratch, status, stream);
+}

@@ -96,6 +96,23 @@ int dwdp_dispatch(const int64_t* topk_idx, const void* topk_weights, int weight_
                   void* packed_weights, const void* hidden, int hidden_size, void* packed_hidden,
                   void* scratch, int* status, void* stream);
 
+/* Allocation-free variant of dwdp_dispatch (no counterpart in the reference).
+ * For callers that cannot allocate device memory at dispatch time: a serving
+ * loop under a fixed memory budget, a plugin that only sees one call's tensors,
+ * a host with no device allocator. Same arguments and results as dwdp_dispatch
+ * minus `scratch`: the histogram scratch is a fixed 1 MiB array inside the
+ * library (held by every GPU that loads it until exit), so
+ * ceil(T*K/256) * E must be <= 262144 or DWDP_ERR_CAPACITY is returned. The
+ * first call on a device looks the array up (cudaGetSymbolAddress) and should
+ * come before any stream capture; calls that overlap on the GPU share the array
+ * and race. It allocates nothing. */
+int dwdp_dispatch_noalloc(const int64_t* topk_idx, const void* topk_weights, int weight_dtype,
+                          int64_t num_tokens, int top_k, int num_experts, int64_t* counts,
+                          int64_t* offsets, int64_t* perm, int64_t* inv, int64_t* ids, int64_t* tok,
+                          void* packed_weights, const void* hidden, int hidden_size,
+                          void* packed_hidden, int* status, void* stream);
+size_t dwdp_dispatch_noalloc_max_scratch_bytes(void);
+
 /* ======================================================================== *
  * Round-robin schedule over active experts in ascending id
  * (build_round_robin_schedule, round_robin.py:8-80), padded to E entries:
