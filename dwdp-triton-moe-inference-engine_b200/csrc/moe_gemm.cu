@@ -35,6 +35,26 @@
 
 namespace dwdp {
 
+#ifdef DWDP_PROFILE_ROLES
+// Diagnostic build only: per-CTA cycle accounting of each role, written once at exit.
+__device__ unsigned long long g_role_cycles[160][64];
+#define PROF_DECL unsigned long long prof_[8] = {0, 0, 0, 0, 0, 0, 0, 0}; long long pt_ = 0; (void)pt_;
+#define PROF_T0 pt_ = clock64();
+#define PROF_ADD(i) prof_[i] += (unsigned long long)(clock64() - pt_);
+#define PROF_STORE(base) { for (int q_ = 0; q_ < 4; ++q_) g_role_cycles[blockIdx.x][32 * MODE + 2 * (base) + q_] = prof_[q_]; g_role_cycles[blockIdx.x][32 * MODE + 2 * (base) + 4] = prof_[7]; }
+#define TW(i, call) ([&]() { const long long t_ = clock64(); const bool r_ = (call); prof_[i] += (unsigned long long)(clock64() - t_); return r_; }())
+#define PROF_START const long long pstart_ = clock64();
+#define PROF_END(i) prof_[i] = (unsigned long long)(clock64() - pstart_);
+#else
+#define TW(i, call) (call)
+#define PROF_START
+#define PROF_END(i)
+#define PROF_DECL
+#define PROF_T0
+#define PROF_ADD(i)
+#define PROF_STORE(base) {}
+#endif
+
 constexpr int BM = 128;                    // weight rows per tile (MMA M)
 constexpr int BK = 64;                     // K elements per pipeline stage (128 bytes of bf16)
 constexpr int BN_MAX = 128;                // max tokens per tile (MMA N)
@@ -78,7 +98,8 @@ template <int MODE, bool WFP8>
 struct Cfg {
   static constexpr int NMAT = MODE == 0 ? 2 : 1;
   static constexpr int S = MODE == 0 ? 4 : 6;  // load stages
-  static constexpr int SC = WFP8 ? 2 : 0;      // converted-weight stages
+  static constexpr int CONV_GROUPS = 2;        // independent converter warp groups
+  static constexpr int SC = WFP8 ? CONV_GROUPS : 0;  // converted-weight slots (one per group)
   static constexpr int W_STAGE_BYTES = NMAT * (WFP8 ? kFp8TileBytes : kConvTileBytes);
   static constexpr int CONV_STAGE_BYTES = NMAT * kConvTileBytes;
   static constexpr int NUM_WARPS = WFP8 ? 14 : 6;
@@ -94,27 +115,35 @@ struct Cfg {
 
 // 16 e4m3 values of row r, elements [sub*16, sub*16+16) -> 32 bytes of bf16
 // written to their 128B-swizzled positions.
-template <bool SCALED>
-__device__ __forceinline__ void convert_chunk(const uint8_t* src16, uint8_t* conv_tile, int r, int sub,
-                                              float s) {
-  const uint4 raw = *reinterpret_cast<const uint4*>(src16);
-  const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
-  uint32_t outw[8];
+// Four e4m3 bytes -> four bf16 (two words); exact unless `scaled` folds a block
+// scale in (one rounding).
+__device__ __forceinline__ void e4m3x4_to_bf16x4(uint32_t w, float s, bool scaled, uint32_t& o0, uint32_t& o1) {
+  uint32_t out[2];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-#pragma unroll
-    for (int hlf = 0; hlf < 2; ++hlf) {
-      const __nv_fp8x2_storage_t pair = (__nv_fp8x2_storage_t)((wv[q] >> (16 * hlf)) & 0xFFFFu);
-      const __half2_raw h2 = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
-      const __nv_bfloat162 b = SCALED ? __floats2bfloat162_rn(f.x * s, f.y * s) : __floats2bfloat162_rn(f.x, f.y);
-      outw[q * 2 + hlf] = *reinterpret_cast<const uint32_t*>(&b);
-    }
+  for (int hlf = 0; hlf < 2; ++hlf) {
+    const __nv_fp8x2_storage_t pair = (__nv_fp8x2_storage_t)((w >> (16 * hlf)) & 0xFFFFu);
+    const __half2_raw h2 = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+    const __nv_bfloat162 bv = scaled ? __floats2bfloat162_rn(f.x * s, f.y * s) : __floats2bfloat162_rn(f.x, f.y);
+    out[hlf] = *reinterpret_cast<const uint32_t*>(&bv);
   }
+  o0 = out[0];
+  o1 = out[1];
+}
+
+// One 16-byte chunk (16 e4m3 of row r, elements [sub*16, sub*16+16)) -> 32 bytes
+// of bf16 at their 128B-swizzled positions in the converted tile.
+__device__ __forceinline__ void convert_chunk(const uint4 raw, uint8_t* conv_tile, int r, int sub, float s,
+                                              bool scaled) {
+  uint32_t o[8];
+  e4m3x4_to_bf16x4(raw.x, s, scaled, o[0], o[1]);
+  e4m3x4_to_bf16x4(raw.y, s, scaled, o[2], o[3]);
+  e4m3x4_to_bf16x4(raw.z, s, scaled, o[4], o[5]);
+  e4m3x4_to_bf16x4(raw.w, s, scaled, o[6], o[7]);
   const int c0 = sub * 2;  // 16-byte chunk index of the first 8 elements
   uint8_t* row = conv_tile + r * 128;
-  *reinterpret_cast<uint4*>(row + ((c0 ^ (r & 7)) << 4)) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
-  *reinterpret_cast<uint4*>(row + (((c0 + 1) ^ (r & 7)) << 4)) = make_uint4(outw[4], outw[5], outw[6], outw[7]);
+  *reinterpret_cast<uint4*>(row + ((c0 ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+  *reinterpret_cast<uint4*>(row + (((c0 + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
 template <int MODE, bool WFP8>
@@ -171,6 +200,7 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
+      PROF_DECL PROF_START
       uint32_t it = 0;
       for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
         const WorkItem wi = p.items[item];
@@ -180,23 +210,25 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
         const uint32_t b_bytes = (uint32_t)g.box_rows * 128u;
         for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
           const int s = it % C::S;
-          if (!mbar_wait(&ld_empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 1)) break;
+          if (!TW(0, mbar_wait(&ld_empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 1 + 8 * MODE))) break;
           mbar_arrive_expect_tx(&ld_full[s], C::W_STAGE_BYTES + b_bytes);
           const size_t woff = ((size_t)wi.rb * KB + kb) * C::W_STAGE_BYTES;
           bulk_g2s(sW + s * C::W_STAGE_BYTES, wbase + woff, C::W_STAGE_BYTES, &ld_full[s]);
           tma_load_2d(sB + s * kBTileBytes, &g.tmap_b, kb * BK, wi.row0, &ld_full[s]);
         }
       }
+      PROF_END(7) PROF_STORE(0)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
+      PROF_DECL PROF_START
       uint32_t it = 0, cit = 0;
       int li = 0;
       for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++li) {
         const WorkItem wi = p.items[item];
         const int a = li & 1;
-        if (!mbar_wait(&acc_empty[a], ((li >> 1) & 1) ^ 1, &s_abort, st, 2)) break;
+        if (!TW(0, mbar_wait(&acc_empty[a], ((li >> 1) & 1) ^ 1, &s_abort, st, 2 + 8 * MODE))) break;
         tc_fence_after();
         const int n_mma = max(16, (wi.nrows + 15) & ~15);
         const uint32_t idesc = idesc_bf16(BM, n_mma);
@@ -204,28 +236,32 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
         bool ok = true;
         for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
           const int s = it % C::S;
-          if (!mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 3)) { ok = false; break; }
+          if (!TW(1, mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 3 + 8 * MODE))) { ok = false; break; }
           const uint8_t* wtile;
           int c = 0;
           if constexpr (WFP8) {
-            c = cit % 2;
-            if (!mbar_wait(&cv_full[c], (cit / 2) & 1, &s_abort, st, 4)) { ok = false; break; }
+            c = cit % C::SC;
+            if (!TW(2, mbar_wait(&cv_full[c], (cit / C::SC) & 1, &s_abort, st, 4 + 8 * MODE))) { ok = false; break; }
             wtile = sC + c * C::CONV_STAGE_BYTES;
           } else {
             wtile = sW + s * C::W_STAGE_BYTES;
           }
           tc_fence_after();
-          const uint32_t b_addr = smem_u32(sB + s * kBTileBytes);
+          // Descriptors are built once per stage; a K step of 16 bf16 (32 bytes) is +2 in
+          // the encoded start address, the second weight matrix is +kConvTileBytes/16.
+          const uint64_t b_desc0 = smem_desc_sw128(smem_u32(sB + s * kBTileBytes));
+          const uint64_t a_desc0 = smem_desc_sw128(smem_u32(wtile));
+          const uint32_t acc_first = kb > wi.kb_begin ? 1u : 0u;
+          PROF_T0
 #pragma unroll
           for (int m = 0; m < C::NMAT; ++m) {
-            const uint32_t a_addr = smem_u32(wtile + m * kConvTileBytes);
 #pragma unroll
             for (int kk = 0; kk < BK / 16; ++kk) {
-              mma_bf16_ss(d_base + m * BN_MAX, smem_desc_sw128(a_addr + kk * 32),
-                          smem_desc_sw128(b_addr + kk * 32), idesc,
-                          (kb > wi.kb_begin || kk > 0) ? 1u : 0u);
+              mma_bf16_ss(d_base + m * BN_MAX, a_desc0 + (uint64_t)(m * (kConvTileBytes >> 4) + 2 * kk),
+                          b_desc0 + (uint64_t)(2 * kk), idesc, kk > 0 ? 1u : acc_first);
             }
           }
+          PROF_ADD(3)
           mma_commit(&ld_empty[s]);
           if constexpr (WFP8) {
             mma_commit(&cv_empty[c]);
@@ -235,9 +271,11 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
         if (!ok) break;
         mma_commit(&acc_full[a]);
       }
+      PROF_END(7) PROF_STORE(4)
     }
   } else if (warp < 6) {
     // ------------------------------------------------------------ epilogue
+    PROF_DECL PROF_START
     const int quad = warp & 3;
     const int lrow = quad * 32 + lane;  // weight row inside the 128-row block
     int li = 0;
@@ -245,7 +283,7 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
       const WorkItem wi = p.items[item];
       const GroupParams& g = p.g[wi.group];
       const int a = li & 1;
-      if (!mbar_wait(&acc_full[a], (li >> 1) & 1, &s_abort, st, 5)) break;
+      if (!TW(0, mbar_wait(&acc_full[a], (li >> 1) & 1, &s_abort, st, 5 + 8 * MODE))) break;
       tc_fence_after();
       const uint32_t t_acc = tmem_base + a * C::ACC_STRIDE + ((uint32_t)(quad * 32) << 16);
       const int feat = wi.rb * BM + lrow;
@@ -289,12 +327,19 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
       tc_fence_before();
       mbar_arrive(&acc_empty[a]);
     }
+    PROF_END(7) if (lane == 0 && quad == 0) PROF_STORE(8)
   } else if constexpr (WFP8) {
     // ------------------------------------------------------------ converter (fp8 -> bf16)
     // CHANNEL scales are applied in the epilogue, so the conversion is exact
     // (e4m3 values are representable in bf16); BLOCK128 scales vary with K and
     // are folded in here with one rounding.
+    // The converter warps form C::CONV_GROUPS independent groups; group g converts
+    // the stages with index % CONV_GROUPS == g into conversion slot g, so several
+    // stages convert at once (conversion is latency-, not throughput-bound).
+    PROF_DECL PROF_START
     const int ct = threadIdx.x - 6 * 32;  // 0..255
+    constexpr int kGroupThreads = C::CONV_THREADS / C::CONV_GROUPS;
+    const int grp = ct / kGroupThreads, gt = ct % kGroupThreads;
     uint32_t it = 0, cit = 0;
     for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
       const WorkItem wi = p.items[item];
@@ -303,36 +348,42 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
       const float* sc = g.s[wi.expert];
       bool ok = true;
       for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it, ++cit) {
+        if ((int)(cit % C::CONV_GROUPS) != grp) continue;
         const int s = it % C::S;
-        const int c = cit % 2;
+        const int c = cit % C::SC;
         float sblk[C::NMAT];
 #pragma unroll
         for (int m = 0; m < C::NMAT; ++m)
           sblk[m] = block_scaled ? sc[((size_t)m * (g.R / 128) + wi.rb) * (g.K / 128) + (kb >> 1)] : 1.0f;
-        if (!mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 6)) { ok = false; break; }
-        if (!mbar_wait(&cv_empty[c], ((cit / 2) & 1) ^ 1, &s_abort, st, 7)) { ok = false; break; }
+        if (!TW(0, mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 6 + 8 * MODE))) { ok = false; break; }
+        if (!TW(1, mbar_wait(&cv_empty[c], ((cit / C::SC) & 1) ^ 1, &s_abort, st, 7 + 8 * MODE))) { ok = false; break; }
         const uint8_t* raw = sW + s * C::W_STAGE_BYTES;
         uint8_t* conv = sC + c * C::CONV_STAGE_BYTES;
         constexpr int kChunks = C::NMAT * kFp8TileBytes / 16;  // 16-byte chunks per stage
+        constexpr int kPer = kChunks / kGroupThreads;          // chunks per converter thread
+        uint4 rawv[kPer];
 #pragma unroll
-        for (int q = ct; q < kChunks; q += C::CONV_THREADS) {
-          const int m = q / (kFp8TileBytes / 16);
-          const int rem = q % (kFp8TileBytes / 16);
-          const int r = rem >> 2, sub = rem & 3;
-          if (block_scaled)
-            convert_chunk<true>(raw + m * kFp8TileBytes + r * BK + sub * 16, conv + m * kConvTileBytes, r, sub, sblk[m]);
-          else
-            convert_chunk<false>(raw + m * kFp8TileBytes + r * BK + sub * 16, conv + m * kConvTileBytes, r, sub, 1.0f);
+        for (int j = 0; j < kPer; ++j) {  // issue every shared load first
+          const int q = gt + j * kGroupThreads;
+          const int m = q / (kFp8TileBytes / 16), rem = q % (kFp8TileBytes / 16);
+          rawv[j] = *reinterpret_cast<const uint4*>(raw + m * kFp8TileBytes + (rem >> 2) * BK + (rem & 3) * 16);
+        }
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+          const int q = gt + j * kGroupThreads;
+          const int m = q / (kFp8TileBytes / 16), rem = q % (kFp8TileBytes / 16);
+          convert_chunk(rawv[j], conv + m * kConvTileBytes, rem >> 2, rem & 3, sblk[m], block_scaled);
         }
         fence_proxy_async_smem();
-        named_bar_sync(1, C::CONV_THREADS);
-        if (ct == 0) {
+        named_bar_sync(1 + grp, kGroupThreads);
+        if (gt == 0) {
           mbar_arrive(&cv_full[c]);
           mbar_arrive(&ld_empty[s]);
         }
       }
       if (!ok) break;
     }
+    PROF_END(7) if (ct == 0) PROF_STORE(12)
   }
 
   tc_fence_before();
@@ -629,3 +680,9 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   }
   return rc;
 }
+
+#ifdef DWDP_PROFILE_ROLES
+extern "C" int dwdp_debug_role_cycles(unsigned long long* out) {
+  return cudaMemcpyFromSymbol(out, dwdp::g_role_cycles, sizeof(dwdp::g_role_cycles)) == cudaSuccess ? 0 : -3;
+}
+#endif
