@@ -415,11 +415,63 @@ struct PlanParams {
   DeviceStatus* st;
 };
 
-__global__ void __launch_bounds__(1024) plan_kernel(const PlanParams pp) {
-  __shared__ int s_scan[1024];
-  __shared__ int s_total;
+constexpr int kPlanThreads = 256;
+constexpr int kPlanBlocks = 64;
+
+// Multi-CTA planner: every CTA rebuilds the (small) per-expert tile prefix in
+// shared memory, then writes its slice of the flat work-item index space of both
+// phases. Items are (shared tiles) followed by (expert ascending, weight block,
+// token tile); an item's expert is found by binary search over the prefix.
+__global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanParams pp) {
+  __shared__ int s_pre[1025];   // exclusive prefix of token tiles per expert
+  __shared__ int s_bn[1024];    // rows per tile of each expert
+  __shared__ int s_nt[1024];    // token tiles of each expert
+  __shared__ int s_part[kPlanThreads];
   const int tid = threadIdx.x;
-  const int T = pp.T;
+  const int T = pp.T, E = pp.E;
+  // per-expert tiles, scanned in chunks of kPlanThreads * 4
+  int carry = 0;
+  for (int e0 = 0; e0 < E; e0 += kPlanThreads * 4) {
+    int loc[4], sum = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int e = e0 + tid * 4 + q;
+      int nt = 0, bn = 0;
+      if (e < E) {
+        const int cnt = (int)pp.counts[e];
+        if (cnt > 0) {
+          nt = (cnt + BN_MAX - 1) / BN_MAX;
+          bn = (((cnt + nt - 1) / nt) + 15) & ~15;
+        }
+        s_nt[e] = nt;
+        s_bn[e] = bn;
+      }
+      loc[q] = nt;
+      sum += nt;
+    }
+    s_part[tid] = sum;
+    __syncthreads();
+    for (int o = 1; o < kPlanThreads; o <<= 1) {
+      const int add = tid >= o ? s_part[tid - o] : 0;
+      __syncthreads();
+      s_part[tid] += add;
+      __syncthreads();
+    }
+    int run = carry + s_part[tid] - sum;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int e = e0 + tid * 4 + q;
+      if (e < E) s_pre[e] = run;
+      run += loc[q];
+    }
+    const int total = s_part[kPlanThreads - 1];
+    __syncthreads();
+    carry += total;
+  }
+  if (tid == 0) s_pre[E] = carry;
+  __syncthreads();
+  const int routed_tiles = carry;
+
   int n_sh_tiles = 0, bn_s = 0;
   if (pp.has_shared && T > 0) {
     n_sh_tiles = (T + BN_MAX - 1) / BN_MAX;
@@ -427,71 +479,55 @@ __global__ void __launch_bounds__(1024) plan_kernel(const PlanParams pp) {
   }
   const int base_gu = n_sh_tiles * pp.rb_gu_s;
   const int base_dn = n_sh_tiles * pp.rb_dn_s * pp.sdn_parts;
-  for (int i = tid; i < base_gu; i += blockDim.x) {
-    const int rb = i / n_sh_tiles, j = i % n_sh_tiles;
-    const int row0 = j * bn_s;
-    if (i < pp.cap_gu) pp.items_gu[i] = WorkItem{1, 0, rb, row0, min(bn_s, T - row0), 0, pp.kb_gu, 0};
-  }
-  const int kb_part = pp.sdn_parts > 0 ? pp.kb_dn_s / pp.sdn_parts : 0;
-  for (int i = tid; i < base_dn; i += blockDim.x) {
-    const int part = i / (n_sh_tiles * pp.rb_dn_s);
-    const int rem = i % (n_sh_tiles * pp.rb_dn_s);
-    const int rb = rem / n_sh_tiles, j = rem % n_sh_tiles;
-    const int row0 = j * bn_s;
-    if (i < pp.cap_dn)
-      pp.items_dn[i] = WorkItem{1, 0, rb, row0, min(bn_s, T - row0), part * kb_part, (part + 1) * kb_part, part};
-  }
-  int carry = 0;
-  for (int e0 = 0; e0 < pp.E; e0 += 1024) {
-    const int e = e0 + tid;
-    int nt = 0, cnt = 0, bn = 0;
-    int64_t off = 0;
-    if (e < pp.E) {
-      cnt = (int)pp.counts[e];
-      off = pp.offsets[e];
-      if (cnt > 0) {
-        nt = (cnt + BN_MAX - 1) / BN_MAX;
-        bn = (((cnt + nt - 1) / nt) + 15) & ~15;
-      }
-    }
-    s_scan[tid] = nt;
-    __syncthreads();
-    for (int o = 1; o < 1024; o <<= 1) {
-      const int add = tid >= o ? s_scan[tid - o] : 0;
-      __syncthreads();
-      s_scan[tid] += add;
-      __syncthreads();
-    }
-    const int excl = carry + s_scan[tid] - nt;
-    if (e < pp.E && nt > 0) {
-      for (int rb = 0; rb < pp.rb_gu_r; ++rb)
-        for (int j = 0; j < nt; ++j) {
-          const int idx = base_gu + excl * pp.rb_gu_r + rb * nt + j;
-          const int row0 = (int)off + j * bn;
-          if (idx < pp.cap_gu) pp.items_gu[idx] = WorkItem{0, e, rb, row0, min(bn, cnt - j * bn), 0, pp.kb_gu, 0};
-        }
-      for (int rb = 0; rb < pp.rb_dn_r; ++rb)
-        for (int j = 0; j < nt; ++j) {
-          const int idx = base_dn + excl * pp.rb_dn_r + rb * nt + j;
-          const int row0 = (int)off + j * bn;
-          if (idx < pp.cap_dn) pp.items_dn[idx] = WorkItem{0, e, rb, row0, min(bn, cnt - j * bn), 0, pp.kb_dn_r, 0};
-        }
-    }
-    if (tid == 1023) s_total = carry + s_scan[1023];
-    __syncthreads();
-    carry = s_total;
-    __syncthreads();
-  }
-  if (tid == 0) {
-    const int ngu = base_gu + carry * pp.rb_gu_r;
-    const int ndn = base_dn + carry * pp.rb_dn_r;
-    if (ngu > pp.cap_gu || ndn > pp.cap_dn) {
+  const int ngu = base_gu + routed_tiles * pp.rb_gu_r;
+  const int ndn = base_dn + routed_tiles * pp.rb_dn_r;
+  if (ngu > pp.cap_gu || ndn > pp.cap_dn) {
+    if (blockIdx.x == 0 && tid == 0) {
       record_error(pp.st, DWDP_ERR_CAPACITY, 200, ngu);
       pp.n_items[0] = 0;
       pp.n_items[1] = 0;
-    } else {
-      pp.n_items[0] = ngu;
-      pp.n_items[1] = ndn;
+    }
+    return;
+  }
+  if (blockIdx.x == 0 && tid == 0) {
+    pp.n_items[0] = ngu;
+    pp.n_items[1] = ndn;
+  }
+  const int kb_part = pp.sdn_parts > 0 ? pp.kb_dn_s / pp.sdn_parts : 0;
+  const int stride = gridDim.x * blockDim.x;
+  for (int phase = 0; phase < 2; ++phase) {
+    const int n = phase == 0 ? ngu : ndn;
+    const int base = phase == 0 ? base_gu : base_dn;
+    const int rb_r = phase == 0 ? pp.rb_gu_r : pp.rb_dn_r;
+    const int kb_r = phase == 0 ? pp.kb_gu : pp.kb_dn_r;
+    WorkItem* out = phase == 0 ? pp.items_gu : pp.items_dn;
+    for (int i = blockIdx.x * blockDim.x + tid; i < n; i += stride) {
+      WorkItem w;
+      if (i < base) {  // shared expert: (part, rb, token tile)
+        const int per_part = n_sh_tiles * (phase == 0 ? pp.rb_gu_s : pp.rb_dn_s);
+        const int part = phase == 0 ? 0 : i / per_part;
+        const int rem = phase == 0 ? i : i % per_part;
+        const int rb = rem / n_sh_tiles, j = rem % n_sh_tiles;
+        const int row0 = j * bn_s;
+        const int kb0 = phase == 0 ? 0 : part * kb_part;
+        const int kb1 = phase == 0 ? pp.kb_gu : (part + 1) * kb_part;
+        w = WorkItem{1, 0, rb, row0, min(bn_s, T - row0), kb0, kb1, part};
+      } else {         // routed: expert e with s_pre[e]*rb_r <= i - base < s_pre[e+1]*rb_r
+        const int r = i - base;
+        int lo = 0, hi = E - 1;
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (s_pre[mid] * rb_r <= r) lo = mid; else hi = mid - 1;
+        }
+        const int e = lo;
+        const int nt = s_nt[e], bn = s_bn[e];
+        const int local = r - s_pre[e] * rb_r;
+        const int rb = local / nt, j = local % nt;
+        const int cnt = (int)pp.counts[e];
+        const int row0 = (int)pp.offsets[e] + j * bn;
+        w = WorkItem{0, e, rb, row0, min(bn, cnt - j * bn), 0, kb_r, 0};
+      }
+      out[i] = w;
     }
   }
 }
@@ -635,7 +671,7 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   pp.sdn_parts = has_shared ? parts : 0;
   pp.items_gu = items_gu; pp.items_dn = items_dn; pp.n_items = n_items;
   pp.cap_gu = L.cap_gu; pp.cap_dn = L.cap_dn; pp.st = st;
-  plan_kernel<<<1, 1024, 0, stream>>>(pp);
+  plan_kernel<<<kPlanBlocks, kPlanThreads, 0, stream>>>(pp);
   if (cudaGetLastError() != cudaSuccess) return DWDP_ERR_CUDA;
 
   // routed rows per expert tile <= min(T, BN_MAX); shared tiles <= min(T, BN_MAX)

@@ -7,8 +7,9 @@
 // weight 1). Arithmetic is fp32 throughout. Top-k ties resolve to the lower
 // expert id and slots come out in descending logit order.
 //
-// Two launches: router_logits_kernel (x W^T, grid over token tiles x expert
-// groups) and router_topk_kernel (one warp per token).
+// Two launches: the logits (router_logits_mma_kernel on the tensor cores for
+// bf16 inputs, router_logits_kernel on the CUDA cores otherwise) and
+// router_topk_kernel (one warp per token).
 #include "common.cuh"
 
 namespace dwdp {
@@ -121,6 +122,87 @@ router_logits_kernel(const TX* __restrict__ x, const TW* __restrict__ w, const f
   }
 }
 
+// bf16 x bf16 logits on the tensor cores (mma.sync m16n8k16, fp32 accumulate;
+// bf16 products are exact in fp32, so this equals the fp32 CUDA-core result up to
+// summation order). A CTA owns 16 tokens x 32 experts (4 n-tiles of 8); its 8
+// warps split K (warp w takes the 16-wide K steps with index % 8 == w), so each
+// warp has all of its fragment loads in flight at once, and the 8 partial tiles
+// are summed through shared memory in a fixed order (deterministic).
+constexpr int kMmaTok = 16;
+constexpr int kMmaExp = 32;
+constexpr int kMmaWarps = 8;
+
+__device__ __forceinline__ uint32_t ld_b32(const __nv_bfloat16* p) {
+  return *reinterpret_cast<const uint32_t*>(p);
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(kMmaWarps * 32)
+router_logits_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                         const float* __restrict__ bias, const __nv_bfloat16* __restrict__ gate_w, int T,
+                         int H, int E, float score_scale, float* __restrict__ logits,
+                         float* __restrict__ gate_logit) {
+  __shared__ float part[kMmaWarps][16][32];  // per-warp partial [token][expert]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int tok0 = blockIdx.x * kMmaTok;
+  const int e0 = blockIdx.y * kMmaExp;
+  const int rows = E + (gate_w != nullptr ? 1 : 0);
+  const __nv_bfloat16* xa = x + (int64_t)min(tok0 + g, T - 1) * H + 2 * t;
+  const __nv_bfloat16* xb = x + (int64_t)min(tok0 + g + 8, T - 1) * H + 2 * t;
+  const __nv_bfloat16* wr[4];
+  bool wv[4];
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+    const int e = e0 + nt * 8 + g;
+    wv[nt] = e < rows;
+    wr[nt] = wv[nt] ? (e < E ? w + (int64_t)e * H : gate_w) + 2 * t : xa;  // xa: any valid address
+  }
+  float acc[4][4];
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[nt][q] = 0.f;
+#pragma unroll 8
+  for (int k0 = warp * 16; k0 < H; k0 += 16 * kMmaWarps) {
+    const uint32_t a0 = ld_b32(xa + k0), a1 = ld_b32(xb + k0);
+    const uint32_t a2 = ld_b32(xa + k0 + 8), a3 = ld_b32(xb + k0 + 8);
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const uint32_t b0 = wv[nt] ? ld_b32(wr[nt] + k0) : 0u;
+      const uint32_t b1 = wv[nt] ? ld_b32(wr[nt] + k0 + 8) : 0u;
+      mma_bf16_16816(acc[nt], a0, a1, a2, a3, b0, b1);
+    }
+  }
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) part[warp][g + (q >= 2 ? 8 : 0)][nt * 8 + 2 * t + (q & 1)] = acc[nt][q];
+  __syncthreads();
+  for (int i = threadIdx.x; i < 16 * 32; i += kMmaWarps * 32) {
+    const int tt = i >> 5, ee = i & 31;
+    const int tok = tok0 + tt, e = e0 + ee;
+    if (tok >= T || e >= rows) continue;
+    float v = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < kMmaWarps; ++ww) v += part[ww][tt][ee];
+    if (e < E) {
+      if (bias != nullptr) v += bias[e];
+      logits[(int64_t)tok * E + e] = v * score_scale;
+    } else {
+      gate_logit[tok] = v;
+    }
+  }
+}
+
 // Top-k + softmax over the k selected + renormalisation: one warp per token.
 __global__ void __launch_bounds__(kRouterThreads)
 router_topk_kernel(const float* __restrict__ logits, int T, int E, int K, int renorm, float eps,
@@ -214,7 +296,12 @@ extern "C" int dwdp_router_launch(const void* hidden, int hidden_dtype, const vo
     else if (tok == 4) DWDP_LAUNCH_LOGITS(TX, TW, 4);    \
     else DWDP_LAUNCH_LOGITS(TX, TW, 2);                  \
   } while (0)
-  if (hidden_dtype == DWDP_DTYPE_BF16 && weight_dtype == DWDP_DTYPE_BF16)
+  if (hidden_dtype == DWDP_DTYPE_BF16 && weight_dtype == DWDP_DTYPE_BF16 && H % 16 == 0) {
+    const dim3 mgrid((unsigned)((T + kMmaTok - 1) / kMmaTok), (unsigned)((rows + kMmaExp - 1) / kMmaExp));
+    router_logits_mma_kernel<<<mgrid, kMmaWarps * 32, 0, stream>>>(
+        (const __nv_bfloat16*)hidden, (const __nv_bfloat16*)weight, bias,
+        (const __nv_bfloat16*)shared_gate_weight, (int)T, H, E, score_scale, logits, shared_gate);
+  } else if (hidden_dtype == DWDP_DTYPE_BF16 && weight_dtype == DWDP_DTYPE_BF16)
     DWDP_LOGITS_TOK(__nv_bfloat16, __nv_bfloat16);
   else if (hidden_dtype == DWDP_DTYPE_BF16 && weight_dtype == DWDP_DTYPE_F32)
     DWDP_LOGITS_TOK(__nv_bfloat16, float);
