@@ -103,6 +103,34 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_void_p, c_int, c_void_p]
     ),
     "dwdp_moe_shared_parts": (c_int, [c_int64, c_int]),
+    # communication engine
+    "dwdp_engine_last_error": (ctypes.c_char_p, []),
+    "dwdp_ipc_handle_bytes": (c_size_t, []),
+    "dwdp_export_ipc_handle": (c_int, [c_void_p, c_void_p, ctypes.POINTER(c_size_t)]),
+    "dwdp_peer_can_access": (c_int, [c_int, c_int, ctypes.POINTER(c_int)]),
+    "dwdp_engine_create": (c_int, [c_int, c_size_t, c_int, c_int, ctypes.POINTER(c_void_p)]),
+    "dwdp_engine_destroy": (c_int, [c_void_p]),
+    "dwdp_engine_register_local": (c_int, [c_void_p, c_int, c_void_p, c_size_t]),
+    "dwdp_engine_register_ipc": (c_int, [c_void_p, c_int, c_void_p, c_size_t, c_size_t, c_int]),
+    "dwdp_engine_register_peer": (c_int, [c_void_p, c_int, c_void_p, c_size_t, c_int]),
+    "dwdp_engine_prefetch": (c_int, [c_void_p, ctypes.POINTER(c_int), c_int, c_int, c_void_p]),
+    "dwdp_engine_wait": (c_int, [c_void_p, c_int, c_void_p]),
+    "dwdp_engine_resident_pointer": (c_int, [c_void_p, c_int, c_int, ctypes.POINTER(c_void_p)]),
+    "dwdp_engine_is_remote": (c_int, [c_void_p, c_int, ctypes.POINTER(c_int)]),
+    "dwdp_engine_release": (c_int, [c_void_p, c_int]),
+    "dwdp_engine_synchronize": (c_int, [c_void_p]),
+    "dwdp_engine_stats": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_ulonglong),
+                                  ctypes.POINTER(ctypes.c_ulonglong), ctypes.POINTER(c_void_p)]),
+    "dwdp_policy_decide": (c_int, [c_int, c_int, c_int, c_int, c_int]),
+    "dwdp_sched_create": (c_int, [ctypes.POINTER(c_void_p)]),
+    "dwdp_sched_destroy": (c_int, [c_void_p]),
+    "dwdp_sched_submit": (c_int, [c_void_p, c_int, c_int]),
+    "dwdp_sched_take": (c_int, [c_void_p, c_int, ctypes.POINTER(c_int)]),
+    "dwdp_sched_complete": (c_int, [c_void_p, c_int]),
+    "dwdp_sched_fail": (c_int, [c_void_p, c_int, c_int]),
+    "dwdp_sched_cancel": (c_int, [c_void_p, c_int]),
+    "dwdp_sched_close": (c_int, [c_void_p]),
+    "dwdp_sched_state": (c_int, [c_void_p, c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
 }
 
 _lib = None
@@ -136,15 +164,24 @@ def last_error() -> str:
     return msg.decode() if msg else ""
 
 
-def check(rc: int, what: str) -> None:
+def engine_last_error() -> str:
+    msg = load().dwdp_engine_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int, what: str, engine: bool = False) -> None:
     """Translate a C status code into the reference's exception types."""
     if rc == DWDP_OK:
         return
-    msg = last_error() or f"{what} failed with status {rc}"
+    msg = (engine_last_error() if engine else last_error()) or f"{what} failed with status {rc}"
     if rc == DWDP_ERR_INVALID_ARGUMENT:
         raise ValueError(msg)
     if rc == DWDP_ERR_NOT_FOUND:
         raise KeyError(msg)
     if rc == DWDP_ERR_UNSUPPORTED:
         raise NotImplementedError(msg)
+    if rc == DWDP_ERR_DEVICE_TIMEOUT:
+        raise TimeoutError(msg)
+    if rc == DWDP_ERR_STATE:
+        raise RuntimeError(msg)
     raise RuntimeError(msg)

@@ -1,0 +1,231 @@
+"""Python surface of the DWDP communication engine, with the names of the
+reference's pybind module (DWDP/communication/bindings.cpp:32-111):
+``export_ipc_handle``, ``CommunicationEngine``, ``PeerTopology``,
+``TransferScheduler``, ``TransferState``, ``CommunicationPath`` and
+``CommunicationPolicy``. All of them call the C ABI (include/dwdp_b200.h)."""
+from __future__ import annotations
+
+import ctypes
+import enum
+
+import torch
+
+from . import _lib
+
+
+class TransferState(enum.IntEnum):
+    CREATED = 0
+    QUEUED = 1
+    RUNNING = 2
+    WAITING = 3
+    COMPLETED = 4
+    FAILED = 5
+    CANCELLED = 6
+
+
+class CommunicationPath(enum.IntEnum):
+    LOCAL = 0
+    P2P = 1
+    IPC = 2
+    COPY = 3
+
+
+class ResidentState(enum.IntEnum):
+    NONE = 0
+    STAGED = 1
+    ACTIVE = 2
+
+
+def _chk(rc: int, what: str) -> None:
+    _lib.check(rc, what, engine=True)
+
+
+def export_ipc_handle(tensor_or_ptr) -> bytes:
+    """IPC handle of the allocation holding the pointer, followed by the pointer's
+    8-byte little-endian offset inside that allocation (so the importer can reach
+    a sub-allocated tensor)."""
+    ptr = tensor_or_ptr.data_ptr() if isinstance(tensor_or_ptr, torch.Tensor) else int(tensor_or_ptr)
+    lib = _lib.load()
+    n = int(lib.dwdp_ipc_handle_bytes())
+    buf = ctypes.create_string_buffer(n)
+    off = ctypes.c_size_t(0)
+    _chk(lib.dwdp_export_ipc_handle(ptr, buf, ctypes.byref(off)), "export_ipc_handle")
+    return buf.raw + int(off.value).to_bytes(8, "little")
+
+
+def split_ipc_handle(blob: bytes) -> tuple[bytes, int]:
+    n = int(_lib.load().dwdp_ipc_handle_bytes())
+    if len(blob) != n + 8:
+        raise ValueError(f"IPC blob must be {n + 8} bytes, got {len(blob)}")
+    return blob[:n], int.from_bytes(blob[n:], "little")
+
+
+class PeerTopology:
+    """Peer-access queries (topology.cpp:17-41), cached per pair."""
+
+    def __init__(self) -> None:
+        self._cache: dict[tuple[int, int], bool] = {}
+
+    def can_access(self, src: int, dst: int) -> bool:
+        key = (src, dst)
+        if key not in self._cache:
+            out = ctypes.c_int(0)
+            _chk(_lib.load().dwdp_peer_can_access(src, dst, ctypes.byref(out)), "peer_can_access")
+            self._cache[key] = bool(out.value)
+        return self._cache[key]
+
+    canAccess = can_access
+
+
+class CommunicationPolicy:
+    """Path selection (communication_policy.cpp:5-17)."""
+
+    def __init__(self, local_gpu: int) -> None:
+        self.local_gpu = local_gpu
+
+    def decide(self, *, owner_gpu: int, resident: ResidentState = ResidentState.NONE,
+               has_ipc_handle: bool = False, peer_access: bool = False) -> CommunicationPath:
+        return CommunicationPath(_lib.load().dwdp_policy_decide(
+            self.local_gpu, owner_gpu, int(resident), int(has_ipc_handle), int(peer_access)))
+
+
+class TransferScheduler:
+    """Priority queue of expert transfers with coalescing, two retries, cancel
+    while queued and a bounded take (transfer_scheduler.cpp:15-104)."""
+
+    def __init__(self) -> None:
+        h = ctypes.c_void_p()
+        _chk(_lib.load().dwdp_sched_create(ctypes.byref(h)), "sched_create")
+        self._h = h
+
+    def submit(self, expert_id: int, priority: int = 0) -> None:
+        rc = _lib.load().dwdp_sched_submit(self._h, expert_id, priority)
+        if rc == _lib.DWDP_ERR_INVALID_ARGUMENT:
+            raise ValueError(_lib.engine_last_error())
+        if rc == _lib.DWDP_ERR_STATE:
+            raise RuntimeError(_lib.engine_last_error())
+        _chk(rc, "submit")
+
+    def take(self, timeout_ms: int = 1000) -> int | None:
+        """Next expert id (now RUNNING); None once closed and drained."""
+        out = ctypes.c_int(-1)
+        _chk(_lib.load().dwdp_sched_take(self._h, timeout_ms, ctypes.byref(out)), "take")
+        return None if out.value < 0 else out.value
+
+    def complete(self, expert_id: int) -> None:
+        _chk(_lib.load().dwdp_sched_complete(self._h, expert_id), "complete")
+
+    def fail(self, expert_id: int, retryable: bool) -> None:
+        _chk(_lib.load().dwdp_sched_fail(self._h, expert_id, int(retryable)), "fail")
+
+    def cancel(self, expert_id: int) -> None:
+        _chk(_lib.load().dwdp_sched_cancel(self._h, expert_id), "cancel")
+
+    def close(self) -> None:
+        _chk(_lib.load().dwdp_sched_close(self._h), "close")
+
+    def state(self, expert_id: int) -> tuple[TransferState, int]:
+        st, rt = ctypes.c_int(0), ctypes.c_int(0)
+        _chk(_lib.load().dwdp_sched_state(self._h, expert_id, ctypes.byref(st), ctypes.byref(rt)), "state")
+        return TransferState(st.value), rt.value
+
+    def __del__(self) -> None:
+        h = getattr(self, "_h", None)
+        try:
+            if h is not None and h.value:
+                _lib.load().dwdp_sched_destroy(h)
+        except Exception:  # noqa: BLE001 - interpreter teardown
+            pass
+        self._h = None
+
+
+class CommunicationEngine:
+    """Expert-slab prefetch engine (communication_engine.cpp; bindings.cpp:39-60).
+
+    ``initialize(slot_bytes, num_slots, num_buffers)`` allocates the staging
+    buffers; ``register_expert`` / ``register_ipc_expert`` / ``register_peer_expert``
+    declare local and remote slabs; ``prefetch(ids, buffer)`` copies the remote
+    ones into staging on the engine's greatest-priority stream; ``wait(buffer)``
+    orders the current torch stream after those copies."""
+
+    def __init__(self, device_id: int = 0) -> None:
+        self.device_id = device_id
+        self._h = None
+
+    def initialize(self, slot_bytes: int, num_slots: int, num_buffers: int = 2) -> None:
+        if self._h is not None:
+            raise RuntimeError("engine already initialized")
+        h = ctypes.c_void_p()
+        _chk(_lib.load().dwdp_engine_create(self.device_id, slot_bytes, num_slots, num_buffers, ctypes.byref(h)),
+             "engine_create")
+        self._h = h
+        self.num_buffers = num_buffers
+
+    def initialized(self) -> bool:
+        return self._h is not None
+
+    def _eng(self):
+        if self._h is None:
+            raise RuntimeError("communication engine is not initialized")
+        return self._h
+
+    def register_expert(self, expert_id: int, ptr: int, size_bytes: int) -> None:
+        _chk(_lib.load().dwdp_engine_register_local(self._eng(), expert_id, ptr, size_bytes), "register_expert")
+
+    def register_ipc_expert(self, expert_id: int, handle_blob: bytes, size_bytes: int, owner_device: int = -1,
+                            extra_offset: int = 0) -> None:
+        handle, off = split_ipc_handle(handle_blob)
+        _chk(_lib.load().dwdp_engine_register_ipc(self._eng(), expert_id, handle, off + extra_offset, size_bytes,
+                                                  owner_device), "register_ipc_expert")
+
+    def register_peer_expert(self, expert_id: int, ptr: int, size_bytes: int, owner_device: int) -> None:
+        _chk(_lib.load().dwdp_engine_register_peer(self._eng(), expert_id, ptr, size_bytes, owner_device),
+             "register_peer_expert")
+
+    def prefetch(self, expert_ids, buffer: int = 0, after_current_stream: bool = True) -> None:
+        ids = [int(expert_ids)] if isinstance(expert_ids, int) else [int(e) for e in expert_ids]
+        arr = (ctypes.c_int * max(1, len(ids)))(*ids)
+        after = torch.cuda.current_stream(self.device_id).cuda_stream if after_current_stream else None
+        _chk(_lib.load().dwdp_engine_prefetch(self._eng(), arr, len(ids), buffer, after), "prefetch")
+
+    def wait(self, buffer: int = 0, stream: torch.cuda.Stream | None = None) -> None:
+        s = (stream or torch.cuda.current_stream(self.device_id)).cuda_stream
+        _chk(_lib.load().dwdp_engine_wait(self._eng(), buffer, s), "wait")
+
+    def get_resident_pointer(self, expert_id: int, buffer: int = 0) -> int:
+        out = ctypes.c_void_p()
+        _chk(_lib.load().dwdp_engine_resident_pointer(self._eng(), expert_id, buffer, ctypes.byref(out)),
+             "get_resident_pointer")
+        return int(out.value or 0)
+
+    getResidentPointer = get_resident_pointer
+
+    def is_remote(self, expert_id: int) -> bool:
+        out = ctypes.c_int(0)
+        _chk(_lib.load().dwdp_engine_is_remote(self._eng(), expert_id, ctypes.byref(out)), "is_remote")
+        return bool(out.value)
+
+    def is_resident(self, expert_id: int) -> bool:
+        return not self.is_remote(expert_id)
+
+    def release(self, expert_id: int) -> None:
+        _chk(_lib.load().dwdp_engine_release(self._eng(), expert_id), "release")
+
+    def synchronize(self) -> None:
+        _chk(_lib.load().dwdp_engine_synchronize(self._eng()), "synchronize")
+
+    def stats(self) -> dict:
+        b, c, s = ctypes.c_ulonglong(0), ctypes.c_ulonglong(0), ctypes.c_void_p()
+        _chk(_lib.load().dwdp_engine_stats(self._eng(), ctypes.byref(b), ctypes.byref(c), ctypes.byref(s)), "stats")
+        return {"bytes_copied": int(b.value), "copies_issued": int(c.value), "copy_stream": int(s.value or 0)}
+
+    def shutdown(self) -> None:
+        if self._h is not None:
+            _lib.load().dwdp_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self) -> None:
+        try:
+            self.shutdown()
+        except Exception:  # noqa: BLE001 - interpreter teardown
+            pass

@@ -203,6 +203,73 @@ int dwdp_merge(const void* weighted, const int64_t* inv, const void* shared_out,
                int64_t num_tokens, int top_k, int hidden_size, void* out, int out_dtype,
                void* stream);
 
+/* ======================================================================== *
+ * DWDP communication engine (replaces the pybind module dwdp_communication_ext,
+ * DWDP/communication/bindings.cpp:32-111): expert slabs sharded across the GPUs
+ * of one box, remote slabs opened through CUDA IPC (or a peer pointer) and
+ * copied by the copy engines into `num_buffers` staging buffers of `num_slots`
+ * fixed slots on a greatest-priority stream; prefetch/wait per buffer, the wait
+ * ordered on the caller's stream. Messages: dwdp_engine_last_error().
+ * ======================================================================== */
+typedef struct dwdp_engine dwdp_engine;
+const char* dwdp_engine_last_error(void);
+size_t dwdp_ipc_handle_bytes(void);
+/* export_ipc_handle (bindings.cpp:27-30): handle of the allocation holding ptr
+ * plus ptr's byte offset inside it. */
+int dwdp_export_ipc_handle(const void* device_ptr, void* handle_out, size_t* offset_out);
+/* PeerTopology.canAccess (topology.cpp:17-41) */
+int dwdp_peer_can_access(int src_device, int dst_device, int* out);
+int dwdp_engine_create(int device_id, size_t slot_bytes, int num_slots, int num_buffers,
+                       dwdp_engine** out);
+int dwdp_engine_destroy(dwdp_engine* engine);
+int dwdp_engine_register_local(dwdp_engine* engine, int expert_id, const void* ptr, size_t bytes);
+int dwdp_engine_register_ipc(dwdp_engine* engine, int expert_id, const void* handle, size_t offset,
+                             size_t bytes, int owner_device);
+int dwdp_engine_register_peer(dwdp_engine* engine, int expert_id, const void* peer_ptr,
+                              size_t bytes, int owner_device);
+/* Copy the listed remote experts into `buffer` (local ones are skipped); when
+ * after_stream is given the copies start after the work already queued on it. */
+int dwdp_engine_prefetch(dwdp_engine* engine, const int* expert_ids, int n, int buffer,
+                         void* after_stream);
+int dwdp_engine_wait(dwdp_engine* engine, int buffer, void* stream);
+int dwdp_engine_resident_pointer(dwdp_engine* engine, int expert_id, int buffer, void** out);
+int dwdp_engine_is_remote(dwdp_engine* engine, int expert_id, int* out);
+int dwdp_engine_release(dwdp_engine* engine, int expert_id);
+int dwdp_engine_synchronize(dwdp_engine* engine);
+int dwdp_engine_stats(dwdp_engine* engine, unsigned long long* bytes_copied,
+                      unsigned long long* copies_issued, void** copy_stream);
+
+/* CommunicationPolicy.decide (communication_policy.cpp:5-17); CommunicationPath codes. */
+#define DWDP_PATH_LOCAL 0
+#define DWDP_PATH_P2P 1
+#define DWDP_PATH_IPC 2
+#define DWDP_PATH_COPY 3
+#define DWDP_RESIDENT_NONE 0
+#define DWDP_RESIDENT_STAGED 1
+#define DWDP_RESIDENT_ACTIVE 2
+int dwdp_policy_decide(int local_gpu, int owner_gpu, int resident_state, int has_ipc_handle,
+                       int peer_access);
+
+/* TransferScheduler (transfer_scheduler.cpp:15-104): priority queue with
+ * coalescing, two retries, cancel-while-queued, bounded take(). */
+#define DWDP_TRANSFER_CREATED 0
+#define DWDP_TRANSFER_QUEUED 1
+#define DWDP_TRANSFER_RUNNING 2
+#define DWDP_TRANSFER_WAITING 3
+#define DWDP_TRANSFER_COMPLETED 4
+#define DWDP_TRANSFER_FAILED 5
+#define DWDP_TRANSFER_CANCELLED 6
+typedef struct dwdp_sched dwdp_sched;
+int dwdp_sched_create(dwdp_sched** out);
+int dwdp_sched_destroy(dwdp_sched* s);
+int dwdp_sched_submit(dwdp_sched* s, int expert_id, int priority);
+int dwdp_sched_take(dwdp_sched* s, int timeout_ms, int* expert_id);
+int dwdp_sched_complete(dwdp_sched* s, int expert_id);
+int dwdp_sched_fail(dwdp_sched* s, int expert_id, int retryable);
+int dwdp_sched_cancel(dwdp_sched* s, int expert_id);
+int dwdp_sched_close(dwdp_sched* s);
+int dwdp_sched_state(dwdp_sched* s, int expert_id, int* state, int* retries);
+
 #ifdef __cplusplus
 }
 #endif
