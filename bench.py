@@ -2,11 +2,14 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl ours|reference]
 
-One step = one full MoE-layer forward (router -> dispatch -> grouped expert
-GEMMs incl. the shared expert -> merge) over T tokens, replayed from a CUDA
-graph, with the weights (554 MB FP8) larger than L2 and L2 flushed before every
-timed step. Under torchrun each rank runs its own T tokens (weak scaling); the
-reported time is the max over ranks. Rank 0 prints one JSON line.
+One step = L chained MoE-layer forwards (router -> dispatch -> grouped expert
+GEMMs incl. the shared expert -> merge) over T tokens per GPU, L2 flushed before
+every timed step (each layer's weights, 554 MB FP8, exceed L2 anyway). Under
+torchrun each rank runs its own T tokens (weak scaling) with the routed experts
+of every layer sharded over the ranks and the next layer's remote experts
+prefetched over NVLink during the current layer (DWDP); the reported time is
+the max over ranks. value = (N * T * L) / step time = MoE-layer tokens/s.
+Rank 0 prints one JSON line.
 
 ``--impl reference`` times the reference algorithm's CPU path (the oracle
 restatement of the reference's PyTorch executor, all host threads) on the same
@@ -43,26 +46,42 @@ def _peaks() -> dict:
 
 
 # ----------------------------------------------------------------------------- setup
-def make_qwen_layer(pkg, device, seed: int = 1235):
+def _expert_weights(layer_seed: int, e: int, device, H: int, I: int):
+    g = torch.Generator(device=device).manual_seed(layer_seed * 1000 + e)
+    return (torch.randn(I, H, generator=g, device=device) * 0.02,
+            torch.randn(I, H, generator=g, device=device) * 0.02,
+            torch.randn(H, I, generator=g, device=device) * 0.02)
+
+
+def make_qwen_layer(pkg, device, seed: int = 1235, *, rank: int = 0, world: int = 1):
     """Random-init Qwen-shaped layer: router W ~ N(0, 1/H) (logits ~ N(0,1)),
-    experts ~ N(0, 0.02) quantised to FP8 E4M3 with per-output-channel scales,
-    shared expert Is=5632 with sigmoid gate g ~ N(0, 0.02)."""
+    experts ~ N(0, 0.02) quantised to FP8 E4M3 with per-expert per-output-channel
+    scales, shared expert Is=5632 with sigmoid gate g ~ N(0, 0.02). With
+    world > 1 the routed experts are sharded over the ranks (DWDP) and must be
+    connected (``layer.experts.connect()``) before use."""
+    import importlib
+
     H, E, I, K, Is = QWEN["H"], QWEN["E"], QWEN["I"], QWEN["K"], QWEN["Is"]
     g = torch.Generator(device=device).manual_seed(seed)
     wr = (torch.randn(E, H, generator=g, device=device) / H**0.5).bfloat16()
-    store = pkg.ExpertWeightStore(E, H, I, weight_dtype=torch.float8_e4m3fn,
-                                  scale_mode=pkg._lib.SCALE_CHANNEL, device=device)
-    for e in range(E):
-        gw = torch.randn(I, H, generator=g, device=device) * 0.02
-        uw = torch.randn(I, H, generator=g, device=device) * 0.02
-        dw = torch.randn(H, I, generator=g, device=device) * 0.02
-        store.load_expert(e, gw, uw, dw)
+    if world > 1:
+        dw = importlib.import_module("dwdp_b200.dwdp")
+        store = dw.ShardedExpertStore(E, H, I, rank=rank, world_size=world, device=device)
+        experts = store.owned
+    else:
+        store = pkg.ExpertWeightStore(E, H, I, weight_dtype=torch.float8_e4m3fn,
+                                      scale_mode=pkg._lib.SCALE_CHANNEL, device=device)
+        experts = range(E)
+    for e in experts:
+        store.load_expert(e, *_expert_weights(seed, e, device, H, I))
     shared = pkg.ExpertWeightStore(1, H, Is, weight_dtype=torch.float8_e4m3fn,
                                    scale_mode=pkg._lib.SCALE_CHANNEL, device=device)
     shared.load_expert(0, torch.randn(Is, H, generator=g, device=device) * 0.02,
                        torch.randn(Is, H, generator=g, device=device) * 0.02,
                        torch.randn(H, Is, generator=g, device=device) * 0.02)
     gate = (torch.randn(H, generator=g, device=device) * 0.02).bfloat16()
+    if world > 1:
+        store.connect()
     return pkg.MoELayer(wr, store, K, shared_expert=shared, shared_gate_weight=gate)
 
 
@@ -200,31 +219,6 @@ def run_point(pkg, layer, T: int, steps: int, warmup: int, flush, device, rank: 
     }
 
 
-def e2e_point(layer, T: int, steps: int, warmup: int, device, rank: int):
-    """Public-API forward with host buffers: pinned H2D of the inputs, forward,
-    D2H of the output, all inside the timed region of every step."""
-    x_host = make_inputs(T, device, seed=999 + rank).cpu().pin_memory()
-    y_host = torch.empty(T, layer.hidden_size, dtype=torch.bfloat16).pin_memory()
-    x_dev = torch.empty(T, layer.hidden_size, dtype=torch.bfloat16, device=device)
-    out = torch.empty_like(x_dev)
-
-    def step():
-        x_dev.copy_(x_host, non_blocking=True)
-        layer.forward(x_dev, out=out)
-        y_host.copy_(out, non_blocking=True)
-
-    for _ in range(warmup):
-        step()
-    torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(steps):
-        step()
-    b.record()
-    torch.cuda.synchronize()
-    return a.elapsed_time(b), T * layer.hidden_size * 2, T * layer.hidden_size * 2
-
-
 # ----------------------------------------------------------------------------- CPU arm
 def cpu_layer_step(orc, x, router_w, gate_w, experts, shared, K):
     logits = orc.router_logits(x, router_w)
@@ -260,6 +254,39 @@ def cpu_baseline(pkg, layer, T_sample: int, iters: int, device) -> dict:
                       f"CPU {model}", "seconds_per_step": med}
 
 
+# ----------------------------------------------------------------------------- layer stack (headline)
+class LayerStack:
+    """L Qwen-shaped MoE layers with distinct weights, chained (layer l's output
+    is layer l+1's input). With world > 1 every layer's routed experts are
+    sharded over the ranks and the NEXT layer's remote experts are prefetched
+    over NVLink while the current layer computes (DWDP)."""
+
+    def __init__(self, pkg, device, L: int, T: int, rank: int, world: int):
+        self.layers = [make_qwen_layer(pkg, device, seed=1235 + l, rank=rank, world=world) for l in range(L)]
+        self.sharded = world > 1
+        self.T = T
+        self.x0 = make_inputs(T, device, seed=4242 + 7919 * rank)
+        self.outs = [torch.empty_like(self.x0), torch.empty_like(self.x0)]
+        self.ws = [lay.workspace(T) for lay in self.layers]
+        if self.sharded:
+            self.layers[0].experts.prefetch(0)
+
+    def step(self, x: torch.Tensor | None = None) -> torch.Tensor:
+        x = self.x0 if x is None else x
+        L = len(self.layers)
+        for l, lay in enumerate(self.layers):
+            if self.sharded:
+                self.layers[(l + 1) % L].experts.prefetch(0)  # overlaps layer l's kernels
+                lay.experts.wait(0)
+            out = self.outs[l % 2]
+            lay.run(x, self.ws[l], out)
+            x = out
+        return x
+
+    def remote_bytes_per_step(self) -> int:
+        return sum(lay.experts.remote_bytes() for lay in self.layers) if self.sharded else 0
+
+
 # ----------------------------------------------------------------------------- main
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -267,6 +294,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--tokens", type=int, default=4096)
+    ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=256)
@@ -285,21 +313,25 @@ def main() -> None:
         import torch.distributed as dist
 
         dist.init_process_group("nccl", device_id=device)
-    T = args.tokens
-    config = {"workload": f"qwen1.5-moe-a2.7b MoE layer, prefill T={T} per GPU", "model": "Qwen1.5-MoE-A2.7B (shape)",
-              "tokens_per_gpu": T, "hidden": QWEN["H"], "experts": QWEN["E"], "top_k": QWEN["K"],
+    T, L = args.tokens, args.layers
+    config = {"workload": f"{L} chained qwen1.5-moe-a2.7b-shaped MoE layers, prefill T={T} per GPU",
+              "model": "Qwen1.5-MoE-A2.7B (shape)", "tokens_per_gpu": T, "layers_per_step": L,
+              "hidden": QWEN["H"], "experts": QWEN["E"], "top_k": QWEN["K"],
               "moe_intermediate": QWEN["I"], "shared_intermediate": QWEN["Is"],
               "weights": "fp8 e4m3, per-output-channel fp32 scales", "activations": "bf16",
-              "l2": "flushed (256 MB write) before every timed step; weights 554 MB > L2",
-              "parallelism": f"dp{world} (tokens per GPU fixed; experts replicated)"}
+              "l2": "flushed (256 MB write) before every timed step; weights 554 MB/layer > L2",
+              "parallelism": (f"dwdp{world}: tokens data-parallel, routed experts sharded over {world} GPUs, "
+                              "next layer's remote experts prefetched over NVLink during the current layer")
+              if world > 1 else "single GPU, all experts local"}
 
     if args.impl == "reference":
         if rank == 0:
             layer = make_qwen_layer(pkg, device)
-            cb = cpu_baseline(pkg, layer, args.cpu_sample, max(args.steps // 5, 2), device)
+            iters = max(args.steps // 5, 2)
+            cb = cpu_baseline(pkg, layer, args.cpu_sample, iters, device)
             print(json.dumps({
                 "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s",
-                "n_gpus": args.gpus, "steps": max(args.steps // 5, 2), "warmup": 1,
+                "n_gpus": args.gpus, "steps": iters, "warmup": 1,
                 "ms_per_step": cb["seconds_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
                 "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
@@ -310,53 +342,73 @@ def main() -> None:
             torch.distributed.destroy_process_group()
         return
 
-    layer = make_qwen_layer(pkg, device)
     flush = L2Flusher(device)
     peaks = _peaks()
+    stack = LayerStack(pkg, device, L, T, rank, world)
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
+    eng0 = stack.layers[0].experts.engine if stack.sharded else None
     with ClockSampler(local) as clocks:
-        main_pt = run_point(pkg, layer, T, args.steps, args.warmup, flush, device, rank, world)
-    total_ms = sum(main_pt["layer_ms"])
+        step_ms = time_device(stack.step, args.steps, args.warmup, flush)
+    total_ms = sum(step_ms)
     if world > 1:
         t = torch.tensor([total_ms], device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
-    value = world * T / (ms_per_step / 1e3)
-    exp_ms = statistics.mean(main_pt["experts_ms"])
-    tensor_bound = T >= 1024
-    if tensor_bound:
-        ach = main_pt["flops"] / (exp_ms / 1e3) / 1e12
-        roof = {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": ach / peaks["bf16_tflops"], "traffic": None,
-                "kernel": "grouped expert GEMMs (plan + gate/up + down launches), bf16 MMA on fp8 weights",
-                "peak_source": peaks["source"] + " bf16 dense (burst)"}
-    else:
-        ach = main_pt["bytes"] / (exp_ms / 1e3) / 1e9
-        roof = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": ach / peaks["hbm_gbs"], "traffic": None,
-                "kernel": "grouped expert GEMMs (plan + gate/up + down launches)",
-                "peak_source": peaks["source"] + " HBM copy"}
+    value = world * T * L / (ms_per_step / 1e3)
+
+    # roofline of the dominant launches (grouped expert GEMMs) on layer 0, single-layer graph
+    lay0 = stack.layers[0]
+    if stack.sharded:
+        lay0.experts.prefetch(0)
+        lay0.experts.wait(0)
+    pt = run_point(pkg, lay0, T, args.steps, args.warmup, flush, device, rank, world)
+    exp_ms = statistics.mean(pt["experts_ms"])
+    ach = pt["flops"] / (exp_ms / 1e3) / 1e12
+    roof = {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": ach / peaks["bf16_tflops"], "traffic": None,
+            "kernel": "grouped expert GEMMs of one layer (plan + gate/up + down launches), bf16 MMA on fp8 weights",
+            "peak_source": peaks["source"] + " bf16 dense (burst)",
+            "layer_us": statistics.mean(pt["layer_ms"]) * 1e3, "experts_us": exp_ms * 1e3}
 
     sweep = []
-    if not args.no_sweep:
+    if not args.no_sweep and world == 1:
         for Ts in DECODE_SWEEP:
-            pt = run_point(pkg, layer, Ts, args.steps, args.warmup, flush, device, rank, world)
-            lm, em = statistics.mean(pt["layer_ms"]), statistics.mean(pt["experts_ms"])
-            gbs = pt["bytes"] / (em / 1e3) / 1e9
+            p2 = run_point(pkg, lay0, Ts, args.steps, args.warmup, flush, device, rank, world)
+            lm, em = statistics.mean(p2["layer_ms"]), statistics.mean(p2["experts_ms"])
+            gbs = p2["bytes"] / (em / 1e3) / 1e9
             sweep.append({"T": Ts, "layer_us": lm * 1e3, "tokens_per_s": Ts / (lm / 1e3),
-                          "experts_us": em * 1e3, "active_experts": pt["active_experts"],
-                          "expert_bytes": pt["bytes"], "hbm_gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"]})
-        sweep.append({"T": T, "layer_us": ms_per_step * 1e3, "tokens_per_s": T / (ms_per_step / 1e3),
-                      "experts_us": exp_ms * 1e3, "tflops": main_pt["flops"] / (exp_ms / 1e3) / 1e12})
+                          "experts_us": em * 1e3, "active_experts": p2["active_experts"],
+                          "expert_bytes": p2["bytes"], "hbm_gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"]})
 
-    e2e_ms, h2d, d2h = e2e_point(layer, T, args.steps, args.warmup, device, rank)
-    e2e_val = world * T / (e2e_ms / args.steps / 1e3)
+    # end to end: pinned host input -> L layers -> pinned host output, every step
+    x_host = stack.x0.cpu().pin_memory()
+    y_host = torch.empty_like(x_host).pin_memory()
+    x_dev = torch.empty_like(stack.x0)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        y_host.copy_(stack.step(x_dev), non_blocking=True)
+
+    e2e_ms = sum(time_device(e2e_step, args.steps, args.warmup, flush))
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_val = world * T * L / (e2e_ms / args.steps / 1e3)
+
+    nvlink = None
+    if stack.sharded:
+        rb = stack.remote_bytes_per_step()
+        nvlink = {"remote_bytes_per_step_per_gpu": rb,
+                  "prefetch_gbs_lower_bound": rb / (ms_per_step / 1e3) / 1e9,
+                  "note": "copies overlap compute; GB/s is remote bytes / step time (a lower bound on link rate)"}
+
     cb = None
     if rank == 0 and world == 1:
-        cb = cpu_baseline(pkg, layer, args.cpu_sample, 3, device)
+        cb = cpu_baseline(pkg, lay0, args.cpu_sample, 3, device)
         cb = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
     if rank == 0:
         print(json.dumps({
@@ -364,8 +416,9 @@ def main() -> None:
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config,
             "roofline": roof, "cpu_baseline": cb, "clocks": clocks.summary(),
-            "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": 8 * args.steps, "sweep": sweep,
+            "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": x_host.numel() * 2,
+                    "d2h_bytes_per_step": y_host.numel() * 2},
+            "gpu_launches": 9 * L * args.steps, "nvlink": nvlink, "sweep": sweep,
         }), flush=True)
     if world > 1:
         torch.distributed.barrier()
