@@ -6,8 +6,9 @@
 // with a design for one 8xB200 NVSwitch box:
 //
 //  * An expert is one contiguous slab (weights + scales), so a remote expert is
-//    ONE peer copy. Copies run on a greatest-priority non-blocking stream owned by
-//    the engine and go through the copy engines (no SMs taken from the GEMMs).
+//    ONE peer copy. Copies run on greatest-priority non-blocking streams owned by
+//    the engine (experts spread round-robin over kCopyStreams so several copy
+//    engines work at once) and take no SMs from the GEMMs.
 //  * Staging is N buffers of fixed slots (slot = largest registered slab); a
 //    remote expert has the same slot index in every buffer, so the caller's
 //    pointer arrays for buffer b are computed once.
@@ -57,6 +58,8 @@ struct IpcMapping {
 
 }  // namespace
 
+constexpr int kCopyStreams = 4;  // copies of one prefetch spread over this many streams
+
 struct dwdp_engine {
   int device = 0;
   size_t slot_bytes = 0;
@@ -65,7 +68,9 @@ struct dwdp_engine {
   std::vector<void*> buffers;
   std::vector<cudaEvent_t> ready;     // copies of buffer b done
   std::vector<int> buffer_valid;      // buffer b holds the last prefetch
-  cudaStream_t copy_stream = nullptr;
+  cudaStream_t copy_stream = nullptr;  // stream 0 of copy_streams
+  std::vector<cudaStream_t> copy_streams;       // experts spread round-robin (several copy engines)
+  std::vector<cudaEvent_t> stream_done;         // per copy stream, joined into ready[b]
   std::map<int, EngineExpert> experts;
   std::map<std::string, IpcMapping> ipc;  // handle bytes -> opened base
   int next_slot = 0;
@@ -170,15 +175,24 @@ extern "C" int dwdp_engine_create(int device_id, size_t slot_bytes, int num_slot
   int lo = 0, hi = 0;
   cudaError_t e = cudaDeviceGetStreamPriorityRange(&lo, &hi);
   if (e != cudaSuccess) return set_error("cudaDeviceGetStreamPriorityRange", e);
-  e = cudaStreamCreateWithPriority(&eng->copy_stream, cudaStreamNonBlocking, hi);  // greatest priority
-  if (e != cudaSuccess) return set_error("cudaStreamCreateWithPriority", e);
+  for (int i = 0; i < kCopyStreams; ++i) {
+    cudaStream_t cs;
+    e = cudaStreamCreateWithPriority(&cs, cudaStreamNonBlocking, hi);  // greatest priority
+    if (e != cudaSuccess) return set_error("cudaStreamCreateWithPriority", e);
+    eng->copy_streams.push_back(cs);
+    cudaEvent_t ev;
+    cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    eng->stream_done.push_back(ev);
+  }
+  eng->copy_stream = eng->copy_streams[0];
   for (int b = 0; b < num_buffers; ++b) {
     void* p = nullptr;
     if (eng->buffer_bytes > 0) {
       e = cudaMalloc(&p, eng->buffer_bytes);
       if (e != cudaSuccess) {
         for (void* q : eng->buffers) cudaFree(q);
-        cudaStreamDestroy(eng->copy_stream);
+        for (auto cs : eng->copy_streams) cudaStreamDestroy(cs);
+        for (auto ev : eng->stream_done) cudaEventDestroy(ev);
         return set_error("cudaMalloc(staging)", e);
       }
     }
@@ -196,13 +210,14 @@ extern "C" int dwdp_engine_destroy(dwdp_engine* eng) {
   if (eng == nullptr) return DWDP_OK;
   {
     DeviceGuard guard(eng->device);
-    cudaStreamSynchronize(eng->copy_stream);
+    for (auto cs : eng->copy_streams) cudaStreamSynchronize(cs);
     for (void* p : eng->buffers)
       if (p) cudaFree(p);
     for (auto ev : eng->ready) cudaEventDestroy(ev);
     for (auto& kv : eng->ipc)
       if (kv.second.base) cudaIpcCloseMemHandle(kv.second.base);
-    cudaStreamDestroy(eng->copy_stream);
+    for (auto cs : eng->copy_streams) cudaStreamDestroy(cs);
+    for (auto ev : eng->stream_done) cudaEventDestroy(ev);
   }
   delete eng;
   return DWDP_OK;
@@ -293,7 +308,7 @@ extern "C" int dwdp_engine_prefetch(dwdp_engine* eng, const int* expert_ids, int
     e = cudaEventCreateWithFlags(&dep, cudaEventDisableTiming);
     if (e != cudaSuccess) return set_error("cudaEventCreate", e);
     cudaEventRecord(dep, reinterpret_cast<cudaStream_t>(after_stream));
-    cudaStreamWaitEvent(eng->copy_stream, dep, 0);
+    for (auto cs : eng->copy_streams) cudaStreamWaitEvent(cs, dep, 0);
     cudaEventDestroy(dep);
   }
   std::vector<const EngineExpert*> todo;
@@ -306,12 +321,18 @@ extern "C" int dwdp_engine_prefetch(dwdp_engine* eng, const int* expert_ids, int
   for (size_t j = 0; j < todo.size(); ++j) {
     const EngineExpert* x = todo[(j + rot) % todo.size()];
     void* dst = static_cast<char*>(eng->buffers[buffer]) + (size_t)x->slot * eng->slot_bytes;
-    e = cudaMemcpyAsync(dst, x->src, x->bytes, cudaMemcpyDeviceToDevice, eng->copy_stream);
+    e = cudaMemcpyAsync(dst, x->src, x->bytes, cudaMemcpyDeviceToDevice,
+                        eng->copy_streams[j % eng->copy_streams.size()]);
     if (e != cudaSuccess) return set_error("cudaMemcpyAsync(prefetch)", e);
     eng->bytes_copied += x->bytes;
     eng->copies_issued += 1;
   }
-  e = cudaEventRecord(eng->ready[buffer], eng->copy_stream);
+  // join the copy streams into stream 0, then one event marks the buffer ready
+  for (size_t i = 1; i < eng->copy_streams.size(); ++i) {
+    cudaEventRecord(eng->stream_done[i], eng->copy_streams[i]);
+    cudaStreamWaitEvent(eng->copy_streams[0], eng->stream_done[i], 0);
+  }
+  e = cudaEventRecord(eng->ready[buffer], eng->copy_streams[0]);
   if (e != cudaSuccess) return set_error("cudaEventRecord", e);
   eng->buffer_valid[buffer] = 1;
   return DWDP_OK;
@@ -360,8 +381,11 @@ extern "C" int dwdp_engine_release(dwdp_engine* eng, int expert_id) {
 extern "C" int dwdp_engine_synchronize(dwdp_engine* eng) {
   if (eng == nullptr) return fail(DWDP_ERR_INVALID_ARGUMENT, "synchronize: null engine");
   DeviceGuard guard(eng->device);
-  const cudaError_t e = cudaStreamSynchronize(eng->copy_stream);
-  return e == cudaSuccess ? DWDP_OK : set_error("cudaStreamSynchronize", e);
+  for (auto cs : eng->copy_streams) {
+    const cudaError_t e = cudaStreamSynchronize(cs);
+    if (e != cudaSuccess) return set_error("cudaStreamSynchronize", e);
+  }
+  return DWDP_OK;
 }
 
 extern "C" int dwdp_engine_stats(dwdp_engine* eng, unsigned long long* bytes_copied,
