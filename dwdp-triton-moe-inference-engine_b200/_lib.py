@@ -79,6 +79,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p],
     ),
     "dwdp_dispatch_noalloc_max_scratch_bytes": (c_size_t, []),
+    "dwdp_gather_rows": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int64, c_void_p, c_void_p, c_void_p]),
     "dwdp_schedule": (
         c_int,
         [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

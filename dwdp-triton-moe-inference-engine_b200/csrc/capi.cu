@@ -18,6 +18,8 @@ extern "C" int dwdp_dispatch_noalloc_launch(const int64_t*, const void*, int, in
                                             int64_t*, void*, const void*, int, void*, int*,
                                             cudaStream_t);
 extern "C" size_t dwdp_dispatch_noalloc_max_scratch_bytes(void);
+extern "C" int dwdp_gather_rows_launch(const void*, const int64_t*, int64_t, int, int64_t, void*, int*,
+                                       cudaStream_t);
 extern "C" size_t dwdp_dispatch_scratch_bytes(int64_t, int, int);
 extern "C" int dwdp_schedule_launch(const int64_t*, const int64_t*, int, int, int64_t*, int64_t*,
                                     int64_t*, int64_t*, int64_t*, int64_t*, int64_t*, cudaStream_t);
@@ -148,6 +150,18 @@ extern "C" int dwdp_dispatch_noalloc(const int64_t* topk_idx, const void* topk_w
                                             packed_weights, hidden, hidden_size, packed_hidden, status,
                                             as_stream(stream)),
                "dispatch_noalloc");
+}
+
+extern "C" int dwdp_gather_rows(const void* hidden, const int64_t* token_index, int64_t num_rows, int hidden_size,
+                                int64_t num_tokens, void* packed, int* status, void* stream) {
+  g_last_error.clear();
+  if (num_rows < 0 || hidden_size <= 0 || num_tokens < 0)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "gather_rows: bad sizes");
+  if (num_rows > 0 && (hidden == nullptr || token_index == nullptr || packed == nullptr))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "gather_rows: null pointer");
+  return check(dwdp_gather_rows_launch(hidden, token_index, num_rows, hidden_size, num_tokens, packed, status,
+                                       as_stream(stream)),
+               "gather_rows");
 }
 
 extern "C" int dwdp_schedule(const int64_t* counts, const int64_t* offsets, int num_experts,

@@ -153,6 +153,14 @@ gather_rows_kernel(const __nv_bfloat16* __restrict__ hidden, const int64_t* __re
 
 using namespace dwdp;
 
+extern "C" int dwdp_gather_rows_launch(const void* hidden, const int64_t* tok, int64_t N, int H, int64_t T,
+                                       void* packed, int* status, cudaStream_t stream) {
+  if (N <= 0) return DWDP_OK;
+  gather_rows_kernel<<<(unsigned)((N + 7) / 8), 256, 0, stream>>>(
+      (const __nv_bfloat16*)hidden, tok, N, H, T, (__nv_bfloat16*)packed, reinterpret_cast<DeviceStatus*>(status));
+  return cudaGetLastError() == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;
+}
+
 extern "C" size_t dwdp_dispatch_scratch_bytes(int64_t num_tokens, int top_k, int num_experts) {
   const int64_t N = num_tokens * top_k;
   const int64_t ntiles = (N + kTile - 1) / kTile;

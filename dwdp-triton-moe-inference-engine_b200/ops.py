@@ -182,6 +182,22 @@ def dispatch(
     return out
 
 
+def gather_rows(hidden: torch.Tensor, token_index: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """packed[d] = hidden[token_index[d]] (bf16 rows)."""
+    _require_cuda(hidden, token_index)
+    if hidden.dtype != torch.bfloat16:
+        raise ValueError("gather_rows expects bf16 hidden states")
+    H = hidden.shape[-1]
+    x = hidden.reshape(-1, H).contiguous()
+    idx = token_index.to(torch.int64).contiguous()
+    if out is None:
+        out = torch.empty(idx.numel(), H, dtype=torch.bfloat16, device=x.device)
+    rc = _lib.load().dwdp_gather_rows(x.data_ptr(), idx.data_ptr(), idx.numel(), H, x.shape[0], out.data_ptr(),
+                                      None, _stream())
+    _lib.check(rc, "gather_rows")
+    return out
+
+
 # --------------------------------------------------------------------------- schedule
 @dataclass
 class ScheduleResult:

@@ -96,6 +96,11 @@ int dwdp_dispatch(const int64_t* topk_idx, const void* topk_weights, int weight_
                   void* packed_weights, const void* hidden, int hidden_size, void* packed_hidden,
                   void* scratch, int* status, void* stream);
 
+/* Row gather alone (the executor's input gather, executor/ops gather_expert_inputs):
+ * packed[d] = hidden[token_index[d]] for d < num_rows, bf16 rows of hidden_size. */
+int dwdp_gather_rows(const void* hidden, const int64_t* token_index, int64_t num_rows, int hidden_size,
+                     int64_t num_tokens, void* packed, int* status, void* stream);
+
 /* Allocation-free variant of dwdp_dispatch (no counterpart in the reference).
  * For callers that cannot allocate device memory at dispatch time: a serving
  * loop under a fixed memory budget, a plugin that only sees one call's tensors,
