@@ -23,7 +23,9 @@ import torch
 from . import ops
 from .weights import ExpertWeightStore
 
-_CACHE: "weakref.WeakKeyDictionary[torch.Tensor, tuple]" = weakref.WeakKeyDictionary()
+# id(w1) -> (weak reference to w1, stamp, store); tensors cannot key a WeakKeyDictionary
+# because their __eq__ is elementwise.
+_CACHE: dict[int, tuple] = {}
 
 
 def _split_w1(w1: torch.Tensor, H: int, layout: str | None) -> tuple[torch.Tensor, torch.Tensor]:
@@ -67,10 +69,10 @@ def _down(w2: torch.Tensor, H: int, I: int, layout: str | None) -> torch.Tensor:
 
 
 def _store_for(w1: torch.Tensor, w2: torch.Tensor, H: int, layout: str | None) -> ExpertWeightStore:
-    hit = _CACHE.get(w1)
+    hit = _CACHE.get(id(w1))
     stamp = (w1._version, w2._version, w2.data_ptr(), layout)
-    if hit is not None and hit[0] == stamp:
-        return hit[1]
+    if hit is not None and hit[0]() is w1 and hit[1] == stamp:
+        return hit[2]
     if w1.dtype == torch.float8_e4m3fn or w2.dtype == torch.float8_e4m3fn:
         raise ValueError("fused_moe takes unquantised weights; quantised experts go through ExpertWeightStore")
     gate, up = _split_w1(w1, H, layout)
@@ -80,7 +82,8 @@ def _store_for(w1: torch.Tensor, w2: torch.Tensor, H: int, layout: str | None) -
     store = ExpertWeightStore(E, H, I, weight_dtype=torch.bfloat16, device=w1.device)
     for e in range(E):
         store.load_expert(e, gate[e].contiguous(), up[e].contiguous(), down[e].contiguous())
-    _CACHE[w1] = (stamp, store)
+    key = id(w1)
+    _CACHE[key] = (weakref.ref(w1, lambda _r, k=key: _CACHE.pop(k, None)), stamp, store)
     return store
 
 
