@@ -169,6 +169,17 @@ __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, ui
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T, A and B both e4m3 (K = 32 per instruction).
+__device__ __forceinline__ void mma_e4m3_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on an mbarrier once all previously issued tcgen05.mma of this thread complete.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(
@@ -214,6 +225,11 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
          | (1u << 10)                   // B bf16
          | ((uint32_t)(N >> 3) << 17)   // N / 8
          | ((uint32_t)(M >> 4) << 24);  // M / 16
+}
+
+// Instruction descriptor: kind::f8f6f4, A=B=e4m3 (format code 0), D=fp32, K-major.
+__host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + __expf(-g)); }

@@ -79,6 +79,7 @@ struct GroupParams {
   const float* const* s;   // [E] scales (fp8) or nullptr
   void* out;               // bf16 [rows, R]
   const float* row_scale;  // MODE 1: per-row multiplier (routing weight / shared gate) or null
+  const float* x_scale;    // e4m3 activation planes only: per-row activation scale
   int K;                   // reduction size
   int R;                   // output rows of the projection (= out leading dim)
   int scale_mode;
@@ -394,6 +395,204 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
   }
 }
 
+// hi/lo activation planes: lo = (v / s - hi) * kLoPlaneGain (see quant_rows)
+constexpr float kLoPlaneGain = 16.0f;
+
+// ---------------------------------------------------------------------------
+// e4m3 tensor-core path (per-output-channel fp8 weights).
+//
+// The weights are multiplied as e4m3 by tcgen05 kind::f8f6f4 straight from the
+// pre-swizzled 128 x 128 tiles the bulk copy lands in shared memory: no
+// conversion warps, and one MMA covers 32 inputs (twice a bf16 MMA). The
+// activations come as hi/lo e4m3 planes (interleaved rows, see quant_rows), so
+// the MMA N dimension holds 2 columns per token and the epilogue forms
+//   y = s_w[row] * s_x[token] * (acc[2t] + acc[2t + 1] / 16)
+// which keeps bf16-level activation precision. Token tiles are at most 64
+// (N <= 128), so two accumulator buffers of gate+up fit the 512 TMEM columns.
+// Warp roles: 0 producer, 1 TMEM allocator + MMA issuer, 2-5 epilogue.
+// ---------------------------------------------------------------------------
+constexpr int BK8 = 128;                    // e4m3 inputs per pipeline stage
+constexpr int BN8 = 64;                     // max tokens per tile
+constexpr int kW8TileBytes = BM * BK8;      // 128 x 128 weight tile
+constexpr int kB8TileBytes = 2 * BN8 * BK8; // hi/lo activation tile
+
+template <int MODE>
+struct Cfg8 {
+  static constexpr int NMAT = MODE == 0 ? 2 : 1;
+  static constexpr int S = MODE == 0 ? 4 : 6;
+  static constexpr int W_STAGE_BYTES = NMAT * kW8TileBytes;
+  static constexpr int THREADS = 6 * 32;
+  static constexpr int ACC_STRIDE = NMAT * 2 * BN8;  // TMEM columns per accumulator buffer
+  static constexpr int TMEM_COLS = 2 * ACC_STRIDE <= 256 ? 256 : 512;
+  static constexpr int SMEM_BYTES = S * (W_STAGE_BYTES + kB8TileBytes) + 1024 + 256;
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(Cfg8<MODE>::THREADS, 1)
+moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
+  using C = Cfg8<MODE>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sB = smem;
+  uint8_t* sW = sB + C::S * kB8TileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + C::S * C::W_STAGE_BYTES);
+  uint64_t* ld_full = bars;
+  uint64_t* ld_empty = ld_full + C::S;
+  uint64_t* acc_full = ld_empty + C::S;
+  uint64_t* acc_empty = acc_full + 2;
+  __shared__ uint32_t s_tmem_base;
+  __shared__ volatile int s_abort;
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  DeviceStatus* st = p.st;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int i = 0; i < C::S; ++i) {
+      mbar_init(&ld_full[i], 1);
+      mbar_init(&ld_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&s_tmem_base, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    if (p.g[0].enabled) prefetch_tmap(&p.g[0].tmap_b);
+    if (p.g[1].enabled) prefetch_tmap(&p.g[1].tmap_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s_tmem_base;
+  const int n_items = *p.n_items;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
+        const WorkItem wi = p.items[item];
+        const GroupParams& g = p.g[wi.group];
+        const int KB = g.K / BK8;
+        const uint8_t* wbase = reinterpret_cast<const uint8_t*>(g.w[wi.expert]);
+        const uint32_t b_bytes = (uint32_t)g.box_rows * 2u * BK8;
+        for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
+          const int s = it % C::S;
+          if (!mbar_wait(&ld_empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 21 + 8 * MODE)) break;
+          mbar_arrive_expect_tx(&ld_full[s], C::W_STAGE_BYTES + b_bytes);
+          const size_t woff = ((size_t)wi.rb * KB + kb) * C::W_STAGE_BYTES;
+          bulk_g2s(sW + s * C::W_STAGE_BYTES, wbase + woff, C::W_STAGE_BYTES, &ld_full[s]);
+          tma_load_2d(sB + s * kB8TileBytes, &g.tmap_b, kb * BK8, 2 * wi.row0, &ld_full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0;
+      int li = 0;
+      for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++li) {
+        const WorkItem wi = p.items[item];
+        const int a = li & 1;
+        if (!mbar_wait(&acc_empty[a], ((li >> 1) & 1) ^ 1, &s_abort, st, 22 + 8 * MODE)) break;
+        tc_fence_after();
+        const int n_tok = max(16, (wi.nrows + 15) & ~15);
+        const uint32_t idesc = idesc_e4m3(BM, 2 * n_tok);
+        const uint32_t d_base = tmem_base + a * C::ACC_STRIDE;
+        bool ok = true;
+        for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
+          const int s = it % C::S;
+          if (!mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 23 + 8 * MODE)) { ok = false; break; }
+          tc_fence_after();
+          // a K step of 32 e4m3 (32 bytes) is +2 in the encoded start address
+          const uint64_t b_desc0 = smem_desc_sw128(smem_u32(sB + s * kB8TileBytes));
+          const uint64_t a_desc0 = smem_desc_sw128(smem_u32(sW + s * C::W_STAGE_BYTES));
+          const uint32_t acc_first = kb > wi.kb_begin ? 1u : 0u;
+#pragma unroll
+          for (int m = 0; m < C::NMAT; ++m) {
+#pragma unroll
+            for (int kk = 0; kk < BK8 / 32; ++kk) {
+              mma_e4m3_ss(d_base + m * 2 * BN8, a_desc0 + (uint64_t)(m * (kW8TileBytes >> 4) + 2 * kk),
+                          b_desc0 + (uint64_t)(2 * kk), idesc, kk > 0 ? 1u : acc_first);
+            }
+          }
+          mma_commit(&ld_empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[a]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;
+    const int lrow = quad * 32 + lane;
+    int li = 0;
+    for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++li) {
+      const WorkItem wi = p.items[item];
+      const GroupParams& g = p.g[wi.group];
+      const int a = li & 1;
+      if (!mbar_wait(&acc_full[a], (li >> 1) & 1, &s_abort, st, 24 + 8 * MODE)) break;
+      tc_fence_after();
+      const uint32_t t_acc = tmem_base + a * C::ACC_STRIDE + ((uint32_t)(quad * 32) << 16);
+      const int feat = wi.rb * BM + lrow;
+      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)wi.part * g.part_stride;
+      const float* sc = g.s[wi.expert];
+      const float s0 = sc[feat];
+      const float s1 = MODE == 0 ? sc[g.R + feat] : 1.0f;
+      const float* xs = g.x_scale + wi.row0;
+      for (int c0 = 0; c0 < 2 * wi.nrows; c0 += 16) {
+        const int t0 = c0 >> 1;
+        if constexpr (MODE == 0) {
+          float gv[16], uv[16];
+          tmem_ld16(t_acc + c0, gv);
+          tmem_ld16(t_acc + 2 * BN8 + c0, uv);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int t = t0 + j;
+            if (t < wi.nrows) {
+              const float sx = xs[t];
+              const float gg = (gv[2 * j] + gv[2 * j + 1] * (1.0f / kLoPlaneGain)) * (s0 * sx);
+              const float uu = (uv[2 * j] + uv[2 * j + 1] * (1.0f / kLoPlaneGain)) * (s1 * sx);
+              out[(size_t)(wi.row0 + t) * g.R + feat] = __float2bfloat16_rn(silu(gg) * uu);
+            }
+          }
+        } else {
+          float yv[16];
+          tmem_ld16(t_acc + c0, yv);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int t = t0 + j;
+            if (t < wi.nrows) {
+              const int row = wi.row0 + t;
+              const float rs = g.row_scale != nullptr ? g.row_scale[row] : 1.0f;
+              const float y = (yv[2 * j] + yv[2 * j + 1] * (1.0f / kLoPlaneGain)) * (s0 * xs[t]);
+              out[(size_t)row * g.R + feat] = __float2bfloat16_rn(y * rs);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[a]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Device tile planner (the scheduler's job, DWDP/scheduler/ops/round_robin.py:
 // active experts in ascending id), run on device so no counts reach the host.
@@ -408,6 +607,7 @@ struct PlanParams {
   int rb_gu_r, rb_dn_r, rb_gu_s, rb_dn_s;  // 128-row weight blocks per projection
   int kb_gu, kb_dn_r, kb_dn_s;              // 64-wide K steps per projection
   int sdn_parts;                            // K splits of the shared down projection
+  int bn_max;                               // token-tile cap (rows per work item)
   WorkItem* items_gu;
   WorkItem* items_dn;
   int* n_items;
@@ -422,7 +622,7 @@ constexpr int kPlanBlocks = 64;
 // shared memory, then writes its slice of the flat work-item index space of both
 // phases. Items are (shared tiles) followed by (expert ascending, weight block,
 // token tile); an item's expert is found by binary search over the prefix.
-__global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanParams pp) {
+__device__ __forceinline__ void plan_body(const PlanParams& pp) {
   __shared__ int s_pre[1025];   // exclusive prefix of token tiles per expert
   __shared__ int s_bn[1024];    // rows per tile of each expert
   __shared__ int s_nt[1024];    // token tiles of each expert
@@ -440,7 +640,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanParams pp)
       if (e < E) {
         const int cnt = (int)pp.counts[e];
         if (cnt > 0) {
-          nt = (cnt + BN_MAX - 1) / BN_MAX;
+          nt = (cnt + pp.bn_max - 1) / pp.bn_max;
           bn = (((cnt + nt - 1) / nt) + 15) & ~15;
         }
         s_nt[e] = nt;
@@ -474,7 +674,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanParams pp)
 
   int n_sh_tiles = 0, bn_s = 0;
   if (pp.has_shared && T > 0) {
-    n_sh_tiles = (T + BN_MAX - 1) / BN_MAX;
+    n_sh_tiles = (T + pp.bn_max - 1) / pp.bn_max;
     bn_s = (((T + n_sh_tiles - 1) / n_sh_tiles) + 15) & ~15;
   }
   const int base_gu = n_sh_tiles * pp.rb_gu_s;
@@ -494,7 +694,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanParams pp)
     pp.n_items[1] = ndn;
   }
   const int kb_part = pp.sdn_parts > 0 ? pp.kb_dn_s / pp.sdn_parts : 0;
-  const int stride = gridDim.x * blockDim.x;
+  const int stride = kPlanBlocks * kPlanThreads;
   for (int phase = 0; phase < 2; ++phase) {
     const int n = phase == 0 ? ngu : ndn;
     const int base = phase == 0 ? base_gu : base_dn;
@@ -532,6 +732,94 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanParams pp)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Activation planes for the e4m3 tensor-core path. A bf16 row v[0..K) becomes
+// two e4m3 rows with one fp32 scale s = amax / 448:
+//   hi = e4m3(v / s),  lo = e4m3((v / s - hi) * 16),  v ~= s * (hi + lo / 16)
+// (about 8 significant bits, like bf16). The planes are stored interleaved,
+// row 2i = hi of row i, row 2i + 1 = lo of row i, so one TMA box brings both
+// and the MMA's N columns alternate hi/lo per token.
+// ---------------------------------------------------------------------------
+struct QuantSeg {
+  const __nv_bfloat16* src;  // [rows, K]
+  uint8_t* dst;              // [2 * rows, K]
+  float* scale;              // [rows]
+  int rows, K;
+};
+struct QuantParams {
+  QuantSeg seg[2];
+};
+
+__device__ __forceinline__ void quant_rows(const QuantParams& q, int wglobal, int nwarps) {
+  const int lane = threadIdx.x & 31;
+  for (int si = 0; si < 2; ++si) {
+    const QuantSeg g = q.seg[si];
+    for (int row = wglobal; row < g.rows; row += nwarps) {
+      const __nv_bfloat16* src = g.src + (size_t)row * g.K;
+      float amax = 0.f;
+      for (int c = lane * 8; c < g.K; c += 256) {
+        const uint4 v = *reinterpret_cast<const uint4*>(src + c);
+        const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(b[j]);
+          amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float inv = amax > 0.f ? 448.0f / amax : 0.f;
+      uint8_t* hi = g.dst + (size_t)(2 * row) * g.K;
+      uint8_t* lo = hi + g.K;
+      for (int c = lane * 16; c < g.K; c += 512) {
+        uint4 v[2];
+        v[0] = *reinterpret_cast<const uint4*>(src + c);
+        v[1] = *reinterpret_cast<const uint4*>(src + c + 8);
+        const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(v);
+        uint32_t h4[4], l4[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t hw = 0, lw = 0;
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const float2 f = __bfloat1622float2(b[2 * j + t]);
+            const float2 x = make_float2(f.x * inv, f.y * inv);
+            const __nv_fp8x2_storage_t hq = __nv_cvt_float2_to_fp8x2(x, __NV_SATFINITE, __NV_E4M3);
+            const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(hq, __NV_E4M3);
+            const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+            const float2 r = make_float2((x.x - hf.x) * kLoPlaneGain, (x.y - hf.y) * kLoPlaneGain);
+            const __nv_fp8x2_storage_t lq = __nv_cvt_float2_to_fp8x2(r, __NV_SATFINITE, __NV_E4M3);
+            hw |= (uint32_t)hq << (16 * t);
+            lw |= (uint32_t)lq << (16 * t);
+          }
+          h4[j] = hw;
+          l4[j] = lw;
+        }
+        *reinterpret_cast<uint4*>(hi + c) = make_uint4(h4[0], h4[1], h4[2], h4[3]);
+        *reinterpret_cast<uint4*>(lo + c) = make_uint4(l4[0], l4[1], l4[2], l4[3]);
+      }
+      if (lane == 0) g.scale[row] = amax > 0.f ? amax / 448.0f : 0.f;
+    }
+  }
+}
+
+// One launch before the gate/up GEMM: blocks [0, kPlanBlocks) build the work
+// lists, the rest quantise the activation rows (when the e4m3 path runs).
+__global__ void __launch_bounds__(kPlanThreads) prep_kernel(const PlanParams pp, const QuantParams qp) {
+  if (blockIdx.x < kPlanBlocks) {
+    plan_body(pp);
+    return;
+  }
+  constexpr int kWarps = kPlanThreads / 32;
+  quant_rows(qp, (blockIdx.x - kPlanBlocks) * kWarps + warp_id(), (gridDim.x - kPlanBlocks) * kWarps);
+}
+
+// Quantisation of the SwiGLU intermediate rows between the two GEMMs.
+__global__ void __launch_bounds__(kPlanThreads) quant_kernel(const QuantParams qp) {
+  constexpr int kWarps = kPlanThreads / 32;
+  quant_rows(qp, blockIdx.x * kWarps + warp_id(), gridDim.x * kWarps);
+}
+
 }  // namespace dwdp
 
 using namespace dwdp;
@@ -564,49 +852,93 @@ bool make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int
   return r == CUDA_SUCCESS;
 }
 
+// 2-D map over the interleaved hi/lo e4m3 planes [2 * rows, cols], box {128, 2 * box_rows}.
+bool make_tmap_planes(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows) {
+  auto enc = get_encode_fn();
+  if (enc == nullptr || rows <= 0) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)(2 * rows)};
+  cuuint64_t strides[1] = {(cuuint64_t)cols};
+  cuuint32_t box[2] = {(cuuint32_t)BK8, (cuuint32_t)(2 * box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // K splits of the shared expert's down projection. Its K (= shared intermediate
 // size) is several times the routed one, so at decode sizes its few long tiles
 // would be the critical path; splitting K yields partial rows that the merge
 // sums. Prefill has enough tiles to balance without it.
+// Splits are counted in 128-input blocks so both GEMM variants cut K at the
+// same places.
 int shared_down_parts(int64_t T, int Is) {
   if (Is <= 0) return 0;
-  const int kb = Is / BK;
+  const int kb = Is / 128;
   if (T > 256) return 1;
   for (int parts = 8; parts > 1; --parts)
-    if (kb % parts == 0 && kb / parts >= 16) return parts;
+    if (kb % parts == 0 && kb / parts >= 8) return parts;
   return 1;
 }
 
-inline int box_rows_for(int64_t max_rows) {
+inline int box_rows_for(int64_t max_rows, int cap) {
   const int64_t r = ((max_rows + 15) / 16) * 16;
-  return (int)std::min<int64_t>(BN_MAX, std::max<int64_t>(16, r));
+  return (int)std::min<int64_t>(cap, std::max<int64_t>(16, r));
 }
 
 struct WsLayout {
-  size_t h_routed, h_shared, items_gu, items_dn, n_items, total;
+  size_t h_routed, h_shared, items_gu, items_dn, n_items;
+  size_t x8_r, x8_s, h8_r, h8_s, sx_r, sx_s, sh_r, sh_s, total;
   int cap_gu, cap_dn;
 };
 
+// Work-item capacity is sized for the smaller (64-token) tile cap, which bounds
+// both variants; the e4m3 activation planes are laid out for every call.
 WsLayout ws_layout(int64_t T, int K, int E, int I, int H, int Is) {
   const int64_t N = T * K;
-  const int64_t tiles_r = N / BN_MAX + std::min<int64_t>(E, N) + 1;
-  const int64_t tiles_s = Is > 0 ? (T + BN_MAX - 1) / BN_MAX : 0;
+  const int64_t Isz = Is > 0 ? Is : 0;
+  const int64_t tiles_r = N / BN8 + std::min<int64_t>(E, N) + 1;
+  const int64_t tiles_s = Is > 0 ? (T + BN8 - 1) / BN8 : 0;
   WsLayout w{};
   w.cap_gu = (int)(tiles_r * (I / BM) + tiles_s * (Is / BM));
   w.cap_dn = (int)((tiles_r + tiles_s * shared_down_parts(T, Is)) * (H / BM));
   size_t o = 0;
   w.h_routed = o; o = align256(o + (size_t)N * I * 2);
-  w.h_shared = o; o = align256(o + (size_t)T * (Is > 0 ? Is : 0) * 2);
+  w.h_shared = o; o = align256(o + (size_t)T * Isz * 2);
   w.items_gu = o; o = align256(o + (size_t)w.cap_gu * sizeof(WorkItem));
   w.items_dn = o; o = align256(o + (size_t)w.cap_dn * sizeof(WorkItem));
   w.n_items = o; o = align256(o + 16);
+  w.x8_r = o; o = align256(o + (size_t)N * H * 2);
+  w.x8_s = o; o = align256(o + (size_t)(Is > 0 ? T : 0) * H * 2);
+  w.h8_r = o; o = align256(o + (size_t)N * I * 2);
+  w.h8_s = o; o = align256(o + (size_t)T * Isz * 2);
+  w.sx_r = o; o = align256(o + (size_t)N * 4);
+  w.sx_s = o; o = align256(o + (size_t)T * 4);
+  w.sh_r = o; o = align256(o + (size_t)N * 4);
+  w.sh_s = o; o = align256(o + (size_t)T * 4);
   w.total = o;
   return w;
 }
 
 int g_num_sms = 0;
+
+template <int MODE>
+int launch_gemm_f8(const GemmParams& prm, int grid, cudaStream_t stream) {
+  using C = Cfg8<MODE>;
+  auto kfn = moe_gemm_f8_kernel<MODE>;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
+    return DWDP_ERR_CUDA;
+  kfn<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(prm);
+  return cudaGetLastError() == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;
+}
+
+// blocks for quantising `rows` rows, one warp per row, at most a few waves
+inline int quant_blocks(int64_t rows) {
+  const int64_t b = (rows + kPlanThreads / 32 - 1) / (kPlanThreads / 32);
+  return (int)std::max<int64_t>(1, std::min<int64_t>(b, 148 * 8));
+}
 
 template <int MODE, bool WFP8>
 int launch_gemm(const GemmParams& prm, int grid, cudaStream_t stream) {
@@ -649,6 +981,14 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   if (H % 128 || I % 128 || Is % 128 || E <= 0 || E > 1024) return DWDP_ERR_INVALID_ARGUMENT;
   const bool fp8 = routed->weight_dtype == DWDP_DTYPE_FP8_E4M3;
   if (!fp8 && routed->weight_dtype != DWDP_DTYPE_BF16) return DWDP_ERR_UNSUPPORTED;
+  if (shared != nullptr &&
+      (shared->weight_dtype != routed->weight_dtype || shared->scale_mode != routed->scale_mode))
+    return DWDP_ERR_UNSUPPORTED;  // both groups share one tile layout per launch
+  // per-channel e4m3 weights run on the e4m3 tensor-core kernels; block-scaled
+  // e4m3 and bf16 weights on the bf16 kernels
+  const bool native = fp8 && routed->scale_mode == DWDP_SCALE_CHANNEL;
+  const int bk = native ? BK8 : BK;
+  const int bn = native ? BN8 : BN_MAX;
   const int64_t N = T * K;
   const WsLayout L = ws_layout(T, K, E, I, H, Is);
   if (workspace == nullptr || workspace_bytes < L.total) return DWDP_ERR_CAPACITY;
@@ -659,6 +999,10 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   WorkItem* items_gu = reinterpret_cast<WorkItem*>(ws + L.items_gu);
   WorkItem* items_dn = reinterpret_cast<WorkItem*>(ws + L.items_dn);
   int* n_items = reinterpret_cast<int*>(ws + L.n_items);
+  float* sx_r = reinterpret_cast<float*>(ws + L.sx_r);
+  float* sx_s = reinterpret_cast<float*>(ws + L.sx_s);
+  float* sh_r = reinterpret_cast<float*>(ws + L.sh_r);
+  float* sh_s = reinterpret_cast<float*>(ws + L.sh_s);
   DeviceStatus* st = reinterpret_cast<DeviceStatus*>(status);
   const int has_shared = shared != nullptr ? 1 : 0;
 
@@ -667,36 +1011,55 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   pp.counts = counts; pp.offsets = offsets; pp.E = E; pp.T = (int)T; pp.has_shared = has_shared;
   pp.rb_gu_r = I / BM; pp.rb_dn_r = H / BM;
   pp.rb_gu_s = has_shared ? Is / BM : 0; pp.rb_dn_s = has_shared ? H / BM : 0;
-  pp.kb_gu = H / BK; pp.kb_dn_r = I / BK; pp.kb_dn_s = has_shared ? Is / BK : 0;
+  pp.kb_gu = H / bk; pp.kb_dn_r = I / bk; pp.kb_dn_s = has_shared ? Is / bk : 0;
   pp.sdn_parts = has_shared ? parts : 0;
+  pp.bn_max = bn;
   pp.items_gu = items_gu; pp.items_dn = items_dn; pp.n_items = n_items;
   pp.cap_gu = L.cap_gu; pp.cap_dn = L.cap_dn; pp.st = st;
-  plan_kernel<<<kPlanBlocks, kPlanThreads, 0, stream>>>(pp);
+  QuantParams qx{}, qh{};
+  if (native) {
+    qx.seg[0] = QuantSeg{reinterpret_cast<const __nv_bfloat16*>(packed_hidden), ws + L.x8_r, sx_r, (int)N, H};
+    if (has_shared)
+      qx.seg[1] = QuantSeg{reinterpret_cast<const __nv_bfloat16*>(hidden), ws + L.x8_s, sx_s, (int)T, H};
+    qh.seg[0] = QuantSeg{h_r, ws + L.h8_r, sh_r, (int)N, I};
+    if (has_shared) qh.seg[1] = QuantSeg{h_s, ws + L.h8_s, sh_s, (int)T, Is};
+  }
+  const int qx_blocks = native ? quant_blocks(N + (has_shared ? T : 0)) : 0;
+  prep_kernel<<<kPlanBlocks + qx_blocks, kPlanThreads, 0, stream>>>(pp, qx);
   if (cudaGetLastError() != cudaSuccess) return DWDP_ERR_CUDA;
 
-  // routed rows per expert tile <= min(T, BN_MAX); shared tiles <= min(T, BN_MAX)
-  const int box = box_rows_for(T);
+  // The activation box must cover the largest tile: a routed tile holds at most
+  // min(T * K, bn) rows (an expert may be picked more than once per token), a
+  // shared tile at most min(T, bn).
+  const int box_r = box_rows_for(N, bn), box_s = box_rows_for(T, bn);
+  auto map = [&](CUtensorMap* m, const void* bf16, size_t planes_off, int64_t rows, int64_t cols, int box) {
+    return native ? make_tmap_planes(m, ws + planes_off, rows, cols, box) : make_tmap(m, bf16, rows, cols, box);
+  };
   GemmParams gu{}, dn{};
   gu.g[0].enabled = N > 0;
-  if (N > 0 && !make_tmap(&gu.g[0].tmap_b, packed_hidden, N, H, box)) return DWDP_ERR_CUDA;
+  if (N > 0 && !map(&gu.g[0].tmap_b, packed_hidden, L.x8_r, N, H, box_r)) return DWDP_ERR_CUDA;
   gu.g[0].w = routed->w13; gu.g[0].s = routed->s13; gu.g[0].out = h_r; gu.g[0].row_scale = nullptr;
-  gu.g[0].K = H; gu.g[0].R = I; gu.g[0].scale_mode = routed->scale_mode; gu.g[0].box_rows = box;
+  gu.g[0].x_scale = sx_r;
+  gu.g[0].K = H; gu.g[0].R = I; gu.g[0].scale_mode = routed->scale_mode; gu.g[0].box_rows = box_r;
   gu.g[1].enabled = has_shared;
   if (has_shared) {
-    if (!make_tmap(&gu.g[1].tmap_b, hidden, T, H, box)) return DWDP_ERR_CUDA;
+    if (!map(&gu.g[1].tmap_b, hidden, L.x8_s, T, H, box_s)) return DWDP_ERR_CUDA;
     gu.g[1].w = shared->w13; gu.g[1].s = shared->s13; gu.g[1].out = h_s; gu.g[1].row_scale = nullptr;
-    gu.g[1].K = H; gu.g[1].R = Is; gu.g[1].scale_mode = shared->scale_mode; gu.g[1].box_rows = box;
+    gu.g[1].x_scale = sx_s;
+    gu.g[1].K = H; gu.g[1].R = Is; gu.g[1].scale_mode = shared->scale_mode; gu.g[1].box_rows = box_s;
   }
   gu.items = items_gu; gu.n_items = n_items; gu.st = st;
 
   dn.g[0].enabled = N > 0;
-  if (N > 0 && !make_tmap(&dn.g[0].tmap_b, h_r, N, I, box)) return DWDP_ERR_CUDA;
-  dn.g[0].w = routed->w2; dn.g[0].s = routed->s2; dn.g[0].out = weighted_out; dn.g[0].box_rows = box;
+  if (N > 0 && !map(&dn.g[0].tmap_b, h_r, L.h8_r, N, I, box_r)) return DWDP_ERR_CUDA;
+  dn.g[0].w = routed->w2; dn.g[0].s = routed->s2; dn.g[0].out = weighted_out; dn.g[0].box_rows = box_r;
+  dn.g[0].x_scale = sh_r;
   dn.g[0].row_scale = packed_weights; dn.g[0].K = I; dn.g[0].R = H; dn.g[0].scale_mode = routed->scale_mode;
   dn.g[1].enabled = has_shared;
   if (has_shared) {
-    if (!make_tmap(&dn.g[1].tmap_b, h_s, T, Is, box)) return DWDP_ERR_CUDA;
-    dn.g[1].w = shared->w2; dn.g[1].s = shared->s2; dn.g[1].out = shared_out; dn.g[1].box_rows = box;
+    if (!map(&dn.g[1].tmap_b, h_s, L.h8_s, T, Is, box_s)) return DWDP_ERR_CUDA;
+    dn.g[1].w = shared->w2; dn.g[1].s = shared->s2; dn.g[1].out = shared_out; dn.g[1].box_rows = box_s;
+    dn.g[1].x_scale = sh_s;
     dn.g[1].row_scale = shared_gate; dn.g[1].K = Is; dn.g[1].R = H; dn.g[1].scale_mode = shared->scale_mode;
     dn.g[1].part_stride = (long long)T * H;
   }
@@ -707,7 +1070,14 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   const int grid_gu = std::max(1, std::min(sms, L.cap_gu));
   const int grid_dn = std::max(1, std::min(sms, L.cap_dn));
   int rc;
-  if (fp8) {
+  if (native) {
+    rc = launch_gemm_f8<0>(gu, grid_gu, stream);
+    if (rc == DWDP_OK) {
+      quant_kernel<<<quant_blocks(N + (has_shared ? T : 0)), kPlanThreads, 0, stream>>>(qh);
+      rc = cudaGetLastError() == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;
+    }
+    if (rc == DWDP_OK) rc = launch_gemm_f8<1>(dn, grid_dn, stream);
+  } else if (fp8) {
     rc = launch_gemm<0, true>(gu, grid_gu, stream);
     if (rc == DWDP_OK) rc = launch_gemm<1, true>(dn, grid_dn, stream);
   } else {

@@ -8,17 +8,23 @@
 // the e4m3 conversion rounds to nearest even with saturation, as torch does for
 // in-range values, so the quantised bytes equal torch's.
 //
-// Tile layout: tile (rb, kb) of matrix p at index (rb * KB + kb) * P + p;
-// 128 rows x 64 inputs per tile.
-//   fp8 : 64-byte rows, plain row-major (the converter warps read them)
-//   bf16: 128-byte rows in the 128B-swizzled smem image (16-byte chunk c of
-//         row r stored at chunk c ^ (r & 7)), ready for tcgen05 operands.
+// Tile layout: tile (rb, kb) of matrix p at index (rb * KB + kb) * P + p.
+//   fp8 CHANNEL : 128 rows x 128 inputs, 128-byte rows in the 128B-swizzled smem
+//                 image (16-byte chunk c of row r stored at chunk c ^ (r & 7)):
+//                 the e4m3 operand the tcgen05 kind::f8f6f4 MMA reads directly.
+//   fp8 BLOCK128: 128 rows x 64 inputs, 64-byte rows, plain row-major (the
+//                 converter warps fold the block scale in while widening).
+//   bf16        : 128 rows x 64 inputs, 128-byte rows in the swizzled image.
 #include "common.cuh"
 
 namespace dwdp {
 
 constexpr int kTileRows = 128;
-constexpr int kTileCols = 64;
+
+// inputs per tile for a (dtype, scale mode) pair
+__host__ __device__ inline int tile_cols(int dst_dtype, int mode) {
+  return dst_dtype == DWDP_DTYPE_FP8_E4M3 && mode == DWDP_SCALE_CHANNEL ? 128 : 64;
+}
 
 template <typename TS>
 __device__ __forceinline__ float ldf(const TS* p, int64_t i);
@@ -73,6 +79,7 @@ __global__ void __launch_bounds__(128)
 tile_kernel(MatPtrs src, int R, int C, int P, int dst_dtype, int mode,
             const float* __restrict__ scales, uint8_t* __restrict__ dst) {
   const int kb = blockIdx.x, rb = blockIdx.y, p = blockIdx.z;
+  const int kTileCols = tile_cols(dst_dtype, mode);
   const int KB = C / kTileCols;
   const int r = threadIdx.x;
   const int grow = rb * kTileRows + r;
@@ -80,15 +87,17 @@ tile_kernel(MatPtrs src, int R, int C, int P, int dst_dtype, int mode,
   const int64_t tile_index = ((int64_t)rb * KB + kb) * P + p;
   const int64_t row_base = (int64_t)grow * C + kb * kTileCols;
   if (dst_dtype == DWDP_DTYPE_FP8_E4M3) {
+    const bool channel = mode == DWDP_SCALE_CHANNEL;
     float s;
-    if (mode == DWDP_SCALE_CHANNEL) s = scales[(int64_t)p * R + grow];
+    if (channel) s = scales[(int64_t)p * R + grow];
     else s = scales[((int64_t)p * (R / 128) + rb) * (C / 128) + (kb * kTileCols) / 128];
     uint8_t* out = dst + tile_index * (kTileRows * kTileCols) + r * kTileCols;
     for (int c = 0; c < kTileCols; c += 16) {
       alignas(16) uint8_t b[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) b[j] = to_e4m3(__fdiv_rn(ldf(w, row_base + c + j), s));
-      *reinterpret_cast<uint4*>(out + c) = *reinterpret_cast<uint4*>(b);
+      const int pos = channel ? (((c >> 4) ^ (r & 7)) << 4) : c;
+      *reinterpret_cast<uint4*>(out + pos) = *reinterpret_cast<uint4*>(b);
     }
   } else {
     uint8_t* out = dst + tile_index * (kTileRows * kTileCols * 2) + r * 128;
@@ -105,19 +114,21 @@ __global__ void __launch_bounds__(128)
 untile_kernel(const uint8_t* __restrict__ tiles, const float* __restrict__ scales, int R, int C,
               int P, int dst_dtype, int mode, float* __restrict__ out) {
   const int kb = blockIdx.x, rb = blockIdx.y, p = blockIdx.z;
+  const int kTileCols = tile_cols(dst_dtype, mode);
   const int KB = C / kTileCols;
   const int r = threadIdx.x;
   const int grow = rb * kTileRows + r;
   const int64_t tile_index = ((int64_t)rb * KB + kb) * P + p;
   float* o = out + ((int64_t)p * R + grow) * C + kb * kTileCols;
   if (dst_dtype == DWDP_DTYPE_FP8_E4M3) {
+    const bool channel = mode == DWDP_SCALE_CHANNEL;
     float s;
-    if (mode == DWDP_SCALE_CHANNEL) s = scales[(int64_t)p * R + grow];
+    if (channel) s = scales[(int64_t)p * R + grow];
     else s = scales[((int64_t)p * (R / 128) + rb) * (C / 128) + (kb * kTileCols) / 128];
     const uint8_t* in = tiles + tile_index * (kTileRows * kTileCols) + r * kTileCols;
     for (int c = 0; c < kTileCols; ++c) {
       __nv_fp8_e4m3 q;
-      q.__x = in[c];
+      q.__x = in[channel ? ((((c >> 4) ^ (r & 7)) << 4) | (c & 15)) : c];
       o[c] = float(q) * s;
     }
   } else {
@@ -162,7 +173,7 @@ extern "C" int dwdp_pack_launch(const void* const* src_mats, int src_dtype, int 
   if (dst_dtype == DWDP_DTYPE_FP8_E4M3 && scales == nullptr) return DWDP_ERR_INVALID_ARGUMENT;
   MatPtrs m{};
   for (int p = 0; p < P; ++p) m.p[p] = src_mats[p];
-  const dim3 tgrid(cols / kTileCols, rows / kTileRows, P);
+  const dim3 tgrid(cols / tile_cols(dst_dtype, mode), rows / kTileRows, P);
 #define DWDP_PACK(TS)                                                                          \
   do {                                                                                         \
     if (dst_dtype == DWDP_DTYPE_FP8_E4M3) {                                                    \
@@ -186,7 +197,7 @@ extern "C" int dwdp_unpack_launch(const void* tiles, const float* scales, int ro
                                   int P, int dst_dtype, int mode, float* out,
                                   cudaStream_t stream) {
   if (!pack_args_ok(rows, cols, P, dst_dtype, mode)) return DWDP_ERR_INVALID_ARGUMENT;
-  const dim3 tgrid(cols / kTileCols, rows / kTileRows, P);
+  const dim3 tgrid(cols / tile_cols(dst_dtype, mode), rows / kTileRows, P);
   untile_kernel<<<tgrid, 128, 0, stream>>>((const uint8_t*)tiles, scales, rows, cols, P,
                                            dst_dtype, mode, out);
   return cudaGetLastError() == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;

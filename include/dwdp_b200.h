@@ -133,11 +133,14 @@ int dwdp_schedule(const int64_t* counts, const int64_t* offsets, int num_experts
 /* ======================================================================== *
  * Expert weight store. Weights are kept pre-tiled in the layout the grouped
  * GEMM streams: for an [R, Kd] projection (R output rows, Kd inputs, both
- * multiples of 128) tiles of 128 rows x 64 inputs, tile (rb, kb) of matrix p
- * of a P-matrix pack at tile index (rb * (Kd/64) + kb) * P + p.
- *   FP8: 8192-byte tiles, rows of 64 bytes, scales fp32
- *        (CHANNEL: [P][R]; BLOCK128: [P][R/128][Kd/128]).
- *   BF16: 16384-byte tiles stored in the 128-byte-swizzled smem image.
+ * multiples of 128) tiles of 128 rows x TK inputs, tile (rb, kb) of matrix p
+ * of a P-matrix pack at tile index (rb * (Kd/TK) + kb) * P + p.
+ *   FP8 CHANNEL : TK = 128, 16384-byte tiles of 128-byte rows in the
+ *                 128-byte-swizzled smem image (chunk c of row r at c ^ (r&7));
+ *                 scales fp32 [P][R].
+ *   FP8 BLOCK128: TK = 64, 8192-byte tiles, plain rows of 64 bytes; scales
+ *                 fp32 [P][R/128][Kd/128].
+ *   BF16        : TK = 64, 16384-byte tiles in the 128-byte-swizzled image.
  * Quantisation follows DWDP/executor/fp8.py:118-146: scale = max(amax, 1e-5)
  * / 448, q = e4m3(w / scale) (round to nearest even, IEEE division).
  * Gate/up are packed together (P = 2, gate then up) so one tile fetch brings

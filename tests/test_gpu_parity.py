@@ -116,9 +116,17 @@ def test_router_top1_weight_is_one(pkg):
     assert torch.equal(res.topk_weights.cpu(), torch.ones(5, 1))
 
 
-def _decode_fp8_tiles(tiles: torch.Tensor, R: int, C: int, P: int) -> torch.Tensor:
-    t = tiles.cpu().view(R // 128, C // 64, P, 128, 64)
-    return t.permute(2, 0, 3, 1, 4).reshape(P, R, C)
+def _decode_fp8_tiles(tiles: torch.Tensor, R: int, C: int, P: int, channel: bool) -> torch.Tensor:
+    """Undo the packed tiling: CHANNEL tiles are 128 x 128 in the 128-byte-swizzled
+    image (16-byte chunk c of row r at c ^ (r % 8)), BLOCK128 tiles 128 x 64 plain."""
+    if not channel:
+        t = tiles.cpu().view(R // 128, C // 64, P, 128, 64)
+        return t.permute(2, 0, 3, 1, 4).reshape(P, R, C)
+    t = tiles.cpu().view(R // 128, C // 128, P, 128, 8, 16)
+    r = torch.arange(128).view(128, 1)
+    src_chunk = torch.arange(8).view(1, 8) ^ (r % 8)  # logical chunk c sits at c ^ (r % 8)
+    t = torch.gather(t, 4, src_chunk.view(1, 1, 1, 128, 8, 1).expand_as(t))
+    return t.reshape(R // 128, C // 128, P, 128, 128).permute(2, 0, 3, 1, 4).reshape(P, R, C)
 
 
 @pytest.mark.parametrize("mode", ["channel", "block"])
@@ -129,7 +137,7 @@ def test_pack_fp8_bit_exact(pkg, orc, mode):
     b = torch.randn(R, C, generator=g) * 0.5
     m = pkg._lib.SCALE_CHANNEL if mode == "channel" else pkg._lib.SCALE_BLOCK128
     tiles, scales = pkg.ops.pack_weights([a.to(DEV), b.to(DEV)], torch.float8_e4m3fn, m)
-    q = _decode_fp8_tiles(tiles, R, C, 2)
+    q = _decode_fp8_tiles(tiles, R, C, 2, mode == "channel")
     for p, src in enumerate((a, b)):
         rq, rs = orc.quantize_channel(src) if mode == "channel" else orc.quantize_blockwise(src)
         assert torch.equal(q[p], rq.view(torch.uint8)), f"mat {p}: quantised bytes differ"
@@ -258,3 +266,42 @@ def test_moe_layer_shared_k_split(pkg, orc, T):
     layer = _make_layer(pkg, 8, 256, 128, 2, 2048, torch.float8_e4m3fn, pkg._lib.SCALE_BLOCK128)
     assert pkg.ops.moe_shared_parts(T, 2048) == 2
     _check_layer(pkg, orc, layer, T, FP8_TOL)
+
+
+@pytest.mark.parametrize("mode", ["channel", "block"])
+@pytest.mark.parametrize("T", [1, 5, 200])
+def test_moe_layer_shared_k_split_modes(pkg, orc, mode, T):
+    m = pkg._lib.SCALE_CHANNEL if mode == "channel" else pkg._lib.SCALE_BLOCK128
+    layer = _make_layer(pkg, 8, 256, 128, 2, 2048, torch.float8_e4m3fn, m, seed=4)
+    _check_layer(pkg, orc, layer, T, FP8_TOL)
+
+
+@pytest.mark.parametrize("mode", ["channel", "block", "bf16"])
+def test_moe_experts_repeated_expert(pkg, orc, mode):
+    """Routing that names one expert K times per token (a hand-built plan no
+    top-k router produces): one expert then holds T * K rows, more than T, and
+    its tiles must still be covered by the activation box."""
+    wdtype = torch.bfloat16 if mode == "bf16" else torch.float8_e4m3fn
+    m = {"channel": pkg._lib.SCALE_CHANNEL, "block": pkg._lib.SCALE_BLOCK128, "bf16": pkg._lib.SCALE_NONE}[mode]
+    layer = _make_layer(pkg, 4, 256, 256, 4, 0, wdtype, m, seed=6)
+    T, K = 20, 4
+    x = torch.randn(T, 256, generator=torch.Generator().manual_seed(2)).bfloat16()
+    ids = torch.zeros(T, K, dtype=torch.int64)
+    ids[:, 3] = 2
+    wts = torch.rand(T, K, generator=torch.Generator().manual_seed(3))
+    ws = layer.workspace(T)
+    ws.router.topk_indices.copy_(ids)
+    ws.router.topk_weights.copy_(wts)
+    xd = x.to(DEV)
+    pkg.ops.dispatch(ws.router.topk_indices, ws.router.topk_weights, layer.num_experts, hidden=xd,
+                     scratch=ws.dispatch_scratch, out=ws.dispatch, status=ws.status)
+    pkg.ops.moe_experts(layer._routed_group, None, ws.dispatch.packed_hidden, xd, K,
+                        ws.dispatch.expert_counts, ws.dispatch.expert_offsets,
+                        ws.dispatch.packed_routing_weights, None, ws.weighted, None, ws.moe_ws, ws.status)
+    y = pkg.ops.merge(ws.weighted, ws.dispatch.inverse_permutation, T, K, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert layer.read_status(T)[0] == 0
+    experts = [tuple(t.cpu() for t in layer.experts.dequantized(e)) for e in range(layer.num_experts)]
+    ref = orc.moe_forward(x.float(), ids, wts, experts)
+    err = orc.rel_frobenius(y.cpu(), ref)
+    assert err < (BF16_TOL if mode == "bf16" else FP8_TOL), err
