@@ -100,6 +100,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
          c_void_p, c_void_p],
     ),
+    "dwdp_moe_experts_indexed": (
+        c_int,
+        [ctypes.POINTER(ExpertGroup), ctypes.POINTER(ExpertGroup), c_void_p, c_void_p, c_int64,
+         c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+         c_void_p, c_void_p],
+    ),
     "dwdp_merge": (
         c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_void_p, c_int, c_void_p]
     ),

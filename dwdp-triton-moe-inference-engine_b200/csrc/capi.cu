@@ -29,7 +29,7 @@ extern "C" int dwdp_unpack_launch(const void*, const float*, int, int, int, int,
                                   cudaStream_t);
 extern "C" size_t dwdp_moe_workspace_bytes_impl(int64_t, int, int, int, int, int);
 extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group*, const dwdp_expert_group*,
-                                       const void*, const void*, int64_t, int, const int64_t*,
+                                       const void*, const int64_t*, const void*, int64_t, int, const int64_t*,
                                        const int64_t*, const float*, const float*, void*, void*,
                                        void*, size_t, int*, cudaStream_t);
 extern "C" int dwdp_merge_launch(const void*, const int64_t*, const void*, int, int64_t, int, int,
@@ -204,11 +204,12 @@ extern "C" size_t dwdp_moe_workspace_bytes(int64_t num_tokens, int top_k, int nu
                                        shared_intermediate_size);
 }
 
-extern "C" int dwdp_moe_experts(const dwdp_expert_group* routed, const dwdp_expert_group* shared,
-                                const void* packed_hidden, const void* hidden, int64_t num_tokens, int top_k,
-                                const int64_t* counts, const int64_t* offsets, const float* packed_weights,
-                                const float* shared_gate, void* weighted_out, void* shared_out, void* workspace,
-                                size_t workspace_bytes, int* status, void* stream) {
+namespace {
+int moe_experts_checked(const dwdp_expert_group* routed, const dwdp_expert_group* shared,
+                        const void* packed_hidden, const int64_t* packed_tok, const void* hidden,
+                        int64_t num_tokens, int top_k, const int64_t* counts, const int64_t* offsets,
+                        const float* packed_weights, const float* shared_gate, void* weighted_out,
+                        void* shared_out, void* workspace, size_t workspace_bytes, int* status, void* stream) {
   g_last_error.clear();
   if (routed == nullptr) return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_experts: routed group is required");
   if (routed->hidden_size <= 0 || routed->hidden_size > 8192)
@@ -220,13 +221,17 @@ extern "C" int dwdp_moe_experts(const dwdp_expert_group* routed, const dwdp_expe
       routed->scale_mode != DWDP_SCALE_BLOCK128)
     return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_experts: fp8 weights need a CHANNEL or BLOCK128 scale mode");
   if (shared != nullptr && (shared->num_experts != 1 || shared->hidden_size != routed->hidden_size ||
-                            shared->weight_dtype != routed->weight_dtype))
+                            shared->weight_dtype != routed->weight_dtype ||
+                            shared->scale_mode != routed->scale_mode))
     return fail(DWDP_ERR_INVALID_ARGUMENT,
-                "moe_experts: shared group must hold one expert of the routed hidden size and weight dtype");
+                "moe_experts: shared group must hold one expert of the routed hidden size, weight dtype and "
+                "scale mode");
   if (top_k <= 0 || num_tokens < 0) return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_experts: bad top_k/num_tokens");
   if (num_tokens > 0 && (counts == nullptr || offsets == nullptr || weighted_out == nullptr ||
-                         packed_weights == nullptr || packed_hidden == nullptr))
+                         packed_weights == nullptr || (packed_hidden == nullptr && packed_tok == nullptr)))
     return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_experts: null pointer");
+  if (packed_tok != nullptr && hidden == nullptr)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_experts: packed token indices need hidden");
   if (shared != nullptr && (hidden == nullptr || shared_out == nullptr))
     return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_experts: shared group needs hidden and shared_out");
   const size_t need = dwdp_moe_workspace_bytes(num_tokens, top_k, routed->num_experts,
@@ -234,10 +239,32 @@ extern "C" int dwdp_moe_experts(const dwdp_expert_group* routed, const dwdp_expe
                                                shared ? shared->intermediate_size : 0);
   if (workspace == nullptr || workspace_bytes < need)
     return fail(DWDP_ERR_CAPACITY, "moe_experts: workspace of %zu bytes < required %zu", workspace_bytes, need);
-  return check(dwdp_moe_experts_launch(routed, shared, packed_hidden, hidden, num_tokens, top_k, counts, offsets,
-                                       packed_weights, shared_gate, weighted_out, shared_out, workspace,
-                                       workspace_bytes, status, as_stream(stream)),
+  return check(dwdp_moe_experts_launch(routed, shared, packed_hidden, packed_tok, hidden, num_tokens, top_k,
+                                       counts, offsets, packed_weights, shared_gate, weighted_out, shared_out,
+                                       workspace, workspace_bytes, status, as_stream(stream)),
                "moe_experts");
+}
+}  // namespace
+
+extern "C" int dwdp_moe_experts(const dwdp_expert_group* routed, const dwdp_expert_group* shared,
+                                const void* packed_hidden, const void* hidden, int64_t num_tokens, int top_k,
+                                const int64_t* counts, const int64_t* offsets, const float* packed_weights,
+                                const float* shared_gate, void* weighted_out, void* shared_out, void* workspace,
+                                size_t workspace_bytes, int* status, void* stream) {
+  return moe_experts_checked(routed, shared, packed_hidden, nullptr, hidden, num_tokens, top_k, counts, offsets,
+                             packed_weights, shared_gate, weighted_out, shared_out, workspace, workspace_bytes,
+                             status, stream);
+}
+
+extern "C" int dwdp_moe_experts_indexed(const dwdp_expert_group* routed, const dwdp_expert_group* shared,
+                                        const int64_t* packed_token_indices, const void* hidden,
+                                        int64_t num_tokens, int top_k, const int64_t* counts,
+                                        const int64_t* offsets, const float* packed_weights,
+                                        const float* shared_gate, void* weighted_out, void* shared_out,
+                                        void* workspace, size_t workspace_bytes, int* status, void* stream) {
+  return moe_experts_checked(routed, shared, nullptr, packed_token_indices, hidden, num_tokens, top_k, counts,
+                             offsets, packed_weights, shared_gate, weighted_out, shared_out, workspace,
+                             workspace_bytes, status, stream);
 }
 
 extern "C" int dwdp_merge(const void* weighted, const int64_t* inv, const void* shared_out, int shared_parts,

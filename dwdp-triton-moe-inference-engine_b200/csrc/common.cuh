@@ -10,6 +10,9 @@
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 #include <stdint.h>
+#include <stdlib.h>
+
+#include <utility>
 
 #include "dwdp_b200.h"
 
@@ -236,5 +239,54 @@ __device__ __forceinline__ float silu(float g) { return g / (1.0f + __expf(-g));
 
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch. Every kernel of the layer chain is launched
+// with programmatic stream serialisation: it lets its successor launch at once
+// (griddep_launch at entry) and waits for its predecessor's completion and
+// memory (griddep_wait) just before its first global-memory access, so launch
+// latency and prologues (barrier init, TMEM allocation, descriptor prefetch)
+// overlap the previous kernel's tail. Both instructions are no-ops when the
+// launch carried no programmatic dependency. DWDP_NO_PDL=1 launches plainly.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("DWDP_NO_PDL");
+    return v == nullptr || v[0] == '\0' || v[0] == '0';
+  }();
+  return on;
+}
+
+// cudaLaunchKernelEx with the programmatic-serialisation attribute and, when
+// cluster_y > 1, a (1, cluster_y, 1) thread-block cluster.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_chained(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                  cudaStream_t stream, unsigned cluster_y, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_y > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = cluster_y;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace dwdp

@@ -9,9 +9,10 @@
 //   perm[dest]  = i,  inv[i] = dest,  ids[dest] = e_i,
 //   tok[dest]   = i / K,  packed_w[dest] = w_i (bit copy)
 //
-// Three launches, no host synchronisation:
+// Up to three launches, no host synchronisation:
 //   1. tile histogram: each CTA of kTile assignments writes int32 counts [E]
-//      into the caller's scratch
+//      into the caller's scratch (skipped for a single tile, T * K <= kTile:
+//      the scatter CTA counts its own elements)
 //   2. scatter: each CTA reduces the tile histograms before it (its exclusive
 //      start inside each expert segment) and all of them (global counts ->
 //      offsets), ranks its own elements stably with warp match masks plus
@@ -28,6 +29,8 @@ constexpr int kMaxExperts = 1024;
 __global__ void __launch_bounds__(kTile)
 dispatch_hist_kernel(const int64_t* __restrict__ idx, int64_t N, int E, int* __restrict__ tile_hist,
                      DeviceStatus* st) {
+  griddep_launch();
+  griddep_wait();
   __shared__ int h[kMaxExperts];
   for (int e = threadIdx.x; e < E; e += blockDim.x) h[e] = 0;
   __syncthreads();
@@ -51,7 +54,9 @@ dispatch_scatter_kernel(const int64_t* __restrict__ idx, const TWt* __restrict__
                         int64_t* __restrict__ counts, int64_t* __restrict__ offsets,
                         int64_t* __restrict__ perm, int64_t* __restrict__ inv,
                         int64_t* __restrict__ ids, int64_t* __restrict__ tok,
-                        TWt* __restrict__ packed_w) {
+                        TWt* __restrict__ packed_w, DeviceStatus* st) {
+  griddep_launch();
+  griddep_wait();
   __shared__ int s_start[kMaxExperts];  // offsets[e] + tiles-before prefix
   __shared__ int s_tot[kMaxExperts];
   __shared__ int s_scan[kTile];
@@ -60,15 +65,29 @@ dispatch_scatter_kernel(const int64_t* __restrict__ idx, const TWt* __restrict__
   const int tile = blockIdx.x;
 
   // 1. per expert: total count and the count in the tiles before this one
-  for (int e = tid; e < E; e += kTile) {
-    int pre = 0, tot = 0;
-    for (int t = 0; t < ntiles; ++t) {
-      const int v = tile_hist[(int64_t)t * E + e];
-      tot += v;
-      pre += (t < tile) ? v : 0;
+  //    (a single tile, tile_hist == nullptr, counts its own elements here)
+  if (tile_hist == nullptr) {
+    for (int e = tid; e < E; e += kTile) {
+      s_tot[e] = 0;
+      s_start[e] = 0;
     }
-    s_tot[e] = tot;
-    s_start[e] = pre;
+    __syncthreads();
+    if (tid < N) {
+      const int64_t ev = idx[tid];
+      if (ev >= 0 && ev < E) atomicAdd(&s_tot[ev], 1);
+      else record_error(st, DWDP_ERR_DEVICE_BOUNDS, 100, tid);
+    }
+  } else {
+    for (int e = tid; e < E; e += kTile) {
+      int pre = 0, tot = 0;
+      for (int t = 0; t < ntiles; ++t) {
+        const int v = tile_hist[(int64_t)t * E + e];
+        tot += v;
+        pre += (t < tile) ? v : 0;
+      }
+      s_tot[e] = tot;
+      s_start[e] = pre;
+    }
   }
   for (int i = tid; i < (kTile / 32) * E; i += kTile) s_wcnt[i] = 0;
   __syncthreads();
@@ -130,6 +149,8 @@ __global__ void __launch_bounds__(256)
 gather_rows_kernel(const __nv_bfloat16* __restrict__ hidden, const int64_t* __restrict__ tok,
                    int64_t N, int H, int64_t T, __nv_bfloat16* __restrict__ packed,
                    DeviceStatus* st) {
+  griddep_launch();
+  griddep_wait();
   const int64_t d = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (d >= N) return;
   const int lane = threadIdx.x & 31;
@@ -156,9 +177,11 @@ using namespace dwdp;
 extern "C" int dwdp_gather_rows_launch(const void* hidden, const int64_t* tok, int64_t N, int H, int64_t T,
                                        void* packed, int* status, cudaStream_t stream) {
   if (N <= 0) return DWDP_OK;
-  gather_rows_kernel<<<(unsigned)((N + 7) / 8), 256, 0, stream>>>(
-      (const __nv_bfloat16*)hidden, tok, N, H, T, (__nv_bfloat16*)packed, reinterpret_cast<DeviceStatus*>(status));
-  return cudaGetLastError() == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;
+  return launch_chained(gather_rows_kernel, dim3((unsigned)((N + 7) / 8)), dim3(256), 0, stream, 1u,
+                        (const __nv_bfloat16*)hidden, tok, N, H, T, (__nv_bfloat16*)packed,
+                        reinterpret_cast<DeviceStatus*>(status)) == cudaSuccess
+             ? DWDP_OK
+             : DWDP_ERR_CUDA;
 }
 
 extern "C" size_t dwdp_dispatch_scratch_bytes(int64_t num_tokens, int top_k, int num_experts) {
@@ -182,24 +205,31 @@ extern "C" int dwdp_dispatch_launch(const int64_t* idx, const void* wts, int wei
     return DWDP_OK;
   }
   const int ntiles = (int)((N + kTile - 1) / kTile);
-  int* tile_hist = reinterpret_cast<int*>(scratch);
-  dispatch_hist_kernel<<<ntiles, kTile, 0, stream>>>(idx, N, E, tile_hist, st);
+  // one tile (T * K <= 256, decode batches): the scatter CTA builds its own histogram
+  int* tile_hist = ntiles > 1 ? reinterpret_cast<int*>(scratch) : nullptr;
+  if (ntiles > 1 && launch_chained(dispatch_hist_kernel, dim3(ntiles), dim3(kTile), 0, stream, 1u, idx, N, E,
+                                   tile_hist, st) != cudaSuccess)
+    return DWDP_ERR_CUDA;
   const size_t smem = sizeof(int) * (size_t)(kTile / 32) * E;
   if (weight_dtype == DWDP_DTYPE_F32) {
-    auto kfn = dispatch_scatter_kernel<float>;
-    kfn<<<ntiles, kTile, smem, stream>>>(idx, (const float*)wts, N, K, E, ntiles, tile_hist, counts,
-                                         offsets, perm, inv, ids, tok, (float*)packed_w);
+    if (launch_chained(dispatch_scatter_kernel<float>, dim3(ntiles), dim3(kTile), smem, stream, 1u, idx,
+                       (const float*)wts, N, K, E, ntiles, (const int*)tile_hist, counts, offsets, perm, inv, ids,
+                       tok, (float*)packed_w, st) != cudaSuccess)
+      return DWDP_ERR_CUDA;
   } else if (weight_dtype == DWDP_DTYPE_BF16 || weight_dtype == DWDP_DTYPE_F16) {
-    auto kfn = dispatch_scatter_kernel<uint16_t>;
-    kfn<<<ntiles, kTile, smem, stream>>>(idx, (const uint16_t*)wts, N, K, E, ntiles, tile_hist,
-                                         counts, offsets, perm, inv, ids, tok, (uint16_t*)packed_w);
+    if (launch_chained(dispatch_scatter_kernel<uint16_t>, dim3(ntiles), dim3(kTile), smem, stream, 1u, idx,
+                       (const uint16_t*)wts, N, K, E, ntiles, (const int*)tile_hist, counts, offsets, perm, inv,
+                       ids, tok, (uint16_t*)packed_w, st) != cudaSuccess)
+      return DWDP_ERR_CUDA;
   } else {
     return DWDP_ERR_UNSUPPORTED;
   }
   if (hidden != nullptr && packed_hidden != nullptr) {
     const int64_t blocks = (N + 7) / 8;
-    gather_rows_kernel<<<(unsigned)blocks, 256, 0, stream>>>(
-        (const __nv_bfloat16*)hidden, tok, N, H, T, (__nv_bfloat16*)packed_hidden, st);
+    if (launch_chained(gather_rows_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, 1u,
+                       (const __nv_bfloat16*)hidden, (const int64_t*)tok, N, H, T, (__nv_bfloat16*)packed_hidden,
+                       st) != cudaSuccess)
+      return DWDP_ERR_CUDA;
   }
   return cudaGetLastError() == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;
 }

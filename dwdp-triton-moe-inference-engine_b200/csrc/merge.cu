@@ -13,47 +13,65 @@
 
 namespace dwdp {
 
+constexpr int kMergeMaxK = 16;
+constexpr int kMergeMaxParts = 8;
+
+// 8 bf16 of a 16-byte vector added into acc[0..8)
+__device__ __forceinline__ void add8(float (&acc)[8], const uint4& v) {
+  const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float2 f = __bfloat1622float2(b[q]);
+    acc[2 * q] += f.x;
+    acc[2 * q + 1] += f.y;
+  }
+}
+
+// One CTA per token. Thread 0 sorts the token's K packed rows ascending in
+// shared memory; every thread then issues all of its row loads (and the shared
+// partials) before summing them in that fixed order, so a token costs about one
+// memory latency.
 template <typename TOut>
 __global__ void __launch_bounds__(256)
 merge_kernel(const __nv_bfloat16* __restrict__ weighted, const int64_t* __restrict__ inv,
              const __nv_bfloat16* __restrict__ shared_out, int shared_parts, int64_t T, int K, int H,
-             int64_t nrows,
-             TOut* __restrict__ out, DeviceStatus* st) {
+             int64_t nrows, TOut* __restrict__ out, DeviceStatus* st) {
+  griddep_launch();
+  __shared__ int64_t s_rows[kMergeMaxK];
+  __shared__ int s_nk;
   const int64_t t = blockIdx.x;
-  int64_t rows[16];
-  int nk = 0;
-  for (int k = 0; k < K; ++k) {
-    const int64_t r = inv[t * K + k];
-    if (r < 0 || r >= nrows) {
-      if (threadIdx.x == 0) record_error(st, DWDP_ERR_DEVICE_BOUNDS, 300, (int)t);
-      continue;
+  griddep_wait();
+  if (threadIdx.x == 0) {
+    int nk = 0;
+    for (int k = 0; k < K; ++k) {
+      const int64_t r = inv[t * K + k];
+      if (r < 0 || r >= nrows) {
+        record_error(st, DWDP_ERR_DEVICE_BOUNDS, 300, (int)t);
+        continue;
+      }
+      int p = nk++;  // insertion into ascending order
+      while (p > 0 && s_rows[p - 1] > r) { s_rows[p] = s_rows[p - 1]; --p; }
+      s_rows[p] = r;
     }
-    int p = nk++;  // insertion into ascending order
-    while (p > 0 && rows[p - 1] > r) { rows[p] = rows[p - 1]; --p; }
-    rows[p] = r;
+    s_nk = nk;
   }
+  __syncthreads();
+  const int nk = s_nk;
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    uint4 v[kMergeMaxK], sv[kMergeMaxParts];
+#pragma unroll
+    for (int j = 0; j < kMergeMaxK; ++j)
+      if (j < nk) v[j] = *reinterpret_cast<const uint4*>(weighted + s_rows[j] * H + c);
+#pragma unroll
+    for (int sp = 0; sp < kMergeMaxParts; ++sp)
+      if (sp < shared_parts) sv[sp] = *reinterpret_cast<const uint4*>(shared_out + ((int64_t)sp * T + t) * H + c);
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < nk; ++j) {
-      const uint4 v = *reinterpret_cast<const uint4*>(weighted + rows[j] * H + c);
-      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 f = __bfloat1622float2(b[q]);
-        acc[2 * q] += f.x;
-        acc[2 * q + 1] += f.y;
-      }
-    }
-    for (int sp = 0; sp < shared_parts; ++sp) {
-      const uint4 v = *reinterpret_cast<const uint4*>(shared_out + ((int64_t)sp * T + t) * H + c);
-      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
+    for (int j = 0; j < kMergeMaxK; ++j)
+      if (j < nk) add8(acc, v[j]);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 f = __bfloat1622float2(b[q]);
-        acc[2 * q] += f.x;
-        acc[2 * q + 1] += f.y;
-      }
-    }
+    for (int sp = 0; sp < kMergeMaxParts; ++sp)
+      if (sp < shared_parts) add8(acc, sv[sp]);
     if constexpr (sizeof(TOut) == 2) {
       uint4 o;
       __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&o);
@@ -76,19 +94,22 @@ extern "C" int dwdp_merge_launch(const void* weighted, const int64_t* inv, const
                                  int shared_parts, int64_t T, int K, int H, void* out, int out_dtype,
                                  int* status,
                                  cudaStream_t stream) {
-  if (K <= 0 || K > 16 || (H & 7) != 0 || T < 0) return DWDP_ERR_INVALID_ARGUMENT;
+  if (K <= 0 || K > kMergeMaxK || (H & 7) != 0 || T < 0 || shared_parts < 0) return DWDP_ERR_INVALID_ARGUMENT;
+  if (shared_out != nullptr && shared_parts > kMergeMaxParts) return DWDP_ERR_UNSUPPORTED;
   if (T == 0) return DWDP_OK;
   if (shared_out == nullptr) shared_parts = 0;
   DeviceStatus* st = reinterpret_cast<DeviceStatus*>(status);
   const int threads = H / 8 >= 256 ? 256 : ((H / 8 + 31) / 32) * 32;
   if (out_dtype == DWDP_DTYPE_BF16) {
-    merge_kernel<__nv_bfloat16><<<(unsigned)T, threads, 0, stream>>>(
-        (const __nv_bfloat16*)weighted, inv, (const __nv_bfloat16*)shared_out, shared_parts, T, K, H, T * K,
-        (__nv_bfloat16*)out, st);
+    if (launch_chained(merge_kernel<__nv_bfloat16>, dim3((unsigned)T), dim3(threads), 0, stream, 1u,
+                       (const __nv_bfloat16*)weighted, inv, (const __nv_bfloat16*)shared_out, shared_parts, T, K, H,
+                       T * K, (__nv_bfloat16*)out, st) != cudaSuccess)
+      return DWDP_ERR_CUDA;
   } else if (out_dtype == DWDP_DTYPE_F32) {
-    merge_kernel<float><<<(unsigned)T, threads, 0, stream>>>(
-        (const __nv_bfloat16*)weighted, inv, (const __nv_bfloat16*)shared_out, shared_parts, T, K, H, T * K,
-        (float*)out, st);
+    if (launch_chained(merge_kernel<float>, dim3((unsigned)T), dim3(threads), 0, stream, 1u,
+                       (const __nv_bfloat16*)weighted, inv, (const __nv_bfloat16*)shared_out, shared_parts, T, K, H,
+                       T * K, (float*)out, st) != cudaSuccess)
+      return DWDP_ERR_CUDA;
   } else {
     return DWDP_ERR_UNSUPPORTED;
   }

@@ -169,6 +169,7 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
   const int warp = warp_id();
   const int lane = lane_id();
   DeviceStatus* st = p.st;
+  griddep_launch();
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -196,6 +197,7 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = s_tmem_base;
+  griddep_wait();  // the work list and operands come from the previous launches
   const int n_items = *p.n_items;
 
   if (warp == 0) {
@@ -446,6 +448,7 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
   const int warp = warp_id();
   const int lane = lane_id();
   DeviceStatus* st = p.st;
+  griddep_launch();
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -471,6 +474,7 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = s_tmem_base;
+  griddep_wait();  // the work list and operands come from the previous launches
   const int n_items = *p.n_items;
 
   if (warp == 0) {
@@ -741,83 +745,134 @@ __device__ __forceinline__ void plan_body(const PlanParams& pp) {
 // and the MMA's N columns alternate hi/lo per token.
 // ---------------------------------------------------------------------------
 struct QuantSeg {
-  const __nv_bfloat16* src;  // [rows, K]
+  const __nv_bfloat16* src;  // [src_rows, K]
   uint8_t* dst;              // [2 * rows, K]
   float* scale;              // [rows]
   int rows, K;
+  const int64_t* row_index;  // row r reads src row row_index[r] (null: row r)
+  int64_t src_rows;
 };
 struct QuantParams {
   QuantSeg seg[2];
+  DeviceStatus* st;
 };
 
-__device__ __forceinline__ void quant_rows(const QuantParams& q, int wglobal, int nwarps) {
-  const int lane = threadIdx.x & 31;
-  for (int si = 0; si < 2; ++si) {
-    const QuantSeg g = q.seg[si];
-    for (int row = wglobal; row < g.rows; row += nwarps) {
-      const __nv_bfloat16* src = g.src + (size_t)row * g.K;
-      float amax = 0.f;
-      for (int c = lane * 8; c < g.K; c += 256) {
-        const uint4 v = *reinterpret_cast<const uint4*>(src + c);
-        const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
+// 8 bf16 (one 16-byte load) -> 8 hi bytes and 8 lo bytes
+__device__ __forceinline__ void quant8(const uint4 v, float inv, uint2& hi8, uint2& lo8) {
+  const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
+  uint32_t h[2] = {0, 0}, l[2] = {0, 0};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __bfloat1622float2(b[j]);
-          amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
-        }
-      }
+  for (int q = 0; q < 4; ++q) {
+    const float2 f = __bfloat1622float2(b[q]);
+    const float2 xs = make_float2(f.x * inv, f.y * inv);
+    const __nv_fp8x2_storage_t hq = __nv_cvt_float2_to_fp8x2(xs, __NV_SATFINITE, __NV_E4M3);
+    const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(hq, __NV_E4M3);
+    const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+    const float2 r = make_float2((xs.x - hf.x) * kLoPlaneGain, (xs.y - hf.y) * kLoPlaneGain);
+    const __nv_fp8x2_storage_t lq = __nv_cvt_float2_to_fp8x2(r, __NV_SATFINITE, __NV_E4M3);
+    h[q >> 1] |= (uint32_t)hq << (16 * (q & 1));
+    l[q >> 1] |= (uint32_t)lq << (16 * (q & 1));
+  }
+  hi8 = make_uint2(h[0], h[1]);
+  lo8 = make_uint2(l[0], l[1]);
+}
+
+__device__ __forceinline__ float amax8(const uint4 v, float m) {
+  const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      const float inv = amax > 0.f ? 448.0f / amax : 0.f;
-      uint8_t* hi = g.dst + (size_t)(2 * row) * g.K;
-      uint8_t* lo = hi + g.K;
-      for (int c = lane * 16; c < g.K; c += 512) {
-        uint4 v[2];
-        v[0] = *reinterpret_cast<const uint4*>(src + c);
-        v[1] = *reinterpret_cast<const uint4*>(src + c + 8);
-        const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(v);
-        uint32_t h4[4], l4[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t hw = 0, lw = 0;
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const float2 f = __bfloat1622float2(b[2 * j + t]);
-            const float2 x = make_float2(f.x * inv, f.y * inv);
-            const __nv_fp8x2_storage_t hq = __nv_cvt_float2_to_fp8x2(x, __NV_SATFINITE, __NV_E4M3);
-            const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(hq, __NV_E4M3);
-            const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&hr));
-            const float2 r = make_float2((x.x - hf.x) * kLoPlaneGain, (x.y - hf.y) * kLoPlaneGain);
-            const __nv_fp8x2_storage_t lq = __nv_cvt_float2_to_fp8x2(r, __NV_SATFINITE, __NV_E4M3);
-            hw |= (uint32_t)hq << (16 * t);
-            lw |= (uint32_t)lq << (16 * t);
-          }
-          h4[j] = hw;
-          l4[j] = lw;
-        }
-        *reinterpret_cast<uint4*>(hi + c) = make_uint4(h4[0], h4[1], h4[2], h4[3]);
-        *reinterpret_cast<uint4*>(lo + c) = make_uint4(l4[0], l4[1], l4[2], l4[3]);
-      }
-      if (lane == 0) g.scale[row] = amax > 0.f ? amax / 448.0f : 0.f;
+  for (int q = 0; q < 4; ++q) {
+    const float2 f = __bfloat1622float2(b[q]);
+    m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+  }
+  return m;
+}
+
+// One CTA (kPlanThreads threads) quantises one row: every 16-byte load of the
+// row is issued before the amax reduction (rows up to kQuantRegChunks * 2048
+// elements stay in registers; longer rows re-read their tail), so a row costs
+// about one memory latency.
+constexpr int kQuantRegChunks = 4;
+
+__device__ __forceinline__ void quant_row_block(const QuantSeg& g, int row, float* red, DeviceStatus* st) {
+  const int tid = threadIdx.x;
+  int64_t sr = row;
+  if (g.row_index != nullptr) {
+    sr = g.row_index[row];
+    if (sr < 0 || sr >= g.src_rows) {  // bad index: record it, quantise a zero row
+      if (tid == 0) record_error(st, DWDP_ERR_DEVICE_BOUNDS, 210, row);
+      sr = -1;
     }
+  }
+  const __nv_bfloat16* src = sr >= 0 ? g.src + (size_t)sr * g.K : nullptr;
+  const int K = src != nullptr ? g.K : 0;  // a zero row reads nothing
+  constexpr int kStride = kPlanThreads * 8;
+  uint4 v[kQuantRegChunks];
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < kQuantRegChunks; ++j) {
+    const int c = j * kStride + tid * 8;
+    v[j] = c < K ? *reinterpret_cast<const uint4*>(src + c) : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int j = 0; j < kQuantRegChunks; ++j) amax = amax8(v[j], amax);
+  for (int c = kQuantRegChunks * kStride + tid * 8; c < K; c += kStride)
+    amax = amax8(*reinterpret_cast<const uint4*>(src + c), amax);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((tid & 31) == 0) red[tid >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int i = 1; i < kPlanThreads / 32; ++i) amax = fmaxf(amax, red[i]);
+  __syncthreads();  // red is reused by the next row
+  const float inv = amax > 0.f ? 448.0f / amax : 0.f;
+  uint8_t* hi = g.dst + (size_t)(2 * row) * g.K;
+  uint8_t* lo = hi + g.K;
+#pragma unroll
+  for (int j = 0; j < kQuantRegChunks; ++j) {
+    const int c = j * kStride + tid * 8;
+    if (c < g.K) {
+      uint2 h8, l8;
+      quant8(v[j], inv, h8, l8);
+      *reinterpret_cast<uint2*>(hi + c) = h8;
+      *reinterpret_cast<uint2*>(lo + c) = l8;
+    }
+  }
+  for (int c = kQuantRegChunks * kStride + tid * 8; c < g.K; c += kStride) {
+    uint2 h8, l8;
+    quant8(K > 0 ? *reinterpret_cast<const uint4*>(src + c) : make_uint4(0, 0, 0, 0), inv, h8, l8);
+    *reinterpret_cast<uint2*>(hi + c) = h8;
+    *reinterpret_cast<uint2*>(lo + c) = l8;
+  }
+  if (tid == 0) g.scale[row] = amax > 0.f ? amax / 448.0f : 0.f;
+}
+
+__device__ __forceinline__ void quant_rows(const QuantParams& q, int first, int stride) {
+  __shared__ float red[kPlanThreads / 32];
+  const int total = q.seg[0].rows + q.seg[1].rows;
+  for (int r = first; r < total; r += stride) {
+    if (r < q.seg[0].rows) quant_row_block(q.seg[0], r, red, q.st);
+    else quant_row_block(q.seg[1], r - q.seg[0].rows, red, q.st);
   }
 }
 
 // One launch before the gate/up GEMM: blocks [0, kPlanBlocks) build the work
 // lists, the rest quantise the activation rows (when the e4m3 path runs).
 __global__ void __launch_bounds__(kPlanThreads) prep_kernel(const PlanParams pp, const QuantParams qp) {
+  griddep_launch();
+  griddep_wait();
   if (blockIdx.x < kPlanBlocks) {
     plan_body(pp);
     return;
   }
-  constexpr int kWarps = kPlanThreads / 32;
-  quant_rows(qp, (blockIdx.x - kPlanBlocks) * kWarps + warp_id(), (gridDim.x - kPlanBlocks) * kWarps);
+  quant_rows(qp, blockIdx.x - kPlanBlocks, gridDim.x - kPlanBlocks);
 }
 
 // Quantisation of the SwiGLU intermediate rows between the two GEMMs.
 __global__ void __launch_bounds__(kPlanThreads) quant_kernel(const QuantParams qp) {
-  constexpr int kWarps = kPlanThreads / 32;
-  quant_rows(qp, blockIdx.x * kWarps + warp_id(), gridDim.x * kWarps);
+  griddep_launch();
+  griddep_wait();
+  quant_rows(qp, blockIdx.x, gridDim.x);
 }
 
 }  // namespace dwdp
@@ -930,14 +985,14 @@ int launch_gemm_f8(const GemmParams& prm, int grid, cudaStream_t stream) {
   auto kfn = moe_gemm_f8_kernel<MODE>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return DWDP_ERR_CUDA;
-  kfn<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(prm);
-  return cudaGetLastError() == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;
+  return launch_chained(kfn, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, stream, 1u, prm) == cudaSuccess
+             ? DWDP_OK
+             : DWDP_ERR_CUDA;
 }
 
-// blocks for quantising `rows` rows, one warp per row, at most a few waves
+// blocks for quantising `rows` rows, one CTA per row, at most a few waves
 inline int quant_blocks(int64_t rows) {
-  const int64_t b = (rows + kPlanThreads / 32 - 1) / (kPlanThreads / 32);
-  return (int)std::max<int64_t>(1, std::min<int64_t>(b, 148 * 8));
+  return (int)std::max<int64_t>(1, std::min<int64_t>(rows, 148 * 8));
 }
 
 template <int MODE, bool WFP8>
@@ -946,8 +1001,9 @@ int launch_gemm(const GemmParams& prm, int grid, cudaStream_t stream) {
   auto kfn = moe_gemm_kernel<MODE, WFP8>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return DWDP_ERR_CUDA;
-  kfn<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(prm);
-  return cudaGetLastError() == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;
+  return launch_chained(kfn, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, stream, 1u, prm) == cudaSuccess
+             ? DWDP_OK
+             : DWDP_ERR_CUDA;
 }
 
 }  // namespace
@@ -969,8 +1025,14 @@ extern "C" size_t dwdp_moe_workspace_bytes_impl(int64_t T, int K, int E, int H, 
   return ws_layout(T, K, E, I, H, Is).total;
 }
 
+extern "C" int dwdp_gather_rows_launch(const void* hidden, const int64_t* tok, int64_t N, int H, int64_t T,
+                                       void* packed, int* status, cudaStream_t stream);
+
+// packed_hidden == nullptr: routed row d is hidden[packed_tok[d]] (the e4m3 path
+// quantises straight from hidden; the bf16 path gathers into the workspace).
 extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dwdp_expert_group* shared,
-                                       const void* packed_hidden, const void* hidden, int64_t T,
+                                       const void* packed_hidden, const int64_t* packed_tok,
+                                       const void* hidden, int64_t T,
                                        int K, const int64_t* counts, const int64_t* offsets,
                                        const float* packed_weights, const float* shared_gate,
                                        void* weighted_out, void* shared_out, void* workspace,
@@ -1017,16 +1079,28 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   pp.items_gu = items_gu; pp.items_dn = items_dn; pp.n_items = n_items;
   pp.cap_gu = L.cap_gu; pp.cap_dn = L.cap_dn; pp.st = st;
   QuantParams qx{}, qh{};
+  qx.st = st;
+  qh.st = st;
+  const bool indexed = packed_hidden == nullptr;
+  if (indexed && packed_tok == nullptr) return DWDP_ERR_INVALID_ARGUMENT;
   if (native) {
-    qx.seg[0] = QuantSeg{reinterpret_cast<const __nv_bfloat16*>(packed_hidden), ws + L.x8_r, sx_r, (int)N, H};
-    if (has_shared)
-      qx.seg[1] = QuantSeg{reinterpret_cast<const __nv_bfloat16*>(hidden), ws + L.x8_s, sx_s, (int)T, H};
-    qh.seg[0] = QuantSeg{h_r, ws + L.h8_r, sh_r, (int)N, I};
-    if (has_shared) qh.seg[1] = QuantSeg{h_s, ws + L.h8_s, sh_s, (int)T, Is};
+    const __nv_bfloat16* hid = reinterpret_cast<const __nv_bfloat16*>(hidden);
+    qx.seg[0] = indexed ? QuantSeg{hid, ws + L.x8_r, sx_r, (int)N, H, packed_tok, T}
+                        : QuantSeg{reinterpret_cast<const __nv_bfloat16*>(packed_hidden), ws + L.x8_r, sx_r,
+                                   (int)N, H, nullptr, N};
+    if (has_shared) qx.seg[1] = QuantSeg{hid, ws + L.x8_s, sx_s, (int)T, H, nullptr, T};
+    qh.seg[0] = QuantSeg{h_r, ws + L.h8_r, sh_r, (int)N, I, nullptr, N};
+    if (has_shared) qh.seg[1] = QuantSeg{h_s, ws + L.h8_s, sh_s, (int)T, Is, nullptr, T};
+  } else if (indexed && N > 0) {
+    // the bf16 kernels stream packed rows by TMA: gather them into the (unused) plane area
+    const int rc = dwdp_gather_rows_launch(hidden, packed_tok, N, H, T, ws + L.x8_r, status, stream);
+    if (rc != DWDP_OK) return rc;
+    packed_hidden = ws + L.x8_r;
   }
   const int qx_blocks = native ? quant_blocks(N + (has_shared ? T : 0)) : 0;
-  prep_kernel<<<kPlanBlocks + qx_blocks, kPlanThreads, 0, stream>>>(pp, qx);
-  if (cudaGetLastError() != cudaSuccess) return DWDP_ERR_CUDA;
+  if (launch_chained(prep_kernel, dim3(kPlanBlocks + qx_blocks), dim3(kPlanThreads), 0, stream, 1u, pp, qx) !=
+      cudaSuccess)
+    return DWDP_ERR_CUDA;
 
   // The activation box must cover the largest tile: a routed tile holds at most
   // min(T * K, bn) rows (an expert may be picked more than once per token), a
@@ -1073,8 +1147,10 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   if (native) {
     rc = launch_gemm_f8<0>(gu, grid_gu, stream);
     if (rc == DWDP_OK) {
-      quant_kernel<<<quant_blocks(N + (has_shared ? T : 0)), kPlanThreads, 0, stream>>>(qh);
-      rc = cudaGetLastError() == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;
+      rc = launch_chained(quant_kernel, dim3(quant_blocks(N + (has_shared ? T : 0))), dim3(kPlanThreads), 0,
+                          stream, 1u, qh) == cudaSuccess
+               ? DWDP_OK
+               : DWDP_ERR_CUDA;
     }
     if (rc == DWDP_OK) rc = launch_gemm_f8<1>(dn, grid_dn, stream);
   } else if (fp8) {

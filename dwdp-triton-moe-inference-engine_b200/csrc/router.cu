@@ -7,10 +7,15 @@
 // weight 1). Arithmetic is fp32 throughout. Top-k ties resolve to the lower
 // expert id and slots come out in descending logit order.
 //
-// Two launches: the logits (router_logits_mma_kernel on the tensor cores for
-// bf16 inputs, router_logits_kernel on the CUDA cores otherwise) and
+// bf16 inputs with E <= 256: ONE launch (router_fused_kernel). Otherwise two:
+// the logits (router_logits_mma_kernel on the tensor cores for bf16 inputs,
+// router_logits_kernel on the CUDA cores for fp32 inputs) and
 // router_topk_kernel (one warp per token).
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace dwdp {
 
@@ -57,6 +62,8 @@ __global__ void __launch_bounds__(kRouterThreads)
 router_logits_kernel(const TX* __restrict__ x, const TW* __restrict__ w, const float* __restrict__ bias,
                      const TW* __restrict__ gate_w, int T, int H, int E, float score_scale,
                      float* __restrict__ logits, float* __restrict__ gate_logit) {
+  griddep_launch();
+  griddep_wait();
   extern __shared__ __align__(16) uint8_t xs_raw[];
   TX* xs = reinterpret_cast<TX*>(xs_raw);  // [TOK][H] in the input dtype (exact)
   const int t0 = blockIdx.x * TOK;
@@ -150,6 +157,8 @@ router_logits_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat1
                          const float* __restrict__ bias, const __nv_bfloat16* __restrict__ gate_w, int T,
                          int H, int E, float score_scale, float* __restrict__ logits,
                          float* __restrict__ gate_logit) {
+  griddep_launch();
+  griddep_wait();
   __shared__ float part[kMmaWarps][16][32];  // per-warp partial [token][expert]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -203,22 +212,36 @@ router_logits_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat1
   }
 }
 
-// Top-k + softmax over the k selected + renormalisation: one warp per token.
-__global__ void __launch_bounds__(kRouterThreads)
-router_topk_kernel(const float* __restrict__ logits, int T, int E, int K, int renorm, float eps,
-                   float* __restrict__ probs, int64_t* __restrict__ idx_out, float* __restrict__ w_out,
-                   float* __restrict__ shared_gate) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * (kRouterThreads / 32) + warp;
-  if (t >= T) return;
-  const float* lr = logits + (int64_t)t * E;
-  if (shared_gate != nullptr && lane == 0) shared_gate[t] = 1.0f / (1.0f + expf(-shared_gate[t]));
+// ---------------------------------------------------------------------------
+// Fused bf16 router: logits + top-k + softmax-over-k + renormalisation + shared
+// gate in ONE launch. A cluster of G CTAs (grid.y, G <= 8) owns 16 tokens; CTA r
+// of the cluster computes expert rows [r * slice, (r + 1) * slice) in passes of
+// 64 rows (8 mma n-tiles), and rank 0 gathers the logit slices through
+// distributed shared memory and runs the top-k. G grows at decode sizes so
+// that more SMs share the weight stream. kFusedWarps warps split K in 32-wide chunks; within a
+// chunk lane (g, t) loads 8 consecutive elements [8t, 8t + 8) of its token rows
+// g and g + 8 and of expert row g of each n-tile (16-byte loads) and feeds
+// elements 0-3 to one m16n8k16 MMA and 4-7 to a second: both operands see the
+// same permutation of K, so each MMA still forms sum_k x[k] w[k]. Products of
+// bf16 are exact in fp32; the per-warp partials are summed through shared
+// memory in a fixed order (deterministic).
+// ---------------------------------------------------------------------------
+constexpr int kFusedWarps = 16;
+constexpr int kFusedPass = 64;  // expert rows per pass
+constexpr int kFusedMaxRows = 257;
+
+// One warp, one token: K rounds of a warp argmax (ties to the lower expert id);
+// lane k keeps slot k in registers, then the softmax over the k selected and
+// the renormalisation run lane-parallel. Returns nothing; lanes < K write.
+__device__ __forceinline__ void topk_warp(const float* lr, int E, int K, int renorm, float eps, int64_t t,
+                                          float* probs, int64_t* idx_out, float* w_out) {
+  const int lane = threadIdx.x & 31;
   float mine[8];  // this lane's experts lane + 32 * j (E <= 256)
 #pragma unroll
   for (int j = 0; j < 8; ++j) mine[j] = (lane + 32 * j < E) ? lr[lane + 32 * j] : -INFINITY;
   uint32_t taken = 0;
-  float sel_v[16];
-  int sel_i[16];
+  float my_v = -INFINITY, top = 0.f;
+  int my_i = 0;
   for (int k = 0; k < K; ++k) {
     float best = -INFINITY;
     int bi = 0x7fffffff;
@@ -240,24 +263,147 @@ router_topk_kernel(const float* __restrict__ logits, int T, int E, int K, int re
       }
     }
     if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-    sel_v[k] = best;
-    sel_i[k] = bi;
-  }
-  if (lane == 0) {
-    const float m = sel_v[0];
-    float p[16];
-    float s = 0.f;
-    for (int k = 0; k < K; ++k) { p[k] = expf(sel_v[k] - m); s += p[k]; }
-    float psum = 0.f;
-    for (int k = 0; k < K; ++k) { p[k] = p[k] / s; psum += p[k]; }
-    const float den = fmaxf(psum, eps);
-    for (int k = 0; k < K; ++k) {
-      const int64_t o = (int64_t)t * K + k;
-      idx_out[o] = sel_i[k];
-      if (probs != nullptr) probs[o] = p[k];
-      w_out[o] = (K == 1) ? 1.0f : (renorm ? p[k] / den : p[k]);
+    if (k == 0) top = best;
+    if (lane == k) {
+      my_v = best;
+      my_i = bi;
     }
   }
+  // softmax over the K selected (max = slot 0), then renormalise by max(sum, eps)
+  float p = lane < K ? expf(my_v - top) : 0.f;
+  float s = p;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  p = p / s;
+  float psum = p;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
+  if (lane < K) {
+    const int64_t o = t * K + lane;
+    idx_out[o] = my_i;
+    if (probs != nullptr) probs[o] = p;
+    w_out[o] = (K == 1) ? 1.0f : (renorm ? p / fmaxf(psum, eps) : p);
+  }
+}
+
+__global__ void __launch_bounds__(kFusedWarps * 32, 1)
+router_fused_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                    const float* __restrict__ bias, const __nv_bfloat16* __restrict__ gate_w, int T, int H,
+                    int E, int K, float score_scale, int renorm, float eps, float* __restrict__ logits,
+                    float* __restrict__ probs, int64_t* __restrict__ idx_out, float* __restrict__ w_out,
+                    float* __restrict__ shared_gate) {
+  extern __shared__ float fsm[];
+  float* part = fsm;                                   // [kFusedWarps][16][kFusedPass]
+  float* lg = part + kFusedWarps * 16 * kFusedPass;    // [16][kFusedMaxRows]
+  cg::cluster_group cluster = cg::this_cluster();
+  const int G = (int)cluster.num_blocks();            // CTAs sharing this token tile
+  const int rank = (int)cluster.block_rank();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int tok0 = blockIdx.x * 16;
+  const int rows = E + (gate_w != nullptr ? 1 : 0);
+  const int slice = ((rows + G * 8 - 1) / (G * 8)) * 8;  // expert rows per CTA (whole n-tiles)
+  const int e_lo = min(rows, rank * slice), e_hi = min(rows, e_lo + slice);
+  const __nv_bfloat16* xa = x + (int64_t)min(tok0 + g, T - 1) * H + 8 * t;
+  const __nv_bfloat16* xb = x + (int64_t)min(tok0 + g + 8, T - 1) * H + 8 * t;
+  griddep_launch();
+  griddep_wait();
+  for (int e0 = e_lo; e0 < e_hi; e0 += kFusedPass) {
+    const int nts = min(8, (e_hi - e0 + 7) / 8);  // live n-tiles this pass (CTA-uniform)
+    const __nv_bfloat16* wr[8];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const int e = e0 + nt * 8 + g;
+      wr[nt] = e < e_hi ? (e < E ? w + (int64_t)e * H : gate_w) + 8 * t : xa;  // xa: any valid row
+    }
+    float acc[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[nt][q] = 0.f;
+#pragma unroll 2
+    for (int k0 = warp * 32; k0 < H; k0 += 32 * kFusedWarps) {
+      const uint4 va = *reinterpret_cast<const uint4*>(xa + k0);
+      const uint4 vb = *reinterpret_cast<const uint4*>(xb + k0);
+      uint4 bw[8];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+        bw[nt] = nt < nts ? *reinterpret_cast<const uint4*>(wr[nt] + k0) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        if (nt < nts) {
+          mma_bf16_16816(acc[nt], va.x, vb.x, va.y, vb.y, bw[nt].x, bw[nt].y);
+          mma_bf16_16816(acc[nt], va.z, vb.z, va.w, vb.w, bw[nt].z, bw[nt].w);
+        }
+      }
+    }
+    float* pw = part + warp * 16 * kFusedPass;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+      if (nt < nts) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          pw[(g + (q >= 2 ? 8 : 0)) * kFusedPass + nt * 8 + 2 * t + (q & 1)] = acc[nt][q];
+      }
+    __syncthreads();
+    const int width = nts * 8;
+    for (int i = threadIdx.x; i < 16 * width; i += kFusedWarps * 32) {
+      const int tt = i / width, ee = i % width;
+      const int tok = tok0 + tt, e = e0 + ee;
+      if (tok >= T || e >= e_hi) continue;
+      float v = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < kFusedWarps; ++ww) v += part[(ww * 16 + tt) * kFusedPass + ee];
+      if (e < E) {
+        if (bias != nullptr) v += bias[e];
+        v *= score_scale;
+        logits[(int64_t)tok * E + e] = v;
+      }
+      lg[tt * kFusedMaxRows + e] = v;
+    }
+    __syncthreads();
+  }
+  if (G > 1) {
+    // rank 0 collects the other CTAs' logit slices through distributed shared memory
+    cluster.sync();
+    if (rank == 0) {
+      for (int r = 1; r < G; ++r) {
+        const int lo = min(rows, r * slice), hi = min(rows, lo + slice);
+        const float* rlg = cluster.map_shared_rank(lg, r);
+        for (int i = threadIdx.x; i < 16 * (hi - lo); i += kFusedWarps * 32) {
+          const int tt = i / (hi - lo), e = lo + i % (hi - lo);
+          lg[tt * kFusedMaxRows + e] = rlg[tt * kFusedMaxRows + e];
+        }
+      }
+    }
+    cluster.sync();  // the other CTAs stay resident until rank 0 has read them
+    if (rank != 0) return;
+  }
+  // one warp per token: top-k, softmax over k, renormalisation, sigmoid shared gate
+  if (warp < 16) {
+    const int tok = tok0 + warp;
+    if (tok < T) {
+      const float* lr = lg + warp * kFusedMaxRows;
+      topk_warp(lr, E, K, renorm, eps, tok, probs, idx_out, w_out);
+      if (lane == 0 && gate_w != nullptr) shared_gate[tok] = 1.0f / (1.0f + expf(-lr[E]));
+    }
+  }
+}
+
+constexpr size_t kFusedSmem = (size_t)(kFusedWarps * 16 * kFusedPass + 16 * kFusedMaxRows) * sizeof(float);
+
+// Top-k + softmax over the k selected + renormalisation: one warp per token.
+__global__ void __launch_bounds__(kRouterThreads)
+router_topk_kernel(const float* __restrict__ logits, int T, int E, int K, int renorm, float eps,
+                   float* __restrict__ probs, int64_t* __restrict__ idx_out, float* __restrict__ w_out,
+                   float* __restrict__ shared_gate) {
+  griddep_launch();
+  griddep_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (kRouterThreads / 32) + warp;
+  if (t >= T) return;
+  if (shared_gate != nullptr && lane == 0) shared_gate[t] = 1.0f / (1.0f + expf(-shared_gate[t]));
+  topk_warp(logits + (int64_t)t * E, E, K, renorm, eps, t, probs, idx_out, w_out);
 }
 
 }  // namespace dwdp
@@ -285,9 +431,10 @@ extern "C" int dwdp_router_launch(const void* hidden, int hidden_dtype, const vo
     if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=         \
         cudaSuccess)                                                                                  \
       return DWDP_ERR_CUDA;                                                                           \
-    kfn<<<grid, kRouterThreads, smem, stream>>>((const TX*)hidden, (const TW*)weight, bias,           \
-                                                (const TW*)shared_gate_weight, (int)T, H, E,          \
-                                                score_scale, logits, shared_gate);                    \
+    if (launch_chained(kfn, grid, dim3(kRouterThreads), smem, stream, 1u, (const TX*)hidden,          \
+                       (const TW*)weight, bias, (const TW*)shared_gate_weight, (int)T, H, E,          \
+                       score_scale, logits, shared_gate) != cudaSuccess)                              \
+      return DWDP_ERR_CUDA;                                                                           \
   } while (0)
 #define DWDP_LOGITS_TOK(TX, TW)                          \
   do {                                                   \
@@ -296,11 +443,29 @@ extern "C" int dwdp_router_launch(const void* hidden, int hidden_dtype, const vo
     else if (tok == 4) DWDP_LAUNCH_LOGITS(TX, TW, 4);    \
     else DWDP_LAUNCH_LOGITS(TX, TW, 2);                  \
   } while (0)
+  if (hidden_dtype == DWDP_DTYPE_BF16 && weight_dtype == DWDP_DTYPE_BF16 && H % 32 == 0 && E <= 256 &&
+      K <= 16) {
+    if (cudaFuncSetAttribute(router_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kFusedSmem) != cudaSuccess)
+      return DWDP_ERR_CUDA;
+    // expert slices per token tile: enough CTAs to cover the SMs at decode sizes
+    const int64_t tiles = (T + 15) / 16;
+    int G = 1;
+    while (G < 8 && tiles * G < 148 && G * 8 < rows) G *= 2;
+    if (launch_chained(router_fused_kernel, dim3((unsigned)tiles, (unsigned)G, 1), dim3(kFusedWarps * 32, 1, 1),
+                       kFusedSmem, stream, (unsigned)G, (const __nv_bfloat16*)hidden,
+                       (const __nv_bfloat16*)weight, bias, (const __nv_bfloat16*)shared_gate_weight, (int)T, H, E, K,
+                       score_scale, renorm, eps, logits, probs, idx, topk_w, shared_gate) != cudaSuccess)
+      return DWDP_ERR_CUDA;
+    return cudaGetLastError() == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;
+  }
   if (hidden_dtype == DWDP_DTYPE_BF16 && weight_dtype == DWDP_DTYPE_BF16 && H % 16 == 0) {
     const dim3 mgrid((unsigned)((T + kMmaTok - 1) / kMmaTok), (unsigned)((rows + kMmaExp - 1) / kMmaExp));
-    router_logits_mma_kernel<<<mgrid, kMmaWarps * 32, 0, stream>>>(
-        (const __nv_bfloat16*)hidden, (const __nv_bfloat16*)weight, bias,
-        (const __nv_bfloat16*)shared_gate_weight, (int)T, H, E, score_scale, logits, shared_gate);
+    if (launch_chained(router_logits_mma_kernel, mgrid, dim3(kMmaWarps * 32), 0, stream, 1u,
+                       (const __nv_bfloat16*)hidden, (const __nv_bfloat16*)weight, bias,
+                       (const __nv_bfloat16*)shared_gate_weight, (int)T, H, E, score_scale, logits,
+                       shared_gate) != cudaSuccess)
+      return DWDP_ERR_CUDA;
   } else if (hidden_dtype == DWDP_DTYPE_BF16 && weight_dtype == DWDP_DTYPE_BF16)
     DWDP_LOGITS_TOK(__nv_bfloat16, __nv_bfloat16);
   else if (hidden_dtype == DWDP_DTYPE_BF16 && weight_dtype == DWDP_DTYPE_F32)
@@ -314,7 +479,9 @@ extern "C" int dwdp_router_launch(const void* hidden, int hidden_dtype, const vo
 #undef DWDP_LOGITS_TOK
 #undef DWDP_LAUNCH_LOGITS
   const unsigned tk_grid = (unsigned)((T + 7) / 8);
-  router_topk_kernel<<<tk_grid, kRouterThreads, 0, stream>>>(logits, (int)T, E, K, renorm, eps, probs, idx,
-                                                             topk_w, shared_gate_weight ? shared_gate : nullptr);
+  if (launch_chained(router_topk_kernel, dim3(tk_grid), dim3(kRouterThreads), 0, stream, 1u, (const float*)logits,
+                     (int)T, E, K, renorm, eps, probs, idx, topk_w,
+                     shared_gate_weight ? shared_gate : (float*)nullptr) != cudaSuccess)
+    return DWDP_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;
 }

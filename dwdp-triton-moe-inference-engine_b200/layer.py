@@ -103,7 +103,7 @@ class MoELayer:
             packed_expert_ids=torch.empty(N, dtype=torch.int64, device=dev),
             packed_token_indices=torch.empty(N, dtype=torch.int64, device=dev),
             packed_routing_weights=torch.empty(N, dtype=torch.float32, device=dev),
-            packed_hidden=torch.empty(N, H, dtype=torch.bfloat16, device=dev),
+            packed_hidden=None,  # the expert kernels read hidden through packed_token_indices
         )
         Is = self.shared_expert.intermediate_size if has_shared else 0
         parts = ops.moe_shared_parts(T, Is) if has_shared else 0
@@ -154,17 +154,33 @@ class MoELayer:
             x, self.router_weight, K, bias=self.router_bias, shared_gate_weight=gate_w,
             score_scale=self.score_scale, renormalize=self.renormalize, eps=self.eps, out=ws.router,
         )
+        # the expert kernels read routed rows through packed_token_indices: no gathered copy
         ops.dispatch(
-            ws.router.topk_indices, ws.router.topk_weights, self.num_experts, hidden=x,
+            ws.router.topk_indices, ws.router.topk_weights, self.num_experts,
             scratch=ws.dispatch_scratch, out=ws.dispatch, status=ws.status,
         )
-        ops.moe_experts(
-            self._routed_group, self._shared_group, ws.dispatch.packed_hidden, x, K,
-            ws.dispatch.expert_counts, ws.dispatch.expert_offsets, ws.dispatch.packed_routing_weights,
-            ws.router.shared_gate, ws.weighted, ws.shared_out, ws.moe_ws, ws.status,
-        )
+        self.run_experts(x, ws)
         ops.merge(ws.weighted, ws.dispatch.inverse_permutation, T, K, shared_out=ws.shared_out,
                   shared_parts=ws.shared_parts, out=out)
+
+    def run_experts(self, x: torch.Tensor, ws: LayerWorkspace) -> None:
+        """The grouped expert GEMMs of :meth:`run` on a dispatched workspace."""
+        ops.moe_experts(
+            self._routed_group, self._shared_group, None, x, self.top_k,
+            ws.dispatch.expert_counts, ws.dispatch.expert_offsets, ws.dispatch.packed_routing_weights,
+            ws.router.shared_gate, ws.weighted, ws.shared_out, ws.moe_ws, ws.status,
+            packed_token_indices=ws.dispatch.packed_token_indices,
+        )
+
+    def kernel_launches(self, num_tokens: int) -> int:
+        """Kernels one forward launches: router (1 for bf16 weights, else logits +
+        top-k), dispatch (scatter, plus a histogram above 256 assignments), expert
+        plan (+ activation planes), [row gather,] gate/up GEMM, [intermediate
+        planes,] down GEMM, merge."""
+        router = 1 if self.router_weight.dtype == torch.bfloat16 and self.num_experts <= 256 else 2
+        dispatch = 1 if num_tokens * self.top_k <= 256 else 2
+        experts = 4  # e4m3 weights: planes in the plan launch + one between the GEMMs; else one row gather
+        return router + dispatch + experts + 1
 
     def read_status(self, num_tokens: int) -> tuple[int, ...]:
         """Device status word {code, where, detail, count} of the last forward."""

@@ -300,7 +300,7 @@ def moe_workspace_bytes(num_tokens: int, top_k: int, num_experts: int, intermedi
 def moe_experts(
     routed: _lib.ExpertGroup,
     shared: _lib.ExpertGroup | None,
-    packed_hidden: torch.Tensor,
+    packed_hidden: torch.Tensor | None,
     hidden: torch.Tensor,
     top_k: int,
     counts: torch.Tensor,
@@ -311,18 +311,31 @@ def moe_experts(
     shared_out: torch.Tensor | None,
     workspace: torch.Tensor,
     status: torch.Tensor | None = None,
+    *,
+    packed_token_indices: torch.Tensor | None = None,
 ) -> None:
-    """Grouped tcgen05 expert GEMMs (gate/up + SwiGLU, down + routing weight)."""
-    _require_cuda(packed_hidden, hidden, counts, offsets, packed_weights, weighted_out, workspace)
+    """Grouped tcgen05 expert GEMMs (gate/up + SwiGLU, down + routing weight).
+
+    Routed rows come from ``packed_hidden`` or, when it is None, from
+    ``hidden[packed_token_indices]`` read inside the kernels (no gathered copy)."""
+    _require_cuda(packed_hidden, hidden, counts, offsets, packed_weights, weighted_out, workspace,
+                  packed_token_indices)
     if packed_weights.dtype != torch.float32:
         raise ValueError("packed routing weights must be fp32 for the grouped GEMM")
     T = hidden.shape[0]
-    rc = _lib.load().dwdp_moe_experts(
-        ctypes.byref(routed), ctypes.byref(shared) if shared is not None else None,
-        packed_hidden.data_ptr(), hidden.data_ptr(), T, top_k, counts.data_ptr(), offsets.data_ptr(),
-        packed_weights.data_ptr(), _ptr(shared_gate), weighted_out.data_ptr(), _ptr(shared_out),
-        workspace.data_ptr(), workspace.numel(), _ptr(status), _stream(),
-    )
+    lib = _lib.load()
+    shared_ref = ctypes.byref(shared) if shared is not None else None
+    tail = (T, top_k, counts.data_ptr(), offsets.data_ptr(), packed_weights.data_ptr(), _ptr(shared_gate),
+            weighted_out.data_ptr(), _ptr(shared_out), workspace.data_ptr(), workspace.numel(), _ptr(status),
+            _stream())
+    if packed_hidden is not None:
+        rc = lib.dwdp_moe_experts(ctypes.byref(routed), shared_ref, packed_hidden.data_ptr(), hidden.data_ptr(),
+                                  *tail)
+    else:
+        if packed_token_indices is None or packed_token_indices.dtype != torch.int64:
+            raise ValueError("moe_experts needs packed_hidden or int64 packed_token_indices")
+        rc = lib.dwdp_moe_experts_indexed(ctypes.byref(routed), shared_ref, packed_token_indices.data_ptr(),
+                                          hidden.data_ptr(), *tail)
     _lib.check(rc, "moe_experts")
 
 

@@ -339,9 +339,8 @@ class B200Executor(nn.Module):
         if x.dtype != torch.bfloat16:
             x = x.to(torch.bfloat16)
         x = x.contiguous()
+        # without a gathered copy the kernels read hidden through packed_token_indices
         packed = getattr(dispatch_plan, "packed_hidden", None)
-        if packed is None:
-            packed = ops.gather_rows(x, dispatch_plan.assignments.packed_token_indices)
         T, K = md.num_tokens, md.top_k
         key = (T, K)
         if key not in self._ws:
@@ -353,7 +352,8 @@ class B200Executor(nn.Module):
             w = w.float()
         weighted = torch.empty(md.num_assignments, H, dtype=torch.bfloat16, device=x.device)
         ops.moe_experts(self._group, None, packed, x, K, md.expert_counts, md.expert_offsets, w, None,
-                        weighted, None, self._ws[key])
+                        weighted, None, self._ws[key],
+                        packed_token_indices=dispatch_plan.assignments.packed_token_indices)
         return ExecutorOutput(packed_expert_outputs=None, weighted_expert_outputs=weighted,
                               backend=self.config.backend, deterministic=True,
                               inverse_permutation=md.inverse_permutation, token_shape=tuple(md.token_shape),

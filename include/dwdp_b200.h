@@ -183,9 +183,14 @@ typedef struct dwdp_expert_group {
  *   sum_p shared_out[p][t] = shared_gate[t] * down_s(silu(gate_s(x_t)) * up_s(x_t))
  * (shared_gate NULL = 1; p < dwdp_moe_shared_parts(T, Is), shared_out is
  * [parts][T][H] bf16). bf16 activations, fp32 accumulation in TMEM,
- * bf16 outputs. Two persistent tcgen05 launches (gate/up+SwiGLU, down+scale).
- * Expert row ranges come from device offsets; no host synchronisation.
- * hidden_size <= 8192.
+ * bf16 outputs. Two persistent tcgen05 GEMM launches (gate/up+SwiGLU,
+ * down+scale) after a planning launch. Per-channel fp8 weights run as e4m3
+ * MMAs (kind::f8f6f4) against activations carried as two e4m3 planes
+ * (hi + lo/16, one fp32 scale per row, about bf16 precision), quantised in the
+ * planning launch and in one launch between the GEMMs; block-scaled fp8 and
+ * bf16 weights run as bf16 MMAs. Expert row ranges come from device offsets;
+ * no host synchronisation. hidden_size <= 8192. The shared group must use the
+ * routed group's weight dtype and scale mode.
  * ======================================================================== */
 /* Number of [T, H] partial slabs `shared_out` must hold: the shared expert's
  * down projection is split along K at decode sizes (its K is several times the
@@ -200,11 +205,22 @@ int dwdp_moe_experts(const dwdp_expert_group* routed, const dwdp_expert_group* s
                      void* shared_out, void* workspace, size_t workspace_bytes, int* status,
                      void* stream);
 
+/* As dwdp_moe_experts, with routed row d read as hidden[packed_token_indices[d]]
+ * (the dispatcher's packed_token_indices) instead of from a gathered
+ * packed_hidden: the e4m3 path quantises straight from `hidden`, so the
+ * dispatcher's row gather can be skipped. */
+int dwdp_moe_experts_indexed(const dwdp_expert_group* routed, const dwdp_expert_group* shared,
+                             const int64_t* packed_token_indices, const void* hidden, int64_t num_tokens,
+                             int top_k, const int64_t* counts, const int64_t* offsets,
+                             const float* packed_weights, const float* shared_gate, void* weighted_out,
+                             void* shared_out, void* workspace, size_t workspace_bytes, int* status,
+                             void* stream);
+
 /* ======================================================================== *
  * Merge (reference_merge, merger/kernels/reference.py:6-27): deterministic
  * token-major reduction. out[t] = sum over the K rows inv[t*K+k] of
  * weighted[row] taken in ascending row order, plus shared_out[p][t] for
- * p < shared_parts when shared_out is given. fp32 accumulation; out_dtype
+ * p < shared_parts (<= 8) when shared_out is given. fp32 accumulation; out_dtype
  * bf16|f32; weighted/shared bf16. K <= 16.
  * ======================================================================== */
 int dwdp_merge(const void* weighted, const int64_t* inv, const void* shared_out, int shared_parts,

@@ -276,8 +276,9 @@ def test_moe_layer_shared_k_split_modes(pkg, orc, mode, T):
     _check_layer(pkg, orc, layer, T, FP8_TOL)
 
 
+@pytest.mark.parametrize("indexed", [False, True])
 @pytest.mark.parametrize("mode", ["channel", "block", "bf16"])
-def test_moe_experts_repeated_expert(pkg, orc, mode):
+def test_moe_experts_repeated_expert(pkg, orc, mode, indexed):
     """Routing that names one expert K times per token (a hand-built plan no
     top-k router produces): one expert then holds T * K rows, more than T, and
     its tiles must still be covered by the activation box."""
@@ -295,9 +296,10 @@ def test_moe_experts_repeated_expert(pkg, orc, mode):
     xd = x.to(DEV)
     pkg.ops.dispatch(ws.router.topk_indices, ws.router.topk_weights, layer.num_experts, hidden=xd,
                      scratch=ws.dispatch_scratch, out=ws.dispatch, status=ws.status)
-    pkg.ops.moe_experts(layer._routed_group, None, ws.dispatch.packed_hidden, xd, K,
+    pkg.ops.moe_experts(layer._routed_group, None, None if indexed else ws.dispatch.packed_hidden, xd, K,
                         ws.dispatch.expert_counts, ws.dispatch.expert_offsets,
-                        ws.dispatch.packed_routing_weights, None, ws.weighted, None, ws.moe_ws, ws.status)
+                        ws.dispatch.packed_routing_weights, None, ws.weighted, None, ws.moe_ws, ws.status,
+                        packed_token_indices=ws.dispatch.packed_token_indices)
     y = pkg.ops.merge(ws.weighted, ws.dispatch.inverse_permutation, T, K, out_dtype=torch.float32)
     torch.cuda.synchronize()
     assert layer.read_status(T)[0] == 0
@@ -305,3 +307,21 @@ def test_moe_experts_repeated_expert(pkg, orc, mode):
     ref = orc.moe_forward(x.float(), ids, wts, experts)
     err = orc.rel_frobenius(y.cpu(), ref)
     assert err < (BF16_TOL if mode == "bf16" else FP8_TOL), err
+
+
+def test_moe_experts_indexed_bad_index_records_status(pkg):
+    """An out-of-range packed token index is recorded in the status word, not read."""
+    layer = _make_layer(pkg, 4, 256, 256, 2, 0, torch.float8_e4m3fn, pkg._lib.SCALE_CHANNEL, seed=6)
+    T, K = 4, 2
+    ws = layer.workspace(T)
+    ws.router.topk_indices.copy_(torch.tensor([[0, 1], [1, 2], [2, 3], [3, 0]]))
+    ws.router.topk_weights.fill_(0.5)
+    x = torch.randn(T, 256, device=DEV).bfloat16()
+    pkg.ops.dispatch(ws.router.topk_indices, ws.router.topk_weights, layer.num_experts,
+                     scratch=ws.dispatch_scratch, out=ws.dispatch, status=ws.status)
+    ws.dispatch.packed_token_indices[3] = 99
+    ws.status.zero_()
+    layer.run_experts(x, ws)
+    torch.cuda.synchronize()
+    st = layer.read_status(T)
+    assert st[0] == pkg._lib.DWDP_ERR_DEVICE_BOUNDS and st[3] >= 1
