@@ -71,6 +71,8 @@ struct WorkItem {
   int kb_begin;  // first / one-past-last 64-wide K step of this item (split K)
   int kb_end;
   int part;      // K-split index: output goes to out + part * part_stride
+  const uint8_t* wtiles;  // first weight tile of this item's 128-row block (set by the planner)
+  const float* scales;    // the expert's scales (fp8) or nullptr
 };
 
 struct GroupParams {
@@ -92,6 +94,7 @@ struct GemmParams {
   GroupParams g[2];
   const WorkItem* items;
   const int* n_items;
+  int cap;  // work-item capacity (grid <= cap, so items[blockIdx.x] is always addressable)
   DeviceStatus* st;
 };
 
@@ -205,17 +208,18 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
     if (lane == 0) {
       PROF_DECL PROF_START
       uint32_t it = 0;
+      WorkItem wn = p.items[blockIdx.x];  // fetched with n_items; the next one is prefetched
       for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
-        const WorkItem wi = p.items[item];
+        const WorkItem wi = wn;
+        if (item + (int)gridDim.x < p.cap) wn = p.items[item + gridDim.x];
         const GroupParams& g = p.g[wi.group];
-        const int KB = g.K / BK;
-        const uint8_t* wbase = reinterpret_cast<const uint8_t*>(g.w[wi.expert]);
+        const uint8_t* wbase = wi.wtiles;
         const uint32_t b_bytes = (uint32_t)g.box_rows * 128u;
         for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
           const int s = it % C::S;
           if (!TW(0, mbar_wait(&ld_empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 1 + 8 * MODE))) break;
           mbar_arrive_expect_tx(&ld_full[s], C::W_STAGE_BYTES + b_bytes);
-          const size_t woff = ((size_t)wi.rb * KB + kb) * C::W_STAGE_BYTES;
+          const size_t woff = (size_t)kb * C::W_STAGE_BYTES;
           bulk_g2s(sW + s * C::W_STAGE_BYTES, wbase + woff, C::W_STAGE_BYTES, &ld_full[s]);
           tma_load_2d(sB + s * kBTileBytes, &g.tmap_b, kb * BK, wi.row0, &ld_full[s]);
         }
@@ -228,8 +232,10 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
       PROF_DECL PROF_START
       uint32_t it = 0, cit = 0;
       int li = 0;
+      WorkItem wn = p.items[blockIdx.x];  // fetched with n_items; the next one is prefetched
       for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++li) {
-        const WorkItem wi = p.items[item];
+        const WorkItem wi = wn;
+        if (item + (int)gridDim.x < p.cap) wn = p.items[item + gridDim.x];
         const int a = li & 1;
         if (!TW(0, mbar_wait(&acc_empty[a], ((li >> 1) & 1) ^ 1, &s_abort, st, 2 + 8 * MODE))) break;
         tc_fence_after();
@@ -282,22 +288,23 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
     const int quad = warp & 3;
     const int lrow = quad * 32 + lane;  // weight row inside the 128-row block
     int li = 0;
+    WorkItem wn = p.items[blockIdx.x];  // fetched with n_items; the next one is prefetched
     for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++li) {
-      const WorkItem wi = p.items[item];
+      const WorkItem wi = wn;
+      if (item + (int)gridDim.x < p.cap) wn = p.items[item + gridDim.x];
       const GroupParams& g = p.g[wi.group];
       const int a = li & 1;
+      const int feat = wi.rb * BM + lrow;
+      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)wi.part * g.part_stride;
+      // per-output-channel weight scales are exact per-thread constants here (loaded while the MMAs run)
+      float s0 = 1.0f, s1 = 1.0f;
+      if (WFP8 && g.scale_mode == DWDP_SCALE_CHANNEL) {
+        s0 = wi.scales[feat];
+        if (MODE == 0) s1 = wi.scales[g.R + feat];
+      }
       if (!TW(0, mbar_wait(&acc_full[a], (li >> 1) & 1, &s_abort, st, 5 + 8 * MODE))) break;
       tc_fence_after();
       const uint32_t t_acc = tmem_base + a * C::ACC_STRIDE + ((uint32_t)(quad * 32) << 16);
-      const int feat = wi.rb * BM + lrow;
-      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)wi.part * g.part_stride;
-      // per-output-channel weight scales are exact per-thread constants here
-      float s0 = 1.0f, s1 = 1.0f;
-      if (WFP8 && g.scale_mode == DWDP_SCALE_CHANNEL) {
-        const float* sc = g.s[wi.expert];
-        s0 = sc[feat];
-        if (MODE == 0) s1 = sc[g.R + feat];
-      }
       for (int c0 = 0; c0 < wi.nrows; c0 += 16) {
         if constexpr (MODE == 0) {
           float gv[16], uv[16];
@@ -344,11 +351,13 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
     constexpr int kGroupThreads = C::CONV_THREADS / C::CONV_GROUPS;
     const int grp = ct / kGroupThreads, gt = ct % kGroupThreads;
     uint32_t it = 0, cit = 0;
+    WorkItem wn = p.items[blockIdx.x];  // fetched with n_items; the next one is prefetched
     for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
-      const WorkItem wi = p.items[item];
+      const WorkItem wi = wn;
+      if (item + (int)gridDim.x < p.cap) wn = p.items[item + gridDim.x];
       const GroupParams& g = p.g[wi.group];
       const bool block_scaled = g.scale_mode == DWDP_SCALE_BLOCK128;
-      const float* sc = g.s[wi.expert];
+      const float* sc = wi.scales;
       bool ok = true;
       for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it, ++cit) {
         if ((int)(cit % C::CONV_GROUPS) != grp) continue;
@@ -481,17 +490,18 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       uint32_t it = 0;
+      WorkItem wn = p.items[blockIdx.x];  // fetched with n_items; the next one is prefetched
       for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
-        const WorkItem wi = p.items[item];
+        const WorkItem wi = wn;
+        if (item + (int)gridDim.x < p.cap) wn = p.items[item + gridDim.x];
         const GroupParams& g = p.g[wi.group];
-        const int KB = g.K / BK8;
-        const uint8_t* wbase = reinterpret_cast<const uint8_t*>(g.w[wi.expert]);
+        const uint8_t* wbase = wi.wtiles;
         const uint32_t b_bytes = (uint32_t)g.box_rows * 2u * BK8;
         for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
           const int s = it % C::S;
           if (!mbar_wait(&ld_empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 21 + 8 * MODE)) break;
           mbar_arrive_expect_tx(&ld_full[s], C::W_STAGE_BYTES + b_bytes);
-          const size_t woff = ((size_t)wi.rb * KB + kb) * C::W_STAGE_BYTES;
+          const size_t woff = (size_t)kb * C::W_STAGE_BYTES;
           bulk_g2s(sW + s * C::W_STAGE_BYTES, wbase + woff, C::W_STAGE_BYTES, &ld_full[s]);
           tma_load_2d(sB + s * kB8TileBytes, &g.tmap_b, kb * BK8, 2 * wi.row0, &ld_full[s]);
         }
@@ -502,8 +512,10 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
     if (lane == 0) {
       uint32_t it = 0;
       int li = 0;
+      WorkItem wn = p.items[blockIdx.x];  // fetched with n_items; the next one is prefetched
       for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++li) {
-        const WorkItem wi = p.items[item];
+        const WorkItem wi = wn;
+        if (item + (int)gridDim.x < p.cap) wn = p.items[item + gridDim.x];
         const int a = li & 1;
         if (!mbar_wait(&acc_empty[a], ((li >> 1) & 1) ^ 1, &s_abort, st, 22 + 8 * MODE)) break;
         tc_fence_after();
@@ -538,19 +550,20 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
     const int quad = warp & 3;
     const int lrow = quad * 32 + lane;
     int li = 0;
+    WorkItem wn = p.items[blockIdx.x];  // fetched with n_items; the next one is prefetched
     for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++li) {
-      const WorkItem wi = p.items[item];
+      const WorkItem wi = wn;
+      if (item + (int)gridDim.x < p.cap) wn = p.items[item + gridDim.x];
       const GroupParams& g = p.g[wi.group];
       const int a = li & 1;
+      const int feat = wi.rb * BM + lrow;
+      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)wi.part * g.part_stride;
+      const float s0 = wi.scales[feat];  // loaded while the MMAs run
+      const float s1 = MODE == 0 ? wi.scales[g.R + feat] : 1.0f;
+      const float* xs = g.x_scale + wi.row0;
       if (!mbar_wait(&acc_full[a], (li >> 1) & 1, &s_abort, st, 24 + 8 * MODE)) break;
       tc_fence_after();
       const uint32_t t_acc = tmem_base + a * C::ACC_STRIDE + ((uint32_t)(quad * 32) << 16);
-      const int feat = wi.rb * BM + lrow;
-      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)wi.part * g.part_stride;
-      const float* sc = g.s[wi.expert];
-      const float s0 = sc[feat];
-      const float s1 = MODE == 0 ? sc[g.R + feat] : 1.0f;
-      const float* xs = g.x_scale + wi.row0;
       for (int c0 = 0; c0 < 2 * wi.nrows; c0 += 16) {
         const int t0 = c0 >> 1;
         if constexpr (MODE == 0) {
@@ -612,6 +625,11 @@ struct PlanParams {
   int kb_gu, kb_dn_r, kb_dn_s;              // 64-wide K steps per projection
   int sdn_parts;                            // K splits of the shared down projection
   int bn_max;                               // token-tile cap (rows per work item)
+  const void* const* w_gu[2];               // [group] per-expert weight slabs (routed, shared)
+  const void* const* w_dn[2];
+  const float* const* s_gu[2];              // [group] per-expert scales (or nullptr)
+  const float* const* s_dn[2];
+  long long rbb_gu[2], rbb_dn[2];           // bytes of one 128-row weight block
   WorkItem* items_gu;
   WorkItem* items_dn;
   int* n_items;
@@ -715,7 +733,7 @@ __device__ __forceinline__ void plan_body(const PlanParams& pp) {
         const int row0 = j * bn_s;
         const int kb0 = phase == 0 ? 0 : part * kb_part;
         const int kb1 = phase == 0 ? pp.kb_gu : (part + 1) * kb_part;
-        w = WorkItem{1, 0, rb, row0, min(bn_s, T - row0), kb0, kb1, part};
+        w = WorkItem{1, 0, rb, row0, min(bn_s, T - row0), kb0, kb1, part, nullptr, nullptr};
       } else {         // routed: expert e with s_pre[e]*rb_r <= i - base < s_pre[e+1]*rb_r
         const int r = i - base;
         int lo = 0, hi = E - 1;
@@ -729,8 +747,13 @@ __device__ __forceinline__ void plan_body(const PlanParams& pp) {
         const int rb = local / nt, j = local % nt;
         const int cnt = (int)pp.counts[e];
         const int row0 = (int)pp.offsets[e] + j * bn;
-        w = WorkItem{0, e, rb, row0, min(bn, cnt - j * bn), 0, kb_r, 0};
+        w = WorkItem{0, e, rb, row0, min(bn, cnt - j * bn), 0, kb_r, 0, nullptr, nullptr};
       }
+      const void* const* wp = phase == 0 ? pp.w_gu[w.group] : pp.w_dn[w.group];
+      const float* const* sp = phase == 0 ? pp.s_gu[w.group] : pp.s_dn[w.group];
+      const long long rbb = phase == 0 ? pp.rbb_gu[w.group] : pp.rbb_dn[w.group];
+      w.wtiles = reinterpret_cast<const uint8_t*>(wp[w.expert]) + (size_t)w.rb * rbb;
+      w.scales = sp != nullptr ? sp[w.expert] : nullptr;
       out[i] = w;
     }
   }
@@ -945,7 +968,8 @@ inline int box_rows_for(int64_t max_rows, int cap) {
 
 struct WsLayout {
   size_t h_routed, h_shared, items_gu, items_dn, n_items;
-  size_t x8_r, x8_s, h8_r, h8_s, sx_r, sx_s, sh_r, sh_s, total;
+  size_t x8_r, x8_s, h8_r, h8_s, sx_r, sx_s, sh_r, sh_s;
+  size_t total;
   int cap_gu, cap_dn;
 };
 
@@ -1076,6 +1100,13 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   pp.kb_gu = H / bk; pp.kb_dn_r = I / bk; pp.kb_dn_s = has_shared ? Is / bk : 0;
   pp.sdn_parts = has_shared ? parts : 0;
   pp.bn_max = bn;
+  const long long esz = fp8 ? 1 : 2;
+  pp.w_gu[0] = routed->w13; pp.w_dn[0] = routed->w2; pp.s_gu[0] = routed->s13; pp.s_dn[0] = routed->s2;
+  pp.rbb_gu[0] = 128LL * H * 2 * esz; pp.rbb_dn[0] = 128LL * I * esz;
+  if (has_shared) {
+    pp.w_gu[1] = shared->w13; pp.w_dn[1] = shared->w2; pp.s_gu[1] = shared->s13; pp.s_dn[1] = shared->s2;
+    pp.rbb_gu[1] = 128LL * H * 2 * esz; pp.rbb_dn[1] = 128LL * Is * esz;
+  }
   pp.items_gu = items_gu; pp.items_dn = items_dn; pp.n_items = n_items;
   pp.cap_gu = L.cap_gu; pp.cap_dn = L.cap_dn; pp.st = st;
   QuantParams qx{}, qh{};
@@ -1122,7 +1153,7 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
     gu.g[1].x_scale = sx_s;
     gu.g[1].K = H; gu.g[1].R = Is; gu.g[1].scale_mode = shared->scale_mode; gu.g[1].box_rows = box_s;
   }
-  gu.items = items_gu; gu.n_items = n_items; gu.st = st;
+  gu.items = items_gu; gu.n_items = n_items; gu.st = st; gu.cap = L.cap_gu;
 
   dn.g[0].enabled = N > 0;
   if (N > 0 && !map(&dn.g[0].tmap_b, h_r, L.h8_r, N, I, box_r)) return DWDP_ERR_CUDA;
@@ -1137,7 +1168,7 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
     dn.g[1].row_scale = shared_gate; dn.g[1].K = Is; dn.g[1].R = H; dn.g[1].scale_mode = shared->scale_mode;
     dn.g[1].part_stride = (long long)T * H;
   }
-  dn.items = items_dn; dn.n_items = n_items + 1; dn.st = st;
+  dn.items = items_dn; dn.n_items = n_items + 1; dn.st = st; dn.cap = L.cap_dn;
 
   const int sms = dwdp_device_sm_count();
   if (sms <= 0) return DWDP_ERR_CUDA;
