@@ -31,13 +31,13 @@ __device__ __forceinline__ void add8(float (&acc)[8], const uint4& v) {
 // shared memory; every thread then issues all of its row loads (and the shared
 // partials) before summing them in that fixed order, so a token costs about one
 // memory latency.
-template <typename TOut>
+template <typename TOut, int KMAX, int PMAX>
 __global__ void __launch_bounds__(256)
 merge_kernel(const __nv_bfloat16* __restrict__ weighted, const int64_t* __restrict__ inv,
              const __nv_bfloat16* __restrict__ shared_out, int shared_parts, int64_t T, int K, int H,
              int64_t nrows, TOut* __restrict__ out, DeviceStatus* st) {
   griddep_launch();
-  __shared__ int64_t s_rows[kMergeMaxK];
+  __shared__ int64_t s_rows[KMAX];
   __shared__ int s_nk;
   const int64_t t = blockIdx.x;
   griddep_wait();
@@ -58,19 +58,19 @@ merge_kernel(const __nv_bfloat16* __restrict__ weighted, const int64_t* __restri
   __syncthreads();
   const int nk = s_nk;
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
-    uint4 v[kMergeMaxK], sv[kMergeMaxParts];
+    uint4 v[KMAX], sv[PMAX];
 #pragma unroll
-    for (int j = 0; j < kMergeMaxK; ++j)
+    for (int j = 0; j < KMAX; ++j)
       if (j < nk) v[j] = *reinterpret_cast<const uint4*>(weighted + s_rows[j] * H + c);
 #pragma unroll
-    for (int sp = 0; sp < kMergeMaxParts; ++sp)
+    for (int sp = 0; sp < PMAX; ++sp)
       if (sp < shared_parts) sv[sp] = *reinterpret_cast<const uint4*>(shared_out + ((int64_t)sp * T + t) * H + c);
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < kMergeMaxK; ++j)
+    for (int j = 0; j < KMAX; ++j)
       if (j < nk) add8(acc, v[j]);
 #pragma unroll
-    for (int sp = 0; sp < kMergeMaxParts; ++sp)
+    for (int sp = 0; sp < PMAX; ++sp)
       if (sp < shared_parts) add8(acc, sv[sp]);
     if constexpr (sizeof(TOut) == 2) {
       uint4 o;
@@ -100,18 +100,23 @@ extern "C" int dwdp_merge_launch(const void* weighted, const int64_t* inv, const
   if (shared_out == nullptr) shared_parts = 0;
   DeviceStatus* st = reinterpret_cast<DeviceStatus*>(status);
   const int threads = H / 8 >= 256 ? 256 : ((H / 8 + 31) / 32) * 32;
-  if (out_dtype == DWDP_DTYPE_BF16) {
-    if (launch_chained(merge_kernel<__nv_bfloat16>, dim3((unsigned)T), dim3(threads), 0, stream, 1u,
-                       (const __nv_bfloat16*)weighted, inv, (const __nv_bfloat16*)shared_out, shared_parts, T, K, H,
-                       T * K, (__nv_bfloat16*)out, st) != cudaSuccess)
-      return DWDP_ERR_CUDA;
-  } else if (out_dtype == DWDP_DTYPE_F32) {
-    if (launch_chained(merge_kernel<float>, dim3((unsigned)T), dim3(threads), 0, stream, 1u,
-                       (const __nv_bfloat16*)weighted, inv, (const __nv_bfloat16*)shared_out, shared_parts, T, K, H,
-                       T * K, (float*)out, st) != cudaSuccess)
-      return DWDP_ERR_CUDA;
-  } else {
-    return DWDP_ERR_UNSUPPORTED;
-  }
+  // register staging sized to the call: K rows and the shared partials
+  auto go = [&](auto kfn, auto* typed_out) {
+    return launch_chained(kfn, dim3((unsigned)T), dim3(threads), 0, stream, 1u, (const __nv_bfloat16*)weighted, inv,
+                          (const __nv_bfloat16*)shared_out, shared_parts, T, K, H, T * K, typed_out, st);
+  };
+  const bool f32 = out_dtype == DWDP_DTYPE_F32;
+  if (!f32 && out_dtype != DWDP_DTYPE_BF16) return DWDP_ERR_UNSUPPORTED;
+  cudaError_t e;
+#define DWDP_MERGE(KM, PM)                                                                          \
+  e = f32 ? go(merge_kernel<float, KM, PM>, static_cast<float*>(out))                              \
+          : go(merge_kernel<__nv_bfloat16, KM, PM>, static_cast<__nv_bfloat16*>(out))
+  if (K <= 4 && shared_parts <= 1) DWDP_MERGE(4, 1);
+  else if (K <= 4) DWDP_MERGE(4, 8);
+  else if (K <= 8 && shared_parts <= 1) DWDP_MERGE(8, 1);
+  else if (K <= 8) DWDP_MERGE(8, 8);
+  else DWDP_MERGE(16, 8);
+#undef DWDP_MERGE
+  if (e != cudaSuccess) return DWDP_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;
 }

@@ -778,6 +778,7 @@ struct QuantSeg {
 struct QuantParams {
   QuantSeg seg[2];
   DeviceStatus* st;
+  int per_warp;  // 1: one warp per row (many rows); 0: one CTA per row (few, long rows)
 };
 
 // 8 bf16 (one 16-byte load) -> 8 hi bytes and 8 lo bytes
@@ -870,10 +871,68 @@ __device__ __forceinline__ void quant_row_block(const QuantSeg& g, int row, floa
   if (tid == 0) g.scale[row] = amax > 0.f ? amax / 448.0f : 0.f;
 }
 
-__device__ __forceinline__ void quant_rows(const QuantParams& q, int first, int stride) {
+// One warp quantises one row: the first 8 chunks of 16 bytes per lane (rows up
+// to 2048 elements) stay in registers, longer rows re-read their tail.
+__device__ __forceinline__ void quant_row_warp(const QuantSeg& g, int row, DeviceStatus* st) {
+  const int lane = threadIdx.x & 31;
+  int64_t sr = row;
+  if (g.row_index != nullptr) {
+    sr = g.row_index[row];
+    if (sr < 0 || sr >= g.src_rows) {
+      if (lane == 0) record_error(st, DWDP_ERR_DEVICE_BOUNDS, 211, row);
+      sr = -1;
+    }
+  }
+  const __nv_bfloat16* src = sr >= 0 ? g.src + (size_t)sr * g.K : nullptr;
+  const int K = src != nullptr ? g.K : 0;
+  constexpr int kC = 8;
+  uint4 v[kC];
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < kC; ++j) {
+    const int c = (j * 32 + lane) * 8;
+    v[j] = c < K ? *reinterpret_cast<const uint4*>(src + c) : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int j = 0; j < kC; ++j) amax = amax8(v[j], amax);
+  for (int c = (kC * 32 + lane) * 8; c < K; c += 256) amax = amax8(*reinterpret_cast<const uint4*>(src + c), amax);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float inv = amax > 0.f ? 448.0f / amax : 0.f;
+  uint8_t* hi = g.dst + (size_t)(2 * row) * g.K;
+  uint8_t* lo = hi + g.K;
+#pragma unroll
+  for (int j = 0; j < kC; ++j) {
+    const int c = (j * 32 + lane) * 8;
+    if (c < g.K) {
+      uint2 h8, l8;
+      quant8(v[j], inv, h8, l8);
+      *reinterpret_cast<uint2*>(hi + c) = h8;
+      *reinterpret_cast<uint2*>(lo + c) = l8;
+    }
+  }
+  for (int c = (kC * 32 + lane) * 8; c < g.K; c += 256) {
+    uint2 h8, l8;
+    quant8(K > 0 ? *reinterpret_cast<const uint4*>(src + c) : make_uint4(0, 0, 0, 0), inv, h8, l8);
+    *reinterpret_cast<uint2*>(hi + c) = h8;
+    *reinterpret_cast<uint2*>(lo + c) = l8;
+  }
+  if (lane == 0) g.scale[row] = amax > 0.f ? amax / 448.0f : 0.f;
+}
+
+// Rows of both segments, one per `first + i * stride` unit (a warp or a CTA).
+__device__ __forceinline__ void quant_rows(const QuantParams& q, int block, int nblocks) {
   __shared__ float red[kPlanThreads / 32];
   const int total = q.seg[0].rows + q.seg[1].rows;
-  for (int r = first; r < total; r += stride) {
+  if (q.per_warp) {
+    constexpr int kW = kPlanThreads / 32;
+    for (int r = block * kW + (int)(threadIdx.x >> 5); r < total; r += nblocks * kW) {
+      if (r < q.seg[0].rows) quant_row_warp(q.seg[0], r, q.st);
+      else quant_row_warp(q.seg[1], r - q.seg[0].rows, q.st);
+    }
+    return;
+  }
+  for (int r = block; r < total; r += nblocks) {
     if (r < q.seg[0].rows) quant_row_block(q.seg[0], r, red, q.st);
     else quant_row_block(q.seg[1], r - q.seg[0].rows, red, q.st);
   }
@@ -1014,9 +1073,13 @@ int launch_gemm_f8(const GemmParams& prm, int grid, cudaStream_t stream) {
              : DWDP_ERR_CUDA;
 }
 
-// blocks for quantising `rows` rows, one CTA per row, at most a few waves
+// One warp per row once the rows fill every SM's warps; below that a CTA per
+// row (decode: a few long rows want more loads in flight than one warp has).
+constexpr int64_t kQuantWarpRows = 148 * 8;
+inline int quant_per_warp(int64_t rows) { return rows >= kQuantWarpRows ? 1 : 0; }
 inline int quant_blocks(int64_t rows) {
-  return (int)std::max<int64_t>(1, std::min<int64_t>(rows, 148 * 8));
+  const int64_t b = quant_per_warp(rows) ? (rows + kPlanThreads / 32 - 1) / (kPlanThreads / 32) : rows;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(b, 148 * 16));
 }
 
 template <int MODE, bool WFP8>
@@ -1112,6 +1175,7 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   QuantParams qx{}, qh{};
   qx.st = st;
   qh.st = st;
+  qx.per_warp = qh.per_warp = quant_per_warp(N + (has_shared ? T : 0));
   const bool indexed = packed_hidden == nullptr;
   if (indexed && packed_tok == nullptr) return DWDP_ERR_INVALID_ARGUMENT;
   if (native) {
