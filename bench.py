@@ -284,6 +284,49 @@ class LayerStack:
         return sum(lay.experts.remote_bytes() for lay in self.layers) if self.sharded else 0
 
 
+# ----------------------------------------------------------------------------- DWDP transfer comparison
+def transfer_comparison(store, world: int, steps: int, device) -> dict:
+    """One layer's remote experts moved two ways, nothing else running, max over ranks:
+    the engine's peer copies into staging (the DWDP path) and an NCCL all-gather of
+    every rank's expert shard (the comparison the north star names). GB/s counts the
+    bytes each GPU receives."""
+    import torch.distributed as dist
+
+    def timed(fn, n):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b) / n], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    n = max(3, min(steps, 10))
+    recv = store.remote_bytes()
+
+    def p2p():
+        store.prefetch(0)
+        store.wait(0)
+
+    p2p_ms = timed(p2p, n)
+    shard = store.local.slabs.view(-1)
+    per_rank = -(-store.num_experts // world) * store.slab_bytes  # every rank's shard padded to ceil(E/G)
+    src = torch.zeros(per_rank, dtype=torch.uint8, device=device)
+    src[: shard.numel()].copy_(shard[:per_rank])
+    dst = torch.empty(world * per_rank, dtype=torch.uint8, device=device)
+    ag_ms = timed(lambda: dist.all_gather_into_tensor(dst, src), n)
+    ag_recv = (world - 1) * per_rank
+    return {"p2p_prefetch_ms_per_layer": p2p_ms, "p2p_prefetch_gbs": recv / (p2p_ms / 1e3) / 1e9,
+            "nccl_all_gather_ms_per_layer": ag_ms, "nccl_all_gather_gbs": ag_recv / (ag_ms / 1e3) / 1e9,
+            "bytes_received_per_gpu": {"p2p": recv, "nccl": ag_recv}}
+
+
 # ----------------------------------------------------------------------------- main
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -405,6 +448,7 @@ def main() -> None:
         nvlink = {"remote_bytes_per_step_per_gpu": rb,
                   "prefetch_gbs_lower_bound": rb / (ms_per_step / 1e3) / 1e9,
                   "note": "copies overlap compute; GB/s is remote bytes / step time (a lower bound on link rate)"}
+        nvlink.update(transfer_comparison(stack.layers[0].experts, world, args.steps, device))
 
     cb = None
     if rank == 0 and world == 1:
