@@ -71,6 +71,7 @@ struct WorkItem {
   int kb_begin;  // first / one-past-last 64-wide K step of this item (split K)
   int kb_end;
   int part;      // K-split index: output goes to out + part * part_stride
+  int nmat;      // weight matrices of the item: gate+up (2), or 1-2 consecutive down row blocks
   const uint8_t* wtiles;  // first weight tile of this item's 128-row block (set by the planner)
   const float* scales;    // the expert's scales (fp8) or nullptr
 };
@@ -88,6 +89,8 @@ struct GroupParams {
   int enabled;
   int box_rows;            // activation rows per TMA box (multiple of 16, <= BN_MAX)
   long long part_stride;   // elements between K-split partial outputs
+  long long mstride;       // e4m3 path: bytes between an item's weight matrices
+  long long kstride;       // e4m3 path: bytes between an item's 128-input stages
 };
 
 struct GemmParams {
@@ -427,10 +430,11 @@ constexpr int BN8 = 64;                     // max tokens per tile
 constexpr int kW8TileBytes = BM * BK8;      // 128 x 128 weight tile
 constexpr int kB8TileBytes = 2 * BN8 * BK8; // hi/lo activation tile
 
-template <int MODE>
+// NM = weight matrices per stage: 2 for gate+up or paired down row blocks, 1 for single down blocks
+template <int MODE, int NM>
 struct Cfg8 {
-  static constexpr int NMAT = MODE == 0 ? 2 : 1;
-  static constexpr int S = MODE == 0 ? 4 : 6;
+  static constexpr int NMAT = NM;
+  static constexpr int S = NM == 2 ? 4 : 6;
   static constexpr int W_STAGE_BYTES = NMAT * kW8TileBytes;
   static constexpr int THREADS = 6 * 32;
   static constexpr int ACC_STRIDE = NMAT * 2 * BN8;  // TMEM columns per accumulator buffer
@@ -438,10 +442,10 @@ struct Cfg8 {
   static constexpr int SMEM_BYTES = S * (W_STAGE_BYTES + kB8TileBytes) + 1024 + 256;
 };
 
-template <int MODE>
-__global__ void __launch_bounds__(Cfg8<MODE>::THREADS, 1)
+template <int MODE, int NM>
+__global__ void __launch_bounds__(Cfg8<MODE, NM>::THREADS, 1)
 moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
-  using C = Cfg8<MODE>;
+  using C = Cfg8<MODE, NM>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sB = smem;
@@ -500,9 +504,11 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
         for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
           const int s = it % C::S;
           if (!mbar_wait(&ld_empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 21 + 8 * MODE)) break;
-          mbar_arrive_expect_tx(&ld_full[s], C::W_STAGE_BYTES + b_bytes);
-          const size_t woff = (size_t)kb * C::W_STAGE_BYTES;
-          bulk_g2s(sW + s * C::W_STAGE_BYTES, wbase + woff, C::W_STAGE_BYTES, &ld_full[s]);
+          const int nm = min(wi.nmat, C::NMAT);
+          mbar_arrive_expect_tx(&ld_full[s], (uint32_t)(nm * kW8TileBytes) + b_bytes);
+          for (int m = 0; m < nm; ++m)
+            bulk_g2s(sW + s * C::W_STAGE_BYTES + m * kW8TileBytes,
+                     wbase + (size_t)m * g.mstride + (size_t)kb * g.kstride, kW8TileBytes, &ld_full[s]);
           tma_load_2d(sB + s * kB8TileBytes, &g.tmap_b, kb * BK8, 2 * wi.row0, &ld_full[s]);
         }
       }
@@ -531,8 +537,7 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
           const uint64_t b_desc0 = smem_desc_sw128(smem_u32(sB + s * kB8TileBytes));
           const uint64_t a_desc0 = smem_desc_sw128(smem_u32(sW + s * C::W_STAGE_BYTES));
           const uint32_t acc_first = kb > wi.kb_begin ? 1u : 0u;
-#pragma unroll
-          for (int m = 0; m < C::NMAT; ++m) {
+          for (int m = 0; m < min(wi.nmat, C::NMAT); ++m) {
 #pragma unroll
             for (int kk = 0; kk < BK8 / 32; ++kk) {
               mma_e4m3_ss(d_base + m * 2 * BN8, a_desc0 + (uint64_t)(m * (kW8TileBytes >> 4) + 2 * kk),
@@ -558,8 +563,10 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
       const int a = li & 1;
       const int feat = wi.rb * BM + lrow;
       __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)wi.part * g.part_stride;
+      // gate/up: s0, s1 scale the two matrices of one feature; down: two consecutive features
       const float s0 = wi.scales[feat];  // loaded while the MMAs run
-      const float s1 = MODE == 0 ? wi.scales[g.R + feat] : 1.0f;
+      const int nmat = min(wi.nmat, C::NMAT);
+      const float s1 = MODE == 0 ? wi.scales[g.R + feat] : (nmat > 1 ? wi.scales[feat + BM] : 1.0f);
       const float* xs = g.x_scale + wi.row0;
       if (!mbar_wait(&acc_full[a], (li >> 1) & 1, &s_abort, st, 24 + 8 * MODE)) break;
       tc_fence_after();
@@ -582,17 +589,20 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
             }
           }
         } else {
-          float yv[16];
-          tmem_ld16(t_acc + c0, yv);
-          tmem_ld_wait();
+          for (int m = 0; m < nmat; ++m) {
+            float yv[16];
+            tmem_ld16(t_acc + m * 2 * BN8 + c0, yv);
+            tmem_ld_wait();
+            const float sm = m == 0 ? s0 : s1;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int t = t0 + j;
-            if (t < wi.nrows) {
-              const int row = wi.row0 + t;
-              const float rs = g.row_scale != nullptr ? g.row_scale[row] : 1.0f;
-              const float y = (yv[2 * j] + yv[2 * j + 1] * (1.0f / kLoPlaneGain)) * (s0 * xs[t]);
-              out[(size_t)row * g.R + feat] = __float2bfloat16_rn(y * rs);
+            for (int j = 0; j < 8; ++j) {
+              const int t = t0 + j;
+              if (t < wi.nrows) {
+                const int row = wi.row0 + t;
+                const float rs = g.row_scale != nullptr ? g.row_scale[row] : 1.0f;
+                const float y = (yv[2 * j] + yv[2 * j + 1] * (1.0f / kLoPlaneGain)) * (sm * xs[t]);
+                out[(size_t)row * g.R + feat + m * BM] = __float2bfloat16_rn(y * rs);
+              }
             }
           }
         }
@@ -630,6 +640,8 @@ struct PlanParams {
   const float* const* s_gu[2];              // [group] per-expert scales (or nullptr)
   const float* const* s_dn[2];
   long long rbb_gu[2], rbb_dn[2];           // bytes of one 128-row weight block
+  int dn_pair;                              // down items cover two consecutive 128-row blocks
+  int blocks_dn;                            // 128-row blocks of the down projection (H / 128)
   WorkItem* items_gu;
   WorkItem* items_dn;
   int* n_items;
@@ -729,11 +741,12 @@ __device__ __forceinline__ void plan_body(const PlanParams& pp) {
         const int per_part = n_sh_tiles * (phase == 0 ? pp.rb_gu_s : pp.rb_dn_s);
         const int part = phase == 0 ? 0 : i / per_part;
         const int rem = phase == 0 ? i : i % per_part;
-        const int rb = rem / n_sh_tiles, j = rem % n_sh_tiles;
+        const int rbi = rem / n_sh_tiles, j = rem % n_sh_tiles;
+        const int rb = (phase == 1 && pp.dn_pair) ? 2 * rbi : rbi;
         const int row0 = j * bn_s;
         const int kb0 = phase == 0 ? 0 : part * kb_part;
         const int kb1 = phase == 0 ? pp.kb_gu : (part + 1) * kb_part;
-        w = WorkItem{1, 0, rb, row0, min(bn_s, T - row0), kb0, kb1, part, nullptr, nullptr};
+        w = WorkItem{1, 0, rb, row0, min(bn_s, T - row0), kb0, kb1, part, 2, nullptr, nullptr};
       } else {         // routed: expert e with s_pre[e]*rb_r <= i - base < s_pre[e+1]*rb_r
         const int r = i - base;
         int lo = 0, hi = E - 1;
@@ -744,11 +757,13 @@ __device__ __forceinline__ void plan_body(const PlanParams& pp) {
         const int e = lo;
         const int nt = s_nt[e], bn = s_bn[e];
         const int local = r - s_pre[e] * rb_r;
-        const int rb = local / nt, j = local % nt;
+        const int rbi = local / nt, j = local % nt;
+        const int rb = (phase == 1 && pp.dn_pair) ? 2 * rbi : rbi;
         const int cnt = (int)pp.counts[e];
         const int row0 = (int)pp.offsets[e] + j * bn;
-        w = WorkItem{0, e, rb, row0, min(bn, cnt - j * bn), 0, kb_r, 0, nullptr, nullptr};
+        w = WorkItem{0, e, rb, row0, min(bn, cnt - j * bn), 0, kb_r, 0, 2, nullptr, nullptr};
       }
+      if (phase == 1) w.nmat = pp.dn_pair ? min(2, pp.blocks_dn - w.rb) : 1;
       const void* const* wp = phase == 0 ? pp.w_gu[w.group] : pp.w_dn[w.group];
       const float* const* sp = phase == 0 ? pp.s_gu[w.group] : pp.s_dn[w.group];
       const long long rbb = phase == 0 ? pp.rbb_gu[w.group] : pp.rbb_dn[w.group];
@@ -1062,10 +1077,10 @@ WsLayout ws_layout(int64_t T, int K, int E, int I, int H, int Is) {
 
 int g_num_sms = 0;
 
-template <int MODE>
+template <int MODE, int NM>
 int launch_gemm_f8(const GemmParams& prm, int grid, cudaStream_t stream) {
-  using C = Cfg8<MODE>;
-  auto kfn = moe_gemm_f8_kernel<MODE>;
+  using C = Cfg8<MODE, NM>;
+  auto kfn = moe_gemm_f8_kernel<MODE, NM>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return DWDP_ERR_CUDA;
   return launch_chained(kfn, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, stream, 1u, prm) == cudaSuccess
@@ -1158,8 +1173,16 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   const int parts = shared_down_parts(T, Is);
   PlanParams pp{};
   pp.counts = counts; pp.offsets = offsets; pp.E = E; pp.T = (int)T; pp.has_shared = has_shared;
-  pp.rb_gu_r = I / BM; pp.rb_dn_r = H / BM;
-  pp.rb_gu_s = has_shared ? Is / BM : 0; pp.rb_dn_s = has_shared ? H / BM : 0;
+  // e4m3 path at prefill sizes: a down item covers two consecutive 128-row blocks (one activation
+  // tile for two MMAs, half the activation traffic per FLOP). Decode keeps single blocks: there
+  // the halved item count would leave SMs idle or unevenly loaded (pairs need ~4 waves of items).
+  const int sms_now = dwdp_device_sm_count();
+  const int64_t est_tiles = N / BN8 + std::min<int64_t>(E, N) + (has_shared ? (T + BN8 - 1) / BN8 * parts : 0);
+  const bool pair_dn = native && est_tiles * ((H / BM + 1) / 2) >= 4LL * std::max(1, sms_now);
+  const int dn_items_per_tile = pair_dn ? (H / BM + 1) / 2 : H / BM;
+  pp.rb_gu_r = I / BM; pp.rb_dn_r = dn_items_per_tile;
+  pp.rb_gu_s = has_shared ? Is / BM : 0; pp.rb_dn_s = has_shared ? dn_items_per_tile : 0;
+  pp.dn_pair = pair_dn ? 1 : 0; pp.blocks_dn = H / BM;
   pp.kb_gu = H / bk; pp.kb_dn_r = I / bk; pp.kb_dn_s = has_shared ? Is / bk : 0;
   pp.sdn_parts = has_shared ? parts : 0;
   pp.bn_max = bn;
@@ -1210,12 +1233,15 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   gu.g[0].w = routed->w13; gu.g[0].s = routed->s13; gu.g[0].out = h_r; gu.g[0].row_scale = nullptr;
   gu.g[0].x_scale = sx_r;
   gu.g[0].K = H; gu.g[0].R = I; gu.g[0].scale_mode = routed->scale_mode; gu.g[0].box_rows = box_r;
+  // e4m3 tiles: gate/up interleaved per 128-input stage; down row blocks are K/128 tiles apart
+  gu.g[0].mstride = kW8TileBytes; gu.g[0].kstride = 2 * kW8TileBytes;
   gu.g[1].enabled = has_shared;
   if (has_shared) {
     if (!map(&gu.g[1].tmap_b, hidden, L.x8_s, T, H, box_s)) return DWDP_ERR_CUDA;
     gu.g[1].w = shared->w13; gu.g[1].s = shared->s13; gu.g[1].out = h_s; gu.g[1].row_scale = nullptr;
     gu.g[1].x_scale = sx_s;
     gu.g[1].K = H; gu.g[1].R = Is; gu.g[1].scale_mode = shared->scale_mode; gu.g[1].box_rows = box_s;
+    gu.g[1].mstride = kW8TileBytes; gu.g[1].kstride = 2 * kW8TileBytes;
   }
   gu.items = items_gu; gu.n_items = n_items; gu.st = st; gu.cap = L.cap_gu;
 
@@ -1224,12 +1250,14 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   dn.g[0].w = routed->w2; dn.g[0].s = routed->s2; dn.g[0].out = weighted_out; dn.g[0].box_rows = box_r;
   dn.g[0].x_scale = sh_r;
   dn.g[0].row_scale = packed_weights; dn.g[0].K = I; dn.g[0].R = H; dn.g[0].scale_mode = routed->scale_mode;
+  dn.g[0].mstride = (long long)BM * I; dn.g[0].kstride = kW8TileBytes;
   dn.g[1].enabled = has_shared;
   if (has_shared) {
     if (!map(&dn.g[1].tmap_b, h_s, L.h8_s, T, Is, box_s)) return DWDP_ERR_CUDA;
     dn.g[1].w = shared->w2; dn.g[1].s = shared->s2; dn.g[1].out = shared_out; dn.g[1].box_rows = box_s;
     dn.g[1].x_scale = sh_s;
     dn.g[1].row_scale = shared_gate; dn.g[1].K = Is; dn.g[1].R = H; dn.g[1].scale_mode = shared->scale_mode;
+    dn.g[1].mstride = (long long)BM * Is; dn.g[1].kstride = kW8TileBytes;
     dn.g[1].part_stride = (long long)T * H;
   }
   dn.items = items_dn; dn.n_items = n_items + 1; dn.st = st; dn.cap = L.cap_dn;
@@ -1240,14 +1268,14 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   const int grid_dn = std::max(1, std::min(sms, L.cap_dn));
   int rc;
   if (native) {
-    rc = launch_gemm_f8<0>(gu, grid_gu, stream);
+    rc = launch_gemm_f8<0, 2>(gu, grid_gu, stream);
     if (rc == DWDP_OK) {
       rc = launch_chained(quant_kernel, dim3(quant_blocks(N + (has_shared ? T : 0))), dim3(kPlanThreads), 0,
                           stream, 1u, qh) == cudaSuccess
                ? DWDP_OK
                : DWDP_ERR_CUDA;
     }
-    if (rc == DWDP_OK) rc = launch_gemm_f8<1>(dn, grid_dn, stream);
+    if (rc == DWDP_OK) rc = pair_dn ? launch_gemm_f8<1, 2>(dn, grid_dn, stream) : launch_gemm_f8<1, 1>(dn, grid_dn, stream);
   } else if (fp8) {
     rc = launch_gemm<0, true>(gu, grid_gu, stream);
     if (rc == DWDP_OK) rc = launch_gemm<1, true>(dn, grid_dn, stream);
