@@ -31,8 +31,9 @@ extern "C" size_t dwdp_moe_workspace_bytes_impl(int64_t, int, int, int, int, int
 extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group*, const dwdp_expert_group*,
                                        const void*, const int64_t*, const void*, int64_t, int, const int64_t*,
                                        const int64_t*, const float*, const float*, void*, void*,
-                                       void*, size_t, int*, cudaStream_t);
-extern "C" int dwdp_merge_launch(const void*, const int64_t*, const void*, int, int64_t, int, int,
+                                       void*, size_t, int*, int, cudaStream_t);
+extern "C" size_t dwdp_moe_shared_workspace_bytes_impl(int64_t, int, int);
+extern "C" int dwdp_merge_launch(const void*, const int64_t*, const void*, int, const float*, int64_t, int, int,
                                  void*, int, int*, cudaStream_t);
 
 namespace {
@@ -241,7 +242,7 @@ int moe_experts_checked(const dwdp_expert_group* routed, const dwdp_expert_group
     return fail(DWDP_ERR_CAPACITY, "moe_experts: workspace of %zu bytes < required %zu", workspace_bytes, need);
   return check(dwdp_moe_experts_launch(routed, shared, packed_hidden, packed_tok, hidden, num_tokens, top_k,
                                        counts, offsets, packed_weights, shared_gate, weighted_out, shared_out,
-                                       workspace, workspace_bytes, status, as_stream(stream)),
+                                       workspace, workspace_bytes, status, 0, as_stream(stream)),
                "moe_experts");
 }
 }  // namespace
@@ -276,7 +277,44 @@ extern "C" int dwdp_merge(const void* weighted, const int64_t* inv, const void* 
     return fail(DWDP_ERR_INVALID_ARGUMENT, "merge: hidden_size must be a positive multiple of 8");
   if (shared_out != nullptr && (shared_parts < 1 || shared_parts > 64))
     return fail(DWDP_ERR_INVALID_ARGUMENT, "merge: shared_parts must be in [1, 64]");
-  return check(dwdp_merge_launch(weighted, inv, shared_out, shared_parts, num_tokens, top_k, hidden_size, out, out_dtype,
-                                 nullptr, as_stream(stream)),
+  return check(dwdp_merge_launch(weighted, inv, shared_out, shared_parts, nullptr, num_tokens, top_k, hidden_size,
+                                 out, out_dtype, nullptr, as_stream(stream)),
                "merge");
+}
+
+extern "C" int dwdp_merge_gated(const void* weighted, const int64_t* inv, const void* shared_out, int shared_parts,
+                                const float* shared_gate, int64_t num_tokens, int top_k, int hidden_size, void* out,
+                                int out_dtype, void* stream) {
+  g_last_error.clear();
+  if (top_k <= 0 || top_k > 16) return fail(DWDP_ERR_INVALID_ARGUMENT, "merge: top_k must be in [1, 16]");
+  if (hidden_size <= 0 || hidden_size % 8)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "merge: hidden_size must be a positive multiple of 8");
+  if (shared_out == nullptr || shared_gate == nullptr || shared_parts < 1 || shared_parts > 8)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "merge_gated: needs shared_out, shared_gate and 1..8 shared parts");
+  return check(dwdp_merge_launch(weighted, inv, shared_out, shared_parts, shared_gate, num_tokens, top_k, hidden_size,
+                                 out, out_dtype, nullptr, as_stream(stream)),
+               "merge_gated");
+}
+
+extern "C" size_t dwdp_moe_shared_workspace_bytes(int64_t num_tokens, int hidden_size, int shared_intermediate_size) {
+  return dwdp_moe_shared_workspace_bytes_impl(num_tokens, hidden_size, shared_intermediate_size);
+}
+
+extern "C" int dwdp_moe_shared_expert(const dwdp_expert_group* shared, const void* hidden, int64_t num_tokens,
+                                      void* shared_out, void* workspace, size_t workspace_bytes, int* status,
+                                      void* stream) {
+  g_last_error.clear();
+  if (shared == nullptr || hidden == nullptr || shared_out == nullptr)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_shared_expert: shared group, hidden and shared_out are required");
+  if (shared->num_experts != 1 || shared->hidden_size <= 0 || shared->hidden_size > 8192 ||
+      shared->hidden_size % 128 || shared->intermediate_size <= 0 || shared->intermediate_size % 128)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_shared_expert: one expert, sizes multiples of 128, hidden <= 8192");
+  if (num_tokens < 0) return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_shared_expert: bad num_tokens");
+  const size_t need = dwdp_moe_shared_workspace_bytes_impl(num_tokens, shared->hidden_size, shared->intermediate_size);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(DWDP_ERR_CAPACITY, "moe_shared_expert: workspace of %zu bytes < required %zu", workspace_bytes, need);
+  return check(dwdp_moe_experts_launch(shared, shared, nullptr, nullptr, hidden, num_tokens, 1, nullptr, nullptr,
+                                       nullptr, nullptr, nullptr, shared_out, workspace, workspace_bytes, status, 1,
+                                       as_stream(stream)),
+               "moe_shared_expert");
 }

@@ -34,7 +34,8 @@ __device__ __forceinline__ void add8(float (&acc)[8], const uint4& v) {
 template <typename TOut, int KMAX, int PMAX>
 __global__ void __launch_bounds__(256)
 merge_kernel(const __nv_bfloat16* __restrict__ weighted, const int64_t* __restrict__ inv,
-             const __nv_bfloat16* __restrict__ shared_out, int shared_parts, int64_t T, int K, int H,
+             const __nv_bfloat16* __restrict__ shared_out, int shared_parts,
+             const float* __restrict__ shared_gate, int64_t T, int K, int H,
              int64_t nrows, TOut* __restrict__ out, DeviceStatus* st) {
   griddep_launch();
   __shared__ int64_t s_rows[KMAX];
@@ -57,6 +58,8 @@ merge_kernel(const __nv_bfloat16* __restrict__ weighted, const int64_t* __restri
   }
   __syncthreads();
   const int nk = s_nk;
+  const float* sgate = shared_gate;
+  const float sgate_t = sgate != nullptr ? sgate[t] : 1.0f;
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
     uint4 v[KMAX], sv[PMAX];
 #pragma unroll
@@ -69,9 +72,18 @@ merge_kernel(const __nv_bfloat16* __restrict__ weighted, const int64_t* __restri
 #pragma unroll
     for (int j = 0; j < KMAX; ++j)
       if (j < nk) add8(acc, v[j]);
+    if (sgate == nullptr) {
 #pragma unroll
-    for (int sp = 0; sp < PMAX; ++sp)
-      if (sp < shared_parts) add8(acc, sv[sp]);
+      for (int sp = 0; sp < PMAX; ++sp)
+        if (sp < shared_parts) add8(acc, sv[sp]);
+    } else {  // ungated shared partials: out += gate[t] * sum of parts
+      float sacc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int sp = 0; sp < PMAX; ++sp)
+        if (sp < shared_parts) add8(sacc, sv[sp]);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] += sgate_t * sacc[q];
+    }
     if constexpr (sizeof(TOut) == 2) {
       uint4 o;
       __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&o);
@@ -91,7 +103,8 @@ merge_kernel(const __nv_bfloat16* __restrict__ weighted, const int64_t* __restri
 using namespace dwdp;
 
 extern "C" int dwdp_merge_launch(const void* weighted, const int64_t* inv, const void* shared_out,
-                                 int shared_parts, int64_t T, int K, int H, void* out, int out_dtype,
+                                 int shared_parts, const float* shared_gate, int64_t T, int K, int H, void* out,
+                                 int out_dtype,
                                  int* status,
                                  cudaStream_t stream) {
   if (K <= 0 || K > kMergeMaxK || (H & 7) != 0 || T < 0 || shared_parts < 0) return DWDP_ERR_INVALID_ARGUMENT;
@@ -103,7 +116,7 @@ extern "C" int dwdp_merge_launch(const void* weighted, const int64_t* inv, const
   // register staging sized to the call: K rows and the shared partials
   auto go = [&](auto kfn, auto* typed_out) {
     return launch_chained(kfn, dim3((unsigned)T), dim3(threads), 0, stream, 1u, (const __nv_bfloat16*)weighted, inv,
-                          (const __nv_bfloat16*)shared_out, shared_parts, T, K, H, T * K, typed_out, st);
+                          (const __nv_bfloat16*)shared_out, shared_parts, shared_gate, T, K, H, T * K, typed_out, st);
   };
   const bool f32 = out_dtype == DWDP_DTYPE_F32;
   if (!f32 && out_dtype != DWDP_DTYPE_BF16) return DWDP_ERR_UNSUPPORTED;

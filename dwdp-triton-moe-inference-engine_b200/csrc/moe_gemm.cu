@@ -672,7 +672,7 @@ __device__ __forceinline__ void plan_body(const PlanParams& pp) {
       const int e = e0 + tid * 4 + q;
       int nt = 0, bn = 0;
       if (e < E) {
-        const int cnt = (int)pp.counts[e];
+        const int cnt = pp.counts != nullptr ? (int)pp.counts[e] : 0;
         if (cnt > 0) {
           nt = (cnt + pp.bn_max - 1) / pp.bn_max;
           bn = (((cnt + nt - 1) / nt) + 15) & ~15;
@@ -1127,6 +1127,12 @@ extern "C" size_t dwdp_moe_workspace_bytes_impl(int64_t T, int K, int E, int H, 
   return ws_layout(T, K, E, I, H, Is).total;
 }
 
+// The shared expert alone runs as the launch above with the shared group standing in
+// for the routed one (K = 1, E = 1) and no routed rows.
+extern "C" size_t dwdp_moe_shared_workspace_bytes_impl(int64_t T, int H, int Is) {
+  return ws_layout(T, 1, 1, Is, H, Is).total;
+}
+
 extern "C" int dwdp_gather_rows_launch(const void* hidden, const int64_t* tok, int64_t N, int H, int64_t T,
                                        void* packed, int* status, cudaStream_t stream);
 
@@ -1138,7 +1144,9 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
                                        int K, const int64_t* counts, const int64_t* offsets,
                                        const float* packed_weights, const float* shared_gate,
                                        void* weighted_out, void* shared_out, void* workspace,
-                                       size_t workspace_bytes, int* status, cudaStream_t stream) {
+                                       size_t workspace_bytes, int* status, int shared_only,
+                                       cudaStream_t stream) {
+  // shared_only: the shared expert alone (routed describes its shape; no routed rows)
   if (routed == nullptr || T < 0 || K <= 0) return DWDP_ERR_INVALID_ARGUMENT;
   const int H = routed->hidden_size, I = routed->intermediate_size, E = routed->num_experts;
   const int Is = shared ? shared->intermediate_size : 0;
@@ -1153,7 +1161,7 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   const bool native = fp8 && routed->scale_mode == DWDP_SCALE_CHANNEL;
   const int bk = native ? BK8 : BK;
   const int bn = native ? BN8 : BN_MAX;
-  const int64_t N = T * K;
+  const int64_t N = shared_only ? 0 : T * K;  // routed rows
   const WsLayout L = ws_layout(T, K, E, I, H, Is);
   if (workspace == nullptr || workspace_bytes < L.total) return DWDP_ERR_CAPACITY;
   if (T == 0) return DWDP_OK;
@@ -1172,7 +1180,8 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
 
   const int parts = shared_down_parts(T, Is);
   PlanParams pp{};
-  pp.counts = counts; pp.offsets = offsets; pp.E = E; pp.T = (int)T; pp.has_shared = has_shared;
+  pp.counts = shared_only ? nullptr : counts; pp.offsets = offsets; pp.E = E; pp.T = (int)T;
+  pp.has_shared = has_shared;
   // e4m3 path at prefill sizes: a down item covers two consecutive 128-row blocks (one activation
   // tile for two MMAs, half the activation traffic per FLOP). Decode keeps single blocks: there
   // the halved item count would leave SMs idle or unevenly loaded (pairs need ~4 waves of items).
@@ -1200,7 +1209,7 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   qh.st = st;
   qx.per_warp = qh.per_warp = quant_per_warp(N + (has_shared ? T : 0));
   const bool indexed = packed_hidden == nullptr;
-  if (indexed && packed_tok == nullptr) return DWDP_ERR_INVALID_ARGUMENT;
+  if (indexed && packed_tok == nullptr && N > 0) return DWDP_ERR_INVALID_ARGUMENT;
   if (native) {
     const __nv_bfloat16* hid = reinterpret_cast<const __nv_bfloat16*>(hidden);
     qx.seg[0] = indexed ? QuantSeg{hid, ws + L.x8_r, sx_r, (int)N, H, packed_tok, T}

@@ -31,6 +31,8 @@ class LayerWorkspace:
     shared_parts: int
     moe_ws: torch.Tensor
     status: torch.Tensor
+    shared_ws: torch.Tensor | None = None        # the shared expert's own launches (side stream)
+    side: torch.cuda.Stream | None = None
 
 
 class MoELayer:
@@ -71,6 +73,11 @@ class MoELayer:
         self.num_experts = E
         self.hidden_size = H
         self._ws: dict[int, LayerWorkspace] = {}
+        # The shared expert does not depend on routing, so it CAN run on a side stream from
+        # the start of the forward. Measured slower on B200 at T = 1..4096 (the persistent
+        # GEMMs each size their grid to every SM, so concurrent launches queue behind each
+        # other, and the cross-stream join breaks the programmatic-launch chain): off by default.
+        self.overlap_shared = False
         self.refresh_handles()
 
     def refresh_handles(self) -> None:
@@ -120,6 +127,9 @@ class MoELayer:
                 dtype=torch.uint8, device=dev,
             ),
             status=torch.zeros(4, dtype=torch.int32, device=dev),
+            shared_ws=torch.empty(ops.moe_shared_workspace_bytes(T, H, Is), dtype=torch.uint8, device=dev)
+            if has_shared else None,
+            side=torch.cuda.Stream(device=dev) if has_shared else None,
         )
         self._ws[num_tokens] = ws
         return ws
@@ -146,9 +156,13 @@ class MoELayer:
     __call__ = forward
 
     def run(self, x: torch.Tensor, ws: LayerWorkspace, out: torch.Tensor) -> None:
-        """All launches on the current stream (graph-capturable)."""
+        """All launches on the current stream, the shared expert's on the workspace's side
+        stream joined before the merge (graph-capturable)."""
         K = self.top_k
         T = x.shape[0]
+        overlap = self._overlap(ws)
+        if overlap:
+            self._start_shared(x, ws)
         gate_w = self.shared_gate_weight if self.shared_expert is not None else None
         ops.router_topk(
             x, self.router_weight, K, bias=self.router_bias, shared_gate_weight=gate_w,
@@ -159,16 +173,39 @@ class MoELayer:
             ws.router.topk_indices, ws.router.topk_weights, self.num_experts,
             scratch=ws.dispatch_scratch, out=ws.dispatch, status=ws.status,
         )
-        self.run_experts(x, ws)
-        ops.merge(ws.weighted, ws.dispatch.inverse_permutation, T, K, shared_out=ws.shared_out,
-                  shared_parts=ws.shared_parts, out=out)
+        self._routed(x, ws, with_shared=not overlap)
+        if overlap:
+            torch.cuda.current_stream().wait_stream(ws.side)
+            ops.merge(ws.weighted, ws.dispatch.inverse_permutation, T, K, shared_out=ws.shared_out,
+                      shared_parts=ws.shared_parts, out=out, shared_gate=ws.router.shared_gate)
+        else:
+            ops.merge(ws.weighted, ws.dispatch.inverse_permutation, T, K, shared_out=ws.shared_out,
+                      shared_parts=ws.shared_parts, out=out)
 
     def run_experts(self, x: torch.Tensor, ws: LayerWorkspace) -> None:
-        """The grouped expert GEMMs of :meth:`run` on a dispatched workspace."""
+        """Every expert GEMM of :meth:`run` on a dispatched workspace (weighted rows and
+        shared partials; the shared ones ungated when they run on the side stream)."""
+        overlap = self._overlap(ws)
+        if overlap:
+            self._start_shared(x, ws)
+        self._routed(x, ws, with_shared=not overlap)
+        if overlap:
+            torch.cuda.current_stream().wait_stream(ws.side)
+
+    def _overlap(self, ws: LayerWorkspace) -> bool:
+        return self.overlap_shared and ws.side is not None
+
+    def _start_shared(self, x: torch.Tensor, ws: LayerWorkspace) -> None:
+        ws.side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(ws.side):
+            ops.moe_shared_expert(self._shared_group, x, ws.shared_out, ws.shared_ws, ws.status)
+
+    def _routed(self, x: torch.Tensor, ws: LayerWorkspace, *, with_shared: bool) -> None:
         ops.moe_experts(
-            self._routed_group, self._shared_group, None, x, self.top_k,
+            self._routed_group, self._shared_group if with_shared else None, None, x, self.top_k,
             ws.dispatch.expert_counts, ws.dispatch.expert_offsets, ws.dispatch.packed_routing_weights,
-            ws.router.shared_gate, ws.weighted, ws.shared_out, ws.moe_ws, ws.status,
+            ws.router.shared_gate if with_shared else None, ws.weighted,
+            ws.shared_out if with_shared else None, ws.moe_ws, ws.status,
             packed_token_indices=ws.dispatch.packed_token_indices,
         )
 
@@ -180,6 +217,8 @@ class MoELayer:
         router = 1 if self.router_weight.dtype == torch.bfloat16 and self.num_experts <= 256 else 2
         dispatch = 1 if num_tokens * self.top_k <= 256 else 2
         experts = 4  # e4m3 weights: planes in the plan launch + one between the GEMMs; else one row gather
+        if self.shared_expert is not None and self.overlap_shared:
+            experts += 4  # the shared expert's own plan/gate-up/planes/down launches
         return router + dispatch + experts + 1
 
     def read_status(self, num_tokens: int) -> tuple[int, ...]:

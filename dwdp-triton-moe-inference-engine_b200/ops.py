@@ -339,6 +339,22 @@ def moe_experts(
     _lib.check(rc, "moe_experts")
 
 
+def moe_shared_workspace_bytes(num_tokens: int, hidden_size: int, shared_intermediate_size: int) -> int:
+    return int(_lib.load().dwdp_moe_shared_workspace_bytes(num_tokens, hidden_size, shared_intermediate_size))
+
+
+def moe_shared_expert(shared: _lib.ExpertGroup, hidden: torch.Tensor, shared_out: torch.Tensor,
+                      workspace: torch.Tensor, status: torch.Tensor | None = None) -> None:
+    """The shared expert alone, ungated: ``shared_out`` [parts, T, H] bf16 partials
+    (``moe_shared_parts(T, Is)`` of them); ``merge(..., shared_gate=g)`` applies the gate."""
+    _require_cuda(hidden, shared_out, workspace, status)
+    rc = _lib.load().dwdp_moe_shared_expert(
+        ctypes.byref(shared), hidden.data_ptr(), hidden.shape[0], shared_out.data_ptr(), workspace.data_ptr(),
+        workspace.numel(), _ptr(status), _stream(),
+    )
+    _lib.check(rc, "moe_shared_expert")
+
+
 def merge(
     weighted: torch.Tensor,
     inverse_permutation: torch.Tensor,
@@ -349,17 +365,29 @@ def merge(
     shared_parts: int = 1,
     out: torch.Tensor | None = None,
     out_dtype: torch.dtype = torch.bfloat16,
+    shared_gate: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """Deterministic token-major merge (DWDP/merger/kernels/reference.py:6-27)."""
-    _require_cuda(weighted, inverse_permutation, shared_out)
+    """Deterministic token-major merge (DWDP/merger/kernels/reference.py:6-27). With
+    ``shared_gate`` the shared partials are ungated and scaled by it here."""
+    _require_cuda(weighted, inverse_permutation, shared_out, shared_gate)
     if weighted.dtype != torch.bfloat16:
         raise ValueError("merge expects bf16 weighted rows")
     H = weighted.shape[-1]
     if out is None:
         out = torch.empty(num_tokens, H, dtype=out_dtype, device=weighted.device)
-    rc = _lib.load().dwdp_merge(
-        weighted.data_ptr(), inverse_permutation.contiguous().data_ptr(), _ptr(shared_out), shared_parts, num_tokens,
-        top_k, H, out.data_ptr(), dtype_code(out.dtype), _stream(),
-    )
+    lib = _lib.load()
+    inv = inverse_permutation.contiguous()
+    if shared_gate is not None:
+        if shared_out is None or shared_gate.dtype != torch.float32:
+            raise ValueError("a gated merge needs shared_out and an fp32 shared_gate")
+        rc = lib.dwdp_merge_gated(
+            weighted.data_ptr(), inv.data_ptr(), shared_out.data_ptr(), shared_parts, shared_gate.data_ptr(),
+            num_tokens, top_k, H, out.data_ptr(), dtype_code(out.dtype), _stream(),
+        )
+    else:
+        rc = lib.dwdp_merge(
+            weighted.data_ptr(), inv.data_ptr(), _ptr(shared_out), shared_parts, num_tokens,
+            top_k, H, out.data_ptr(), dtype_code(out.dtype), _stream(),
+        )
     _lib.check(rc, "merge")
     return out

@@ -216,6 +216,15 @@ int dwdp_moe_experts_indexed(const dwdp_expert_group* routed, const dwdp_expert_
                              void* shared_out, void* workspace, size_t workspace_bytes, int* status,
                              void* stream);
 
+/* The shared expert alone, for running it concurrently with routing: for every
+ * token t, sum_p shared_out[p][t] = down_s(silu(gate_s(x_t)) * up_s(x_t)) WITHOUT
+ * the sigmoid gate (dwdp_merge_gated applies it), p < dwdp_moe_shared_parts(T, Is).
+ * It depends only on `hidden`, so it can start before the router. */
+size_t dwdp_moe_shared_workspace_bytes(int64_t num_tokens, int hidden_size, int shared_intermediate_size);
+int dwdp_moe_shared_expert(const dwdp_expert_group* shared, const void* hidden, int64_t num_tokens,
+                           void* shared_out, void* workspace, size_t workspace_bytes, int* status,
+                           void* stream);
+
 /* ======================================================================== *
  * Merge (reference_merge, merger/kernels/reference.py:6-27): deterministic
  * token-major reduction. out[t] = sum over the K rows inv[t*K+k] of
@@ -226,6 +235,11 @@ int dwdp_moe_experts_indexed(const dwdp_expert_group* routed, const dwdp_expert_
 int dwdp_merge(const void* weighted, const int64_t* inv, const void* shared_out, int shared_parts,
                int64_t num_tokens, int top_k, int hidden_size, void* out, int out_dtype,
                void* stream);
+/* As dwdp_merge with ungated shared partials: out[t] = routed sum + shared_gate[t] *
+ * (sum over the shared parts), the gate applied in fp32 (DWDP/adapters/qwen15_moe.py:302-319). */
+int dwdp_merge_gated(const void* weighted, const int64_t* inv, const void* shared_out, int shared_parts,
+                     const float* shared_gate, int64_t num_tokens, int top_k, int hidden_size, void* out,
+                     int out_dtype, void* stream);
 
 /* ======================================================================== *
  * DWDP communication engine (replaces the pybind module dwdp_communication_ext,

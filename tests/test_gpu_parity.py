@@ -325,3 +325,29 @@ def test_moe_experts_indexed_bad_index_records_status(pkg):
     torch.cuda.synchronize()
     st = layer.read_status(T)
     assert st[0] == pkg._lib.DWDP_ERR_DEVICE_BOUNDS and st[3] >= 1
+
+
+@pytest.mark.parametrize("T", [1, 64, 300])
+def test_shared_expert_side_stream(pkg, orc, T):
+    """The shared expert launched alone (ungated partials, gate applied by the merge)
+    matches the oracle, and the layer gives the same result with and without running it
+    concurrently on the side stream."""
+    layer = _make_layer(pkg, 8, 512, 256, 2, 1024, torch.float8_e4m3fn, pkg._lib.SCALE_CHANNEL, seed=T)
+    x = torch.randn(T, 512, generator=torch.Generator().manual_seed(T)).bfloat16()
+    xd = x.to(DEV)
+    parts = pkg.ops.moe_shared_parts(T, 1024)
+    sh_out = torch.empty(parts, T, 512, dtype=torch.bfloat16, device=DEV)
+    wsb = torch.empty(pkg.ops.moe_shared_workspace_bytes(T, 512, 1024), dtype=torch.uint8, device=DEV)
+    pkg.ops.moe_shared_expert(layer._shared_group, xd, sh_out, wsb)
+    torch.cuda.synchronize()
+    ref = orc.swiglu_expert(x.float(), *(t.cpu() for t in layer.shared_expert.dequantized(0)))
+    assert orc.rel_frobenius(sh_out.float().sum(0).cpu(), ref) < FP8_TOL
+    layer.overlap_shared = True
+    y1 = layer(xd)
+    layer.overlap_shared = False
+    y2 = layer(xd)
+    torch.cuda.synchronize()
+    assert orc.rel_frobenius(y1.float().cpu(), y2.float().cpu()) < 5e-3
+    layer.overlap_shared = True
+    _check_layer(pkg, orc, layer, T, FP8_TOL, seed=T)
+    layer.overlap_shared = False
