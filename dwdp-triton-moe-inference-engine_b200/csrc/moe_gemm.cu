@@ -430,26 +430,30 @@ constexpr int BN8 = 64;                     // max tokens per tile
 constexpr int kW8TileBytes = BM * BK8;      // 128 x 128 weight tile
 constexpr int kB8TileBytes = 2 * BN8 * BK8; // hi/lo activation tile
 
-// NM = weight matrices per stage: 2 for gate+up or paired down row blocks, 1 for single down blocks
-template <int MODE, int NM>
+// NM = weight matrices per stage: 2 for gate+up or paired down row blocks, 1 for single down blocks.
+// BNT = tokens per tile (64 at decode sizes, 128 at prefill sizes: twice the MMA work per weight
+// byte). An accumulator buffer holds NM x 2 x BNT columns; two buffers when they fit TMEM's 512.
+template <int MODE, int NM, int BNT>
 struct Cfg8 {
   static constexpr int NMAT = NM;
-  static constexpr int S = NM == 2 ? 4 : 6;
+  static constexpr int B_TILE = 2 * BNT * BK8;                 // hi/lo activation tile
   static constexpr int W_STAGE_BYTES = NMAT * kW8TileBytes;
+  static constexpr int S = (192 * 1024) / (W_STAGE_BYTES + B_TILE);
   static constexpr int THREADS = 6 * 32;
-  static constexpr int ACC_STRIDE = NMAT * 2 * BN8;  // TMEM columns per accumulator buffer
-  static constexpr int TMEM_COLS = 2 * ACC_STRIDE <= 256 ? 256 : 512;
-  static constexpr int SMEM_BYTES = S * (W_STAGE_BYTES + kB8TileBytes) + 1024 + 256;
+  static constexpr int ACC_STRIDE = NMAT * 2 * BNT;            // TMEM columns per accumulator buffer
+  static constexpr int NBUF = 2 * ACC_STRIDE <= 512 ? 2 : 1;
+  static constexpr int TMEM_COLS = NBUF * ACC_STRIDE <= 256 ? 256 : 512;
+  static constexpr int SMEM_BYTES = S * (W_STAGE_BYTES + B_TILE) + 1024 + 256;
 };
 
-template <int MODE, int NM>
-__global__ void __launch_bounds__(Cfg8<MODE, NM>::THREADS, 1)
+template <int MODE, int NM, int BNT>
+__global__ void __launch_bounds__(Cfg8<MODE, NM, BNT>::THREADS, 1)
 moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
-  using C = Cfg8<MODE, NM>;
+  using C = Cfg8<MODE, NM, BNT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sB = smem;
-  uint8_t* sW = sB + C::S * kB8TileBytes;
+  uint8_t* sW = sB + C::S * C::B_TILE;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sW + C::S * C::W_STAGE_BYTES);
   uint64_t* ld_full = bars;
   uint64_t* ld_empty = ld_full + C::S;
@@ -509,7 +513,7 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
           for (int m = 0; m < nm; ++m)
             bulk_g2s(sW + s * C::W_STAGE_BYTES + m * kW8TileBytes,
                      wbase + (size_t)m * g.mstride + (size_t)kb * g.kstride, kW8TileBytes, &ld_full[s]);
-          tma_load_2d(sB + s * kB8TileBytes, &g.tmap_b, kb * BK8, 2 * wi.row0, &ld_full[s]);
+          tma_load_2d(sB + s * C::B_TILE, &g.tmap_b, kb * BK8, 2 * wi.row0, &ld_full[s]);
         }
       }
     }
@@ -522,8 +526,8 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
       for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++li) {
         const WorkItem wi = wn;
         if (item + (int)gridDim.x < p.cap) wn = p.items[item + gridDim.x];
-        const int a = li & 1;
-        if (!mbar_wait(&acc_empty[a], ((li >> 1) & 1) ^ 1, &s_abort, st, 22 + 8 * MODE)) break;
+        const int a = li % C::NBUF;
+        if (!mbar_wait(&acc_empty[a], ((li / C::NBUF) & 1) ^ 1, &s_abort, st, 22 + 8 * MODE)) break;
         tc_fence_after();
         const int n_tok = max(16, (wi.nrows + 15) & ~15);
         const uint32_t idesc = idesc_e4m3(BM, 2 * n_tok);
@@ -534,13 +538,13 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
           if (!mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 23 + 8 * MODE)) { ok = false; break; }
           tc_fence_after();
           // a K step of 32 e4m3 (32 bytes) is +2 in the encoded start address
-          const uint64_t b_desc0 = smem_desc_sw128(smem_u32(sB + s * kB8TileBytes));
+          const uint64_t b_desc0 = smem_desc_sw128(smem_u32(sB + s * C::B_TILE));
           const uint64_t a_desc0 = smem_desc_sw128(smem_u32(sW + s * C::W_STAGE_BYTES));
           const uint32_t acc_first = kb > wi.kb_begin ? 1u : 0u;
           for (int m = 0; m < min(wi.nmat, C::NMAT); ++m) {
 #pragma unroll
             for (int kk = 0; kk < BK8 / 32; ++kk) {
-              mma_e4m3_ss(d_base + m * 2 * BN8, a_desc0 + (uint64_t)(m * (kW8TileBytes >> 4) + 2 * kk),
+              mma_e4m3_ss(d_base + m * 2 * BNT, a_desc0 + (uint64_t)(m * (kW8TileBytes >> 4) + 2 * kk),
                           b_desc0 + (uint64_t)(2 * kk), idesc, kk > 0 ? 1u : acc_first);
             }
           }
@@ -560,7 +564,7 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
       const WorkItem wi = wn;
       if (item + (int)gridDim.x < p.cap) wn = p.items[item + gridDim.x];
       const GroupParams& g = p.g[wi.group];
-      const int a = li & 1;
+      const int a = li % C::NBUF;
       const int feat = wi.rb * BM + lrow;
       __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)wi.part * g.part_stride;
       // gate/up: s0, s1 scale the two matrices of one feature; down: two consecutive features
@@ -568,7 +572,7 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
       const int nmat = min(wi.nmat, C::NMAT);
       const float s1 = MODE == 0 ? wi.scales[g.R + feat] : (nmat > 1 ? wi.scales[feat + BM] : 1.0f);
       const float* xs = g.x_scale + wi.row0;
-      if (!mbar_wait(&acc_full[a], (li >> 1) & 1, &s_abort, st, 24 + 8 * MODE)) break;
+      if (!mbar_wait(&acc_full[a], (li / C::NBUF) & 1, &s_abort, st, 24 + 8 * MODE)) break;
       tc_fence_after();
       const uint32_t t_acc = tmem_base + a * C::ACC_STRIDE + ((uint32_t)(quad * 32) << 16);
       for (int c0 = 0; c0 < 2 * wi.nrows; c0 += 16) {
@@ -576,7 +580,7 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
         if constexpr (MODE == 0) {
           float gv[16], uv[16];
           tmem_ld16(t_acc + c0, gv);
-          tmem_ld16(t_acc + 2 * BN8 + c0, uv);
+          tmem_ld16(t_acc + 2 * BNT + c0, uv);
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
@@ -591,7 +595,7 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
         } else {
           for (int m = 0; m < nmat; ++m) {
             float yv[16];
-            tmem_ld16(t_acc + m * 2 * BN8 + c0, yv);
+            tmem_ld16(t_acc + m * 2 * BNT + c0, yv);
             tmem_ld_wait();
             const float sm = m == 0 ? s0 : s1;
 #pragma unroll
@@ -1077,10 +1081,10 @@ WsLayout ws_layout(int64_t T, int K, int E, int I, int H, int Is) {
 
 int g_num_sms = 0;
 
-template <int MODE, int NM>
+template <int MODE, int NM, int BNT>
 int launch_gemm_f8(const GemmParams& prm, int grid, cudaStream_t stream) {
-  using C = Cfg8<MODE, NM>;
-  auto kfn = moe_gemm_f8_kernel<MODE, NM>;
+  using C = Cfg8<MODE, NM, BNT>;
+  auto kfn = moe_gemm_f8_kernel<MODE, NM, BNT>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return DWDP_ERR_CUDA;
   return launch_chained(kfn, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, stream, 1u, prm) == cudaSuccess
@@ -1160,7 +1164,12 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   // e4m3 and bf16 weights on the bf16 kernels
   const bool native = fp8 && routed->scale_mode == DWDP_SCALE_CHANNEL;
   const int bk = native ? BK8 : BK;
-  const int bn = native ? BN8 : BN_MAX;
+  // e4m3 token tiles: 64 tokens. 128-token tiles (half the weight traffic per FLOP, one TMEM
+  // accumulator buffer for gate/up, 3-deep ring) measured slower at T = 1024 and 4096 on the
+  // Qwen shape; DWDP_WIDE_TILES=1 selects them for tuning.
+  bool wide = false;
+  if (const char* v = getenv("DWDP_WIDE_TILES")) wide = native && v[0] == '1';  // tuning override
+  const int bn = native ? (wide ? 128 : BN8) : BN_MAX;
   const int64_t N = shared_only ? 0 : T * K;  // routed rows
   const WsLayout L = ws_layout(T, K, E, I, H, Is);
   if (workspace == nullptr || workspace_bytes < L.total) return DWDP_ERR_CAPACITY;
@@ -1187,7 +1196,8 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   // the halved item count would leave SMs idle or unevenly loaded (pairs need ~4 waves of items).
   const int sms_now = dwdp_device_sm_count();
   const int64_t est_tiles = N / BN8 + std::min<int64_t>(E, N) + (has_shared ? (T + BN8 - 1) / BN8 * parts : 0);
-  const bool pair_dn = native && est_tiles * ((H / BM + 1) / 2) >= 4LL * std::max(1, sms_now);
+  bool pair_dn = native && est_tiles * ((H / BM + 1) / 2) >= 4LL * std::max(1, sms_now);
+  if (const char* v = getenv("DWDP_PAIR_DOWN")) pair_dn = native && v[0] == '1';  // tuning override
   const int dn_items_per_tile = pair_dn ? (H / BM + 1) / 2 : H / BM;
   pp.rb_gu_r = I / BM; pp.rb_dn_r = dn_items_per_tile;
   pp.rb_gu_s = has_shared ? Is / BM : 0; pp.rb_dn_s = has_shared ? dn_items_per_tile : 0;
@@ -1277,14 +1287,17 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   const int grid_dn = std::max(1, std::min(sms, L.cap_dn));
   int rc;
   if (native) {
-    rc = launch_gemm_f8<0, 2>(gu, grid_gu, stream);
+    rc = wide ? launch_gemm_f8<0, 2, 128>(gu, grid_gu, stream) : launch_gemm_f8<0, 2, 64>(gu, grid_gu, stream);
     if (rc == DWDP_OK) {
       rc = launch_chained(quant_kernel, dim3(quant_blocks(N + (has_shared ? T : 0))), dim3(kPlanThreads), 0,
                           stream, 1u, qh) == cudaSuccess
                ? DWDP_OK
                : DWDP_ERR_CUDA;
     }
-    if (rc == DWDP_OK) rc = pair_dn ? launch_gemm_f8<1, 2>(dn, grid_dn, stream) : launch_gemm_f8<1, 1>(dn, grid_dn, stream);
+    if (rc == DWDP_OK) {
+      if (wide) rc = pair_dn ? launch_gemm_f8<1, 2, 128>(dn, grid_dn, stream) : launch_gemm_f8<1, 1, 128>(dn, grid_dn, stream);
+      else rc = pair_dn ? launch_gemm_f8<1, 2, 64>(dn, grid_dn, stream) : launch_gemm_f8<1, 1, 64>(dn, grid_dn, stream);
+    }
   } else if (fp8) {
     rc = launch_gemm<0, true>(gu, grid_gu, stream);
     if (rc == DWDP_OK) rc = launch_gemm<1, true>(dn, grid_dn, stream);

@@ -351,3 +351,14 @@ def test_shared_expert_side_stream(pkg, orc, T):
     layer.overlap_shared = True
     _check_layer(pkg, orc, layer, T, FP8_TOL, seed=T)
     layer.overlap_shared = False
+
+
+@pytest.mark.parametrize("wide,pair", [("1", "0"), ("1", "1"), ("0", "1"), ("0", "0")])
+@pytest.mark.parametrize("T", [7, 1024])
+def test_moe_layer_tile_variants(pkg, orc, monkeypatch, wide, pair, T):
+    """Every e4m3 kernel variant (64- or 128-token tiles, single or paired down row
+    blocks, one or two TMEM accumulator buffers) against the oracle."""
+    monkeypatch.setenv("DWDP_WIDE_TILES", wide)
+    monkeypatch.setenv("DWDP_PAIR_DOWN", pair)
+    layer = _make_layer(pkg, 8, 512, 256, 2, 512, torch.float8_e4m3fn, pkg._lib.SCALE_CHANNEL, seed=11)
+    _check_layer(pkg, orc, layer, T, FP8_TOL)
