@@ -438,12 +438,14 @@ struct Cfg8 {
   static constexpr int NMAT = NM;
   static constexpr int B_TILE = 2 * BNT * BK8;                 // hi/lo activation tile
   static constexpr int W_STAGE_BYTES = NMAT * kW8TileBytes;
-  static constexpr int S = (192 * 1024) / (W_STAGE_BYTES + B_TILE);
+  static constexpr int OUT_COLS = MODE == 0 ? BM : NMAT * BM;  // output features per item
+  static constexpr int STAGING = BNT * OUT_COLS * 2;            // bf16 [tokens][features] epilogue tile
+  static constexpr int S = (224 * 1024 - STAGING) / (W_STAGE_BYTES + B_TILE);
   static constexpr int THREADS = 6 * 32;
   static constexpr int ACC_STRIDE = NMAT * 2 * BNT;            // TMEM columns per accumulator buffer
   static constexpr int NBUF = 2 * ACC_STRIDE <= 512 ? 2 : 1;
   static constexpr int TMEM_COLS = NBUF * ACC_STRIDE <= 256 ? 256 : 512;
-  static constexpr int SMEM_BYTES = S * (W_STAGE_BYTES + B_TILE) + 1024 + 256;
+  static constexpr int SMEM_BYTES = S * (W_STAGE_BYTES + B_TILE) + STAGING + 1024 + 256;
 };
 
 template <int MODE, int NM, int BNT>
@@ -454,7 +456,8 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sB = smem;
   uint8_t* sW = sB + C::S * C::B_TILE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + C::S * C::W_STAGE_BYTES);
+  __nv_bfloat16* sOut = reinterpret_cast<__nv_bfloat16*>(sW + C::S * C::W_STAGE_BYTES);  // [BNT][OUT_COLS]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sOut) + C::STAGING);
   uint64_t* ld_full = bars;
   uint64_t* ld_empty = ld_full + C::S;
   uint64_t* acc_full = ld_empty + C::S;
@@ -497,6 +500,7 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
+      PROF_DECL PROF_START
       uint32_t it = 0;
       WorkItem wn = p.items[blockIdx.x];  // fetched with n_items; the next one is prefetched
       for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
@@ -507,7 +511,7 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
         const uint32_t b_bytes = (uint32_t)g.box_rows * 2u * BK8;
         for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
           const int s = it % C::S;
-          if (!mbar_wait(&ld_empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 21 + 8 * MODE)) break;
+          if (!TW(0, mbar_wait(&ld_empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 21 + 8 * MODE))) break;
           const int nm = min(wi.nmat, C::NMAT);
           mbar_arrive_expect_tx(&ld_full[s], (uint32_t)(nm * kW8TileBytes) + b_bytes);
           for (int m = 0; m < nm; ++m)
@@ -516,10 +520,12 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
           tma_load_2d(sB + s * C::B_TILE, &g.tmap_b, kb * BK8, 2 * wi.row0, &ld_full[s]);
         }
       }
+      PROF_END(7) PROF_STORE(0)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
+      PROF_DECL PROF_START
       uint32_t it = 0;
       int li = 0;
       WorkItem wn = p.items[blockIdx.x];  // fetched with n_items; the next one is prefetched
@@ -527,7 +533,7 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
         const WorkItem wi = wn;
         if (item + (int)gridDim.x < p.cap) wn = p.items[item + gridDim.x];
         const int a = li % C::NBUF;
-        if (!mbar_wait(&acc_empty[a], ((li / C::NBUF) & 1) ^ 1, &s_abort, st, 22 + 8 * MODE)) break;
+        if (!TW(0, mbar_wait(&acc_empty[a], ((li / C::NBUF) & 1) ^ 1, &s_abort, st, 22 + 8 * MODE))) break;
         tc_fence_after();
         const int n_tok = max(16, (wi.nrows + 15) & ~15);
         const uint32_t idesc = idesc_e4m3(BM, 2 * n_tok);
@@ -535,12 +541,13 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
         bool ok = true;
         for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
           const int s = it % C::S;
-          if (!mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 23 + 8 * MODE)) { ok = false; break; }
+          if (!TW(1, mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 23 + 8 * MODE))) { ok = false; break; }
           tc_fence_after();
           // a K step of 32 e4m3 (32 bytes) is +2 in the encoded start address
           const uint64_t b_desc0 = smem_desc_sw128(smem_u32(sB + s * C::B_TILE));
           const uint64_t a_desc0 = smem_desc_sw128(smem_u32(sW + s * C::W_STAGE_BYTES));
           const uint32_t acc_first = kb > wi.kb_begin ? 1u : 0u;
+          PROF_T0
           for (int m = 0; m < min(wi.nmat, C::NMAT); ++m) {
 #pragma unroll
             for (int kk = 0; kk < BK8 / 32; ++kk) {
@@ -548,14 +555,17 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
                           b_desc0 + (uint64_t)(2 * kk), idesc, kk > 0 ? 1u : acc_first);
             }
           }
+          PROF_ADD(3)
           mma_commit(&ld_empty[s]);
         }
         if (!ok) break;
         mma_commit(&acc_full[a]);
       }
+      PROF_END(7) PROF_STORE(4)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    PROF_DECL PROF_START
     const int quad = warp & 3;
     const int lrow = quad * 32 + lane;
     int li = 0;
@@ -572,40 +582,41 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
       const int nmat = min(wi.nmat, C::NMAT);
       const float s1 = MODE == 0 ? wi.scales[g.R + feat] : (nmat > 1 ? wi.scales[feat + BM] : 1.0f);
       const float* xs = g.x_scale + wi.row0;
-      if (!mbar_wait(&acc_full[a], (li / C::NBUF) & 1, &s_abort, st, 24 + 8 * MODE)) break;
+      if (!TW(0, mbar_wait(&acc_full[a], (li / C::NBUF) & 1, &s_abort, st, 24 + 8 * MODE))) break;
       tc_fence_after();
       const uint32_t t_acc = tmem_base + a * C::ACC_STRIDE + ((uint32_t)(quad * 32) << 16);
-      for (int c0 = 0; c0 < 2 * wi.nrows; c0 += 16) {
+      // 1. drain TMEM into the bf16 staging tile (16 tokens = 32 columns per load), then
+      //    release the accumulator at once so the next item's MMAs can start
+      for (int c0 = 0; c0 < 2 * wi.nrows; c0 += 32) {
         const int t0 = c0 >> 1;
         if constexpr (MODE == 0) {
-          float gv[16], uv[16];
-          tmem_ld16(t_acc + c0, gv);
-          tmem_ld16(t_acc + 2 * BNT + c0, uv);
+          float gv[32], uv[32];
+          tmem_ld32(t_acc + c0, gv);
+          tmem_ld32(t_acc + 2 * BNT + c0, uv);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
+          for (int j = 0; j < 16; ++j) {
             const int t = t0 + j;
             if (t < wi.nrows) {
               const float sx = xs[t];
               const float gg = (gv[2 * j] + gv[2 * j + 1] * (1.0f / kLoPlaneGain)) * (s0 * sx);
               const float uu = (uv[2 * j] + uv[2 * j + 1] * (1.0f / kLoPlaneGain)) * (s1 * sx);
-              out[(size_t)(wi.row0 + t) * g.R + feat] = __float2bfloat16_rn(silu(gg) * uu);
+              sOut[t * C::OUT_COLS + lrow] = __float2bfloat16_rn(silu_fast(gg) * uu);
             }
           }
         } else {
           for (int m = 0; m < nmat; ++m) {
-            float yv[16];
-            tmem_ld16(t_acc + m * 2 * BNT + c0, yv);
+            float yv[32];
+            tmem_ld32(t_acc + m * 2 * BNT + c0, yv);
             tmem_ld_wait();
             const float sm = m == 0 ? s0 : s1;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < 16; ++j) {
               const int t = t0 + j;
               if (t < wi.nrows) {
-                const int row = wi.row0 + t;
-                const float rs = g.row_scale != nullptr ? g.row_scale[row] : 1.0f;
+                const float rs = g.row_scale != nullptr ? g.row_scale[wi.row0 + t] : 1.0f;
                 const float y = (yv[2 * j] + yv[2 * j + 1] * (1.0f / kLoPlaneGain)) * (sm * xs[t]);
-                out[(size_t)row * g.R + feat + m * BM] = __float2bfloat16_rn(y * rs);
+                sOut[t * C::OUT_COLS + m * BM + lrow] = __float2bfloat16_rn(y * rs);
               }
             }
           }
@@ -613,7 +624,21 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[a]);
+      // 2. the tile's rows leave as 16-byte stores (all four epilogue warps)
+      named_bar_sync(3, 128);
+      {
+        const int cols = MODE == 0 ? BM : nmat * BM;  // features of this item
+        const int cpr = cols / 8;                      // 16-byte chunks per token row
+        const int ep = (warp - 2) * 32 + lane;
+        for (int q = ep; q < wi.nrows * cpr; q += 128) {
+          const int t = q / cpr, ch = q - t * cpr;
+          const uint4 v = *reinterpret_cast<const uint4*>(sOut + t * C::OUT_COLS + ch * 8);
+          *reinterpret_cast<uint4*>(out + (size_t)(wi.row0 + t) * g.R + wi.rb * BM + ch * 8) = v;
+        }
+      }
+      named_bar_sync(3, 128);  // the staging tile is rewritten by the next item
     }
+    PROF_END(7) if (lane == 0 && quad == 0) PROF_STORE(8)
   }
 
   tc_fence_before();
