@@ -428,7 +428,6 @@ constexpr float kLoPlaneGain = 16.0f;
 constexpr int BK8 = 128;                    // e4m3 inputs per pipeline stage
 constexpr int BN8 = 64;                     // max tokens per tile
 constexpr int kW8TileBytes = BM * BK8;      // 128 x 128 weight tile
-constexpr int kB8TileBytes = 2 * BN8 * BK8; // hi/lo activation tile
 
 // NM = weight matrices per stage: 2 for gate+up or paired down row blocks, 1 for single down blocks.
 // BNT = tokens per tile (64 at decode sizes, 128 at prefill sizes: twice the MMA work per weight
@@ -441,7 +440,9 @@ struct Cfg8 {
   static constexpr int OUT_COLS = MODE == 0 ? BM : NMAT * BM;  // output features per item
   static constexpr int STAGING = BNT * OUT_COLS * 2;            // bf16 [tokens][features] epilogue tile
   static constexpr int S = (224 * 1024 - STAGING) / (W_STAGE_BYTES + B_TILE);
-  static constexpr int THREADS = 6 * 32;
+  static constexpr int EPI_WARPS = 8;  // two warps per TMEM lane quadrant, alternate column chunks
+  static constexpr int EPI_THREADS = EPI_WARPS * 32;
+  static constexpr int THREADS = (2 + EPI_WARPS) * 32;
   static constexpr int ACC_STRIDE = NMAT * 2 * BNT;            // TMEM columns per accumulator buffer
   static constexpr int NBUF = 2 * ACC_STRIDE <= 512 ? 2 : 1;
   static constexpr int TMEM_COLS = NBUF * ACC_STRIDE <= 256 ? 256 : 512;
@@ -478,7 +479,7 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 128);
+      mbar_init(&acc_empty[i], C::EPI_THREADS);
     }
     fence_barrier_init();
   }
@@ -568,6 +569,8 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
     PROF_DECL PROF_START
     const int quad = warp & 3;
     const int lrow = quad * 32 + lane;
+    const int eg = (warp - 2) >> 2;        // epilogue group (0, 1)
+    const int ep = (warp - 2) * 32 + lane;  // 0 .. EPI_THREADS - 1
     int li = 0;
     WorkItem wn = p.items[blockIdx.x];  // fetched with n_items; the next one is prefetched
     for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++li) {
@@ -585,9 +588,12 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
       if (!TW(0, mbar_wait(&acc_full[a], (li / C::NBUF) & 1, &s_abort, st, 24 + 8 * MODE))) break;
       tc_fence_after();
       const uint32_t t_acc = tmem_base + a * C::ACC_STRIDE + ((uint32_t)(quad * 32) << 16);
-      // 1. drain TMEM into the bf16 staging tile (16 tokens = 32 columns per load), then
-      //    release the accumulator at once so the next item's MMAs can start
-      for (int c0 = 0; c0 < 2 * wi.nrows; c0 += 32) {
+      // Small tiles (decode) store straight from registers; larger ones go through the bf16
+      // staging tile so that the accumulator is released as soon as TMEM is drained and the
+      // rows leave as 16-byte stores. The two warps of a lane quadrant take alternate
+      // 32-column (16-token) chunks.
+      const bool direct = wi.nrows <= 16;
+      for (int c0 = eg * 32; c0 < 2 * wi.nrows; c0 += 64) {
         const int t0 = c0 >> 1;
         if constexpr (MODE == 0) {
           float gv[32], uv[32];
@@ -601,22 +607,30 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
               const float sx = xs[t];
               const float gg = (gv[2 * j] + gv[2 * j + 1] * (1.0f / kLoPlaneGain)) * (s0 * sx);
               const float uu = (uv[2 * j] + uv[2 * j + 1] * (1.0f / kLoPlaneGain)) * (s1 * sx);
-              sOut[t * C::OUT_COLS + lrow] = __float2bfloat16_rn(silu_fast(gg) * uu);
+              const __nv_bfloat16 h = __float2bfloat16_rn(silu_fast(gg) * uu);
+              if (direct) out[(size_t)(wi.row0 + t) * g.R + feat] = h;
+              else sOut[t * C::OUT_COLS + lrow] = h;
             }
           }
         } else {
-          for (int m = 0; m < nmat; ++m) {
-            float yv[32];
-            tmem_ld32(t_acc + m * 2 * BNT + c0, yv);
-            tmem_ld_wait();
-            const float sm = m == 0 ? s0 : s1;
+          float yv[C::NMAT][32];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int t = t0 + j;
-              if (t < wi.nrows) {
-                const float rs = g.row_scale != nullptr ? g.row_scale[wi.row0 + t] : 1.0f;
-                const float y = (yv[2 * j] + yv[2 * j + 1] * (1.0f / kLoPlaneGain)) * (sm * xs[t]);
-                sOut[t * C::OUT_COLS + m * BM + lrow] = __float2bfloat16_rn(y * rs);
+          for (int m = 0; m < C::NMAT; ++m)
+            if (m < nmat) tmem_ld32(t_acc + m * 2 * BNT + c0, yv[m]);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int t = t0 + j;
+            if (t < wi.nrows) {
+              const float f = xs[t] * (g.row_scale != nullptr ? g.row_scale[wi.row0 + t] : 1.0f);
+#pragma unroll
+              for (int m = 0; m < C::NMAT; ++m) {
+                if (m < nmat) {
+                  const float y = (yv[m][2 * j] + yv[m][2 * j + 1] * (1.0f / kLoPlaneGain)) * ((m == 0 ? s0 : s1) * f);
+                  const __nv_bfloat16 yb = __float2bfloat16_rn(y);
+                  if (direct) out[(size_t)(wi.row0 + t) * g.R + feat + m * BM] = yb;
+                  else sOut[t * C::OUT_COLS + m * BM + lrow] = yb;
+                }
               }
             }
           }
@@ -624,19 +638,17 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[a]);
-      // 2. the tile's rows leave as 16-byte stores (all four epilogue warps)
-      named_bar_sync(3, 128);
-      {
+      if (!direct) {
+        named_bar_sync(3, C::EPI_THREADS);
         const int cols = MODE == 0 ? BM : nmat * BM;  // features of this item
         const int cpr = cols / 8;                      // 16-byte chunks per token row
-        const int ep = (warp - 2) * 32 + lane;
-        for (int q = ep; q < wi.nrows * cpr; q += 128) {
+        for (int q = ep; q < wi.nrows * cpr; q += C::EPI_THREADS) {
           const int t = q / cpr, ch = q - t * cpr;
           const uint4 v = *reinterpret_cast<const uint4*>(sOut + t * C::OUT_COLS + ch * 8);
           *reinterpret_cast<uint4*>(out + (size_t)(wi.row0 + t) * g.R + wi.rb * BM + ch * 8) = v;
         }
+        named_bar_sync(3, C::EPI_THREADS);  // the staging tile is rewritten by the next item
       }
-      named_bar_sync(3, 128);  // the staging tile is rewritten by the next item
     }
     PROF_END(7) if (lane == 0 && quad == 0) PROF_STORE(8)
   }
