@@ -21,6 +21,7 @@
 //    and ignored the allocator's sub-allocation offset).
 //  * Transfer scheduling (priority queue, coalescing, two retries) and the path
 //    policy are plain host code with their own C ABI, testable without a GPU.
+#include <cstdlib>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -175,7 +176,9 @@ extern "C" int dwdp_engine_create(int device_id, size_t slot_bytes, int num_slot
   int lo = 0, hi = 0;
   cudaError_t e = cudaDeviceGetStreamPriorityRange(&lo, &hi);
   if (e != cudaSuccess) return set_error("cudaDeviceGetStreamPriorityRange", e);
-  for (int i = 0; i < kCopyStreams; ++i) {
+  int n_streams = kCopyStreams;
+  if (const char* v = std::getenv("DWDP_COPY_STREAMS")) n_streams = std::max(1, std::min(8, std::atoi(v)));  // tuning
+  for (int i = 0; i < n_streams; ++i) {
     cudaStream_t cs;
     e = cudaStreamCreateWithPriority(&cs, cudaStreamNonBlocking, hi);  // greatest priority
     if (e != cudaSuccess) return set_error("cudaStreamCreateWithPriority", e);
