@@ -372,6 +372,80 @@ def transfer_comparison(store, world: int, steps: int, device) -> dict:
 
 
 # ----------------------------------------------------------------------------- main
+# ----------------------------------------------------------------------------- full decode step (row f1)
+def decode_step_bench(pkg, device, batches: list[int], steps: int, warmup: int, flush) -> dict:
+    """24-layer Qwen1.5-MoE-shaped decode step over a paged KV cache at context 2048
+    (every sequence decodes position 2047 against 2047 cached positions), one CUDA graph
+    per batch size. Per batch size: step time, tokens/s, MoE share (the graph of the 24
+    MoE layers alone timed the same way), the attention kernel's HBM roofline, and an
+    end-to-end step through pinned host buffers (inputs H2D, next tokens D2H)."""
+    dec = pkg.decode
+    cfg = dec.QwenMoEConfig()
+    model = dec.QwenMoEDecodeModel(cfg, device, seed=1235, max_batch=max(batches))
+    model.fill_context(seed=11)
+    peaks = _peaks()
+    points = []
+    for B in batches:
+        table = model.admit(B)
+        pos = torch.full((B,), cfg.max_context - 1, dtype=torch.int32)
+        tokens = torch.randint(0, cfg.vocab_size, (B,), generator=torch.Generator().manual_seed(B))
+        model.step(tokens, pos, table, graph=True)
+        bufs = model.buffers(B)
+        torch.cuda.synchronize()
+        step_ms = time_device(bufs.graph.replay, steps, warmup, flush)
+        moe_ms = time_device(bufs.moe_graph.replay, steps, warmup, flush)
+        # attention kernel alone (layer 0), HBM roofline
+        k0, v0 = model.cache.k(0), model.cache.v(0)
+
+        def attn():
+            pkg.ops.paged_attention(bufs.q, k0, v0, bufs.block_table, bufs.seq_lens, cfg.max_context,
+                                    splits=bufs.splits, workspace=bufs.attn_ws, out=bufs.attn)
+
+        attn_ms = time_device(attn, steps, warmup, flush)
+        kv_bytes = B * cfg.max_context * 2 * cfg.num_heads * cfg.head_dim * 2
+        attn_gbs = kv_bytes / (statistics.median(attn_ms) / 1e3) / 1e9
+        # end to end: pinned host inputs copied in, next tokens copied out, every step
+        h_tok = tokens.pin_memory()
+        h_pos = pos.pin_memory()
+        h_tab = table.pin_memory()
+        h_out = torch.empty(B, dtype=torch.int64).pin_memory()
+
+        def e2e():
+            bufs.tokens.copy_(h_tok, non_blocking=True)
+            bufs.positions.copy_(h_pos, non_blocking=True)
+            bufs.seq_lens.copy_(h_pos, non_blocking=True)
+            bufs.seq_lens.add_(1)
+            bufs.block_table.copy_(h_tab, non_blocking=True)
+            bufs.graph.replay()
+            h_out.copy_(bufs.next_tokens, non_blocking=True)
+
+        for _ in range(warmup):
+            e2e()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            e2e()
+            torch.cuda.current_stream().synchronize()
+        e2e_s = (time.perf_counter() - t0) / steps
+        st = model.read_status(B)
+        ms = statistics.median(step_ms)
+        points.append({
+            "batch": B, "ms_per_step": ms, "tokens_per_s": B / (ms / 1e3),
+            "moe_ms": statistics.median(moe_ms), "moe_share": statistics.median(moe_ms) / ms,
+            "attention": {"ms_per_layer": statistics.median(attn_ms), "kv_bytes_per_layer": kv_bytes,
+                          "achieved_gbs": attn_gbs, "frac_of_measured_hbm": attn_gbs / peaks["hbm_gbs"]},
+            "e2e": {"tokens_per_s": B / e2e_s, "ms_per_step": e2e_s * 1e3,
+                    "h2d_bytes_per_step": int(h_tok.nbytes + 2 * h_pos.nbytes + h_tab.nbytes),
+                    "d2h_bytes_per_step": int(h_out.nbytes)},
+            "our_kernel_launches": model.kernel_launches(B), "status": st[0],
+        })
+        model.release(table)
+    return {"workload": "decode_step", "model": "Qwen1.5-MoE-A2.7B (shape, random init, 24 layers, vocab 151936)",
+            "context": cfg.max_context, "block_size": cfg.block_size, "points": points,
+            "l2": "flushed (256 MB write) before every timed step", "hbm_peak_gbs": peaks["hbm_gbs"],
+            "peak_source": peaks["source"]}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -382,6 +456,8 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=256)
+    ap.add_argument("--workload", default="moe_layers", choices=["moe_layers", "decode_step"])
+    ap.add_argument("--batch", default="1,8,64", help="decode_step batch sizes")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -427,6 +503,12 @@ def main() -> None:
         return
 
     flush = L2Flusher(device)
+    if args.workload == "decode_step":
+        res = decode_step_bench(pkg, device, [int(b) for b in args.batch.split(",")], args.steps, args.warmup, flush)
+        if rank == 0:
+            print(json.dumps({"metric": "decode tokens/s (full 24-layer step)", "unit": "tokens/s",
+                              "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, **res}), flush=True)
+        return
     peaks = _peaks()
     stack = LayerStack(pkg, device, L, T, rank, world)
     if world > 1:

@@ -36,6 +36,13 @@ extern "C" size_t dwdp_moe_shared_workspace_bytes_impl(int64_t, int, int);
 extern "C" int dwdp_merge_launch(const void*, const int64_t*, const void*, int, const float*, int64_t, int, int,
                                  void*, int, int*, cudaStream_t);
 
+extern "C" int dwdp_add_rmsnorm_launch(void*, const void*, const void*, int64_t, int, float, void*, cudaStream_t);
+extern "C" int dwdp_rope_append_launch(const void*, const void*, const int32_t*, const int32_t*, int, int, int, int,
+                                       int, float, void*, void*, void*, int*, cudaStream_t);
+extern "C" size_t dwdp_paged_attention_workspace_bytes_impl(int, int, int);
+extern "C" int dwdp_paged_attention_launch(const void*, const void*, const void*, const int32_t*, const int32_t*, int,
+                                           int, int, int, int, int, int, float, void*, void*, cudaStream_t);
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -317,4 +324,55 @@ extern "C" int dwdp_moe_shared_expert(const dwdp_expert_group* shared, const voi
                                        nullptr, nullptr, nullptr, shared_out, workspace, workspace_bytes, status, 1,
                                        as_stream(stream)),
                "moe_shared_expert");
+}
+
+// --------------------------------------------------------------------------- decode-step attention pieces
+extern "C" int dwdp_add_rmsnorm(void* residual, const void* delta, const void* weight, int64_t rows,
+                                int hidden_size, float eps, void* out, void* stream) {
+  g_last_error.clear();
+  if (rows < 0 || hidden_size <= 0 || hidden_size % 8)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "add_rmsnorm: hidden_size must be a positive multiple of 8");
+  if (rows > 0 && (residual == nullptr || weight == nullptr || out == nullptr))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "add_rmsnorm: null pointer");
+  return check(dwdp_add_rmsnorm_launch(residual, delta, weight, rows, hidden_size, eps, out, as_stream(stream)),
+               "add_rmsnorm");
+}
+
+extern "C" int dwdp_rope_append_kv(const void* qkv, const void* qkv_bias, const int32_t* positions,
+                                   const int32_t* block_table, int batch, int max_blocks, int num_heads,
+                                   int head_dim, int block_size, float rope_theta, void* q_out, void* k_cache,
+                                   void* v_cache, int* status, void* stream) {
+  g_last_error.clear();
+  if (batch < 0 || num_heads <= 0 || head_dim <= 0 || head_dim % 2 || head_dim > 1024 || block_size <= 0 ||
+      max_blocks <= 0)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "rope_append_kv: bad sizes");
+  if (batch > 0 && (qkv == nullptr || positions == nullptr || block_table == nullptr || q_out == nullptr ||
+                    k_cache == nullptr || v_cache == nullptr))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "rope_append_kv: null pointer");
+  return check(dwdp_rope_append_launch(qkv, qkv_bias, positions, block_table, batch, max_blocks, num_heads, head_dim,
+                                       block_size, rope_theta, q_out, k_cache, v_cache, status, as_stream(stream)),
+               "rope_append_kv");
+}
+
+extern "C" size_t dwdp_paged_attention_workspace_bytes(int batch, int num_heads, int splits) {
+  if (batch <= 0 || num_heads <= 0 || splits <= 0) return 0;
+  return dwdp_paged_attention_workspace_bytes_impl(batch, num_heads, splits);
+}
+
+extern "C" int dwdp_paged_attention(const void* q, const void* k_cache, const void* v_cache,
+                                    const int32_t* block_table, const int32_t* seq_lens, int batch, int max_blocks,
+                                    int num_heads, int head_dim, int block_size, int max_len, int splits,
+                                    float scale, void* workspace, void* out, void* stream) {
+  g_last_error.clear();
+  if (batch < 0 || num_heads <= 0 || block_size <= 0 || max_blocks <= 0 || splits <= 0 || max_len <= 0 ||
+      max_len > max_blocks * block_size)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "paged_attention: bad sizes");
+  if (head_dim != 128) return fail(DWDP_ERR_UNSUPPORTED, "paged_attention: head_dim must be 128");
+  if (batch > 0 && (q == nullptr || k_cache == nullptr || v_cache == nullptr || block_table == nullptr ||
+                    seq_lens == nullptr || workspace == nullptr || out == nullptr))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "paged_attention: null pointer");
+  return check(dwdp_paged_attention_launch(q, k_cache, v_cache, block_table, seq_lens, batch, max_blocks, num_heads,
+                                           head_dim, block_size, max_len, splits, scale, workspace, out,
+                                           as_stream(stream)),
+               "paged_attention");
 }

@@ -391,3 +391,78 @@ def merge(
         )
     _lib.check(rc, "merge")
     return out
+
+
+# --------------------------------------------------------------------------- decode-step attention pieces
+def add_rmsnorm(residual: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tensor, eps: float,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """residual += delta (in place, when delta is given); returns rmsnorm(residual) * weight
+    (Qwen2MoeRMSNorm, fp32 arithmetic, bf16 rows)."""
+    _require_cuda(residual, delta, weight)
+    if residual.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise ValueError("add_rmsnorm expects bf16 residual and weight")
+    if not residual.is_contiguous() or (delta is not None and (not delta.is_contiguous()
+                                                              or delta.shape != residual.shape)):
+        raise ValueError("add_rmsnorm expects contiguous residual/delta of one shape")
+    H = residual.shape[-1]
+    if out is None:
+        out = torch.empty_like(residual)
+    rc = _lib.load().dwdp_add_rmsnorm(residual.data_ptr(), _ptr(delta), weight.data_ptr(), residual.numel() // H, H,
+                                      float(eps), out.data_ptr(), _stream())
+    _lib.check(rc, "add_rmsnorm")
+    return out
+
+
+def rope_append_kv(qkv: torch.Tensor, qkv_bias: torch.Tensor | None, positions: torch.Tensor,
+                   block_table: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, rope_theta: float,
+                   q_out: torch.Tensor | None = None, status: torch.Tensor | None = None) -> torch.Tensor:
+    """qkv [B, 3*NH*D] (+bias) -> rotated q [B, NH, D]; rotated k and v stored at
+    positions[b] of the paged caches [num_blocks, block_size, NH, D]."""
+    _require_cuda(qkv, qkv_bias, positions, block_table, k_cache, v_cache)
+    if positions.dtype != torch.int32 or block_table.dtype != torch.int32:
+        raise ValueError("positions and block_table must be int32")
+    nb, bs, NH, D = k_cache.shape
+    B = qkv.shape[0]
+    if qkv.shape[-1] != 3 * NH * D or v_cache.shape != k_cache.shape:
+        raise ValueError("qkv width must be 3 * num_heads * head_dim of the cache")
+    if q_out is None:
+        q_out = torch.empty(B, NH, D, dtype=torch.bfloat16, device=qkv.device)
+    rc = _lib.load().dwdp_rope_append_kv(qkv.data_ptr(), _ptr(qkv_bias), positions.data_ptr(), block_table.data_ptr(),
+                                         B, block_table.shape[-1], NH, D, bs, float(rope_theta), q_out.data_ptr(),
+                                         k_cache.data_ptr(), v_cache.data_ptr(), _ptr(status), _stream())
+    _lib.check(rc, "rope_append_kv")
+    return q_out
+
+
+def paged_attention_splits(batch: int, num_heads: int, max_len: int, sm_count: int = 148) -> int:
+    """Context chunks per (sequence, head): enough CTAs for ~4 per SM, chunks of >= 64 positions."""
+    want = max(1, -(-4 * sm_count // max(1, batch * num_heads)))
+    return max(1, min(want, -(-max_len // 64)))
+
+
+def paged_attention_workspace(batch: int, num_heads: int, splits: int, device) -> torch.Tensor:
+    n = _lib.load().dwdp_paged_attention_workspace_bytes(batch, num_heads, splits)
+    return torch.empty(n, dtype=torch.uint8, device=device)
+
+
+def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
+                    seq_lens: torch.Tensor, max_len: int, *, splits: int | None = None, scale: float | None = None,
+                    workspace: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """One-query paged attention: q [B, NH, D] over positions [0, seq_lens[b]) of each
+    sequence's pages -> [B, NH, D] bf16. ``max_len`` bounds every seq_len (fixed per graph)."""
+    _require_cuda(q, k_cache, v_cache, block_table, seq_lens)
+    if seq_lens.dtype != torch.int32 or block_table.dtype != torch.int32:
+        raise ValueError("seq_lens and block_table must be int32")
+    B, NH, D = q.shape
+    bs = k_cache.shape[1]
+    splits = splits or paged_attention_splits(B, NH, max_len)
+    if workspace is None:
+        workspace = paged_attention_workspace(B, NH, splits, q.device)
+    if out is None:
+        out = torch.empty(B, NH, D, dtype=torch.bfloat16, device=q.device)
+    rc = _lib.load().dwdp_paged_attention(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(),
+                                          seq_lens.data_ptr(), B, block_table.shape[-1], NH, D, bs, int(max_len),
+                                          splits, float(scale if scale is not None else D ** -0.5),
+                                          workspace.data_ptr(), out.data_ptr(), _stream())
+    _lib.check(rc, "paged_attention")
+    return out

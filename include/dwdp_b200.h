@@ -242,6 +242,37 @@ int dwdp_merge_gated(const void* weighted, const int64_t* inv, const void* share
                      int out_dtype, void* stream);
 
 /* ======================================================================== *
+ * Decode-step attention pieces (the model around the MoE layers for a full
+ * Qwen1.5-MoE decode step; DWDP/adapters/qwen15_moe.py:526-543 captures the HF
+ * decoder layers around the DWDP blocks). bf16 tensors, fp32 arithmetic.
+ * The paged KV cache follows DWDP/runtime/paged_attention.py:20-76: per layer a
+ * K and a V array [num_blocks, block_size, num_heads, head_dim]; sequence b's
+ * position p lives in block block_table[b * max_blocks + p / block_size] (int32).
+ * ======================================================================== */
+/* residual[r] += delta[r] (skipped when delta is NULL); out[r] = rmsnorm(residual[r]) * weight
+ * (Qwen2RMSNorm: x * rsqrt(mean(x^2) + eps), fp32). hidden_size % 8 == 0. */
+int dwdp_add_rmsnorm(void* residual, const void* delta, const void* weight, int64_t rows, int hidden_size,
+                     float eps, void* out, void* stream);
+/* qkv [batch, 3, num_heads, head_dim] (+ qkv_bias [3, num_heads, head_dim] when given):
+ * q_out [batch, num_heads, head_dim] gets q with the rotary embedding at positions[b]
+ * (NeoX rotate-half, inv_freq_d = rope_theta^(-2d/head_dim)); the rotated k and v are
+ * written into the caches at positions[b]. A negative block id: DWDP_ERR_DEVICE_BOUNDS
+ * in *status, the token skipped. */
+int dwdp_rope_append_kv(const void* qkv, const void* qkv_bias, const int32_t* positions,
+                        const int32_t* block_table, int batch, int max_blocks, int num_heads, int head_dim,
+                        int block_size, float rope_theta, void* q_out, void* k_cache, void* v_cache, int* status,
+                        void* stream);
+size_t dwdp_paged_attention_workspace_bytes(int batch, int num_heads, int splits);
+/* out[b, h] = softmax(scale * q[b, h] . K[b, :seq_lens[b], h]) V[b, :seq_lens[b], h] for one
+ * query per sequence. The context is split into `splits` chunks of ceil(max_len / splits)
+ * positions per (sequence, head), combined with the log-sum-exp rescaling. head_dim 128;
+ * max_len >= every seq_lens[b] and <= max_blocks * block_size. */
+int dwdp_paged_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
+                         const int32_t* seq_lens, int batch, int max_blocks, int num_heads, int head_dim,
+                         int block_size, int max_len, int splits, float scale, void* workspace, void* out,
+                         void* stream);
+
+/* ======================================================================== *
  * DWDP communication engine (replaces the pybind module dwdp_communication_ext,
  * DWDP/communication/bindings.cpp:32-111): expert slabs sharded across the GPUs
  * of one box, remote slabs opened through CUDA IPC (or a peer pointer) and
