@@ -41,7 +41,8 @@ extern "C" int dwdp_rope_append_launch(const void*, const void*, const int32_t*,
                                        int, float, void*, void*, void*, int*, cudaStream_t);
 extern "C" size_t dwdp_paged_attention_workspace_bytes_impl(int, int, int);
 extern "C" int dwdp_paged_attention_launch(const void*, const void*, const void*, const int32_t*, const int32_t*, int,
-                                           int, int, int, int, int, int, float, void*, void*, cudaStream_t);
+                                           int, int, int, int, int, int, float, void*, void*, int*,
+                                           cudaStream_t);
 
 namespace {
 
@@ -362,7 +363,7 @@ extern "C" size_t dwdp_paged_attention_workspace_bytes(int batch, int num_heads,
 extern "C" int dwdp_paged_attention(const void* q, const void* k_cache, const void* v_cache,
                                     const int32_t* block_table, const int32_t* seq_lens, int batch, int max_blocks,
                                     int num_heads, int head_dim, int block_size, int max_len, int splits,
-                                    float scale, void* workspace, void* out, void* stream) {
+                                    float scale, void* workspace, void* out, int* status, void* stream) {
   g_last_error.clear();
   if (batch < 0 || num_heads <= 0 || block_size <= 0 || max_blocks <= 0 || splits <= 0 || max_len <= 0 ||
       max_len > max_blocks * block_size)
@@ -373,6 +374,6 @@ extern "C" int dwdp_paged_attention(const void* q, const void* k_cache, const vo
     return fail(DWDP_ERR_INVALID_ARGUMENT, "paged_attention: null pointer");
   return check(dwdp_paged_attention_launch(q, k_cache, v_cache, block_table, seq_lens, batch, max_blocks, num_heads,
                                            head_dim, block_size, max_len, splits, scale, workspace, out,
-                                           as_stream(stream)),
+                                           status, as_stream(stream)),
                "paged_attention");
 }

@@ -203,7 +203,7 @@ class QwenMoEDecodeModel:
             return b
         cfg, dev = self.cfg, self.device
         H, NH, D = cfg.hidden_size, cfg.num_heads, cfg.head_dim
-        splits = ops.paged_attention_splits(B, NH, cfg.max_context)
+        splits = ops.paged_attention_splits(B, NH, cfg.max_context, cfg.block_size)
         bf = dict(dtype=torch.bfloat16, device=dev)
         b = _StepBuffers(
             B=B, tokens=torch.zeros(B, dtype=torch.int64, device=dev),
@@ -225,7 +225,7 @@ class QwenMoEDecodeModel:
         ops.rope_append_kv(b.qkv, w.bqkv, b.positions, b.block_table, self.cache.k(l), self.cache.v(l),
                            cfg.rope_theta, q_out=b.q, status=b.status)
         ops.paged_attention(b.q, self.cache.k(l), self.cache.v(l), b.block_table, b.seq_lens, cfg.max_context,
-                            splits=b.splits, workspace=b.attn_ws, out=b.attn)
+                            splits=b.splits, workspace=b.attn_ws, out=b.attn, status=b.status)
         torch.matmul(b.attn.view(b.B, -1), w.wo.t(), out=b.delta)
 
     def _step(self, b: _StepBuffers) -> None:

@@ -434,8 +434,23 @@ def rope_append_kv(qkv: torch.Tensor, qkv_bias: torch.Tensor | None, positions: 
     return q_out
 
 
-def paged_attention_splits(batch: int, num_heads: int, max_len: int, sm_count: int = 148) -> int:
-    """Context chunks per (sequence, head): enough CTAs for ~4 per SM, chunks of >= 64 positions."""
+def paged_attention_splits(batch: int, num_heads: int, max_len: int, block_size: int = 16,
+                           sm_count: int = 148) -> int:
+    """Context chunks per sequence for ``paged_attention``. On the bulk-copy path (8, 16 or 32
+    heads, block_size % 4 == 0) a CTA covers one chunk of one sequence for all heads and
+    2 (16 heads), 4 (8) or 1 (32) CTAs fit on an SM: pick the split count, up to chunks of
+    16 positions, whose CTA count fills whole waves best (fewer splits on near ties). The
+    fallback path (one CTA per (sequence, head, chunk)) asks for ~4 CTAs per SM."""
+    if num_heads in (8, 16, 32) and block_size % 4 == 0:
+        slots = sm_count * {8: 4, 16: 2, 32: 1}[num_heads]
+        best, best_eff = 1, -1.0
+        for s in range(1, max(1, max_len // 16) + 1):
+            chunk = -(-(-(-max_len // s)) // 4) * 4
+            ctas = batch * -(-max_len // chunk)
+            eff = ctas / (-(-ctas // slots) * slots)
+            if eff > best_eff + 0.02:
+                best, best_eff = s, eff
+        return best
     want = max(1, -(-4 * sm_count // max(1, batch * num_heads)))
     return max(1, min(want, -(-max_len // 64)))
 
@@ -447,7 +462,8 @@ def paged_attention_workspace(batch: int, num_heads: int, splits: int, device) -
 
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
                     seq_lens: torch.Tensor, max_len: int, *, splits: int | None = None, scale: float | None = None,
-                    workspace: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+                    workspace: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                    status: torch.Tensor | None = None) -> torch.Tensor:
     """One-query paged attention: q [B, NH, D] over positions [0, seq_lens[b]) of each
     sequence's pages -> [B, NH, D] bf16. ``max_len`` bounds every seq_len (fixed per graph)."""
     _require_cuda(q, k_cache, v_cache, block_table, seq_lens)
@@ -455,7 +471,7 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
         raise ValueError("seq_lens and block_table must be int32")
     B, NH, D = q.shape
     bs = k_cache.shape[1]
-    splits = splits or paged_attention_splits(B, NH, max_len)
+    splits = splits or paged_attention_splits(B, NH, max_len, bs)
     if workspace is None:
         workspace = paged_attention_workspace(B, NH, splits, q.device)
     if out is None:
@@ -463,6 +479,6 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     rc = _lib.load().dwdp_paged_attention(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(),
                                           seq_lens.data_ptr(), B, block_table.shape[-1], NH, D, bs, int(max_len),
                                           splits, float(scale if scale is not None else D ** -0.5),
-                                          workspace.data_ptr(), out.data_ptr(), _stream())
+                                          workspace.data_ptr(), out.data_ptr(), _ptr(status), _stream())
     _lib.check(rc, "paged_attention")
     return out

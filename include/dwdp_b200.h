@@ -266,11 +266,12 @@ size_t dwdp_paged_attention_workspace_bytes(int batch, int num_heads, int splits
 /* out[b, h] = softmax(scale * q[b, h] . K[b, :seq_lens[b], h]) V[b, :seq_lens[b], h] for one
  * query per sequence. The context is split into `splits` chunks of ceil(max_len / splits)
  * positions per (sequence, head), combined with the log-sum-exp rescaling. head_dim 128;
- * max_len >= every seq_lens[b] and <= max_blocks * block_size. */
+ * max_len >= every seq_lens[b] and <= max_blocks * block_size. A negative block id or a
+ * pipeline wait that runs out: DWDP_ERR_DEVICE_BOUNDS / _TIMEOUT in *status (may be NULL). */
 int dwdp_paged_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
                          const int32_t* seq_lens, int batch, int max_blocks, int num_heads, int head_dim,
                          int block_size, int max_len, int splits, float scale, void* workspace, void* out,
-                         void* stream);
+                         int* status, void* stream);
 
 /* ======================================================================== *
  * DWDP communication engine (replaces the pybind module dwdp_communication_ext,

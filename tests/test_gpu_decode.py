@@ -92,10 +92,13 @@ def test_rope_append_kv_bad_block_reports_status(pkg):
     assert int(kc.abs().sum()) == 0
 
 
-@pytest.mark.parametrize("splits", [1, None, 37])
-def test_paged_attention_ragged(pkg, splits):
+@pytest.mark.parametrize("NH,bs,splits", [(16, 16, 1), (16, 16, None), (16, 16, 37), (8, 16, None),
+                                          (32, 16, None), (4, 16, None), (16, 6, None)])
+def test_paged_attention_ragged(pkg, NH, bs, splits):
+    """Bulk-copy path (8/16/32 heads, block_size % 4 == 0) and the per-head fallback."""
     g = torch.Generator().manual_seed(17)
-    NH, D, bs, mb = 16, 128, 16, 128
+    D = 128
+    mb = -(-2048 // bs)
     lens = [1, 17, 300, 2048, 1000]
     B = len(lens)
     table, kc, vc = _paged(B, NH, D, bs, mb, g)
