@@ -399,7 +399,7 @@ constexpr size_t bulk_attn_smem() {
 // out[b, h, :] = sum_s e^(m_s - M) acc_s / sum_s e^(m_s - M) l_s. One CTA of kCombineWarps
 // warps per (b, h): warp w folds splits w, w + kCombineWarps, ... with its own running
 // max, then the warps merge through shared memory.
-constexpr int kCombineWarps = 4;
+constexpr int kCombineWarps = 8;
 
 __global__ void __launch_bounds__(kCombineWarps * 32)
 attn_combine_kernel(const float* __restrict__ part_ml, const float* __restrict__ part_acc, int S,
@@ -417,7 +417,7 @@ attn_combine_kernel(const float* __restrict__ part_ml, const float* __restrict__
   for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
   float L = 0.f;
   float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
+#pragma unroll 8
   for (int s = warp; s < S; s += kCombineWarps) {
     const float ms = ml[2 * s];
     const float f = ms == -INFINITY ? 0.f : expf(ms - M);

@@ -278,11 +278,21 @@ __device__ __forceinline__ void topk_warp(const float* lr, int E, int K, int ren
   float psum = p;
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
+  // renorm == 2: the selected experts' probabilities under the softmax over ALL E logits,
+  // not renormalised (Hugging Face Qwen2-MoE with norm_topk_prob = false)
+  float full = 0.f;
+  if (renorm == 2) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (lane + 32 * j < E) full += expf(mine[j] - top);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) full += __shfl_xor_sync(0xffffffffu, full, off);
+  }
   if (lane < K) {
     const int64_t o = t * K + lane;
     idx_out[o] = my_i;
     if (probs != nullptr) probs[o] = p;
-    w_out[o] = (K == 1) ? 1.0f : (renorm ? p / fmaxf(psum, eps) : p);
+    w_out[o] = renorm == 2 ? expf(my_v - top) / full : (K == 1) ? 1.0f : (renorm ? p / fmaxf(psum, eps) : p);
   }
 }
 

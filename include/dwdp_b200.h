@@ -65,7 +65,10 @@ int dwdp_device_sm_count(void);
  * Router: logits = x . W^T (+bias) (*score_scale) in fp32; top-k over logits
  * (ties -> lower expert id, slots in descending logit order); softmax over the
  * k selected; optional renormalisation by sum.clamp_min(eps); k == 1 gives
- * weight 1. Optionally the sigmoid shared-expert gate sigmoid(x . g).
+ * weight 1. renormalize == 2 instead gives each selected expert its probability
+ * under the softmax over all E logits, not renormalised (the Hugging Face
+ * Qwen2-MoE router with norm_topk_prob = false). Optionally the sigmoid
+ * shared-expert gate sigmoid(x . g).
  * Replaces reference_topk_routing + compute_router_logits (fused.py:8-42,
  * linear.py:38-44). E <= 256, K <= 16.
  *   hidden [T,H] (hidden_dtype bf16|f32), weight [E,H] (weight_dtype bf16|f32)
