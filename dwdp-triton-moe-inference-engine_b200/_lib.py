@@ -80,6 +80,16 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "dwdp_dispatch_noalloc_max_scratch_bytes": (c_size_t, []),
     "dwdp_gather_rows": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int64, c_void_p, c_void_p, c_void_p]),
+    "dwdp_ep_buffer_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "dwdp_ep_ret_offset": (c_size_t, [c_int, c_int, c_int]),
+    "dwdp_ipc_open": (c_int, [c_void_p, c_size_t, c_void_p, c_void_p]),
+    "dwdp_ipc_close": (c_int, [c_void_p]),
+    "dwdp_ep_dispatch": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                 c_void_p, c_void_p, c_void_p]),
+    "dwdp_ep_plan": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+                             c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "dwdp_ep_combine": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                                c_void_p, c_void_p]),
     "dwdp_add_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float, c_void_p, c_void_p]),
     "dwdp_rope_append_kv": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                                     c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),

@@ -44,6 +44,15 @@ extern "C" int dwdp_paged_attention_launch(const void*, const void*, const void*
                                            int, int, int, int, int, int, float, void*, void*, int*,
                                            cudaStream_t);
 
+extern "C" size_t dwdp_ep_buffer_bytes(int, int, int);
+extern "C" size_t dwdp_ep_ret_offset(int, int, int);
+extern "C" int dwdp_ep_dispatch_launch(const void*, const int64_t*, const float*, int, int, int, int, int, int, int,
+                                       const unsigned long long*, int*, cudaStream_t);
+extern "C" int dwdp_ep_plan_launch(void*, int, int, int, int, int, int, int, int64_t*, int64_t*, int*, float*, int*,
+                                   int*, void*, int*, cudaStream_t);
+extern "C" int dwdp_ep_combine_launch(void*, int, int, int, int, const void*, const int*, const int*,
+                                      const unsigned long long*, int*, cudaStream_t);
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -376,4 +385,51 @@ extern "C" int dwdp_paged_attention(const void* q, const void* k_cache, const vo
                                            head_dim, block_size, max_len, splits, scale, workspace, out,
                                            status, as_stream(stream)),
                "paged_attention");
+}
+
+// --------------------------------------------------------------------------- expert-parallel decode exchange
+extern "C" int dwdp_ep_dispatch(const void* hidden, const int64_t* topk_idx, const float* topk_weights,
+                                int num_tokens, int top_k, int num_experts, int world, int rank, int hidden_size,
+                                int capacity, const unsigned long long* peers, int* status, void* stream) {
+  g_last_error.clear();
+  if (world < 1 || world > 8 || rank < 0 || rank >= world)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "ep_dispatch: world must be in [1, 8] and rank in [0, world)");
+  if (num_tokens < 0 || top_k <= 0 || num_tokens * top_k > 2048 || num_tokens * top_k > capacity)
+    return fail(DWDP_ERR_CAPACITY, "ep_dispatch: num_tokens * top_k must be <= min(2048, capacity)");
+  if (hidden_size <= 0 || hidden_size % 8 || num_experts <= 0)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "ep_dispatch: bad hidden_size / num_experts");
+  if (num_tokens > 0 && (hidden == nullptr || topk_idx == nullptr || topk_weights == nullptr || peers == nullptr))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "ep_dispatch: null pointer");
+  return check(dwdp_ep_dispatch_launch(hidden, topk_idx, topk_weights, num_tokens, top_k, num_experts, world, rank,
+                                       hidden_size, capacity, peers, status, as_stream(stream)),
+               "ep_dispatch");
+}
+
+extern "C" int dwdp_ep_plan(void* ep_buffer, int world, int rank, int hidden_size, int capacity, int num_experts,
+                            int expert_lo, int local_experts, int64_t* counts, int64_t* offsets, int* packed_src,
+                            float* packed_weights, int* ret_addr, int* total, void* packed_hidden, int* status,
+                            void* stream) {
+  g_last_error.clear();
+  if (world < 1 || world > 8 || rank < 0 || rank >= world || local_experts <= 0 || local_experts > 256)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "ep_plan: world in [1, 8], local_experts in [1, 256]");
+  if (ep_buffer == nullptr || counts == nullptr || offsets == nullptr || packed_src == nullptr ||
+      packed_weights == nullptr || ret_addr == nullptr || total == nullptr || packed_hidden == nullptr)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "ep_plan: null pointer");
+  return check(dwdp_ep_plan_launch(ep_buffer, world, rank, hidden_size, capacity, num_experts, expert_lo,
+                                   local_experts, counts, offsets, packed_src, packed_weights, ret_addr, total,
+                                   packed_hidden, status, as_stream(stream)),
+               "ep_plan");
+}
+
+extern "C" int dwdp_ep_combine(void* ep_buffer, int world, int rank, int hidden_size, int capacity,
+                               const void* weighted, const int* ret_addr, const int* total,
+                               const unsigned long long* peers, int* status, void* stream) {
+  g_last_error.clear();
+  if (world < 1 || world > 8 || rank < 0 || rank >= world)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "ep_combine: world must be in [1, 8] and rank in [0, world)");
+  if (ep_buffer == nullptr || weighted == nullptr || ret_addr == nullptr || total == nullptr || peers == nullptr)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "ep_combine: null pointer");
+  return check(dwdp_ep_combine_launch(ep_buffer, world, rank, hidden_size, capacity, weighted, ret_addr, total,
+                                      peers, status, as_stream(stream)),
+               "ep_combine");
 }

@@ -159,6 +159,27 @@ extern "C" int dwdp_export_ipc_handle(const void* device_ptr, void* handle_out, 
 
 extern "C" size_t dwdp_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
 
+// Open another process's allocation (its export_ipc_handle blob) and return the device
+// address of `offset` inside it; dwdp_ipc_close takes the base that was returned in *base_out.
+extern "C" int dwdp_ipc_open(const void* handle, size_t offset, void** base_out, void** ptr_out) {
+  if (handle == nullptr || base_out == nullptr || ptr_out == nullptr)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "ipc_open: null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return set_error("cudaIpcOpenMemHandle", e);
+  *base_out = base;
+  *ptr_out = static_cast<char*>(base) + offset;
+  return DWDP_OK;
+}
+
+extern "C" int dwdp_ipc_close(void* base) {
+  if (base == nullptr) return DWDP_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(base);
+  return e == cudaSuccess ? DWDP_OK : set_error("cudaIpcCloseMemHandle", e);
+}
+
 // ----------------------------------------------------------------------------- engine
 extern "C" int dwdp_engine_create(int device_id, size_t slot_bytes, int num_slots, int num_buffers,
                                   dwdp_engine** out) {

@@ -277,6 +277,41 @@ int dwdp_paged_attention(const void* q, const void* k_cache, const void* v_cache
                          int* status, void* stream);
 
 /* ======================================================================== *
+ * Expert-parallel decode exchange (replaces the all_to_all_single EP path of
+ * DWDP/adapters/qwen15_moe.py:164-243, used below ep_batch_size_threshold,
+ * DWDP/runtime/config.py:31). Every rank allocates one EP buffer of
+ * dwdp_ep_buffer_bytes(world, H, capacity) bytes (capacity = T_max * top_k rows), exports
+ * it with dwdp_export_ipc_handle and opens the others' with dwdp_ipc_open; `peers` is a
+ * DEVICE array of world base addresses (this rank's own buffer at [rank]). Expert e is
+ * owned by rank min(e / ceil(E / world), world - 1). All ranks run the same num_tokens
+ * and top_k. Per forward, in stream order:
+ *   dwdp_ep_dispatch   rows of every (token, slot) -> the owner's buffer;
+ *   dwdp_ep_plan       owner: wait for every rank, counting sort by local expert into
+ *                      counts/offsets (local_experts entries, int64), packed_src, packed
+ *                      routing weights, return addresses, *total, and the packed rows;
+ *   (grouped GEMMs: dwdp_moe_experts with packed_hidden, top_k' = world * top_k)
+ *   dwdp_ep_combine    weighted rows back to their source's buffer, then wait for all
+ *                      owners; the source's results are then the rows
+ *                      [dwdp_ep_ret_offset(), + num_tokens * top_k * H * 2) of its own
+ *                      buffer in slot order (merge them with an identity inverse).
+ * Waits are bounded (about a second): DWDP_ERR_DEVICE_TIMEOUT in *status.
+ * ======================================================================== */
+size_t dwdp_ep_buffer_bytes(int world, int hidden_size, int capacity);
+size_t dwdp_ep_ret_offset(int world, int hidden_size, int capacity);
+int dwdp_ipc_open(const void* handle, size_t offset, void** base_out, void** ptr_out);
+int dwdp_ipc_close(void* base);
+int dwdp_ep_dispatch(const void* hidden, const int64_t* topk_idx, const float* topk_weights, int num_tokens,
+                     int top_k, int num_experts, int world, int rank, int hidden_size, int capacity,
+                     const unsigned long long* peers, int* status, void* stream);
+int dwdp_ep_plan(void* ep_buffer, int world, int rank, int hidden_size, int capacity, int num_experts,
+                 int expert_lo, int local_experts, int64_t* counts, int64_t* offsets, int* packed_src,
+                 float* packed_weights, int* ret_addr, int* total, void* packed_hidden, int* status,
+                 void* stream);
+int dwdp_ep_combine(void* ep_buffer, int world, int rank, int hidden_size, int capacity, const void* weighted,
+                    const int* ret_addr, const int* total, const unsigned long long* peers, int* status,
+                    void* stream);
+
+/* ======================================================================== *
  * DWDP communication engine (replaces the pybind module dwdp_communication_ext,
  * DWDP/communication/bindings.cpp:32-111): expert slabs sharded across the GPUs
  * of one box, remote slabs opened through CUDA IPC (or a peer pointer) and
