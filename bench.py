@@ -376,6 +376,73 @@ def transfer_comparison(store, world: int, steps: int, device) -> dict:
             "bytes_received_per_gpu": {"p2p": recv, "nccl": ag_recv}}
 
 
+def ep_decode_comparison(pkg, layer, world: int, rank: int, steps: int, device) -> dict:
+    """Decode-sized batches on one layer two ways, each graph-captured and timed on the
+    device, max over ranks: the EP path (token rows to the expert owners and back over
+    NVLink peer memory) and the DWDP path (every remote expert prefetched into staging,
+    then the local grouped GEMM). Bytes are what each GPU receives per layer."""
+    import torch.distributed as dist
+
+    ep = pkg.ep
+    store = layer.experts
+    K, H = layer.top_k, layer.hidden_size
+    ex = ep.EPExchange(world, rank, H, ep.EP_BATCH_SIZE_THRESHOLD, K, device)
+    ex.connect()
+    epl = ep.ExpertParallelMoE(layer.router_weight, store.local, K, ex, shared_expert=layer.shared_expert,
+                               shared_gate_weight=layer.shared_gate_weight)
+
+    def timed(fn, n):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b) / n], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    n = max(5, min(steps, 20))
+    points = []
+    for T in (1, 8, 64):
+        x = make_inputs(T, device, seed=900 + 31 * rank + T)
+        y = torch.empty_like(x)
+        ws = epl.workspace(T)
+        s = torch.cuda.Stream(device=device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                epl.run(x, ws, y)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        dist.barrier()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            epl.run(x, ws, y)
+        ep_ms = timed(g.replay, n)
+        lws = layer.workspace(T)
+
+        def dwdp():
+            store.prefetch(0)
+            store.wait(0)
+            layer.run(x, lws, y)
+
+        dwdp_ms = timed(dwdp, n)
+        st = epl.read_status(T)[0]
+        points.append({"T": T, "ep_us": ep_ms * 1e3, "dwdp_us": dwdp_ms * 1e3,
+                       "ep_bytes_received_per_gpu": int(2 * T * K * H * 2 * (world - 1) / world),
+                       "dwdp_bytes_received_per_gpu": store.remote_bytes(), "ep_status": st})
+    dist.barrier()
+    ex.close()
+    return {"layer": "qwen1.5-moe-a2.7b-shaped MoE layer 0, fp8 e4m3",
+            "ep_threshold_tokens": ep.EP_BATCH_SIZE_THRESHOLD, "ep_kernel_launches": epl.kernel_launches(),
+            "points": points}
+
+
 # ----------------------------------------------------------------------------- main
 # ----------------------------------------------------------------------------- full decode step (row f1)
 def decode_step_bench(pkg, device, batches: list[int], steps: int, warmup: int, flush) -> dict:
@@ -432,6 +499,12 @@ def decode_step_bench(pkg, device, batches: list[int], steps: int, warmup: int, 
             e2e()
             torch.cuda.current_stream().synchronize()
         e2e_s = (time.perf_counter() - t0) / steps
+        # one more replay inside an NVTX range: the launch list of exactly one step for
+        # `ncu --nvtx --nvtx-include "decode_step/"`
+        torch.cuda.nvtx.range_push("decode_step")
+        bufs.graph.replay()
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
         st = model.read_status(B)
         ms = statistics.median(step_ms)
         points.append({
@@ -451,6 +524,38 @@ def decode_step_bench(pkg, device, batches: list[int], steps: int, warmup: int, 
             "peak_source": peaks["source"]}
 
 
+def attention_bench(pkg, device, batches: list[int], steps: int, warmup: int, flush) -> dict:
+    """paged_attention alone (16 heads of 128, block_size 16, every sequence at context 2048,
+    pages in a random order): the kernel pair's time and its HBM roofline per batch size."""
+    peaks = _peaks()
+    NH, D, bs, L = 16, 128, 16, 2048
+    mb = L // bs
+    points = []
+    for B in batches:
+        g = torch.Generator(device=device).manual_seed(B)
+        table = torch.randperm(B * mb, generator=g, device=device).view(B, mb).to(torch.int32)
+        kc = torch.randn(B * mb, bs, NH, D, generator=g, device=device).bfloat16()
+        vc = torch.randn(B * mb, bs, NH, D, generator=g, device=device).bfloat16()
+        q = torch.randn(B, NH, D, generator=g, device=device).bfloat16()
+        lens = torch.full((B,), L, dtype=torch.int32, device=device)
+        splits = pkg.ops.paged_attention_splits(B, NH, L, bs)
+        ws = pkg.ops.paged_attention_workspace(B, NH, splits, device)
+        out = torch.empty_like(q)
+        st = torch.zeros(4, dtype=torch.int32, device=device)
+
+        def run():
+            pkg.ops.paged_attention(q, kc, vc, table, lens, L, splits=splits, workspace=ws, out=out, status=st)
+
+        ms = statistics.median(time_device(run, steps, warmup, flush))
+        kv = B * L * 2 * NH * D * 2
+        points.append({"batch": B, "splits": splits, "us": ms * 1e3, "kv_bytes": kv,
+                       "achieved_gbs": kv / (ms / 1e3) / 1e9,
+                       "frac_of_measured_hbm": kv / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "status": int(st[0])})
+        del kc, vc
+    return {"workload": "paged_attention", "heads": NH, "head_dim": D, "block_size": bs, "context": L,
+            "points": points, "hbm_peak_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"]}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -461,7 +566,7 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=256)
-    ap.add_argument("--workload", default="moe_layers", choices=["moe_layers", "decode_step"])
+    ap.add_argument("--workload", default="moe_layers", choices=["moe_layers", "decode_step", "attention"])
     ap.add_argument("--batch", default="1,8,64", help="decode_step batch sizes")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -508,6 +613,11 @@ def main() -> None:
         return
 
     flush = L2Flusher(device)
+    if args.workload == "attention":
+        res = attention_bench(pkg, device, [int(b) for b in args.batch.split(",")], args.steps, args.warmup, flush)
+        print(json.dumps({"metric": "paged attention HBM GB/s", "unit": "GB/s", "steps": args.steps,
+                          "warmup": args.warmup, **res}), flush=True)
+        return
     if args.workload == "decode_step":
         res = decode_step_bench(pkg, device, [int(b) for b in args.batch.split(",")], args.steps, args.warmup, flush)
         if rank == 0:
@@ -574,6 +684,7 @@ def main() -> None:
                   "prefetch_gbs_lower_bound": rb / (ms_per_step / 1e3) / 1e9,
                   "note": "copies overlap compute; GB/s is remote bytes / step time (a lower bound on link rate)"}
         nvlink.update(transfer_comparison(stack.layers[0].experts, world, args.steps, device))
+        nvlink["ep_decode"] = ep_decode_comparison(pkg, stack.layers[0], world, rank, args.steps, device)
 
     cb = None
     if rank == 0 and world == 1:

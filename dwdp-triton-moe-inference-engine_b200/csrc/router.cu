@@ -462,6 +462,10 @@ extern "C" int dwdp_router_launch(const void* hidden, int hidden_dtype, const vo
     const int64_t tiles = (T + 15) / 16;
     int G = 1;
     while (G < 8 && tiles * G < 148 && G * 8 < rows) G *= 2;
+    if (const char* v = getenv("DWDP_ROUTER_G")) {  // tuning override: cluster size 1, 2, 4 or 8
+      const int g = atoi(v);
+      if (g == 1 || g == 2 || g == 4 || g == 8) G = g;
+    }
     if (launch_chained(router_fused_kernel, dim3((unsigned)tiles, (unsigned)G, 1), dim3(kFusedWarps * 32, 1, 1),
                        kFusedSmem, stream, (unsigned)G, (const __nv_bfloat16*)hidden,
                        (const __nv_bfloat16*)weight, bias, (const __nv_bfloat16*)shared_gate_weight, (int)T, H, E, K,
