@@ -227,8 +227,6 @@ def expert_flops(layer, T: int) -> int:
 
 
 def run_point(pkg, layer, T: int, steps: int, warmup: int, flush, device, rank: int, world: int):
-    from dwdp_b200 import ops
-
     x = make_inputs(T, device, seed=4242 + 7919 * rank + T)
     out = torch.empty(T, layer.hidden_size, dtype=torch.bfloat16, device=device)
     ws = layer.workspace(T)

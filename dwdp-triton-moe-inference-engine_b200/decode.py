@@ -18,7 +18,6 @@ region of HBM.
 from __future__ import annotations
 
 import collections
-import math
 from dataclasses import dataclass
 
 import torch

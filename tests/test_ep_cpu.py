@@ -75,7 +75,7 @@ def test_paged_attention_split_choice(pkg):
     for B in (1, 2, 8, 16, 64, 128, 256):
         s = ops.paged_attention_splits(B, 16, 2048, 16)
         assert 1 <= s <= 2048 // 16
-    assert ops.paged_attention_splits(1, 16, 2048, 16) == 128  # one page-pair per CTA at B = 1
+    assert ops.paged_attention_splits(1, 16, 2048, 16) == 128  # 16-position chunks at B = 1
     # the fallback path (not 8/16/32 heads) sizes for ~4 CTAs per SM per (sequence, head)
     assert ops.paged_attention_splits(4, 4, 2048, 16) == 32
 
