@@ -369,7 +369,20 @@ def transfer_comparison(store, world: int, steps: int, device) -> dict:
     dst = torch.empty(world * per_rank, dtype=torch.uint8, device=device)
     ag_ms = timed(lambda: dist.all_gather_into_tensor(dst, src), n)
     ag_recv = (world - 1) * per_rank
-    return {"p2p_prefetch_ms_per_layer": p2p_ms, "p2p_prefetch_gbs": recv / (p2p_ms / 1e3) / 1e9,
+    # cost model: fit the link on 1-, 4- and 8-expert copies, predict the whole layer's prefetch
+    try:
+        import importlib
+
+        cm = importlib.import_module("dwdp_b200.cost_model")
+        link = cm.measure_link(store)
+        pred = cm.build_cost_model(store.remote, store.slab_bytes, link).total_estimated_latency_us
+        model = {"link": {"latency_us": link.latency_us, "per_stream_gbps": link.bandwidth_gbps,
+                          "aggregate_gbps": link.aggregate_gbps, "streams": link.streams},
+                 "fitted_on_experts": [1, 4, 8], "predicted_prefetch_us_per_layer": pred,
+                 "measured_prefetch_us_per_layer": p2p_ms * 1e3, "remote_experts": len(store.remote)}
+    except Exception as exc:  # the model is a report, never a reason to lose the bench line
+        model = {"error": repr(exc)}
+    return {"cost_model": model, "p2p_prefetch_ms_per_layer": p2p_ms, "p2p_prefetch_gbs": recv / (p2p_ms / 1e3) / 1e9,
             "nccl_all_gather_ms_per_layer": ag_ms, "nccl_all_gather_gbs": ag_recv / (ag_ms / 1e3) / 1e9,
             "bytes_received_per_gpu": {"p2p": recv, "nccl": ag_recv}}
 

@@ -102,6 +102,7 @@ class CommunicationPlan:
     remote_expert_ids: torch.Tensor
     planner_policy: str = "static"
     prefetch_buffer: int = 0
+    cost_model: object | None = None  # cost_model.CommunicationCostModel for remote transfers
 
 
 @dataclass(slots=True)

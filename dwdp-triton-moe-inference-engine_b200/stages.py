@@ -294,6 +294,39 @@ class StaticCommunicationPlanner(nn.Module):
                                  planner_policy=self.config.planner_policy)
 
 
+class DWDPCommunicationPlanner(nn.Module):
+    """Experts sharded over the ranks by owner(e) = e // ceil(E / G) (the reference's
+    expert-parallel planner, DWDP/comms_planner/expert_parallel.py:120-122): the local rank's
+    experts stay local, every other one is prefetched. The plan's cost model is built from a
+    measured ``LinkProfile`` (``cost_model.measure_link``) and the prefetch window the caller
+    expects (the previous layer's compute time), where the reference fills constants."""
+
+    def __init__(self, config: CommunicationPlannerConfig | None = None, *, link=None,
+                 bytes_per_expert: int = 0, prefetch_window_us: float = 0.0) -> None:
+        super().__init__()
+        self.config = config or CommunicationPlannerConfig(planner_policy="dwdp")
+        self.link = link
+        self.bytes_per_expert = bytes_per_expert
+        self.prefetch_window_us = prefetch_window_us
+
+    def forward(self, execution_plan: ExecutionPlan, workspace=None,
+                num_experts: int | None = None) -> CommunicationPlan:
+        from . import cost_model as cm
+        from .dwdp import owner_of
+
+        dev = execution_plan.expert_queue.device
+        E = num_experts if num_experts is not None else execution_plan.expert_queue.numel()
+        G, r = self.config.world_size, self.config.local_rank
+        local = [e for e in range(E) if owner_of(e, E, G) == r]
+        remote = [e for e in range(E) if owner_of(e, E, G) != r]
+        model = (cm.build_cost_model(remote, self.bytes_per_expert, self.link,
+                                     prefetch_window_us=self.prefetch_window_us)
+                 if self.link is not None and remote else None)
+        return CommunicationPlan(local_expert_ids=torch.tensor(local, device=dev, dtype=torch.int64),
+                                 remote_expert_ids=torch.tensor(remote, device=dev, dtype=torch.int64),
+                                 planner_policy=self.config.planner_policy, cost_model=model)
+
+
 # ----------------------------------------------------------------------------- executor
 def _expert_linear_weights(module: nn.Module) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """(gate [I,H], up [I,H], down [H,I]) of a Qwen-style SwiGLU expert module."""
@@ -433,6 +466,7 @@ register_router("b200_linear_topk", B200LinearTopKRouter)
 register_dispatcher("b200_expert_major", B200ExpertMajorDispatcher)
 register_scheduler("b200_round_robin", B200RoundRobinScheduler)
 register_communication_planner("static", StaticCommunicationPlanner)
+register_communication_planner("dwdp", DWDPCommunicationPlanner)
 register_executor("b200", B200Executor)
 register_merger("b200", B200Merger)
 
