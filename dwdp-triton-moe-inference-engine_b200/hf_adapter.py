@@ -24,6 +24,12 @@ false gives the selected experts' probabilities under the softmax over all exper
 (what transformers computes; the reference's own routing always takes the softmax
 over the k selected, available here as ``routing="reference"``).
 
+With ``world_size > 1`` (one process per GPU, ``torch.distributed`` initialised) every block
+holds only its rank's shard of the experts and runs the reference's hybrid
+(``DWDP/adapters/qwen15_moe.py:325-345``): batches above ``ep_batch_size_threshold`` tokens per
+rank prefetch the remote experts over NVLink (DWDP), smaller ones exchange token rows with the
+expert owners (EP); see ``ParallelContext``.
+
 There is no CPU execution: a patched block raises ``RuntimeError`` off CUDA.
 """
 from __future__ import annotations
@@ -182,20 +188,41 @@ def _expert_mats(spec: MoELayerSpec, e: int):
     return "dense", [gu[:I], gu[I:], dn]
 
 
+def _load_expert(load, spec: MoELayerSpec, e: int, device) -> None:
+    """load(e, gate, up, down) with expert e's weights (dequantised first when pre-quantised)."""
+    kind, mats = _expert_mats(spec, e)
+    if kind == "fp8":
+        (gq, gs), (uq, us), (dq, ds) = mats
+        if gs is None or us is None or ds is None:
+            raise ValueError(f"{spec.name}: e4m3 expert {e} without scale tensors")
+        load(e, dequantize_fp8(gq.to(device), gs), dequantize_fp8(uq.to(device), us),
+             dequantize_fp8(dq.to(device), ds))
+    else:
+        load(e, *(t.detach().to(device) for t in mats))
+
+
 def _store_from(spec: MoELayerSpec, weight_dtype: torch.dtype, scale_mode: int, device) -> ExpertWeightStore:
     store = ExpertWeightStore(spec.num_experts, spec.hidden_size, spec.intermediate_size, weight_dtype=weight_dtype,
                               scale_mode=scale_mode if weight_dtype == torch.float8_e4m3fn else _lib.SCALE_NONE,
                               device=device)
     for e in range(spec.num_experts):
-        kind, mats = _expert_mats(spec, e)
-        if kind == "fp8":
-            (gq, gs), (uq, us), (dq, ds) = mats
-            if gs is None or us is None or ds is None:
-                raise ValueError(f"{spec.name}: e4m3 expert {e} without scale tensors")
-            import_fp8_expert(store, e, gq.to(device), gs, uq.to(device), us, dq.to(device), ds)
-        else:
-            g, u, d = (t.detach().to(device) for t in mats)
-            store.load_expert(e, g, u, d)
+        _load_expert(store.load_expert, spec, e, device)
+    return store
+
+
+def _sharded_store_from(spec: MoELayerSpec, weight_dtype: torch.dtype, scale_mode: int, device, rank: int,
+                        world: int, group=None):
+    """This rank's shard (owner(e) = e // ceil(E / G)) of the block's experts, connected to the
+    other ranks' shards (collective over ``group``)."""
+    from .dwdp import ShardedExpertStore
+
+    store = ShardedExpertStore(spec.num_experts, spec.hidden_size, spec.intermediate_size, rank=rank,
+                               world_size=world, weight_dtype=weight_dtype,
+                               scale_mode=scale_mode if weight_dtype == torch.float8_e4m3fn else _lib.SCALE_NONE,
+                               device=device, num_buffers=1)
+    for e in store.owned:
+        _load_expert(store.load_expert, spec, e, device)
+    store.connect(group)
     return store
 
 
@@ -271,6 +298,33 @@ class BlockGraphRunner:
         return graph, xin, yout
 
 
+# --------------------------------------------------------------------------- multi-GPU
+class ParallelContext:
+    """Expert parallelism across ``world`` ranks for every patched block of a model (the
+    reference's hybrid, DWDP/adapters/qwen15_moe.py:325-345): each rank holds its shard of
+    every block's experts; batches of more than ``ep_batch_size_threshold`` tokens per rank
+    prefetch the remote experts over NVLink (DWDP), smaller ones send their token rows to the
+    owners and back (EP, one exchange buffer shared by all blocks). Every rank must run the
+    same blocks in the same order with the same token count."""
+
+    def __init__(self, world_size: int, rank: int, *, ep_batch_size_threshold: int = 64, group=None) -> None:
+        if world_size < 2 or not 0 <= rank < world_size:
+            raise ValueError("ParallelContext needs world_size >= 2 and 0 <= rank < world_size")
+        self.world, self.rank, self.group = world_size, rank, group
+        self.threshold = ep_batch_size_threshold
+        self.exchange = None
+
+    def exchange_for(self, hidden_size: int, top_k: int, device):
+        from .ep import EPExchange
+
+        if self.exchange is None:
+            self.exchange = EPExchange(self.world, self.rank, hidden_size, self.threshold, top_k, device)
+            self.exchange.connect(self.group)
+        elif (self.exchange.H, self.exchange.top_k) != (hidden_size, top_k):
+            raise ValueError("every patched block must share the hidden size and top_k")
+        return self.exchange
+
+
 # --------------------------------------------------------------------------- the block
 class B200MoEBlock(nn.Module):
     """Drop-in for a Qwen-style sparse-MoE block (DWDP/adapters/qwen15_moe.py:43-323):
@@ -279,7 +333,8 @@ class B200MoEBlock(nn.Module):
     is a contiguous bf16 CUDA tensor."""
 
     def __init__(self, spec: MoELayerSpec, *, weight_dtype: torch.dtype = torch.float8_e4m3fn,
-                 scale_mode: int = _lib.SCALE_CHANNEL, routing: str = "hf") -> None:
+                 scale_mode: int = _lib.SCALE_CHANNEL, routing: str = "hf",
+                 parallel: ParallelContext | None = None) -> None:
         super().__init__()
         if routing not in ("hf", "reference"):
             raise ValueError("routing must be 'hf' or 'reference'")
@@ -293,6 +348,8 @@ class B200MoEBlock(nn.Module):
         self.scale_mode = scale_mode
         self.renormalize = 1 if (spec.norm_topk_prob or routing == "reference") else 2
         self.moe: MoELayer | None = None
+        self.parallel = parallel
+        self.ep_layer = None  # the EP path of this block (multi-GPU, small batches)
         self._graph_runner: BlockGraphRunner | None = None
 
     def prepare(self, device: torch.device | str | None = None) -> MoELayer:
@@ -307,16 +364,35 @@ class B200MoEBlock(nn.Module):
         bias = spec.gate_bias.detach().to(dev).float() if spec.gate_bias is not None else None
         gate_lin = getattr(mod, "shared_expert_gate", None)
         gate_w = gate_lin.weight.detach().to(dev, torch.bfloat16).reshape(-1) if gate_lin is not None else None
-        self.moe = MoELayer(router_w, _store_from(spec, self.weight_dtype, self.scale_mode, dev), spec.top_k,
-                            shared_expert=_shared_store(mod, self.weight_dtype, self.scale_mode, dev),
-                            shared_gate_weight=gate_w, router_bias=bias, renormalize=self.renormalize)
+        shared = _shared_store(mod, self.weight_dtype, self.scale_mode, dev)
+        par = self.parallel
+        if par is None:
+            store = _store_from(spec, self.weight_dtype, self.scale_mode, dev)
+        else:
+            store = _sharded_store_from(spec, self.weight_dtype, self.scale_mode, dev, par.rank, par.world, par.group)
+            from .ep import ExpertParallelMoE
+
+            self.ep_layer = ExpertParallelMoE(router_w, store.local, spec.top_k,
+                                              par.exchange_for(spec.hidden_size, spec.top_k, dev),
+                                              shared_expert=shared, shared_gate_weight=gate_w, router_bias=bias,
+                                              renormalize=self.renormalize)
+        self.moe = MoELayer(router_w, store, spec.top_k, shared_expert=shared, shared_gate_weight=gate_w,
+                            router_bias=bias, renormalize=self.renormalize)
         return self.moe
+
+    def _use_ep(self, num_tokens: int) -> bool:
+        return self.ep_layer is not None and num_tokens <= self.parallel.threshold
 
     @property
     def router_weight(self) -> torch.Tensor:
         return self.prepare().router_weight
 
     def _run(self, x: torch.Tensor) -> torch.Tensor:
+        if self._use_ep(x.shape[0]):
+            return self.ep_layer(x)
+        if self.parallel is not None:  # DWDP: the remote experts into staging, then the GEMMs
+            self.moe.experts.prefetch(0)
+            self.moe.experts.wait(0)
         return self.moe(x)
 
     def forward(self, hidden_states: torch.Tensor, *args, **kwargs):
@@ -326,11 +402,14 @@ class B200MoEBlock(nn.Module):
         moe = self.prepare(hidden_states.device)
         shape, dtype = hidden_states.shape, hidden_states.dtype
         x = hidden_states.reshape(-1, self.hidden_size).to(torch.bfloat16).contiguous()
-        y = self._graph_runner(x) if self._graph_runner is not None else self._run(x)
+        T = x.shape[0]
+        # graphs replay the single-GPU and EP paths; the DWDP prefetch runs eagerly
+        graph = self._graph_runner is not None and (self.parallel is None or self._use_ep(T))
+        y = self._graph_runner(x) if graph else self._run(x)
         out = y.to(dtype).reshape(shape)
         if self.returns_router_logits:
-            T = x.shape[0]
-            logits = moe.workspace(T).router.router_logits.to(dtype, copy=True)
+            router = self.ep_layer.workspace(T)["router"] if self._use_ep(T) else moe.workspace(T).router
+            logits = router.router_logits.to(dtype, copy=True)
             return out, logits.reshape(*shape[:-1], self.num_experts)
         return out
 
@@ -347,8 +426,11 @@ class Qwen15MoEAdapter:
     (DWDP/adapters/qwen15_moe.py:434-580)."""
 
     def __init__(self, model: nn.Module, *, weight_dtype: torch.dtype = torch.float8_e4m3fn,
-                 scale_mode: int = _lib.SCALE_CHANNEL, routing: str = "hf") -> None:
+                 scale_mode: int = _lib.SCALE_CHANNEL, routing: str = "hf", world_size: int = 1, rank: int = 0,
+                 ep_batch_size_threshold: int = 64, group=None) -> None:
         self.model = model
+        self.parallel = (ParallelContext(world_size, rank, ep_batch_size_threshold=ep_batch_size_threshold,
+                                         group=group) if world_size > 1 else None)
         self.weight_dtype = weight_dtype
         self.scale_mode = scale_mode
         self.routing = routing
@@ -371,7 +453,7 @@ class Qwen15MoEAdapter:
         self.moe_layer_specs = specs
         for spec in specs:
             block = B200MoEBlock(spec, weight_dtype=self.weight_dtype, scale_mode=self.scale_mode,
-                                 routing=self.routing)
+                                 routing=self.routing, parallel=self.parallel)
             setattr(spec.parent, spec.child_name, block)
             self._records.append((spec, spec.module, block))
         return len(specs)

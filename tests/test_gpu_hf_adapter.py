@@ -161,3 +161,68 @@ def test_cuda_graph_blocks(pkg):
     assert st["captures"] == 2 and st["replays"] == 4 and st["fallbacks"] == 0
     assert torch.equal(g1, g2)
     assert _rel(g1, eager) < 1e-3
+
+
+def _hybrid_worker(rank, world, port, q):
+    import os
+
+    import torch.distributed as dist
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+        global DEV
+        DEV = f"cuda:{rank}"
+        model = _tiny(True, seed=9)  # same weights on every rank
+        ha = pkg.hf_adapter
+        ctx = ha.ParallelContext(world, rank, ep_batch_size_threshold=16)
+        specs = {s.name: s for s in ha.discover_moe_layers(model)}
+        res = []
+        for name in sorted(specs):  # same order on every rank: preparing is collective
+            par = ha.B200MoEBlock(specs[name], parallel=ctx)
+            ref = ha.B200MoEBlock(specs[name])
+            par.prepare(dev)
+            ref.prepare(dev)
+            for T in (8, 96):  # EP below the threshold, DWDP above
+                x = torch.randn(1, T, 256, generator=torch.Generator().manual_seed(50 + rank + T)).bfloat16().to(dev)
+                with torch.no_grad():
+                    y_par, y_ref = par(x), ref(x)
+                torch.cuda.synchronize()
+                st = par.ep_layer.read_status(T)[0] if T <= 16 else par.moe.read_status(T)[0]
+                res.append((name, T, bool(torch.equal(y_par, y_ref)), st))
+        dist.barrier()
+        ctx.exchange.close()
+        q.put((rank, res))
+        dist.destroy_process_group()
+    except Exception as exc:
+        q.put((rank, repr(exc)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_hybrid_ep_dwdp_blocks_match_single_gpu():
+    """world 2: each rank holds half of every block's experts; 8 tokens go the EP way, 96 the
+    DWDP way; both must equal the single-GPU block bit for bit."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_hybrid_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=600) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, res in out:
+        assert not isinstance(res, str), f"rank {rank}: {res}"
+        for name, T, ok, st in res:
+            assert st == 0, f"rank {rank} {name} T={T}: status {st}"
+            assert ok, f"rank {rank} {name} T={T}: differs from the single-GPU block"

@@ -113,3 +113,18 @@ def test_dequantize_fp8_channel_and_block(pkg, orc):
     q2, s2 = orc.quantize_channel(pkg.hf_adapter.dequantize_fp8(q, s))
     assert torch.equal(q2.view(torch.uint8), q.view(torch.uint8))
     torch.testing.assert_close(s2, s, rtol=1e-6, atol=0)
+
+
+def test_parallel_context_wiring(pkg):
+    ha = pkg.hf_adapter
+    with pytest.raises(ValueError):
+        ha.ParallelContext(1, 0)
+    with pytest.raises(ValueError):
+        ha.ParallelContext(2, 2)
+    model = _hf_tiny()
+    ad = ha.Qwen15MoEAdapter(model, world_size=2, rank=1, ep_batch_size_threshold=32)
+    ad.patch_model()
+    ctx = ad.blocks[0].parallel
+    assert ctx is not None and all(b.parallel is ctx for b in ad.blocks)
+    assert (ctx.world, ctx.rank, ctx.threshold) == (2, 1, 32)
+    assert ha.Qwen15MoEAdapter(_hf_tiny()).parallel is None
