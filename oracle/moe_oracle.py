@@ -150,11 +150,16 @@ def dequantize_channel(q: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
 
 
 # --------------------------------------------------------------------------- experts + merge
-def swiglu_expert(x: torch.Tensor, gate: torch.Tensor, up: torch.Tensor, down: torch.Tensor) -> torch.Tensor:
+def swiglu_expert(x: torch.Tensor, gate: torch.Tensor, up: torch.Tensor, down: torch.Tensor,
+                  *, round_intermediate: bool = False) -> torch.Tensor:
     """down(silu(gate x) * up x) in fp32 (the Qwen expert MLP the reference calls
-    as ``module(x)``, DWDP/executor/pytorch.py:369-382)."""
+    as ``module(x)``, DWDP/executor/pytorch.py:369-382). ``round_intermediate`` rounds the
+    SwiGLU product to bf16 before the down projection, as a bf16 execution does."""
     x = x.float()
-    return (torch.nn.functional.silu(x @ gate.float().T) * (x @ up.float().T)) @ down.float().T
+    h = torch.nn.functional.silu(x @ gate.float().T) * (x @ up.float().T)
+    if round_intermediate:
+        h = h.bfloat16().float()
+    return h @ down.float().T
 
 
 def moe_forward(
@@ -165,11 +170,14 @@ def moe_forward(
     *,
     shared: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None,
     shared_gate: torch.Tensor | None = None,
+    bf16_roundings: bool = False,
 ) -> torch.Tensor:
     """Routed experts in ascending expert order over the expert-major packing,
     weighted rows accumulated token-major (PyTorchExecutor + PyTorchMerger,
     DWDP/executor/pytorch.py:66-160, DWDP/merger/kernels/reference.py:6-27), then
-    ``out += gate * shared(x)`` (DWDP/adapters/qwen15_moe.py:302-319). fp32."""
+    ``out += gate * shared(x)`` (DWDP/adapters/qwen15_moe.py:302-319). fp32 arithmetic;
+    ``bf16_roundings`` applies the three roundings of a bf16 data path (SwiGLU intermediate,
+    each weighted expert row, the output) so that only accumulation order differs."""
     x = x.float()
     T, H = x.shape
     K = topk_idx.shape[-1]
@@ -182,14 +190,18 @@ def moe_forward(
             continue
         tok = torch.from_numpy(plan["tok"][s:t])
         w = torch.from_numpy(np.ascontiguousarray(plan["weights"][s:t])).float()
-        y = swiglu_expert(x[tok], *experts[e]) * w[:, None]
+        y = swiglu_expert(x[tok], *experts[e], round_intermediate=bf16_roundings) * w[:, None]
+        if bf16_roundings:
+            y = y.bfloat16().float()
         out.index_add_(0, tok, y)
     if shared is not None:
-        ys = swiglu_expert(x, *shared)
+        ys = swiglu_expert(x, *shared, round_intermediate=bf16_roundings)
         if shared_gate is not None:
             ys = ys * shared_gate.float().reshape(-1, 1)
+        if bf16_roundings:
+            ys = ys.bfloat16().float()
         out = out + ys
-    return out
+    return out.bfloat16().float() if bf16_roundings else out
 
 
 def rel_frobenius(a: torch.Tensor, b: torch.Tensor) -> float:
