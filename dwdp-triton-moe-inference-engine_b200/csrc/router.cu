@@ -226,7 +226,6 @@ router_logits_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat1
 // bf16 are exact in fp32; the per-warp partials are summed through shared
 // memory in a fixed order (deterministic).
 // ---------------------------------------------------------------------------
-constexpr int kFusedWarps = 16;
 constexpr int kFusedPass = 64;  // expert rows per pass
 constexpr int kFusedMaxRows = 257;
 
@@ -296,7 +295,10 @@ __device__ __forceinline__ void topk_warp(const float* lr, int E, int K, int ren
   }
 }
 
-__global__ void __launch_bounds__(kFusedWarps * 32, 1)
+// kFusedWarps = 16 at decode sizes (one CTA per SM, the most warps per token tile); 8 when the
+// token tiles alone cover the SMs (two CTAs per SM: the T = 4096 grid resident in one wave).
+template <int kFusedWarps>
+__global__ void __launch_bounds__(kFusedWarps * 32, 16 / kFusedWarps)
 router_fused_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                     const float* __restrict__ bias, const __nv_bfloat16* __restrict__ gate_w, int T, int H,
                     int E, int K, float score_scale, int renorm, float eps, float* __restrict__ logits,
@@ -390,17 +392,17 @@ router_fused_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __
     if (rank != 0) return;
   }
   // one warp per token: top-k, softmax over k, renormalisation, sigmoid shared gate
-  if (warp < 16) {
-    const int tok = tok0 + warp;
+  for (int tt = warp; tt < 16; tt += kFusedWarps) {
+    const int tok = tok0 + tt;
     if (tok < T) {
-      const float* lr = lg + warp * kFusedMaxRows;
+      const float* lr = lg + tt * kFusedMaxRows;
       topk_warp(lr, E, K, renorm, eps, tok, probs, idx_out, w_out);
       if (lane == 0 && gate_w != nullptr) shared_gate[tok] = 1.0f / (1.0f + expf(-lr[E]));
     }
   }
 }
 
-constexpr size_t kFusedSmem = (size_t)(kFusedWarps * 16 * kFusedPass + 16 * kFusedMaxRows) * sizeof(float);
+constexpr size_t fused_smem(int warps) { return (size_t)(warps * 16 * kFusedPass + 16 * kFusedMaxRows) * sizeof(float); }
 
 // Top-k + softmax over the k selected + renormalisation: one warp per token.
 __global__ void __launch_bounds__(kRouterThreads)
@@ -455,19 +457,21 @@ extern "C" int dwdp_router_launch(const void* hidden, int hidden_dtype, const vo
   } while (0)
   if (hidden_dtype == DWDP_DTYPE_BF16 && weight_dtype == DWDP_DTYPE_BF16 && H % 32 == 0 && E <= 256 &&
       K <= 16) {
-    if (cudaFuncSetAttribute(router_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kFusedSmem) != cudaSuccess)
-      return DWDP_ERR_CUDA;
     // expert slices per token tile: enough CTAs to cover the SMs at decode sizes
     const int64_t tiles = (T + 15) / 16;
+    const bool wide_grid = tiles >= 148;  // prefill: 8-warp CTAs, two per SM
+    auto kfn = wide_grid ? router_fused_kernel<8> : router_fused_kernel<16>;
+    const size_t smem = fused_smem(wide_grid ? 8 : 16);
+    if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return DWDP_ERR_CUDA;
     int G = 1;
     while (G < 8 && tiles * G < 148 && G * 8 < rows) G *= 2;
     if (const char* v = getenv("DWDP_ROUTER_G")) {  // tuning override: cluster size 1, 2, 4 or 8
       const int g = atoi(v);
       if (g == 1 || g == 2 || g == 4 || g == 8) G = g;
     }
-    if (launch_chained(router_fused_kernel, dim3((unsigned)tiles, (unsigned)G, 1), dim3(kFusedWarps * 32, 1, 1),
-                       kFusedSmem, stream, (unsigned)G, (const __nv_bfloat16*)hidden,
+    if (launch_chained(kfn, dim3((unsigned)tiles, (unsigned)G, 1), dim3((wide_grid ? 8 : 16) * 32, 1, 1),
+                       smem, stream, (unsigned)G, (const __nv_bfloat16*)hidden,
                        (const __nv_bfloat16*)weight, bias, (const __nv_bfloat16*)shared_gate_weight, (int)T, H, E, K,
                        score_scale, renorm, eps, logits, probs, idx, topk_w, shared_gate) != cudaSuccess)
       return DWDP_ERR_CUDA;

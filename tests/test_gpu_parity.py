@@ -86,7 +86,7 @@ def test_dispatch_out_of_range_records_status(pkg):
 
 
 @pytest.mark.parametrize("T,E,K,H", [(1, 60, 4, 2048), (64, 60, 4, 2048), (257, 8, 2, 512),
-                                     (100, 256, 8, 384)])
+                                     (100, 256, 8, 384), (4096, 60, 4, 2048)])  # 4096: the 8-warp grid
 def test_router(pkg, orc, T, E, K, H):
     g = torch.Generator().manual_seed(T + E)
     x = torch.randn(T, H, generator=g).bfloat16()
