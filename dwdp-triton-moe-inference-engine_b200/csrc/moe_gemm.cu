@@ -976,6 +976,60 @@ __device__ __forceinline__ void quant_row_warp(const QuantSeg& g, int row, Devic
   if (lane == 0) g.scale[row] = amax > 0.f ? amax / 448.0f : 0.f;
 }
 
+// As quant_row_warp for rows whose width is a multiple of 16: a lane takes 16 consecutive
+// elements per step (two 16-byte loads, one 16-byte store per plane) instead of 8.
+__device__ __forceinline__ void quant_row_warp16(const QuantSeg& g, int row, DeviceStatus* st) {
+  const int lane = threadIdx.x & 31;
+  int64_t sr = row;
+  if (g.row_index != nullptr) {
+    sr = g.row_index[row];
+    if (sr < 0 || sr >= g.src_rows) {
+      if (lane == 0) record_error(st, DWDP_ERR_DEVICE_BOUNDS, 212, row);
+      sr = -1;
+    }
+  }
+  const __nv_bfloat16* src = sr >= 0 ? g.src + (size_t)sr * g.K : nullptr;
+  const int K = src != nullptr ? g.K : 0;
+  constexpr int kP = 4;  // 16-element steps kept in registers (rows up to 2048)
+  uint4 v[2 * kP];
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < kP; ++j) {
+    const int c = (j * 32 + lane) * 16;
+    v[2 * j] = c < K ? *reinterpret_cast<const uint4*>(src + c) : make_uint4(0, 0, 0, 0);
+    v[2 * j + 1] = c < K ? *reinterpret_cast<const uint4*>(src + c + 8) : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int j = 0; j < 2 * kP; ++j) amax = amax8(v[j], amax);
+  for (int c = (kP * 32 + lane) * 16; c < K; c += 512) {
+    amax = amax8(*reinterpret_cast<const uint4*>(src + c), amax);
+    amax = amax8(*reinterpret_cast<const uint4*>(src + c + 8), amax);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float inv = amax > 0.f ? 448.0f / amax : 0.f;
+  uint8_t* hi = g.dst + (size_t)(2 * row) * g.K;
+  uint8_t* lo = hi + g.K;
+  auto put = [&](const uint4 a, const uint4 b, int c) {
+    uint2 ha, la, hb, lb;
+    quant8(a, inv, ha, la);
+    quant8(b, inv, hb, lb);
+    *reinterpret_cast<uint4*>(hi + c) = make_uint4(ha.x, ha.y, hb.x, hb.y);
+    *reinterpret_cast<uint4*>(lo + c) = make_uint4(la.x, la.y, lb.x, lb.y);
+  };
+#pragma unroll
+  for (int j = 0; j < kP; ++j) {
+    const int c = (j * 32 + lane) * 16;
+    if (c < g.K) put(v[2 * j], v[2 * j + 1], c);
+  }
+  for (int c = (kP * 32 + lane) * 16; c < g.K; c += 512) {
+    const uint4 a = K > 0 ? *reinterpret_cast<const uint4*>(src + c) : make_uint4(0, 0, 0, 0);
+    const uint4 b = K > 0 ? *reinterpret_cast<const uint4*>(src + c + 8) : make_uint4(0, 0, 0, 0);
+    put(a, b, c);
+  }
+  if (lane == 0) g.scale[row] = amax > 0.f ? amax / 448.0f : 0.f;
+}
+
 // Rows of both segments, one per `first + i * stride` unit (a warp or a CTA).
 __device__ __forceinline__ void quant_rows(const QuantParams& q, int block, int nblocks) {
   __shared__ float red[kPlanThreads / 32];
@@ -983,8 +1037,10 @@ __device__ __forceinline__ void quant_rows(const QuantParams& q, int block, int 
   if (q.per_warp) {
     constexpr int kW = kPlanThreads / 32;
     for (int r = block * kW + (int)(threadIdx.x >> 5); r < total; r += nblocks * kW) {
-      if (r < q.seg[0].rows) quant_row_warp(q.seg[0], r, q.st);
-      else quant_row_warp(q.seg[1], r - q.seg[0].rows, q.st);
+      const QuantSeg& sg = r < q.seg[0].rows ? q.seg[0] : q.seg[1];
+      const int rr = r < q.seg[0].rows ? r : r - q.seg[0].rows;
+      if (sg.K % 16 == 0) quant_row_warp16(sg, rr, q.st);
+      else quant_row_warp(sg, rr, q.st);
     }
     return;
   }
