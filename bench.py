@@ -35,6 +35,10 @@ sys.path.insert(0, str(ROOT))
 METRIC = "MoE-layer tokens/s (Qwen1.5-MoE-A2.7B shape)"
 QWEN = dict(H=2048, E=60, I=1408, K=4, Is=5632)
 DECODE_SWEEP = [1, 8, 32, 64]
+# The FP8 computation bench.py times: activations quantised to one e4m3 plane per
+# (token, 128 channels) and the SwiGLU intermediate re-quantised the same way, the
+# reference's FP8 executor math (DWDP/executor/fp8.py:86-115, triton_tma.py:185-207).
+ACTIVATION_QUANT = "block128"
 
 
 def _peaks() -> dict:
@@ -53,7 +57,8 @@ def _expert_weights(layer_seed: int, e: int, device, H: int, I: int):
             torch.randn(H, I, generator=g, device=device) * 0.02)
 
 
-def make_qwen_layer(pkg, device, seed: int = 1235, *, rank: int = 0, world: int = 1):
+def make_qwen_layer(pkg, device, seed: int = 1235, *, rank: int = 0, world: int = 1,
+                    activation_quant: str | None = None):
     """Random-init Qwen-shaped layer: router W ~ N(0, 1/H) (logits ~ N(0,1)),
     experts ~ N(0, 0.02) quantised to FP8 E4M3 with per-expert per-output-channel
     scales, shared expert Is=5632 with sigmoid gate g ~ N(0, 0.02). With
@@ -82,7 +87,8 @@ def make_qwen_layer(pkg, device, seed: int = 1235, *, rank: int = 0, world: int 
     gate = (torch.randn(H, generator=g, device=device) * 0.02).bfloat16()
     if world > 1:
         store.connect()
-    return pkg.MoELayer(wr, store, K, shared_expert=shared, shared_gate_weight=gate)
+    return pkg.MoELayer(wr, store, K, shared_expert=shared, shared_gate_weight=gate,
+                        activation_quant=activation_quant or ACTIVATION_QUANT)
 
 
 def make_inputs(T: int, device, seed: int) -> torch.Tensor:

@@ -31,6 +31,10 @@ DTYPE_F32 = 4
 SCALE_NONE = 0
 SCALE_CHANNEL = 1
 SCALE_BLOCK128 = 2
+SCALE_TENSOR = 3
+
+ACT_HILO = 0
+ACT_BLOCK128 = 1
 
 c_void_p = ctypes.c_void_p
 c_int = ctypes.c_int
@@ -52,6 +56,7 @@ class ExpertGroup(ctypes.Structure):
         ("w2", c_void_p),
         ("s13", c_void_p),
         ("s2", c_void_p),
+        ("act_quant", c_int),
     ]
 
 
@@ -79,6 +84,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p],
     ),
     "dwdp_dispatch_noalloc_max_scratch_bytes": (c_size_t, []),
+    "dwdp_quantize_activations_blockwise": (
+        c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p]
+    ),
     "dwdp_gather_rows": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int64, c_void_p, c_void_p, c_void_p]),
     "dwdp_ep_buffer_bytes": (c_size_t, [c_int, c_int, c_int]),
     "dwdp_ep_ret_offset": (c_size_t, [c_int, c_int, c_int]),

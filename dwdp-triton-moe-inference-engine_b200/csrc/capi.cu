@@ -21,6 +21,8 @@ extern "C" size_t dwdp_dispatch_noalloc_max_scratch_bytes(void);
 extern "C" int dwdp_gather_rows_launch(const void*, const int64_t*, int64_t, int, int64_t, void*, int*,
                                        cudaStream_t);
 extern "C" size_t dwdp_dispatch_scratch_bytes(int64_t, int, int);
+extern "C" int dwdp_quantize_activations_launch(const void*, int64_t, const int64_t*, int64_t, int, void*, float*,
+                                                int, int*, cudaStream_t);
 extern "C" int dwdp_schedule_launch(const int64_t*, const int64_t*, int, int, int64_t*, int64_t*,
                                     int64_t*, int64_t*, int64_t*, int64_t*, int64_t*, cudaStream_t);
 extern "C" int dwdp_pack_launch(const void* const*, int, int, int, int, int, int, void*, float*,
@@ -182,6 +184,23 @@ extern "C" int dwdp_gather_rows(const void* hidden, const int64_t* token_index, 
                "gather_rows");
 }
 
+extern "C" int dwdp_quantize_activations_blockwise(const void* src, int64_t src_rows, const int64_t* row_index,
+                                                   int64_t rows, int cols, void* dst, float* scales,
+                                                   int scale_layout, int* status, void* stream) {
+  g_last_error.clear();
+  if (rows < 0 || src_rows < 0 || cols <= 0 || cols % 128 != 0 || rows > INT32_MAX)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "quantize_activations: rows >= 0 and cols a positive multiple of 128");
+  if (scale_layout != 0 && scale_layout != 1)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "quantize_activations: scale_layout must be 0 or 1");
+  if (row_index == nullptr && rows > src_rows)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "quantize_activations: more rows than the source holds");
+  if (rows > 0 && (src == nullptr || dst == nullptr || scales == nullptr))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "quantize_activations: null pointer");
+  return check(dwdp_quantize_activations_launch(src, src_rows, row_index, rows, cols, dst, scales,
+                                                scale_layout == 0 ? 1 : 0, status, as_stream(stream)),
+               "quantize_activations");
+}
+
 extern "C" int dwdp_schedule(const int64_t* counts, const int64_t* offsets, int num_experts,
                              int stream_count, int64_t* expert_queue, int64_t* starts, int64_t* ends,
                              int64_t* active_counts, int64_t* priority, int64_t* stream_ids,
@@ -236,8 +255,10 @@ int moe_experts_checked(const dwdp_expert_group* routed, const dwdp_expert_group
       (shared && (shared->intermediate_size <= 0 || shared->intermediate_size % 128)))
     return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_experts: hidden/intermediate sizes must be multiples of 128");
   if (routed->weight_dtype == DWDP_DTYPE_FP8_E4M3 && routed->scale_mode != DWDP_SCALE_CHANNEL &&
-      routed->scale_mode != DWDP_SCALE_BLOCK128)
-    return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_experts: fp8 weights need a CHANNEL or BLOCK128 scale mode");
+      routed->scale_mode != DWDP_SCALE_BLOCK128 && routed->scale_mode != DWDP_SCALE_TENSOR)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_experts: fp8 weights need a CHANNEL, BLOCK128 or TENSOR scale mode");
+  if (routed->act_quant != DWDP_ACT_HILO && routed->act_quant != DWDP_ACT_BLOCK128)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_experts: act_quant must be DWDP_ACT_HILO or DWDP_ACT_BLOCK128");
   if (shared != nullptr && (shared->num_experts != 1 || shared->hidden_size != routed->hidden_size ||
                             shared->weight_dtype != routed->weight_dtype ||
                             shared->scale_mode != routed->scale_mode))

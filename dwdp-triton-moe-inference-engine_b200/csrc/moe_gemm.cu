@@ -1,8 +1,9 @@
 // Grouped expert GEMMs on tcgen05 (sm_100a): the executor hot path.
 //
 // Replaces the per-expert loop of DWDP/executor/pytorch.py:66-160 (gather,
-// down(silu(gate(x)) * up(x)), times routing weight) and the Triton persistent
-// kernels of DWDP/executor/kernels/persistent.py:241-401 / fp8.py:147-318.
+// down(silu(gate(x)) * up(x)), times routing weight), the Triton persistent
+// kernels of DWDP/executor/kernels/persistent.py:241-401 / fp8.py:147-318 and the
+// block-scaled FP8 executor of DWDP/executor/triton_tma.py:115-261.
 //
 // Orientation ("swap AB"): the weight rows of one 128-row block are the MMA M
 // dimension (TMEM lanes), the tokens of one expert tile are the MMA N dimension
@@ -11,21 +12,23 @@
 // per-thread constant, and a decode step with one token per expert still fills
 // the 128-row MMA with weights.
 //
-// Two launches per layer:
+// Two GEMM launches per layer, after a planning launch:
 //   MODE 0  gate/up: acc_g, acc_u [128 feat x N tok] in TMEM (two MMAs sharing
-//           the activation tile), epilogue h = silu(g) * u -> bf16 h[row, feat]
+//           the activation tile), epilogue h = silu(g) * u
 //   MODE 1  down   : acc [128 out x N tok], epilogue y * row_scale -> bf16 out
 //
-// Warp roles (one CTA per SM, persistent over a device-built work list):
-//   warp 0      producer: one cp.async.bulk for the pre-tiled weight block(s)
-//               + one TMA tile load of the activations per 64-wide K step
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2-5   epilogue (TMEM lane quadrant = warp % 4), double-buffered acc
-//   warps 6-13  (FP8 weights only) converter: e4m3 x scale -> bf16 into the
-//               128B-swizzled operand image, then fence.proxy.async
-// FP8 weights are multiplied as bf16 (e4m3 is exact in bf16; the fp32 scale is
-// folded in with one rounding), so activations stay bf16: quantising them to
-// e4m3 costs ~4.5% relative error, over the 2e-2 parity bar.
+// Three kernel families (warp 0 producer, warp 1 TMEM allocator + single-thread
+// MMA issuer, the rest epilogue; one CTA per SM, persistent over a device-built
+// work list):
+//   moe_gemm_kernel      bf16 weights, kind::f16 MMAs on bf16 activations.
+//   moe_gemm_f8_kernel   e4m3 weights with per-row (channel / tensor) scales and
+//                        hi/lo e4m3 activation planes (DWDP_ACT_HILO): kind::f8f6f4
+//                        MMAs, scales applied once in the epilogue.
+//   moe_gemm_f8p_kernel  e4m3 weights of any scale mode against activations whose
+//                        scale changes every 128 inputs (DWDP_ACT_BLOCK128, or
+//                        128x128 block-scaled weights): every 128-wide K block
+//                        accumulates into its own TMEM slot and the epilogue warps
+//                        promote it into fp32 registers with its scales.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -59,8 +62,7 @@ constexpr int BM = 128;                    // weight rows per tile (MMA M)
 constexpr int BK = 64;                     // K elements per pipeline stage (128 bytes of bf16)
 constexpr int BN_MAX = 128;                // max tokens per tile (MMA N)
 constexpr int kBTileBytes = BN_MAX * 128;  // activation tile: BN_MAX rows x 128 B
-constexpr int kConvTileBytes = BM * 128;   // bf16 weight tile 128 x 64
-constexpr int kFp8TileBytes = BM * BK;     // fp8 weight tile 128 x 64
+constexpr int kBf16TileBytes = BM * 128;   // bf16 weight tile 128 x 64
 
 struct WorkItem {
   int group;     // 0 routed, 1 shared
@@ -68,7 +70,7 @@ struct WorkItem {
   int rb;        // 128-row weight block
   int row0;      // first activation row of the tile
   int nrows;     // rows in this tile (<= BN_MAX)
-  int kb_begin;  // first / one-past-last 64-wide K step of this item (split K)
+  int kb_begin;  // first / one-past-last K step of this item (split K)
   int kb_end;
   int part;      // K-split index: output goes to out + part * part_stride
   int nmat;      // weight matrices of the item: gate+up (2), or 1-2 consecutive down row blocks
@@ -77,12 +79,13 @@ struct WorkItem {
 };
 
 struct GroupParams {
-  CUtensorMap tmap_b;      // activations [rows, K] bf16, box {64, BN_MAX}, 128B swizzle
+  CUtensorMap tmap_b;      // activations (bf16 rows, hi/lo planes or one e4m3 plane)
   const void* const* w;    // [E] packed weight tiles
   const float* const* s;   // [E] scales (fp8) or nullptr
-  void* out;               // bf16 [rows, R]
+  void* out;               // bf16 [rows, R]; e4m3 [rows, R] for the BLOCK128 gate/up epilogue
+  float* out_scale;        // BLOCK128 gate/up: scales of `out`, [R / 128][os_ld]
   const float* row_scale;  // MODE 1: per-row multiplier (routing weight / shared gate) or null
-  const float* x_scale;    // e4m3 activation planes only: per-row activation scale
+  const float* x_scale;    // hi/lo: per-row activation scale; BLOCK128: [K / 128][xs_ld]
   int K;                   // reduction size
   int R;                   // output rows of the projection (= out leading dim)
   int scale_mode;
@@ -91,6 +94,8 @@ struct GroupParams {
   long long part_stride;   // elements between K-split partial outputs
   long long mstride;       // e4m3 path: bytes between an item's weight matrices
   long long kstride;       // e4m3 path: bytes between an item's 128-input stages
+  long long xs_ld;         // BLOCK128: leading dimension of x_scale (activation rows)
+  long long os_ld;         // BLOCK128: leading dimension of out_scale
 };
 
 struct GemmParams {
@@ -101,73 +106,37 @@ struct GemmParams {
   DeviceStatus* st;
 };
 
-template <int MODE, bool WFP8>
+__host__ __device__ inline bool per_row_scales(int mode) {
+  return mode == DWDP_SCALE_CHANNEL || mode == DWDP_SCALE_TENSOR;
+}
+
+template <int MODE>
 struct Cfg {
   static constexpr int NMAT = MODE == 0 ? 2 : 1;
   static constexpr int S = MODE == 0 ? 4 : 6;  // load stages
-  static constexpr int CONV_GROUPS = 2;        // independent converter warp groups
-  static constexpr int SC = WFP8 ? CONV_GROUPS : 0;  // converted-weight slots (one per group)
-  static constexpr int W_STAGE_BYTES = NMAT * (WFP8 ? kFp8TileBytes : kConvTileBytes);
-  static constexpr int CONV_STAGE_BYTES = NMAT * kConvTileBytes;
-  static constexpr int NUM_WARPS = WFP8 ? 14 : 6;
+  static constexpr int W_STAGE_BYTES = NMAT * kBf16TileBytes;
+  static constexpr int NUM_WARPS = 6;
   static constexpr int THREADS = NUM_WARPS * 32;
-  static constexpr int CONV_THREADS = 256;
   static constexpr int TMEM_COLS = NMAT * BN_MAX * 2 <= 256 ? 256 : 512;
   static constexpr int ACC_STRIDE = NMAT * BN_MAX;  // TMEM columns per accumulator buffer
   static constexpr int SMEM_B = S * kBTileBytes;
   static constexpr int SMEM_W = S * W_STAGE_BYTES;
-  static constexpr int SMEM_C = SC * CONV_STAGE_BYTES;
-  static constexpr int SMEM_BYTES = SMEM_B + SMEM_W + SMEM_C + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM_BYTES = SMEM_B + SMEM_W + 1024 /*align*/ + 256 /*barriers*/;
 };
 
-// 16 e4m3 values of row r, elements [sub*16, sub*16+16) -> 32 bytes of bf16
-// written to their 128B-swizzled positions.
-// Four e4m3 bytes -> four bf16 (two words); exact unless `scaled` folds a block
-// scale in (one rounding).
-__device__ __forceinline__ void e4m3x4_to_bf16x4(uint32_t w, float s, bool scaled, uint32_t& o0, uint32_t& o1) {
-  uint32_t out[2];
-#pragma unroll
-  for (int hlf = 0; hlf < 2; ++hlf) {
-    const __nv_fp8x2_storage_t pair = (__nv_fp8x2_storage_t)((w >> (16 * hlf)) & 0xFFFFu);
-    const __half2_raw h2 = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
-    const __nv_bfloat162 bv = scaled ? __floats2bfloat162_rn(f.x * s, f.y * s) : __floats2bfloat162_rn(f.x, f.y);
-    out[hlf] = *reinterpret_cast<const uint32_t*>(&bv);
-  }
-  o0 = out[0];
-  o1 = out[1];
-}
-
-// One 16-byte chunk (16 e4m3 of row r, elements [sub*16, sub*16+16)) -> 32 bytes
-// of bf16 at their 128B-swizzled positions in the converted tile.
-__device__ __forceinline__ void convert_chunk(const uint4 raw, uint8_t* conv_tile, int r, int sub, float s,
-                                              bool scaled) {
-  uint32_t o[8];
-  e4m3x4_to_bf16x4(raw.x, s, scaled, o[0], o[1]);
-  e4m3x4_to_bf16x4(raw.y, s, scaled, o[2], o[3]);
-  e4m3x4_to_bf16x4(raw.z, s, scaled, o[4], o[5]);
-  e4m3x4_to_bf16x4(raw.w, s, scaled, o[6], o[7]);
-  const int c0 = sub * 2;  // 16-byte chunk index of the first 8 elements
-  uint8_t* row = conv_tile + r * 128;
-  *reinterpret_cast<uint4*>(row + ((c0 ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-  *reinterpret_cast<uint4*>(row + (((c0 + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
-}
-
-template <int MODE, bool WFP8>
-__global__ void __launch_bounds__(Cfg<MODE, WFP8>::THREADS, 1)
+// bf16 weights: kind::f16 MMAs on bf16 activation rows (TMA box {64, BN_MAX}).
+template <int MODE>
+__global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
 moe_gemm_kernel(const __grid_constant__ GemmParams p) {
-  using C = Cfg<MODE, WFP8>;
+  using C = Cfg<MODE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sB = smem;
   uint8_t* sW = sB + C::SMEM_B;
-  uint8_t* sC = sW + C::SMEM_W;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sC + C::SMEM_C);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + C::SMEM_W);
   uint64_t* ld_full = bars;
   uint64_t* ld_empty = ld_full + C::S;
-  uint64_t* cv_full = ld_empty + C::S;
-  uint64_t* cv_empty = cv_full + 2;
-  uint64_t* acc_full = cv_empty + 2;
+  uint64_t* acc_full = ld_empty + C::S;
   uint64_t* acc_empty = acc_full + 2;
   __shared__ uint32_t s_tmem_base;
   __shared__ volatile int s_abort;
@@ -181,11 +150,9 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
     s_abort = 0;
     for (int i = 0; i < C::S; ++i) {
       mbar_init(&ld_full[i], 1);
-      mbar_init(&ld_empty[i], WFP8 ? 2 : 1);
+      mbar_init(&ld_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&cv_full[i], 1);
-      mbar_init(&cv_empty[i], 1);
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 128);
     }
@@ -233,7 +200,7 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       PROF_DECL PROF_START
-      uint32_t it = 0, cit = 0;
+      uint32_t it = 0;
       int li = 0;
       WorkItem wn = p.items[blockIdx.x];  // fetched with n_items; the next one is prefetched
       for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++li) {
@@ -249,43 +216,30 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
         for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
           const int s = it % C::S;
           if (!TW(1, mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 3 + 8 * MODE))) { ok = false; break; }
-          const uint8_t* wtile;
-          int c = 0;
-          if constexpr (WFP8) {
-            c = cit % C::SC;
-            if (!TW(2, mbar_wait(&cv_full[c], (cit / C::SC) & 1, &s_abort, st, 4 + 8 * MODE))) { ok = false; break; }
-            wtile = sC + c * C::CONV_STAGE_BYTES;
-          } else {
-            wtile = sW + s * C::W_STAGE_BYTES;
-          }
           tc_fence_after();
           // Descriptors are built once per stage; a K step of 16 bf16 (32 bytes) is +2 in
-          // the encoded start address, the second weight matrix is +kConvTileBytes/16.
+          // the encoded start address, the second weight matrix is +kBf16TileBytes/16.
           const uint64_t b_desc0 = smem_desc_sw128(smem_u32(sB + s * kBTileBytes));
-          const uint64_t a_desc0 = smem_desc_sw128(smem_u32(wtile));
+          const uint64_t a_desc0 = smem_desc_sw128(smem_u32(sW + s * C::W_STAGE_BYTES));
           const uint32_t acc_first = kb > wi.kb_begin ? 1u : 0u;
           PROF_T0
 #pragma unroll
           for (int m = 0; m < C::NMAT; ++m) {
 #pragma unroll
             for (int kk = 0; kk < BK / 16; ++kk) {
-              mma_bf16_ss(d_base + m * BN_MAX, a_desc0 + (uint64_t)(m * (kConvTileBytes >> 4) + 2 * kk),
+              mma_bf16_ss(d_base + m * BN_MAX, a_desc0 + (uint64_t)(m * (kBf16TileBytes >> 4) + 2 * kk),
                           b_desc0 + (uint64_t)(2 * kk), idesc, kk > 0 ? 1u : acc_first);
             }
           }
           PROF_ADD(3)
           mma_commit(&ld_empty[s]);
-          if constexpr (WFP8) {
-            mma_commit(&cv_empty[c]);
-            ++cit;
-          }
         }
         if (!ok) break;
         mma_commit(&acc_full[a]);
       }
       PROF_END(7) PROF_STORE(4)
     }
-  } else if (warp < 6) {
+  } else {
     // ------------------------------------------------------------ epilogue
     PROF_DECL PROF_START
     const int quad = warp & 3;
@@ -299,12 +253,6 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
       const int a = li & 1;
       const int feat = wi.rb * BM + lrow;
       __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)wi.part * g.part_stride;
-      // per-output-channel weight scales are exact per-thread constants here (loaded while the MMAs run)
-      float s0 = 1.0f, s1 = 1.0f;
-      if (WFP8 && g.scale_mode == DWDP_SCALE_CHANNEL) {
-        s0 = wi.scales[feat];
-        if (MODE == 0) s1 = wi.scales[g.R + feat];
-      }
       if (!TW(0, mbar_wait(&acc_full[a], (li >> 1) & 1, &s_abort, st, 5 + 8 * MODE))) break;
       tc_fence_after();
       const uint32_t t_acc = tmem_base + a * C::ACC_STRIDE + ((uint32_t)(quad * 32) << 16);
@@ -318,7 +266,7 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
           for (int j = 0; j < 16; ++j) {
             const int col = c0 + j;
             if (col < wi.nrows) {
-              const float h = silu(gv[j] * s0) * (uv[j] * s1);
+              const float h = silu(gv[j]) * uv[j];
               out[(size_t)(wi.row0 + col) * g.R + feat] = __float2bfloat16_rn(h);
             }
           }
@@ -332,7 +280,7 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
             if (col < wi.nrows) {
               const int row = wi.row0 + col;
               const float sc = g.row_scale != nullptr ? g.row_scale[row] : 1.0f;
-              out[(size_t)row * g.R + feat] = __float2bfloat16_rn(yv[j] * s0 * sc);
+              out[(size_t)row * g.R + feat] = __float2bfloat16_rn(yv[j] * sc);
             }
           }
         }
@@ -341,64 +289,6 @@ moe_gemm_kernel(const __grid_constant__ GemmParams p) {
       mbar_arrive(&acc_empty[a]);
     }
     PROF_END(7) if (lane == 0 && quad == 0) PROF_STORE(8)
-  } else if constexpr (WFP8) {
-    // ------------------------------------------------------------ converter (fp8 -> bf16)
-    // CHANNEL scales are applied in the epilogue, so the conversion is exact
-    // (e4m3 values are representable in bf16); BLOCK128 scales vary with K and
-    // are folded in here with one rounding.
-    // The converter warps form C::CONV_GROUPS independent groups; group g converts
-    // the stages with index % CONV_GROUPS == g into conversion slot g, so several
-    // stages convert at once (conversion is latency-, not throughput-bound).
-    PROF_DECL PROF_START
-    const int ct = threadIdx.x - 6 * 32;  // 0..255
-    constexpr int kGroupThreads = C::CONV_THREADS / C::CONV_GROUPS;
-    const int grp = ct / kGroupThreads, gt = ct % kGroupThreads;
-    uint32_t it = 0, cit = 0;
-    WorkItem wn = p.items[blockIdx.x];  // fetched with n_items; the next one is prefetched
-    for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
-      const WorkItem wi = wn;
-      if (item + (int)gridDim.x < p.cap) wn = p.items[item + gridDim.x];
-      const GroupParams& g = p.g[wi.group];
-      const bool block_scaled = g.scale_mode == DWDP_SCALE_BLOCK128;
-      const float* sc = wi.scales;
-      bool ok = true;
-      for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it, ++cit) {
-        if ((int)(cit % C::CONV_GROUPS) != grp) continue;
-        const int s = it % C::S;
-        const int c = cit % C::SC;
-        float sblk[C::NMAT];
-#pragma unroll
-        for (int m = 0; m < C::NMAT; ++m)
-          sblk[m] = block_scaled ? sc[((size_t)m * (g.R / 128) + wi.rb) * (g.K / 128) + (kb >> 1)] : 1.0f;
-        if (!TW(0, mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 6 + 8 * MODE))) { ok = false; break; }
-        if (!TW(1, mbar_wait(&cv_empty[c], ((cit / C::SC) & 1) ^ 1, &s_abort, st, 7 + 8 * MODE))) { ok = false; break; }
-        const uint8_t* raw = sW + s * C::W_STAGE_BYTES;
-        uint8_t* conv = sC + c * C::CONV_STAGE_BYTES;
-        constexpr int kChunks = C::NMAT * kFp8TileBytes / 16;  // 16-byte chunks per stage
-        constexpr int kPer = kChunks / kGroupThreads;          // chunks per converter thread
-        uint4 rawv[kPer];
-#pragma unroll
-        for (int j = 0; j < kPer; ++j) {  // issue every shared load first
-          const int q = gt + j * kGroupThreads;
-          const int m = q / (kFp8TileBytes / 16), rem = q % (kFp8TileBytes / 16);
-          rawv[j] = *reinterpret_cast<const uint4*>(raw + m * kFp8TileBytes + (rem >> 2) * BK + (rem & 3) * 16);
-        }
-#pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-          const int q = gt + j * kGroupThreads;
-          const int m = q / (kFp8TileBytes / 16), rem = q % (kFp8TileBytes / 16);
-          convert_chunk(rawv[j], conv + m * kConvTileBytes, rem >> 2, rem & 3, sblk[m], block_scaled);
-        }
-        fence_proxy_async_smem();
-        named_bar_sync(1 + grp, kGroupThreads);
-        if (gt == 0) {
-          mbar_arrive(&cv_full[c]);
-          mbar_arrive(&ld_empty[s]);
-        }
-      }
-      if (!ok) break;
-    }
-    PROF_END(7) if (ct == 0) PROF_STORE(12)
   }
 
   tc_fence_before();
@@ -662,6 +552,374 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
 }
 
 // ---------------------------------------------------------------------------
+// e4m3 tensor-core path with per-128-K-block promotion.
+//
+// Used when the product's scale changes along K every 128 inputs: activations
+// quantised per (row, 128 channels) (DWDP_ACT_BLOCK128, the reference's FP8
+// scheme, DWDP/executor/fp8.py:86-115) and/or weights with 128x128 block scales
+// (DWDP/executor/fp8.py:118-146). The reference's kernel applies the scales to
+// its fp32 accumulator once per K block (DWDP/executor/kernels/fp8_tma.py:104-119):
+//   C = sum_kb (Xq Wq^T)_kb * sx[row, kb] * sw[nb, kb]
+// Here every 128-wide K block of an item is multiplied into its own TMEM slot
+// (a ring of NSLOT slots, so the tensor core runs up to NSLOT blocks ahead) and
+// the epilogue warps fold it into fp32 registers:
+//   acc[m][t] += slot[m][t] * (sx[t][kb] * sw[m][kb])
+// PLANES = 1: one e4m3 activation plane, one MMA column per token, sx per
+//             (row, 128). The gate/up epilogue rounds gate/up to bf16, forms the
+//             SwiGLU product in bf16 (as the reference's executor does in its
+//             output dtype) and re-quantises it per (row, 128 features) = per
+//             row of the item's 128-row weight block, writing the e4m3 rows and
+//             their scales for the down projection directly.
+// PLANES = 2: hi/lo planes (block-scaled weights in the high-accuracy mode):
+//             acc += sw[kb] * (hi + lo / 16), the per-row sx applied at the end.
+// Per-row weight scales (CHANNEL / TENSOR) are applied once at the end.
+// Epilogue warp (quadrant q = warp % 4, chunk c) owns TMEM lanes 32q..32q+31
+// (weight rows) and the item's tokens [c * TOKW, (c + 1) * TOKW).
+// ---------------------------------------------------------------------------
+template <int MODE, int NM, int BNT, int PLANES>
+struct CfgP {
+  static constexpr int NMAT = NM;
+  static constexpr int NCOL = PLANES * BNT;               // MMA N per weight matrix (largest tile)
+  static constexpr int B_TILE = NCOL * BK8;               // activation bytes per stage
+  static constexpr int W_STAGE_BYTES = NMAT * kW8TileBytes;
+  static constexpr int SLOT = NMAT * NCOL;                // TMEM columns per K-block slot
+  static constexpr int NSLOT = 512 / SLOT > 4 ? 4 : 512 / SLOT;
+  static constexpr int TMEM_COLS = NSLOT * SLOT <= 256 ? 256 : 512;
+  static constexpr int TOKW = 32 / PLANES;                // tokens per epilogue warp (32 TMEM columns)
+  static constexpr int CHUNKS = BNT / TOKW;
+  static constexpr int EPI_WARPS = 4 * CHUNKS;
+  static constexpr int EPI_THREADS = EPI_WARPS * 32;
+  static constexpr int THREADS = (2 + EPI_WARPS) * 32;
+  // the register file split evenly over the threads (8-register granularity), at most 168
+  static constexpr int MAXREG = 65536 / THREADS / 8 * 8 > 168 ? 168 : 65536 / THREADS / 8 * 8;
+  static constexpr bool QOUT = MODE == 0 && PLANES == 1;   // gate/up writes e4m3 rows + scales
+  static constexpr int STAGING = QOUT ? BNT * BM : 0;      // e4m3 [tokens][128 features]
+  static constexpr int SCL = EPI_WARPS * 2 * NMAT * 32 * 4;  // per-warp factor broadcast buffers
+  static constexpr int RED = QOUT ? 4 * BNT * 4 : 0;       // per-quadrant token amax
+  static constexpr int FIXED = STAGING + SCL + RED + 1024 /*align*/ + 512 /*barriers*/;
+  static constexpr int S = (227 * 1024 - FIXED) / (W_STAGE_BYTES + B_TILE);
+  static constexpr int SMEM_BYTES = S * (W_STAGE_BYTES + B_TILE) + FIXED;
+  static_assert(S >= 2, "pipeline too shallow");
+  static_assert(NSLOT >= 2, "need at least two TMEM slots");
+};
+
+__device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// Lane l ends with max over the warp's 32 lanes of v[l] (31 shuffles): at each step a
+// lane keeps the half of its array whose index bit matches its own lane bit and
+// exchanges the other half with its partner.
+__device__ __forceinline__ float warp_transpose_max(float (&v)[32], int lane) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const bool hi = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      const float keep = hi ? v[i + o] : v[i];
+      const float send = hi ? v[i] : v[i + o];
+      v[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, o));
+    }
+  }
+  return v[0];
+}
+
+template <int MODE, int NM, int BNT, int PLANES>
+__global__ void __maxnreg__((CfgP<MODE, NM, BNT, PLANES>::MAXREG))
+moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
+  using C = CfgP<MODE, NM, BNT, PLANES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sB = smem;
+  uint8_t* sW = sB + C::S * C::B_TILE;
+  uint8_t* sQ = sW + C::S * C::W_STAGE_BYTES;                                  // [BNT][128] e4m3
+  float* sScl = reinterpret_cast<float*>(sQ + C::STAGING);                     // [EPI_WARPS][2][NMAT][32]
+  float* sRed = sScl + C::EPI_WARPS * 2 * C::NMAT * 32;                        // [4][BNT]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sRed) + C::RED);
+  uint64_t* ld_full = bars;
+  uint64_t* ld_empty = ld_full + C::S;
+  uint64_t* acc_full = ld_empty + C::S;
+  uint64_t* acc_empty = acc_full + C::NSLOT;
+  __shared__ uint32_t s_tmem_base;
+  __shared__ volatile int s_abort;
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  DeviceStatus* st = p.st;
+  griddep_launch();
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int i = 0; i < C::S; ++i) {
+      mbar_init(&ld_full[i], 1);
+      mbar_init(&ld_empty[i], 1);
+    }
+    for (int i = 0; i < C::NSLOT; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], C::EPI_WARPS);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&s_tmem_base, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    if (p.g[0].enabled) prefetch_tmap(&p.g[0].tmap_b);
+    if (p.g[1].enabled) prefetch_tmap(&p.g[1].tmap_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s_tmem_base;
+  griddep_wait();  // the work list and operands come from the previous launches
+  const int n_items = *p.n_items;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      WorkItem wn = p.items[blockIdx.x];
+      for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
+        const WorkItem wi = wn;
+        if (item + (int)gridDim.x < p.cap) wn = p.items[item + gridDim.x];
+        const GroupParams& g = p.g[wi.group];
+        const uint8_t* wbase = wi.wtiles;
+        const uint32_t b_bytes = (uint32_t)g.box_rows * PLANES * BK8;
+        const int nm = min(wi.nmat, C::NMAT);
+        for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
+          const int s = it % C::S;
+          if (!mbar_wait(&ld_empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 41 + 8 * MODE)) break;
+          mbar_arrive_expect_tx(&ld_full[s], (uint32_t)(nm * kW8TileBytes) + b_bytes);
+          for (int m = 0; m < nm; ++m)
+            bulk_g2s(sW + s * C::W_STAGE_BYTES + m * kW8TileBytes,
+                     wbase + (size_t)m * g.mstride + (size_t)kb * g.kstride, kW8TileBytes, &ld_full[s]);
+          tma_load_2d(sB + s * C::B_TILE, &g.tmap_b, kb * BK8, PLANES * wi.row0, &ld_full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0, kc = 0;
+      WorkItem wn = p.items[blockIdx.x];
+      bool ok = true;
+      for (int item = blockIdx.x; item < n_items && !s_abort && ok; item += gridDim.x) {
+        const WorkItem wi = wn;
+        if (item + (int)gridDim.x < p.cap) wn = p.items[item + gridDim.x];
+        const int n_tok = max(16, (wi.nrows + 15) & ~15);
+        const uint32_t idesc = idesc_e4m3(BM, PLANES * n_tok);
+        const int nm = min(wi.nmat, C::NMAT);
+        for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it, ++kc) {
+          const int s = it % C::S;
+          const int slot = kc % C::NSLOT;
+          if (!mbar_wait(&acc_empty[slot], ((kc / C::NSLOT) & 1) ^ 1, &s_abort, st, 42 + 8 * MODE)) { ok = false; break; }
+          if (!mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 43 + 8 * MODE)) { ok = false; break; }
+          tc_fence_after();
+          // a K step of 32 e4m3 (32 bytes) is +2 in the encoded start address
+          const uint64_t b_desc0 = smem_desc_sw128(smem_u32(sB + s * C::B_TILE));
+          const uint64_t a_desc0 = smem_desc_sw128(smem_u32(sW + s * C::W_STAGE_BYTES));
+          const uint32_t d_base = tmem_base + slot * C::SLOT;
+          for (int m = 0; m < nm; ++m) {
+#pragma unroll
+            for (int kk = 0; kk < BK8 / 32; ++kk)
+              mma_e4m3_ss(d_base + m * C::NCOL, a_desc0 + (uint64_t)(m * (kW8TileBytes >> 4) + 2 * kk),
+                          b_desc0 + (uint64_t)(2 * kk), idesc, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(&ld_empty[s]);
+          mma_commit(&acc_full[slot]);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (promotion)
+    const int ew = warp - 2;               // 0 .. EPI_WARPS - 1
+    const int quad = warp & 3;             // TMEM lane quadrant this warp may access
+    const int chunk = ew >> 2;
+    const int lrow = quad * 32 + lane;     // weight row inside the 128-row block
+    const int t0 = chunk * C::TOKW;        // first token of this warp inside the tile
+    float* my_scl = sScl + ew * 2 * C::NMAT * 32;
+    uint32_t kc = 0;
+    WorkItem wn = p.items[blockIdx.x];
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && !s_abort && ok; item += gridDim.x) {
+      const WorkItem wi = wn;
+      if (item + (int)gridDim.x < p.cap) wn = p.items[item + gridDim.x];
+      const GroupParams& g = p.g[wi.group];
+      const int nm = min(wi.nmat, C::NMAT);
+      const int ntk = min(C::TOKW, wi.nrows - t0);  // tokens of this warp (<= 0: none)
+      const bool block_w = g.scale_mode == DWDP_SCALE_BLOCK128;
+      const int kbn = g.K / 128;                     // K blocks of the projection
+      const float* wsc = wi.scales;
+      // block-scale index of matrix m at K block kb
+      auto wsc_index = [&](int m, int kb) -> int {
+        return MODE == 0 ? ((m * (g.R / BM) + wi.rb) * kbn + kb) : ((wi.rb + m) * kbn + kb);
+      };
+      float acc[C::NMAT][C::TOKW];
+#pragma unroll
+      for (int m = 0; m < C::NMAT; ++m)
+#pragma unroll
+        for (int j = 0; j < C::TOKW; ++j) acc[m][j] = 0.f;
+      // scale of this lane's token at K block kb (PLANES = 1), prefetched one block ahead
+      auto load_sx = [&](int kb) -> float {
+        if constexpr (PLANES == 1) {
+          return lane < ntk ? g.x_scale[(size_t)kb * g.xs_ld + wi.row0 + t0 + lane] : 0.f;
+        } else {
+          return 0.f;
+        }
+      };
+      auto load_sw = [&](int m, int kb) -> float {
+        return (block_w && m < nm) ? wsc[wsc_index(m, kb)] : 1.0f;
+      };
+      float sx_next = ntk > 0 ? load_sx(wi.kb_begin) : 0.f;
+      float sw_next[C::NMAT];
+#pragma unroll
+      for (int m = 0; m < C::NMAT; ++m) sw_next[m] = ntk > 0 ? load_sw(m, wi.kb_begin) : 1.f;
+      for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++kc) {
+        const int slot = kc % C::NSLOT;
+        const float sx_cur = sx_next;
+        float sw_cur[C::NMAT];
+#pragma unroll
+        for (int m = 0; m < C::NMAT; ++m) sw_cur[m] = sw_next[m];
+        if (ntk > 0 && kb + 1 < wi.kb_end) {  // next block's scales load while this one waits
+          sx_next = load_sx(kb + 1);
+#pragma unroll
+          for (int m = 0; m < C::NMAT; ++m) sw_next[m] = load_sw(m, kb + 1);
+        }
+        // PLANES = 1: this lane's token factor sx * sw per matrix, broadcast through shared memory
+        float* fac = my_scl + (kb & 1) * C::NMAT * 32;
+        if constexpr (PLANES == 1) {
+#pragma unroll
+          for (int m = 0; m < C::NMAT; ++m) fac[m * 32 + lane] = sx_cur * sw_cur[m];
+        }
+        __syncwarp();
+        if (!mbar_wait(&acc_full[slot], (kc / C::NSLOT) & 1, &s_abort, st, 44 + 8 * MODE)) { ok = false; break; }
+        tc_fence_after();
+        if (ntk > 0) {
+          const uint32_t t_acc = tmem_base + slot * C::SLOT + PLANES * t0 + ((uint32_t)(quad * 32) << 16);
+#pragma unroll
+          for (int m = 0; m < C::NMAT; ++m) {
+            if (m < nm) {
+#pragma unroll
+              for (int hf = 0; hf < 2; ++hf) {  // 16 TMEM columns at a time keeps registers in budget
+                float v[16];
+                tmem_ld16(t_acc + m * C::NCOL + 16 * hf, v);
+                tmem_ld_wait();
+                if constexpr (PLANES == 1) {
+                  const float4* f4 = reinterpret_cast<const float4*>(fac + m * 32 + 16 * hf);
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) {
+                    const float4 f = f4[q];
+                    float* a4 = &acc[m][16 * hf + 4 * q];
+                    a4[0] = fmaf(v[4 * q + 0], f.x, a4[0]);
+                    a4[1] = fmaf(v[4 * q + 1], f.y, a4[1]);
+                    a4[2] = fmaf(v[4 * q + 2], f.z, a4[2]);
+                    a4[3] = fmaf(v[4 * q + 3], f.w, a4[3]);
+                  }
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 8; ++j)
+                    acc[m][8 * hf + j] =
+                        fmaf(v[2 * j] + v[2 * j + 1] * (1.0f / kLoPlaneGain), sw_cur[m], acc[m][8 * hf + j]);
+                }
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[slot]);
+      }
+      if (!ok) break;
+
+      // ---------------- item epilogue: per-row scales, SwiGLU / routing weight, stores
+      const int feat = wi.rb * BM + lrow;
+      float s_row[C::NMAT];
+#pragma unroll
+      for (int m = 0; m < C::NMAT; ++m) {
+        s_row[m] = 1.0f;
+        if (per_row_scales(g.scale_mode) && m < nm)
+          s_row[m] = MODE == 0 ? wsc[m * g.R + feat] : wsc[feat + m * BM];
+      }
+      if constexpr (MODE == 0) {
+        if constexpr (C::QOUT) {
+          // h per the reference executor's bf16 arithmetic, then its (token, 128) amax
+          __nv_bfloat162 hp[16];  // h of tokens t0 + j, exact in bf16
+          float hq[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float gb = bf16_round(acc[0][j] * s_row[0]);
+            const float ub = bf16_round(acc[1][j] * s_row[1]);
+            const float sg = bf16_round(1.0f / (1.0f + expf(-gb)));
+            const float h = j < ntk ? bf16_round(bf16_round(gb * sg) * ub) : 0.f;
+            if (j & 1) hp[j >> 1].y = __float2bfloat16_rn(h); else hp[j >> 1].x = __float2bfloat16_rn(h);
+            hq[j] = fabsf(h);
+          }
+          const float wmax = warp_transpose_max(hq, lane);  // this warp's rows, token t0 + lane
+          sRed[quad * BNT + t0 + lane] = wmax;
+          named_bar_sync(3, C::EPI_THREADS);
+          float tmax = sRed[t0 + lane];
+#pragma unroll
+          for (int q = 1; q < 4; ++q) tmax = fmaxf(tmax, sRed[q * BNT + t0 + lane]);
+          const float tsc = __fdiv_rn(fmaxf(tmax, 1e-5f), 448.0f);
+          my_scl[lane] = tsc;
+          __syncwarp();
+          if (quad == 0 && lane < ntk)
+            g.out_scale[(size_t)wi.rb * g.os_ld + wi.row0 + t0 + lane] = tsc;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (j < ntk) {
+              const float hvj = __bfloat162float((j & 1) ? hp[j >> 1].y : hp[j >> 1].x);
+              const float q = __fdiv_rn(hvj, my_scl[j]);
+              sQ[(t0 + j) * BM + lrow] = (uint8_t)__nv_cvt_float_to_fp8(q, __NV_SATFINITE, __NV_E4M3);
+            }
+          }
+          named_bar_sync(3, C::EPI_THREADS);
+          // e4m3 rows of the tile leave as 16-byte stores
+          uint8_t* out8 = reinterpret_cast<uint8_t*>(g.out);
+          const int ep = ew * 32 + lane;
+          for (int q = ep; q < wi.nrows * (BM / 16); q += C::EPI_THREADS) {
+            const int t = q >> 3, ch = q & 7;
+            *reinterpret_cast<uint4*>(out8 + (size_t)(wi.row0 + t) * g.R + wi.rb * BM + ch * 16) =
+                *reinterpret_cast<const uint4*>(sQ + t * BM + ch * 16);
+          }
+          named_bar_sync(3, C::EPI_THREADS);  // sQ and sRed are rewritten by the next item
+        } else {
+          __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out);
+#pragma unroll
+          for (int j = 0; j < C::TOKW; ++j) {
+            if (j < ntk) {
+              const float sx = g.x_scale[wi.row0 + t0 + j];
+              const float gg = acc[0][j] * (s_row[0] * sx);
+              const float uu = acc[1][j] * (s_row[1] * sx);
+              out[(size_t)(wi.row0 + t0 + j) * g.R + feat] = __float2bfloat16_rn(silu_fast(gg) * uu);
+            }
+          }
+        }
+      } else {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)wi.part * g.part_stride;
+#pragma unroll
+        for (int j = 0; j < C::TOKW; ++j) {
+          if (j < ntk) {
+            const int row = wi.row0 + t0 + j;
+            float f = g.row_scale != nullptr ? g.row_scale[row] : 1.0f;
+            if constexpr (PLANES == 2) f *= g.x_scale[row];
+#pragma unroll
+            for (int m = 0; m < C::NMAT; ++m)
+              if (m < nm) out[(size_t)row * g.R + feat + m * BM] = __float2bfloat16_rn(acc[m][j] * (s_row[m] * f));
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Device tile planner (the scheduler's job, DWDP/scheduler/ops/round_robin.py:
 // active experts in ascending id), run on device so no counts reach the host.
 // Shared-expert tiles go first (longest-running work first); routed tiles are
@@ -830,11 +1088,13 @@ struct QuantSeg {
   int rows, K;
   const int64_t* row_index;  // row r reads src row row_index[r] (null: row r)
   int64_t src_rows;
+  int scale_rowmajor;        // single-plane quantiser: scales [rows][K / 128] instead of [K / 128][rows]
 };
 struct QuantParams {
   QuantSeg seg[2];
   DeviceStatus* st;
   int per_warp;  // 1: one warp per row (many rows); 0: one CTA per row (few, long rows)
+  int blk;       // 1: one e4m3 plane, scales per (row, 128): dst [rows, K], scale [K / 128][rows]
 };
 
 // 8 bf16 (one 16-byte load) -> 8 hi bytes and 8 lo bytes
@@ -1030,8 +1290,75 @@ __device__ __forceinline__ void quant_row_warp16(const QuantSeg& g, int row, Dev
   if (lane == 0) g.scale[row] = amax > 0.f ? amax / 448.0f : 0.f;
 }
 
+// One e4m3 plane with one scale per (row, 128 channels), as
+// DWDP/executor/fp8.py:86-115 quantize_activations_blockwise computes it:
+// scale = max(amax of the block, 1e-5) / 448 and q = e4m3(v / scale), both with
+// IEEE division and round-to-nearest-even, so the bytes and scales equal the
+// reference's. One warp handles 512 columns of one row (a lane 16 consecutive
+// elements, 8 lanes per 128-block); scales are stored transposed, [K / 128][rows],
+// so that the GEMM epilogue reads one K block's scales of consecutive rows.
+__device__ __forceinline__ void quant_seg_blk(const QuantSeg& g, int row, int part, DeviceStatus* st) {
+  const int lane = threadIdx.x & 31;
+  int64_t sr = row;
+  if (g.row_index != nullptr) {
+    sr = g.row_index[row];
+    if (sr < 0 || sr >= g.src_rows) {
+      if (lane == 0) record_error(st, DWDP_ERR_DEVICE_BOUNDS, 213, row);
+      sr = -1;
+    }
+  }
+  const int c = part * 512 + lane * 16;
+  const bool in = c < g.K;
+  uint4 a = make_uint4(0, 0, 0, 0), b = make_uint4(0, 0, 0, 0);
+  if (in && sr >= 0) {
+    const __nv_bfloat16* src = g.src + (size_t)sr * g.K + c;
+    a = *reinterpret_cast<const uint4*>(src);
+    b = *reinterpret_cast<const uint4*>(src + 8);
+  }
+  float amax = amax8(b, amax8(a, 0.f));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+  const float scale = __fdiv_rn(fmaxf(amax, 1e-5f), 448.0f);
+  if (!in) return;
+  const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&a);
+  const __nv_bfloat162* pb = reinterpret_cast<const __nv_bfloat162*>(&b);
+  auto q2 = [&](const __nv_bfloat162 v) -> uint32_t {
+    const float2 f = __bfloat1622float2(v);
+    const float2 qv = make_float2(__fdiv_rn(f.x, scale), __fdiv_rn(f.y, scale));
+    return (uint32_t)__nv_cvt_float2_to_fp8x2(qv, __NV_SATFINITE, __NV_E4M3);
+  };
+  uint32_t w[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const __nv_bfloat162 lo = k < 2 ? pa[2 * k] : pb[2 * k - 4];
+    const __nv_bfloat162 hi = k < 2 ? pa[2 * k + 1] : pb[2 * k - 3];
+    w[k] = q2(lo) | (q2(hi) << 16);
+  }
+  *reinterpret_cast<uint4*>(g.dst + (size_t)row * g.K + c) = make_uint4(w[0], w[1], w[2], w[3]);
+  if ((lane & 7) == 0) {
+    const size_t si = g.scale_rowmajor ? (size_t)row * (g.K >> 7) + (c >> 7) : (size_t)(c >> 7) * g.rows + row;
+    g.scale[si] = scale;
+  }
+}
+
+__device__ __forceinline__ void quant_rows_blk(const QuantParams& q, int block, int nblocks) {
+  constexpr int kW = kPlanThreads / 32;
+  const int np0 = (q.seg[0].K + 511) / 512, np1 = (q.seg[1].K + 511) / 512;
+  const int u0 = q.seg[0].rows * np0;
+  const int total = u0 + q.seg[1].rows * np1;
+  for (int u = block * kW + (int)(threadIdx.x >> 5); u < total; u += nblocks * kW) {
+    if (u < u0) quant_seg_blk(q.seg[0], u / np0, u % np0, q.st);
+    else quant_seg_blk(q.seg[1], (u - u0) / np1, (u - u0) % np1, q.st);
+  }
+}
+
 // Rows of both segments, one per `first + i * stride` unit (a warp or a CTA).
 __device__ __forceinline__ void quant_rows(const QuantParams& q, int block, int nblocks) {
+  if (q.blk) {
+    quant_rows_blk(q, block, nblocks);
+    return;
+  }
   __shared__ float red[kPlanThreads / 32];
   const int total = q.seg[0].rows + q.seg[1].rows;
   if (q.per_warp) {
@@ -1101,13 +1428,14 @@ bool make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int
   return r == CUDA_SUCCESS;
 }
 
-// 2-D map over the interleaved hi/lo e4m3 planes [2 * rows, cols], box {128, 2 * box_rows}.
-bool make_tmap_planes(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows) {
+// 2-D map over e4m3 activation rows: `planes` = 2 for the interleaved hi/lo planes
+// [2 * rows, cols] (box {128, 2 * box_rows}), 1 for one plane [rows, cols].
+bool make_tmap_planes(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows, int planes) {
   auto enc = get_encode_fn();
   if (enc == nullptr || rows <= 0) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)(2 * rows)};
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)(planes * rows)};
   cuuint64_t strides[1] = {(cuuint64_t)cols};
-  cuuint32_t box[2] = {(cuuint32_t)BK8, (cuuint32_t)(2 * box_rows)};
+  cuuint32_t box[2] = {(cuuint32_t)BK8, (cuuint32_t)(planes * box_rows)};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -1164,10 +1492,11 @@ WsLayout ws_layout(int64_t T, int K, int E, int I, int H, int Is) {
   w.x8_s = o; o = align256(o + (size_t)(Is > 0 ? T : 0) * H * 2);
   w.h8_r = o; o = align256(o + (size_t)N * I * 2);
   w.h8_s = o; o = align256(o + (size_t)T * Isz * 2);
-  w.sx_r = o; o = align256(o + (size_t)N * 4);
-  w.sx_s = o; o = align256(o + (size_t)T * 4);
-  w.sh_r = o; o = align256(o + (size_t)N * 4);
-  w.sh_s = o; o = align256(o + (size_t)T * 4);
+  // activation scales: one per row (hi/lo) or per (row, 128 inputs) (BLOCK128)
+  w.sx_r = o; o = align256(o + (size_t)N * (H / 128) * 4);
+  w.sx_s = o; o = align256(o + (size_t)T * (H / 128) * 4);
+  w.sh_r = o; o = align256(o + (size_t)N * (I / 128) * 4);
+  w.sh_s = o; o = align256(o + (size_t)T * (Isz / 128) * 4);
   w.total = o;
   return w;
 }
@@ -1194,10 +1523,27 @@ inline int quant_blocks(int64_t rows) {
   return (int)std::max<int64_t>(1, std::min<int64_t>(b, 148 * 16));
 }
 
-template <int MODE, bool WFP8>
+// one warp per (row, 512-column part) for the single-plane quantiser
+inline int quant_blocks_blk(int64_t units) {
+  const int64_t b = (units + kPlanThreads / 32 - 1) / (kPlanThreads / 32);
+  return (int)std::max<int64_t>(1, std::min<int64_t>(b, 148 * 16));
+}
+
+template <int MODE>
 int launch_gemm(const GemmParams& prm, int grid, cudaStream_t stream) {
-  using C = Cfg<MODE, WFP8>;
-  auto kfn = moe_gemm_kernel<MODE, WFP8>;
+  using C = Cfg<MODE>;
+  auto kfn = moe_gemm_kernel<MODE>;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
+    return DWDP_ERR_CUDA;
+  return launch_chained(kfn, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, stream, 1u, prm) == cudaSuccess
+             ? DWDP_OK
+             : DWDP_ERR_CUDA;
+}
+
+template <int MODE, int NM, int BNT, int PLANES>
+int launch_gemm_f8p(const GemmParams& prm, int grid, cudaStream_t stream) {
+  using C = CfgP<MODE, NM, BNT, PLANES>;
+  auto kfn = moe_gemm_f8p_kernel<MODE, NM, BNT, PLANES>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return DWDP_ERR_CUDA;
   return launch_chained(kfn, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, stream, 1u, prm) == cudaSuccess
@@ -1253,17 +1599,24 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   if (shared != nullptr &&
       (shared->weight_dtype != routed->weight_dtype || shared->scale_mode != routed->scale_mode))
     return DWDP_ERR_UNSUPPORTED;  // both groups share one tile layout per launch
-  // per-channel e4m3 weights run on the e4m3 tensor-core kernels; block-scaled
-  // e4m3 and bf16 weights on the bf16 kernels
-  const bool native = fp8 && routed->scale_mode == DWDP_SCALE_CHANNEL;
-  const int bk = native ? BK8 : BK;
-  // e4m3 token tiles: 64 tokens. 128-token tiles (half the weight traffic per FLOP, one TMEM
-  // accumulator buffer for gate/up, 3-deep ring) measured slower at T = 1024 and 4096 on the
-  // Qwen shape; DWDP_WIDE_TILES=1 selects them for tuning.
-  bool wide = false;
-  if (const char* v = getenv("DWDP_WIDE_TILES")) wide = native && v[0] == '1';  // tuning override
-  const int bn = native ? (wide ? 128 : BN8) : BN_MAX;
+  // Kernel family: per-row-scaled e4m3 weights with hi/lo activations need no promotion
+  // (moe_gemm_f8_kernel); activations scaled per (row, 128) or block-scaled weights promote
+  // every 128-wide K block (moe_gemm_f8p_kernel, one or two activation planes); bf16
+  // weights run kind::f16 MMAs (moe_gemm_kernel).
+  const bool act_blk = fp8 && routed->act_quant == DWDP_ACT_BLOCK128;
+  const bool hilo_native = fp8 && !act_blk && per_row_scales(routed->scale_mode);
+  const bool promote = fp8 && !hilo_native;
+  const int planes = act_blk ? 1 : 2;  // e4m3 activation planes (fp8 paths)
+  const int bk = fp8 ? BK8 : BK;
   const int64_t N = shared_only ? 0 : T * K;  // routed rows
+  // Token tiles. hi/lo: 64 (128-token tiles, half the weight traffic per FLOP but one TMEM
+  // accumulator buffer for gate/up and a 3-deep ring, measured slower on the Qwen shape).
+  // One plane: 128 once experts average 96+ rows (the MMA then carries 128 useful columns,
+  // the per-stage activation bytes of the hi/lo 64-token tile). DWDP_WIDE_TILES=0|1 forces.
+  bool wide = act_blk && N >= 96LL * E;
+  if (const char* v = getenv("DWDP_WIDE_TILES"))  // tuning override
+    wide = (hilo_native || act_blk) && v[0] == '1';
+  const int bn = fp8 ? (wide ? 128 : BN8) : BN_MAX;
   const WsLayout L = ws_layout(T, K, E, I, H, Is);
   if (workspace == nullptr || workspace_bytes < L.total) return DWDP_ERR_CAPACITY;
   if (T == 0) return DWDP_OK;
@@ -1284,13 +1637,15 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   PlanParams pp{};
   pp.counts = shared_only ? nullptr : counts; pp.offsets = offsets; pp.E = E; pp.T = (int)T;
   pp.has_shared = has_shared;
-  // e4m3 path at prefill sizes: a down item covers two consecutive 128-row blocks (one activation
-  // tile for two MMAs, half the activation traffic per FLOP). Decode keeps single blocks: there
-  // the halved item count would leave SMs idle or unevenly loaded (pairs need ~4 waves of items).
+  // e4m3 64-token tiles at prefill sizes: a down item covers two consecutive 128-row blocks
+  // (one activation tile for two MMAs, half the activation traffic per FLOP). Decode keeps
+  // single blocks: there the halved item count would leave SMs idle or unevenly loaded (pairs
+  // need ~4 waves of items). 128-token tiles always run single down blocks.
   const int sms_now = dwdp_device_sm_count();
   const int64_t est_tiles = N / BN8 + std::min<int64_t>(E, N) + (has_shared ? (T + BN8 - 1) / BN8 * parts : 0);
-  bool pair_dn = native && est_tiles * ((H / BM + 1) / 2) >= 4LL * std::max(1, sms_now);
-  if (const char* v = getenv("DWDP_PAIR_DOWN")) pair_dn = native && v[0] == '1';  // tuning override
+  bool pair_dn = fp8 && !(act_blk && wide) && est_tiles * ((H / BM + 1) / 2) >= 4LL * std::max(1, sms_now);
+  if (const char* v = getenv("DWDP_PAIR_DOWN"))  // tuning override
+    pair_dn = fp8 && !(act_blk && wide) && v[0] == '1';
   const int dn_items_per_tile = pair_dn ? (H / BM + 1) / 2 : H / BM;
   pp.rb_gu_r = I / BM; pp.rb_dn_r = dn_items_per_tile;
   pp.rb_gu_s = has_shared ? Is / BM : 0; pp.rb_dn_s = has_shared ? dn_items_per_tile : 0;
@@ -1310,10 +1665,12 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   QuantParams qx{}, qh{};
   qx.st = st;
   qh.st = st;
-  qx.per_warp = qh.per_warp = quant_per_warp(N + (has_shared ? T : 0));
+  const int64_t q_rows = N + (has_shared ? T : 0);
+  qx.per_warp = qh.per_warp = quant_per_warp(q_rows);
+  qx.blk = act_blk ? 1 : 0;
   const bool indexed = packed_hidden == nullptr;
   if (indexed && packed_tok == nullptr && N > 0) return DWDP_ERR_INVALID_ARGUMENT;
-  if (native) {
+  if (fp8) {
     const __nv_bfloat16* hid = reinterpret_cast<const __nv_bfloat16*>(hidden);
     qx.seg[0] = indexed ? QuantSeg{hid, ws + L.x8_r, sx_r, (int)N, H, packed_tok, T}
                         : QuantSeg{reinterpret_cast<const __nv_bfloat16*>(packed_hidden), ws + L.x8_r, sx_r,
@@ -1327,7 +1684,9 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
     if (rc != DWDP_OK) return rc;
     packed_hidden = ws + L.x8_r;
   }
-  const int qx_blocks = native ? quant_blocks(N + (has_shared ? T : 0)) : 0;
+  int qx_blocks = 0;
+  if (fp8) qx_blocks = act_blk ? quant_blocks_blk(N * ((H + 511) / 512) + (has_shared ? T * ((H + 511) / 512) : 0))
+                               : quant_blocks(q_rows);
   if (launch_chained(prep_kernel, dim3(kPlanBlocks + qx_blocks), dim3(kPlanThreads), 0, stream, 1u, pp, qx) !=
       cudaSuccess)
     return DWDP_ERR_CUDA;
@@ -1337,21 +1696,25 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   // shared tile at most min(T, bn).
   const int box_r = box_rows_for(N, bn), box_s = box_rows_for(T, bn);
   auto map = [&](CUtensorMap* m, const void* bf16, size_t planes_off, int64_t rows, int64_t cols, int box) {
-    return native ? make_tmap_planes(m, ws + planes_off, rows, cols, box) : make_tmap(m, bf16, rows, cols, box);
+    return fp8 ? make_tmap_planes(m, ws + planes_off, rows, cols, box, planes) : make_tmap(m, bf16, rows, cols, box);
   };
   GemmParams gu{}, dn{};
   gu.g[0].enabled = N > 0;
   if (N > 0 && !map(&gu.g[0].tmap_b, packed_hidden, L.x8_r, N, H, box_r)) return DWDP_ERR_CUDA;
-  gu.g[0].w = routed->w13; gu.g[0].s = routed->s13; gu.g[0].out = h_r; gu.g[0].row_scale = nullptr;
-  gu.g[0].x_scale = sx_r;
+  gu.g[0].w = routed->w13; gu.g[0].s = routed->s13; gu.g[0].row_scale = nullptr;
+  gu.g[0].out = act_blk ? static_cast<void*>(ws + L.h8_r) : static_cast<void*>(h_r);
+  gu.g[0].out_scale = sh_r; gu.g[0].os_ld = N;
+  gu.g[0].x_scale = sx_r; gu.g[0].xs_ld = N;
   gu.g[0].K = H; gu.g[0].R = I; gu.g[0].scale_mode = routed->scale_mode; gu.g[0].box_rows = box_r;
   // e4m3 tiles: gate/up interleaved per 128-input stage; down row blocks are K/128 tiles apart
   gu.g[0].mstride = kW8TileBytes; gu.g[0].kstride = 2 * kW8TileBytes;
   gu.g[1].enabled = has_shared;
   if (has_shared) {
     if (!map(&gu.g[1].tmap_b, hidden, L.x8_s, T, H, box_s)) return DWDP_ERR_CUDA;
-    gu.g[1].w = shared->w13; gu.g[1].s = shared->s13; gu.g[1].out = h_s; gu.g[1].row_scale = nullptr;
-    gu.g[1].x_scale = sx_s;
+    gu.g[1].w = shared->w13; gu.g[1].s = shared->s13; gu.g[1].row_scale = nullptr;
+    gu.g[1].out = act_blk ? static_cast<void*>(ws + L.h8_s) : static_cast<void*>(h_s);
+    gu.g[1].out_scale = sh_s; gu.g[1].os_ld = T;
+    gu.g[1].x_scale = sx_s; gu.g[1].xs_ld = T;
     gu.g[1].K = H; gu.g[1].R = Is; gu.g[1].scale_mode = shared->scale_mode; gu.g[1].box_rows = box_s;
     gu.g[1].mstride = kW8TileBytes; gu.g[1].kstride = 2 * kW8TileBytes;
   }
@@ -1360,14 +1723,14 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   dn.g[0].enabled = N > 0;
   if (N > 0 && !map(&dn.g[0].tmap_b, h_r, L.h8_r, N, I, box_r)) return DWDP_ERR_CUDA;
   dn.g[0].w = routed->w2; dn.g[0].s = routed->s2; dn.g[0].out = weighted_out; dn.g[0].box_rows = box_r;
-  dn.g[0].x_scale = sh_r;
+  dn.g[0].x_scale = sh_r; dn.g[0].xs_ld = N;
   dn.g[0].row_scale = packed_weights; dn.g[0].K = I; dn.g[0].R = H; dn.g[0].scale_mode = routed->scale_mode;
   dn.g[0].mstride = (long long)BM * I; dn.g[0].kstride = kW8TileBytes;
   dn.g[1].enabled = has_shared;
   if (has_shared) {
     if (!map(&dn.g[1].tmap_b, h_s, L.h8_s, T, Is, box_s)) return DWDP_ERR_CUDA;
     dn.g[1].w = shared->w2; dn.g[1].s = shared->s2; dn.g[1].out = shared_out; dn.g[1].box_rows = box_s;
-    dn.g[1].x_scale = sh_s;
+    dn.g[1].x_scale = sh_s; dn.g[1].xs_ld = T;
     dn.g[1].row_scale = shared_gate; dn.g[1].K = Is; dn.g[1].R = H; dn.g[1].scale_mode = shared->scale_mode;
     dn.g[1].mstride = (long long)BM * Is; dn.g[1].kstride = kW8TileBytes;
     dn.g[1].part_stride = (long long)T * H;
@@ -1378,27 +1741,60 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   if (sms <= 0) return DWDP_ERR_CUDA;
   const int grid_gu = std::max(1, std::min(sms, L.cap_gu));
   const int grid_dn = std::max(1, std::min(sms, L.cap_dn));
-  int rc;
-  if (native) {
-    rc = wide ? launch_gemm_f8<0, 2, 128>(gu, grid_gu, stream) : launch_gemm_f8<0, 2, 64>(gu, grid_gu, stream);
-    if (rc == DWDP_OK) {
-      rc = launch_chained(quant_kernel, dim3(quant_blocks(N + (has_shared ? T : 0))), dim3(kPlanThreads), 0,
-                          stream, 1u, qh) == cudaSuccess
+  auto quant_h = [&]() {
+    return launch_chained(quant_kernel, dim3(quant_blocks(q_rows)), dim3(kPlanThreads), 0, stream, 1u, qh) ==
+                   cudaSuccess
                ? DWDP_OK
                : DWDP_ERR_CUDA;
-    }
+  };
+  int rc;
+  if (hilo_native) {
+    rc = wide ? launch_gemm_f8<0, 2, 128>(gu, grid_gu, stream) : launch_gemm_f8<0, 2, 64>(gu, grid_gu, stream);
+    if (rc == DWDP_OK) rc = quant_h();
     if (rc == DWDP_OK) {
       if (wide) rc = pair_dn ? launch_gemm_f8<1, 2, 128>(dn, grid_dn, stream) : launch_gemm_f8<1, 1, 128>(dn, grid_dn, stream);
       else rc = pair_dn ? launch_gemm_f8<1, 2, 64>(dn, grid_dn, stream) : launch_gemm_f8<1, 1, 64>(dn, grid_dn, stream);
     }
-  } else if (fp8) {
-    rc = launch_gemm<0, true>(gu, grid_gu, stream);
-    if (rc == DWDP_OK) rc = launch_gemm<1, true>(dn, grid_dn, stream);
+  } else if (promote && act_blk) {
+    // the gate/up epilogue writes the e4m3 intermediate and its scales: no launch between
+    if (wide) {
+      rc = launch_gemm_f8p<0, 2, 128, 1>(gu, grid_gu, stream);
+      if (rc == DWDP_OK) rc = launch_gemm_f8p<1, 1, 128, 1>(dn, grid_dn, stream);
+    } else {
+      rc = launch_gemm_f8p<0, 2, 64, 1>(gu, grid_gu, stream);
+      if (rc == DWDP_OK)
+        rc = pair_dn ? launch_gemm_f8p<1, 2, 64, 1>(dn, grid_dn, stream) : launch_gemm_f8p<1, 1, 64, 1>(dn, grid_dn, stream);
+    }
+  } else if (promote) {
+    rc = launch_gemm_f8p<0, 2, 64, 2>(gu, grid_gu, stream);
+    if (rc == DWDP_OK) rc = quant_h();
+    if (rc == DWDP_OK)
+      rc = pair_dn ? launch_gemm_f8p<1, 2, 64, 2>(dn, grid_dn, stream) : launch_gemm_f8p<1, 1, 64, 2>(dn, grid_dn, stream);
   } else {
-    rc = launch_gemm<0, false>(gu, grid_gu, stream);
-    if (rc == DWDP_OK) rc = launch_gemm<1, false>(dn, grid_dn, stream);
+    rc = launch_gemm<0>(gu, grid_gu, stream);
+    if (rc == DWDP_OK) rc = launch_gemm<1>(dn, grid_dn, stream);
   }
   return rc;
+}
+
+// The reference's quantize_activations_blockwise (DWDP/executor/fp8.py:86-115) alone:
+// rows of `src` (bf16 [src_rows, K], row r read from row_index[r] when given) -> e4m3
+// [rows, K] and fp32 scales [rows][K / 128] (scale_rowmajor) or [K / 128][rows].
+extern "C" int dwdp_quantize_activations_launch(const void* src, int64_t src_rows, const int64_t* row_index,
+                                                int64_t rows, int K, void* dst, float* scales, int scale_rowmajor,
+                                                int* status, cudaStream_t stream) {
+  if (rows < 0 || K <= 0 || K % 128 != 0 || rows > INT32_MAX) return DWDP_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return DWDP_OK;
+  QuantParams q{};
+  q.seg[0] = QuantSeg{reinterpret_cast<const __nv_bfloat16*>(src), reinterpret_cast<uint8_t*>(dst), scales,
+                      (int)rows, K, row_index, src_rows, scale_rowmajor};
+  q.st = reinterpret_cast<DeviceStatus*>(status);
+  q.blk = 1;
+  q.per_warp = 1;
+  return launch_chained(quant_kernel, dim3(quant_blocks_blk(rows * ((K + 511) / 512))), dim3(kPlanThreads), 0,
+                        stream, 1u, q) == cudaSuccess
+             ? DWDP_OK
+             : DWDP_ERR_CUDA;
 }
 
 #ifdef DWDP_PROFILE_ROLES

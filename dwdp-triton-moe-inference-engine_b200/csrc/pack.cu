@@ -8,12 +8,16 @@
 // the e4m3 conversion rounds to nearest even with saturation, as torch does for
 // in-range values, so the quantised bytes equal torch's.
 //
+// Per-tensor scales (DWDP/executor/fp8.py:45-49, convert_qwen_weights_to_fp8_once
+// with a scale_map: scale = max(amax of the whole matrix, 1e-5) / 448) are stored
+// per output row like CHANNEL scales, every row of a matrix holding the same value,
+// so the GEMMs treat both modes alike.
+//
 // Tile layout: tile (rb, kb) of matrix p at index (rb * KB + kb) * P + p.
-//   fp8 CHANNEL : 128 rows x 128 inputs, 128-byte rows in the 128B-swizzled smem
-//                 image (16-byte chunk c of row r stored at chunk c ^ (r & 7)):
+//   fp8 (all modes): 128 rows x 128 inputs, 128-byte rows in the 128B-swizzled
+//                 smem image (16-byte chunk c of row r stored at chunk c ^ (r & 7)):
 //                 the e4m3 operand the tcgen05 kind::f8f6f4 MMA reads directly.
-//   fp8 BLOCK128: 128 rows x 64 inputs, 64-byte rows, plain row-major (the
-//                 converter warps fold the block scale in while widening).
+//                 A BLOCK128 tile is exactly one scale block.
 //   bf16        : 128 rows x 64 inputs, 128-byte rows in the swizzled image.
 #include "common.cuh"
 
@@ -23,7 +27,8 @@ constexpr int kTileRows = 128;
 
 // inputs per tile for a (dtype, scale mode) pair
 __host__ __device__ inline int tile_cols(int dst_dtype, int mode) {
-  return dst_dtype == DWDP_DTYPE_FP8_E4M3 && mode == DWDP_SCALE_CHANNEL ? 128 : 64;
+  (void)mode;
+  return dst_dtype == DWDP_DTYPE_FP8_E4M3 ? 128 : 64;
 }
 
 template <typename TS>
@@ -39,7 +44,12 @@ struct MatPtrs {
   const void* p[2];
 };
 
-// amax per output row (CHANNEL) or per 128x128 block (BLOCK128) -> scales
+__host__ __device__ inline bool row_scaled(int mode) {
+  return mode == DWDP_SCALE_CHANNEL || mode == DWDP_SCALE_TENSOR;
+}
+
+// amax per output row (CHANNEL, TENSOR) or per 128x128 block (BLOCK128) -> scales.
+// TENSOR writes the raw row amax; tensor_scale_kernel then folds the rows.
 template <typename TS>
 __global__ void scale_kernel(MatPtrs src, int R, int C, int mode, float* __restrict__ scales) {
   const int p = blockIdx.z;
@@ -47,7 +57,7 @@ __global__ void scale_kernel(MatPtrs src, int R, int C, int mode, float* __restr
   __shared__ float red[32];
   float m = 0.f;
   int64_t out_index;
-  if (mode == DWDP_SCALE_CHANNEL) {
+  if (row_scaled(mode)) {
     const int r = blockIdx.x;
     for (int c = threadIdx.x; c < C; c += blockDim.x) m = fmaxf(m, fabsf(ldf(w, (int64_t)r * C + c)));
     out_index = (int64_t)p * R + r;
@@ -65,8 +75,24 @@ __global__ void scale_kernel(MatPtrs src, int R, int C, int mode, float* __restr
   if (threadIdx.x == 0) {
     float a = 0.f;
     for (int i = 0; i < (int)(blockDim.x >> 5); ++i) a = fmaxf(a, red[i]);
-    scales[out_index] = __fdiv_rn(fmaxf(a, 1e-5f), 448.0f);
+    scales[out_index] = mode == DWDP_SCALE_TENSOR ? a : __fdiv_rn(fmaxf(a, 1e-5f), 448.0f);
   }
+}
+
+// TENSOR: matrix p's row amaxes [p][R] -> max over the rows, scale written to every row.
+__global__ void tensor_scale_kernel(int R, float* __restrict__ scales) {
+  float* s = scales + (int64_t)blockIdx.x * R;
+  __shared__ float red[32];
+  float m = 0.f;
+  for (int r = threadIdx.x; r < R; r += blockDim.x) m = fmaxf(m, s[r]);
+  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  float a = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) a = fmaxf(a, red[i]);
+  __syncthreads();
+  const float sc = __fdiv_rn(fmaxf(a, 1e-5f), 448.0f);
+  for (int r = threadIdx.x; r < R; r += blockDim.x) s[r] = sc;
 }
 
 __device__ __forceinline__ uint8_t to_e4m3(float v) {
@@ -87,17 +113,15 @@ tile_kernel(MatPtrs src, int R, int C, int P, int dst_dtype, int mode,
   const int64_t tile_index = ((int64_t)rb * KB + kb) * P + p;
   const int64_t row_base = (int64_t)grow * C + kb * kTileCols;
   if (dst_dtype == DWDP_DTYPE_FP8_E4M3) {
-    const bool channel = mode == DWDP_SCALE_CHANNEL;
     float s;
-    if (channel) s = scales[(int64_t)p * R + grow];
+    if (row_scaled(mode)) s = scales[(int64_t)p * R + grow];
     else s = scales[((int64_t)p * (R / 128) + rb) * (C / 128) + (kb * kTileCols) / 128];
     uint8_t* out = dst + tile_index * (kTileRows * kTileCols) + r * kTileCols;
     for (int c = 0; c < kTileCols; c += 16) {
       alignas(16) uint8_t b[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) b[j] = to_e4m3(__fdiv_rn(ldf(w, row_base + c + j), s));
-      const int pos = channel ? (((c >> 4) ^ (r & 7)) << 4) : c;
-      *reinterpret_cast<uint4*>(out + pos) = *reinterpret_cast<uint4*>(b);
+      *reinterpret_cast<uint4*>(out + (((c >> 4) ^ (r & 7)) << 4)) = *reinterpret_cast<uint4*>(b);
     }
   } else {
     uint8_t* out = dst + tile_index * (kTileRows * kTileCols * 2) + r * 128;
@@ -121,14 +145,13 @@ untile_kernel(const uint8_t* __restrict__ tiles, const float* __restrict__ scale
   const int64_t tile_index = ((int64_t)rb * KB + kb) * P + p;
   float* o = out + ((int64_t)p * R + grow) * C + kb * kTileCols;
   if (dst_dtype == DWDP_DTYPE_FP8_E4M3) {
-    const bool channel = mode == DWDP_SCALE_CHANNEL;
     float s;
-    if (channel) s = scales[(int64_t)p * R + grow];
+    if (row_scaled(mode)) s = scales[(int64_t)p * R + grow];
     else s = scales[((int64_t)p * (R / 128) + rb) * (C / 128) + (kb * kTileCols) / 128];
     const uint8_t* in = tiles + tile_index * (kTileRows * kTileCols) + r * kTileCols;
     for (int c = 0; c < kTileCols; ++c) {
       __nv_fp8_e4m3 q;
-      q.__x = in[channel ? ((((c >> 4) ^ (r & 7)) << 4) | (c & 15)) : c];
+      q.__x = in[(((c >> 4) ^ (r & 7)) << 4) | (c & 15)];
       o[c] = float(q) * s;
     }
   } else {
@@ -152,7 +175,7 @@ extern "C" size_t dwdp_packed_weight_bytes(int rows, int cols, int num_mats, int
 }
 
 extern "C" size_t dwdp_packed_scale_floats(int rows, int cols, int num_mats, int scale_mode) {
-  if (scale_mode == DWDP_SCALE_CHANNEL) return (size_t)num_mats * rows;
+  if (scale_mode == DWDP_SCALE_CHANNEL || scale_mode == DWDP_SCALE_TENSOR) return (size_t)num_mats * rows;
   if (scale_mode == DWDP_SCALE_BLOCK128) return (size_t)num_mats * (rows / 128) * (cols / 128);
   return 0;
 }
@@ -160,7 +183,8 @@ extern "C" size_t dwdp_packed_scale_floats(int rows, int cols, int num_mats, int
 static bool pack_args_ok(int rows, int cols, int P, int dst_dtype, int mode) {
   if (rows <= 0 || cols <= 0 || (rows % 128) != 0 || (cols % 128) != 0) return false;
   if (P != 1 && P != 2) return false;
-  if (dst_dtype == DWDP_DTYPE_FP8_E4M3) return mode == DWDP_SCALE_CHANNEL || mode == DWDP_SCALE_BLOCK128;
+  if (dst_dtype == DWDP_DTYPE_FP8_E4M3)
+    return mode == DWDP_SCALE_CHANNEL || mode == DWDP_SCALE_BLOCK128 || mode == DWDP_SCALE_TENSOR;
   if (dst_dtype == DWDP_DTYPE_BF16) return mode == DWDP_SCALE_NONE;
   return false;
 }
@@ -177,11 +201,12 @@ extern "C" int dwdp_pack_launch(const void* const* src_mats, int src_dtype, int 
 #define DWDP_PACK(TS)                                                                          \
   do {                                                                                         \
     if (dst_dtype == DWDP_DTYPE_FP8_E4M3) {                                                    \
-      if (mode == DWDP_SCALE_CHANNEL)                                                          \
+      if (row_scaled(mode))                                                                    \
         scale_kernel<TS><<<dim3(rows, 1, P), 256, 0, stream>>>(m, rows, cols, mode, scales);   \
       else                                                                                     \
         scale_kernel<TS><<<dim3(rows / 128, cols / 128, P), 256, 0, stream>>>(m, rows, cols,   \
                                                                               mode, scales);   \
+      if (mode == DWDP_SCALE_TENSOR) tensor_scale_kernel<<<P, 1024, 0, stream>>>(rows, scales); \
     }                                                                                          \
     tile_kernel<TS><<<tgrid, 128, 0, stream>>>(m, rows, cols, P, dst_dtype, mode, scales,      \
                                                (uint8_t*)dst);                                 \

@@ -19,7 +19,7 @@ import torch
 
 from . import _lib, ops
 from .communication import CommunicationEngine, export_ipc_handle
-from .weights import ExpertWeightStore
+from .weights import ExpertWeightStore, act_quant_code
 
 
 def owner_of(expert_id: int, num_experts: int, world_size: int) -> int:
@@ -70,6 +70,7 @@ class ShardedExpertStore:
         scale_mode: int = _lib.SCALE_CHANNEL,
         device: torch.device | str = "cuda",
         num_buffers: int = 1,
+        activation_quant: str = "hilo",
     ) -> None:
         self.num_experts = num_experts
         self.hidden_size = hidden_size
@@ -80,7 +81,8 @@ class ShardedExpertStore:
         self.owned = owned_experts(rank, num_experts, world_size)
         self.local_index = {e: i for i, e in enumerate(self.owned)}
         self.local = ExpertWeightStore(max(1, len(self.owned)), hidden_size, intermediate_size,
-                                       weight_dtype=weight_dtype, scale_mode=scale_mode, device=self.device)
+                                       weight_dtype=weight_dtype, scale_mode=scale_mode, device=self.device,
+                                       activation_quant=activation_quant)
         self.weight_dtype = self.local.weight_dtype
         self.scale_mode = self.local.scale_mode
         self.slab_bytes = self.local.slab_bytes
@@ -152,11 +154,12 @@ class ShardedExpertStore:
     def select_buffer(self, buffer: int) -> None:
         self.buffer = buffer
 
-    def group(self) -> _lib.ExpertGroup:
+    def group(self, activation_quant: str | None = None) -> _lib.ExpertGroup:
         if not self._ptrs:
             raise RuntimeError("ShardedExpertStore.connect() has not run")
         w13, w2, s13, s2 = self._ptrs[self.buffer]
         g = _lib.ExpertGroup()
+        g.act_quant = act_quant_code(activation_quant or self.local.activation_quant)
         g.num_experts = self.num_experts
         g.hidden_size = self.hidden_size
         g.intermediate_size = self.intermediate_size

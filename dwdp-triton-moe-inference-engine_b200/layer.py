@@ -39,7 +39,9 @@ class MoELayer:
     """One MoE layer: ``E`` routed SwiGLU experts (top-k over the router logits,
     softmax over the k selected, optional renormalisation) plus an optional
     sigmoid-gated shared expert. Activations are bf16; weights are fp8
-    (per-channel or 128x128 block scales) or bf16, held in an ExpertWeightStore."""
+    (per-channel, per-tensor or 128x128 block scales) or bf16, held in an
+    ExpertWeightStore. ``activation_quant`` ("hilo" or "block128", see
+    ExpertWeightStore) chooses how the e4m3 GEMMs carry the activations."""
 
     def __init__(
         self,
@@ -53,6 +55,7 @@ class MoELayer:
         renormalize: bool = True,
         eps: float = 1e-9,
         score_scale: float = 1.0,
+        activation_quant: str | None = None,
     ) -> None:
         E, H = router_weight.shape
         if experts.num_experts != E or experts.hidden_size != H:
@@ -70,6 +73,9 @@ class MoELayer:
         self.renormalize = renormalize
         self.eps = eps
         self.score_scale = score_scale
+        # e4m3 activation scheme of both groups' GEMMs (the store's own setting unless given)
+        self.activation_quant = activation_quant or getattr(experts, "activation_quant", None) or \
+            getattr(getattr(experts, "local", None), "activation_quant", "hilo")
         self.num_experts = E
         self.hidden_size = H
         self._ws: dict[int, LayerWorkspace] = {}
@@ -82,8 +88,9 @@ class MoELayer:
 
     def refresh_handles(self) -> None:
         """Rebuild the C handles (call after swapping pointer-array tensors)."""
-        self._routed_group = self.experts.group()
-        self._shared_group = self.shared_expert.group() if self.shared_expert is not None else None
+        aq = self.activation_quant
+        self._routed_group = self.experts.group(aq)
+        self._shared_group = self.shared_expert.group(aq) if self.shared_expert is not None else None
 
     # ------------------------------------------------------------------ workspace
     def workspace(self, num_tokens: int) -> LayerWorkspace:
@@ -216,9 +223,12 @@ class MoELayer:
         planes,] down GEMM, merge."""
         router = 1 if self.router_weight.dtype == torch.bfloat16 and self.num_experts <= 256 else 2
         dispatch = 1 if num_tokens * self.top_k <= 256 else 2
-        experts = 4  # e4m3 weights: planes in the plan launch + one between the GEMMs; else one row gather
+        # e4m3 hi/lo: plan(+planes), gate/up, planes, down; e4m3 block128: the gate/up epilogue
+        # writes the intermediate's e4m3 rows, so no launch between the GEMMs; bf16: row gather
+        fp8 = self.experts.weight_dtype == torch.float8_e4m3fn
+        experts = 3 if (fp8 and self.activation_quant == "block128") else 4
         if self.shared_expert is not None and self.overlap_shared:
-            experts += 4  # the shared expert's own plan/gate-up/planes/down launches
+            experts += experts  # the shared expert's own launches
         return router + dispatch + experts + 1
 
     def read_status(self, num_tokens: int) -> tuple[int, ...]:

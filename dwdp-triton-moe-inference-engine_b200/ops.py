@@ -198,6 +198,33 @@ def gather_rows(hidden: torch.Tensor, token_index: torch.Tensor, out: torch.Tens
     return out
 
 
+def quantize_activations_blockwise(
+    source: torch.Tensor, row_index: torch.Tensor | None = None, *, status: torch.Tensor | None = None,
+    scale_layout: str = "rows",
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """The reference's ``quantize_activations_blockwise`` (DWDP/executor/fp8.py:86-115) on
+    the GPU: bf16 [M, K] -> (float8_e4m3fn [M, K], fp32 scales [M, K/128]), one scale per
+    (row, 128 channels). ``row_index`` quantises source rows ``row_index[r]`` instead of
+    row r; ``scale_layout="blocks"`` returns the scales transposed, [K/128, M]."""
+    _require_cuda(source)
+    if source.dtype != torch.bfloat16 or source.dim() != 2:
+        raise ValueError("quantize_activations_blockwise expects a 2D bf16 [tokens, channels] tensor")
+    if scale_layout not in ("rows", "blocks"):
+        raise ValueError("scale_layout must be 'rows' or 'blocks'")
+    x = source.contiguous()
+    M0, K = x.shape
+    idx = row_index.to(torch.int64).contiguous() if row_index is not None else None
+    M = idx.numel() if idx is not None else M0
+    q = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=x.device)
+    shape = (M, K // 128) if scale_layout == "rows" else (K // 128, M)
+    sc = torch.empty(shape, dtype=torch.float32, device=x.device)
+    rc = _lib.load().dwdp_quantize_activations_blockwise(
+        x.data_ptr(), M0, _ptr(idx), M, K, q.data_ptr(), sc.data_ptr(), 0 if scale_layout == "rows" else 1,
+        _ptr(status), _stream())
+    _lib.check(rc, "quantize_activations_blockwise")
+    return q, sc
+
+
 # --------------------------------------------------------------------------- schedule
 @dataclass
 class ScheduleResult:

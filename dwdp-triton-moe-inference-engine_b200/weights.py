@@ -17,6 +17,19 @@ import torch
 from . import _lib, ops
 
 
+ACTIVATION_QUANT = {"hilo": _lib.ACT_HILO, "block128": _lib.ACT_BLOCK128}
+
+
+def check_activation_quant(mode: str) -> str:
+    if mode not in ACTIVATION_QUANT:
+        raise ValueError(f"activation_quant must be one of {sorted(ACTIVATION_QUANT)}, got {mode!r}")
+    return mode
+
+
+def act_quant_code(mode: str) -> int:
+    return ACTIVATION_QUANT[check_activation_quant(mode)]
+
+
 def _align(x: int, a: int = 256) -> int:
     return (x + a - 1) // a * a
 
@@ -24,7 +37,12 @@ def _align(x: int, a: int = 256) -> int:
 class ExpertWeightStore:
     """Packed weights of ``num_experts`` SwiGLU experts with hidden size H and
     intermediate size I. ``weight_dtype`` is ``torch.float8_e4m3fn`` (with
-    ``scale_mode`` CHANNEL or BLOCK128) or ``torch.bfloat16`` (no scale)."""
+    ``scale_mode`` CHANNEL, BLOCK128 or TENSOR) or ``torch.bfloat16`` (no scale).
+
+    ``activation_quant`` picks how the e4m3 GEMMs carry the activations:
+    ``"hilo"`` (two e4m3 planes per row, about bf16 precision) or ``"block128"``
+    (one e4m3 plane with one scale per (row, 128 channels), the reference's FP8
+    scheme, DWDP/executor/fp8.py:86-115; the tensor core does half the work)."""
 
     def __init__(
         self,
@@ -36,14 +54,15 @@ class ExpertWeightStore:
         scale_mode: int = _lib.SCALE_CHANNEL,
         device: torch.device | str = "cuda",
         slabs: torch.Tensor | None = None,
+        activation_quant: str = "hilo",
     ) -> None:
         if hidden_size % 128 or intermediate_size % 128:
             raise ValueError("hidden_size and intermediate_size must be multiples of 128")
         if weight_dtype == torch.bfloat16:
             scale_mode = _lib.SCALE_NONE
         elif weight_dtype == torch.float8_e4m3fn:
-            if scale_mode not in (_lib.SCALE_CHANNEL, _lib.SCALE_BLOCK128):
-                raise ValueError("fp8 weights need SCALE_CHANNEL or SCALE_BLOCK128")
+            if scale_mode not in (_lib.SCALE_CHANNEL, _lib.SCALE_BLOCK128, _lib.SCALE_TENSOR):
+                raise ValueError("fp8 weights need SCALE_CHANNEL, SCALE_BLOCK128 or SCALE_TENSOR")
         else:
             raise ValueError("weight_dtype must be torch.float8_e4m3fn or torch.bfloat16")
         self.num_experts = num_experts
@@ -51,13 +70,15 @@ class ExpertWeightStore:
         self.intermediate_size = I = intermediate_size
         self.weight_dtype = weight_dtype
         self.scale_mode = scale_mode
+        self.activation_quant = check_activation_quant(activation_quant)
         self.device = torch.device(device)
         esz = 1 if weight_dtype == torch.float8_e4m3fn else 2
         self.w13_bytes = 2 * I * H * esz
         self.w2_bytes = H * I * esz
         if weight_dtype == torch.float8_e4m3fn:
-            self.s13_floats = 2 * I if scale_mode == _lib.SCALE_CHANNEL else 2 * (I // 128) * (H // 128)
-            self.s2_floats = H if scale_mode == _lib.SCALE_CHANNEL else (H // 128) * (I // 128)
+            per_row = scale_mode != _lib.SCALE_BLOCK128  # CHANNEL and TENSOR keep one scale per row
+            self.s13_floats = 2 * I if per_row else 2 * (I // 128) * (H // 128)
+            self.s2_floats = H if per_row else (H // 128) * (I // 128)
         else:
             self.s13_floats = self.s2_floats = 0
         self.off_w2 = _align(self.w13_bytes)
@@ -131,10 +152,12 @@ class ExpertWeightStore:
         weight_dtype: torch.dtype = torch.float8_e4m3fn,
         scale_mode: int = _lib.SCALE_CHANNEL,
         device: torch.device | str = "cuda",
+        activation_quant: str = "hilo",
     ) -> "ExpertWeightStore":
         """Build from stacked [E, I, H] gate/up and [E, H, I] down weights."""
         E, I, H = gate.shape
-        store = cls(E, H, I, weight_dtype=weight_dtype, scale_mode=scale_mode, device=device)
+        store = cls(E, H, I, weight_dtype=weight_dtype, scale_mode=scale_mode, device=device,
+                    activation_quant=activation_quant)
         for e in range(E):
             store.load_expert(e, gate[e], up[e], down[e])
         return store
@@ -158,9 +181,11 @@ class ExpertWeightStore:
         return w13[0], w13[1], w2[0]
 
     # ------------------------------------------------------------------ handles
-    def group(self) -> _lib.ExpertGroup:
-        """The ``dwdp_expert_group`` handle the C ABI takes."""
+    def group(self, activation_quant: str | None = None) -> _lib.ExpertGroup:
+        """The ``dwdp_expert_group`` handle the C ABI takes (``activation_quant``
+        overrides the store's setting for this handle)."""
         g = _lib.ExpertGroup()
+        g.act_quant = act_quant_code(activation_quant or self.activation_quant)
         g.num_experts = self.num_experts
         g.hidden_size = self.hidden_size
         g.intermediate_size = self.intermediate_size

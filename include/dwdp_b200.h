@@ -51,6 +51,21 @@ extern "C" {
 #define DWDP_SCALE_NONE 0     /* bf16 weights, no scale                     */
 #define DWDP_SCALE_CHANNEL 1  /* fp8, one fp32 scale per output row         */
 #define DWDP_SCALE_BLOCK128 2 /* fp8, one fp32 scale per 128x128 block      */
+#define DWDP_SCALE_TENSOR 3   /* fp8, one fp32 scale per expert matrix
+                                 (convert_qwen_weights_to_fp8_once with a
+                                 scale_map, DWDP/executor/fp8.py:45-49);
+                                 stored per row like CHANNEL, every row of a
+                                 matrix holding the same value              */
+
+/* ---- activation quantisation of the e4m3 expert GEMMs ------------------ */
+#define DWDP_ACT_HILO 0     /* two e4m3 planes per row, v ~ s * (hi + lo/16),
+                               one fp32 scale per row: about bf16 precision  */
+#define DWDP_ACT_BLOCK128 1 /* one e4m3 plane, one fp32 scale per (row, 128
+                               channels) = max(amax, 1e-5) / 448: the
+                               reference's FP8 activation scheme
+                               (DWDP/executor/fp8.py:86-115); the SwiGLU
+                               intermediate is re-quantised the same way
+                               (DWDP/executor/triton_tma.py:194-203)         */
 
 /* Device status word: int[4] {code, where, detail, count} in device memory,
  * zeroed by the caller. Kernels record bounded-wait timeouts and failed bounds
@@ -122,6 +137,23 @@ int dwdp_dispatch_noalloc(const int64_t* topk_idx, const void* topk_weights, int
 size_t dwdp_dispatch_noalloc_max_scratch_bytes(void);
 
 /* ======================================================================== *
+ * Activation quantisation alone (quantize_activations_blockwise,
+ * DWDP/executor/fp8.py:86-115): one e4m3 plane with one fp32 scale per
+ * (row, 128 channels), scale = max(amax, 1e-5) / 448, q = e4m3(v / scale)
+ * (IEEE division, round to nearest even): bytes and scales equal the
+ * reference's. The grouped GEMMs run the same quantiser in their planning
+ * launch (DWDP_ACT_BLOCK128).
+ *   src bf16 [src_rows, cols]; row r of the output reads src row row_index[r]
+ *   (int64, NULL = row r; an out-of-range index quantises a zero row and sets
+ *   DWDP_ERR_DEVICE_BOUNDS in *status). cols % 128 == 0.
+ *   dst e4m3 [rows, cols]; scales fp32 [rows][cols/128] (scale_layout 0, the
+ *   reference's layout) or [cols/128][rows] (scale_layout 1).
+ * ======================================================================== */
+int dwdp_quantize_activations_blockwise(const void* src, int64_t src_rows, const int64_t* row_index,
+                                        int64_t rows, int cols, void* dst, float* scales, int scale_layout,
+                                        int* status, void* stream);
+
+/* ======================================================================== *
  * Round-robin schedule over active experts in ascending id
  * (build_round_robin_schedule, round_robin.py:8-80), padded to E entries:
  * rows [0, num_active) hold the reference values, the rest are -1.
@@ -138,11 +170,10 @@ int dwdp_schedule(const int64_t* counts, const int64_t* offsets, int num_experts
  * GEMM streams: for an [R, Kd] projection (R output rows, Kd inputs, both
  * multiples of 128) tiles of 128 rows x TK inputs, tile (rb, kb) of matrix p
  * of a P-matrix pack at tile index (rb * (Kd/TK) + kb) * P + p.
- *   FP8 CHANNEL : TK = 128, 16384-byte tiles of 128-byte rows in the
- *                 128-byte-swizzled smem image (chunk c of row r at c ^ (r&7));
- *                 scales fp32 [P][R].
- *   FP8 BLOCK128: TK = 64, 8192-byte tiles, plain rows of 64 bytes; scales
- *                 fp32 [P][R/128][Kd/128].
+ *   FP8 (every scale mode): TK = 128, 16384-byte tiles of 128-byte rows in
+ *                 the 128-byte-swizzled smem image (chunk c of row r at
+ *                 c ^ (r&7)); scales fp32 [P][R] (CHANNEL, TENSOR) or
+ *                 [P][R/128][Kd/128] (BLOCK128).
  *   BF16        : TK = 64, 16384-byte tiles in the 128-byte-swizzled image.
  * Quantisation follows DWDP/executor/fp8.py:118-146: scale = max(amax, 1e-5)
  * / 448, q = e4m3(w / scale) (round to nearest even, IEEE division).
@@ -176,6 +207,8 @@ typedef struct dwdp_expert_group {
   const void* const* w2;   /* [E] packed down tiles (num_mats = 1)        */
   const float* const* s13; /* [E] gate/up scales                          */
   const float* const* s2;  /* [E] down scales                             */
+  int act_quant;           /* DWDP_ACT_* (e4m3 weights only; a shared group
+                              follows the routed group's setting)          */
 } dwdp_expert_group;
 
 /* ======================================================================== *

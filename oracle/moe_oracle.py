@@ -139,6 +139,18 @@ def quantize_channel(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return (w.float() / scales[:, None]).to(torch.float8_e4m3fn), scales
 
 
+def quantize_tensor(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """One scale per matrix: scale = max(amax |w|, 1e-5) / 448, q = e4m3(w / scale)
+    (DWDP/executor/fp8.py:45-49, convert_qwen_weights_to_fp8_once with a scale_map).
+    Returns (e4m3 [N, K], fp32 scalar tensor)."""
+    scale = w.float().abs().max().clamp(min=1e-5) / FP8_E4M3_MAX
+    return (w.float() / scale).to(torch.float8_e4m3fn), scale
+
+
+def dequantize_tensor(q: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    return q.float() * scale
+
+
 def dequantize_blockwise(q: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
     N, K = q.shape
     s = scales.repeat_interleave(128, 0)[:N].repeat_interleave(128, 1)[:, :K]
@@ -162,6 +174,27 @@ def swiglu_expert(x: torch.Tensor, gate: torch.Tensor, up: torch.Tensor, down: t
     return h @ down.float().T
 
 
+def swiglu_expert_fp8_act(x: torch.Tensor, gate: torch.Tensor, up: torch.Tensor,
+                          down: torch.Tensor) -> torch.Tensor:
+    """One expert as the reference's FP8 TMA executor computes it
+    (DWDP/executor/triton_tma.py:185-207, kernels/fp8_tma.py:66-121), on dequantised
+    weights: the activation rows are quantised to e4m3 with one scale per (row, 128
+    channels) (DWDP/executor/fp8.py:86-115) and multiplied dequantised; gate and up
+    outputs are rounded to bf16 (the executor's output dtype), the SwiGLU product is
+    formed in bf16 (``gate * sigmoid(gate) * up``, each op rounded), re-quantised per
+    (row, 128) the same way, and the down projection is rounded to bf16. A GEMM that
+    promotes every 128-wide K block in fp32 (``acc += (Xq Wq^T)_kb * sx * sw``) equals
+    this dequantised product up to fp32 summation order."""
+    xq, xs = quantize_activations_blockwise(x)
+    xd = dequantize_activations_blockwise(xq, xs)
+    g = (xd @ gate.float().T).bfloat16()
+    u = (xd @ up.float().T).bfloat16()
+    h = g * torch.sigmoid(g) * u
+    hq, hs = quantize_activations_blockwise(h.float())
+    hd = dequantize_activations_blockwise(hq, hs)
+    return (hd @ down.float().T).bfloat16().float()
+
+
 def moe_forward(
     x: torch.Tensor,
     topk_idx: torch.Tensor,
@@ -171,13 +204,21 @@ def moe_forward(
     shared: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None,
     shared_gate: torch.Tensor | None = None,
     bf16_roundings: bool = False,
+    act_quant: str = "none",
 ) -> torch.Tensor:
     """Routed experts in ascending expert order over the expert-major packing,
     weighted rows accumulated token-major (PyTorchExecutor + PyTorchMerger,
     DWDP/executor/pytorch.py:66-160, DWDP/merger/kernels/reference.py:6-27), then
     ``out += gate * shared(x)`` (DWDP/adapters/qwen15_moe.py:302-319). fp32 arithmetic;
     ``bf16_roundings`` applies the three roundings of a bf16 data path (SwiGLU intermediate,
-    each weighted expert row, the output) so that only accumulation order differs."""
+    each weighted expert row, the output) so that only accumulation order differs.
+    ``act_quant="block128"`` runs every expert (the shared one included) as the
+    reference's FP8 executor does (:func:`swiglu_expert_fp8_act`), the weighted row
+    rounded to bf16 as that executor's ``expert_out * weights`` is; ``experts`` may be
+    any indexable whose item ``e`` is only looked up for experts the routing selects."""
+    if act_quant not in ("none", "block128"):
+        raise ValueError(f"unknown act_quant {act_quant!r}")
+    fp8_act = act_quant == "block128"
     x = x.float()
     T, H = x.shape
     K = topk_idx.shape[-1]
@@ -190,12 +231,16 @@ def moe_forward(
             continue
         tok = torch.from_numpy(plan["tok"][s:t])
         w = torch.from_numpy(np.ascontiguousarray(plan["weights"][s:t])).float()
-        y = swiglu_expert(x[tok], *experts[e], round_intermediate=bf16_roundings) * w[:, None]
+        if fp8_act:
+            y = (swiglu_expert_fp8_act(x[tok], *experts[e]).bfloat16() * w[:, None].bfloat16()).float()
+        else:
+            y = swiglu_expert(x[tok], *experts[e], round_intermediate=bf16_roundings) * w[:, None]
         if bf16_roundings:
             y = y.bfloat16().float()
         out.index_add_(0, tok, y)
     if shared is not None:
-        ys = swiglu_expert(x, *shared, round_intermediate=bf16_roundings)
+        ys = swiglu_expert_fp8_act(x, *shared) if fp8_act else \
+            swiglu_expert(x, *shared, round_intermediate=bf16_roundings)
         if shared_gate is not None:
             ys = ys * shared_gate.float().reshape(-1, 1)
         if bf16_roundings:
@@ -220,3 +265,9 @@ def quantize_activations_blockwise(x: torch.Tensor) -> tuple[torch.Tensor, torch
     scales = work.abs().amax(dim=-1).clamp(min=1e-5) / FP8_E4M3_MAX
     q = (work / scales.unsqueeze(-1)).view(M, kb * 128)[:, :K]
     return q.to(torch.float8_e4m3fn), scales.contiguous()
+
+
+def dequantize_activations_blockwise(q: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """Inverse of :func:`quantize_activations_blockwise`: q * scale of its (row, 128) block."""
+    M, K = q.shape
+    return q.float() * scales.repeat_interleave(128, 1)[:, :K]

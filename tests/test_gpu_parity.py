@@ -117,11 +117,8 @@ def test_router_top1_weight_is_one(pkg):
 
 
 def _decode_fp8_tiles(tiles: torch.Tensor, R: int, C: int, P: int, channel: bool) -> torch.Tensor:
-    """Undo the packed tiling: CHANNEL tiles are 128 x 128 in the 128-byte-swizzled
-    image (16-byte chunk c of row r at c ^ (r % 8)), BLOCK128 tiles 128 x 64 plain."""
-    if not channel:
-        t = tiles.cpu().view(R // 128, C // 64, P, 128, 64)
-        return t.permute(2, 0, 3, 1, 4).reshape(P, R, C)
+    """Undo the packed tiling: e4m3 tiles (every scale mode) are 128 x 128 in the
+    128-byte-swizzled image (16-byte chunk c of row r at c ^ (r % 8))."""
     t = tiles.cpu().view(R // 128, C // 128, P, 128, 8, 16)
     r = torch.arange(128).view(128, 1)
     src_chunk = torch.arange(8).view(1, 8) ^ (r % 8)  # logical chunk c sits at c ^ (r % 8)
@@ -129,24 +126,28 @@ def _decode_fp8_tiles(tiles: torch.Tensor, R: int, C: int, P: int, channel: bool
     return t.reshape(R // 128, C // 128, P, 128, 128).permute(2, 0, 3, 1, 4).reshape(P, R, C)
 
 
-@pytest.mark.parametrize("mode", ["channel", "block"])
+@pytest.mark.parametrize("mode", ["channel", "block", "tensor"])
 def test_pack_fp8_bit_exact(pkg, orc, mode):
     R, C = 384, 256
     g = torch.Generator().manual_seed(3)
     a = torch.randn(R, C, generator=g) * 0.02
     b = torch.randn(R, C, generator=g) * 0.5
-    m = pkg._lib.SCALE_CHANNEL if mode == "channel" else pkg._lib.SCALE_BLOCK128
+    m = {"channel": pkg._lib.SCALE_CHANNEL, "block": pkg._lib.SCALE_BLOCK128, "tensor": pkg._lib.SCALE_TENSOR}[mode]
+    quant = {"channel": orc.quantize_channel, "block": orc.quantize_blockwise, "tensor": orc.quantize_tensor}[mode]
     tiles, scales = pkg.ops.pack_weights([a.to(DEV), b.to(DEV)], torch.float8_e4m3fn, m)
-    q = _decode_fp8_tiles(tiles, R, C, 2, mode == "channel")
+    q = _decode_fp8_tiles(tiles, R, C, 2, True)
     for p, src in enumerate((a, b)):
-        rq, rs = orc.quantize_channel(src) if mode == "channel" else orc.quantize_blockwise(src)
+        rq, rs = quant(src)
         assert torch.equal(q[p], rq.view(torch.uint8)), f"mat {p}: quantised bytes differ"
-        n = rs.numel()
-        assert torch.equal(scales[p * n:(p + 1) * n].cpu(), rs.reshape(-1))
+        if mode == "tensor":  # one scale per matrix, stored on every row
+            assert torch.equal(scales[p * R:(p + 1) * R].cpu(), rs.reshape(1).expand(R))
+        else:
+            n = rs.numel()
+            assert torch.equal(scales[p * n:(p + 1) * n].cpu(), rs.reshape(-1))
     deq = pkg.ops.unpack_weights(tiles, scales, R, C, 2, torch.float8_e4m3fn, m).cpu()
-    ref = orc.dequantize_channel(*orc.quantize_channel(a)) if mode == "channel" else \
-        orc.dequantize_blockwise(*orc.quantize_blockwise(a))
-    assert torch.equal(deq[0], ref)
+    deqf = {"channel": orc.dequantize_channel, "block": orc.dequantize_blockwise,
+            "tensor": orc.dequantize_tensor}[mode]
+    assert torch.equal(deq[0], deqf(*quant(a)))
 
 
 def test_pack_bf16_roundtrip(pkg):
@@ -194,7 +195,7 @@ def test_merge_reference_golden(pkg):
     assert out[:, :2].tolist() == [[3.0, 10.0], [23.0, 20.0]]
 
 
-def _make_layer(pkg, E, H, I, K, Is, wdtype, mode, seed=0):
+def _make_layer(pkg, E, H, I, K, Is, wdtype, mode, seed=0, act="hilo"):
     g = torch.Generator().manual_seed(seed)
     wr = (torch.randn(E, H, generator=g) / H**0.5).bfloat16()
     gw = torch.randn(E, I, H, generator=g) * 0.02
@@ -210,7 +211,7 @@ def _make_layer(pkg, E, H, I, K, Is, wdtype, mode, seed=0):
         shared = pkg.ExpertWeightStore.from_weights(sg.to(DEV), su.to(DEV), sd.to(DEV),
                                                    weight_dtype=wdtype, scale_mode=mode, device=DEV)
         gate = (torch.randn(H, generator=g) * 0.02).bfloat16().to(DEV)
-    layer = pkg.MoELayer(wr.to(DEV), store, K, shared_expert=shared, shared_gate_weight=gate)
+    layer = pkg.MoELayer(wr.to(DEV), store, K, shared_expert=shared, shared_gate_weight=gate, activation_quant=act)
     return layer
 
 
@@ -225,10 +226,17 @@ def _check_layer(pkg, orc, layer, T, tol, seed=1):
     shared = tuple(t.cpu() for t in layer.shared_expert.dequantized(0)) if layer.shared_expert else None
     sgate = ws.router.shared_gate.cpu() if ws.router.shared_gate is not None else None
     ref = orc.moe_forward(x.float(), ws.router.topk_indices.cpu(), ws.router.topk_weights.cpu(), experts,
-                          shared=shared, shared_gate=sgate)
+                          shared=shared, shared_gate=sgate, act_quant=oracle_act_quant(layer))
     err = orc.rel_frobenius(y.float().cpu(), ref)
     assert err < tol, f"T={T}: rel Frobenius {err:.3e} >= {tol}"
     return err
+
+
+def oracle_act_quant(layer) -> str:
+    """The oracle mode matching the layer: e4m3 GEMMs on block128 activations are checked
+    against the reference's FP8 executor math, everything else against fp32."""
+    fp8 = layer.experts.weight_dtype == torch.float8_e4m3fn
+    return "block128" if (fp8 and layer.activation_quant == "block128") else "none"
 
 
 @pytest.mark.parametrize("T", [1, 7, 64, 300])
@@ -381,3 +389,80 @@ def test_moe_layer_tile_variants(pkg, orc, monkeypatch, wide, pair, T):
     monkeypatch.setenv("DWDP_PAIR_DOWN", pair)
     layer = _make_layer(pkg, 8, 512, 256, 2, 512, torch.float8_e4m3fn, pkg._lib.SCALE_CHANNEL, seed=11)
     _check_layer(pkg, orc, layer, T, FP8_TOL)
+
+
+# --------------------------------------------------------------------------- block128 activations
+@pytest.mark.parametrize("M,K", [(1, 128), (37, 384), (300, 1408), (64, 2048), (5, 5632)])
+def test_quantize_activations_blockwise_bit_exact(pkg, orc, M, K):
+    """The single-plane quantiser equals the reference's quantize_activations_blockwise
+    (pinned by tests/golden/quant_cases.npz): every e4m3 byte and every scale, including an
+    all-zero block (scale clamped to 1e-5 / 448), in both scale layouts and through a row index."""
+    g = torch.Generator().manual_seed(M * 7 + K)
+    x = (torch.randn(M, K, generator=g) * torch.rand(M, 1, generator=g) * 4).bfloat16()
+    x[0, :128] = 0
+    rq, rs = orc.quantize_activations_blockwise(x.float())
+    q, s = pkg.ops.quantize_activations_blockwise(x.to(DEV))
+    assert torch.equal(q.cpu().view(torch.uint8), rq.view(torch.uint8))
+    assert torch.equal(s.cpu(), rs)
+    idx = torch.randint(0, M, (2 * M + 1,), generator=g)
+    q2, s2 = pkg.ops.quantize_activations_blockwise(x.to(DEV), idx.to(DEV), scale_layout="blocks")
+    assert torch.equal(q2.cpu().view(torch.uint8), rq.view(torch.uint8)[idx])
+    assert torch.equal(s2.cpu(), rs[idx].T)
+
+
+def test_quantize_activations_bad_index_records_status(pkg):
+    x = torch.randn(4, 256, device=DEV).bfloat16()
+    st = torch.zeros(4, dtype=torch.int32, device=DEV)
+    q, _ = pkg.ops.quantize_activations_blockwise(x, torch.tensor([0, 9, 2], device=DEV), status=st)
+    torch.cuda.synchronize()
+    assert st.cpu().tolist()[0] == pkg._lib.DWDP_ERR_DEVICE_BOUNDS
+    assert (q[1].cpu().view(torch.uint8) == 0).all()
+
+
+@pytest.mark.parametrize("T", [1, 7, 64, 300, 1024])
+@pytest.mark.parametrize("wcfg", ["channel", "block", "tensor"])
+def test_moe_layer_block128_activations(pkg, orc, T, wcfg):
+    """One e4m3 activation plane per (row, 128) with per-K-block promotion, against the
+    reference FP8 executor's math on the same dequantised weights (within 2e-2)."""
+    mode = {"channel": pkg._lib.SCALE_CHANNEL, "block": pkg._lib.SCALE_BLOCK128,
+            "tensor": pkg._lib.SCALE_TENSOR}[wcfg]
+    layer = _make_layer(pkg, 8, 512, 256, 2, 512, torch.float8_e4m3fn, mode, seed=T + 3, act="block128")
+    err = _check_layer(pkg, orc, layer, T, FP8_TOL)
+    assert err < 1e-2, err  # the same quantised operands: only summation order and h's re-quantisation differ
+
+
+@pytest.mark.parametrize("wide,pair", [("1", "0"), ("0", "1"), ("0", "0")])
+@pytest.mark.parametrize("T", [7, 1024])
+def test_moe_layer_block128_tile_variants(pkg, orc, monkeypatch, wide, pair, T):
+    """Every single-plane kernel variant (64- or 128-token tiles, single or paired down row
+    blocks) against the oracle, with a shared expert whose down projection splits K at T = 7."""
+    monkeypatch.setenv("DWDP_WIDE_TILES", wide)
+    monkeypatch.setenv("DWDP_PAIR_DOWN", pair)
+    layer = _make_layer(pkg, 8, 512, 256, 2, 2048, torch.float8_e4m3fn, pkg._lib.SCALE_CHANNEL, seed=12,
+                        act="block128")
+    _check_layer(pkg, orc, layer, T, FP8_TOL)
+
+
+@pytest.mark.parametrize("mode", ["channel", "block"])
+def test_moe_experts_repeated_expert_block128(pkg, orc, mode):
+    """A hand-built plan that puts T * K rows on one expert, single-plane activations."""
+    m = pkg._lib.SCALE_CHANNEL if mode == "channel" else pkg._lib.SCALE_BLOCK128
+    layer = _make_layer(pkg, 4, 256, 256, 4, 0, torch.float8_e4m3fn, m, seed=6, act="block128")
+    T, K = 40, 4
+    x = torch.randn(T, 256, generator=torch.Generator().manual_seed(2)).bfloat16()
+    ids = torch.zeros(T, K, dtype=torch.int64)
+    ids[:, 3] = 2
+    wts = torch.rand(T, K, generator=torch.Generator().manual_seed(3))
+    ws = layer.workspace(T)
+    ws.router.topk_indices.copy_(ids)
+    ws.router.topk_weights.copy_(wts)
+    xd = x.to(DEV)
+    pkg.ops.dispatch(ws.router.topk_indices, ws.router.topk_weights, layer.num_experts,
+                     scratch=ws.dispatch_scratch, out=ws.dispatch, status=ws.status)
+    layer.run_experts(xd, ws)
+    y = pkg.ops.merge(ws.weighted, ws.dispatch.inverse_permutation, T, K, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert layer.read_status(T)[0] == 0
+    experts = [tuple(t.cpu() for t in layer.experts.dequantized(e)) for e in range(layer.num_experts)]
+    ref = orc.moe_forward(x.float(), ids, wts, experts, act_quant="block128")
+    assert orc.rel_frobenius(y.cpu(), ref) < FP8_TOL
