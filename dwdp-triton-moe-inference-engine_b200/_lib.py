@@ -100,10 +100,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                 c_void_p, c_void_p]),
     "dwdp_add_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float, c_void_p, c_void_p]),
     "dwdp_rope_append_kv": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
-                                    c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+                                    c_int, c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "dwdp_paged_attention_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "dwdp_paged_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
-                                     c_int, c_int, c_int, c_float, c_void_p, c_void_p, c_void_p, c_void_p]),
+                                     c_int, c_int, c_int, c_int, c_float, c_void_p, c_void_p, c_void_p, c_void_p]),
     "dwdp_schedule": (
         c_int,
         [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

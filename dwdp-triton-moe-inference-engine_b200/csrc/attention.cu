@@ -77,7 +77,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(__nv_bfloat16* __restr
 // ---------------------------------------------------------------------------
 __global__ void rope_append_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ bias,
                                    const int32_t* __restrict__ pos, const int32_t* __restrict__ block_table,
-                                   int max_blocks, int NH, int D, int block_size, float theta,
+                                   int max_blocks, int num_blocks, int NH, int D, int block_size, float theta,
                                    __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_cache,
                                    __nv_bfloat16* __restrict__ v_cache, DeviceStatus* st) {
   griddep_launch();
@@ -85,8 +85,9 @@ __global__ void rope_append_kernel(const __nv_bfloat16* __restrict__ qkv, const 
   const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;  // d < D/2
   const int half = D / 2;
   const int p = pos[b];
-  const int blk = block_table[(size_t)b * max_blocks + p / block_size];
-  if (blk < 0) {
+  // the position must lie inside the block table and its block inside the cache
+  const int blk = (p >= 0 && p < max_blocks * block_size) ? block_table[(size_t)b * max_blocks + p / block_size] : -1;
+  if (blk < 0 || blk >= num_blocks) {
     if (d == 0) record_error(st, DWDP_ERR_DEVICE_BOUNDS, 400, b);
     return;
   }
@@ -127,8 +128,9 @@ constexpr int kPos = 8;
 __global__ void __launch_bounds__(kAttnWarps * 32)
 paged_decode_attn_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_cache,
                          const __nv_bfloat16* __restrict__ v_cache, const int32_t* __restrict__ block_table,
-                         const int32_t* __restrict__ seq_lens, int max_blocks, int NH, int block_size, int chunk,
-                         float scale, float* __restrict__ part_ml, float* __restrict__ part_acc) {
+                         const int32_t* __restrict__ seq_lens, int max_blocks, int num_blocks, int NH,
+                         int block_size, int chunk, float scale, float* __restrict__ part_ml,
+                         float* __restrict__ part_acc, DeviceStatus* st) {
   griddep_launch();
   griddep_wait();
   __shared__ float s_m[kAttnWarps], s_l[kAttnWarps];
@@ -150,17 +152,23 @@ paged_decode_attn_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat1
   float m = -INFINITY, l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
   for (int g0 = p0 + warp * kPos; g0 < p1; g0 += kAttnWarps * kPos) {
     uint2 ku[kPos], vu[kPos];
+    bool use[kPos];  // inside the chunk and in a valid block (a bad block id is recorded and skipped)
 #pragma unroll
     for (int j = 0; j < kPos; ++j) {
       const int p = g0 + j;
+      use[j] = false;
+      ku[j] = make_uint2(0u, 0u);
+      vu[j] = make_uint2(0u, 0u);
       if (p < p1) {
         const int blk = block_table[(size_t)b * max_blocks + p / block_size];
-        const size_t off = (((size_t)blk * block_size + p % block_size) * NH + h) * kHeadDim + 4 * lane;
-        ku[j] = __ldg(reinterpret_cast<const uint2*>(k_cache + off));
-        vu[j] = __ldg(reinterpret_cast<const uint2*>(v_cache + off));
-      } else {
-        ku[j] = make_uint2(0u, 0u);
-        vu[j] = make_uint2(0u, 0u);
+        if (blk < 0 || blk >= num_blocks) {
+          if (lane == 0) record_error(st, DWDP_ERR_DEVICE_BOUNDS, 402, b);
+        } else {
+          const size_t off = (((size_t)blk * block_size + p % block_size) * NH + h) * kHeadDim + 4 * lane;
+          ku[j] = __ldg(reinterpret_cast<const uint2*>(k_cache + off));
+          vu[j] = __ldg(reinterpret_cast<const uint2*>(v_cache + off));
+          use[j] = true;
+        }
       }
     }
     float sc[kPos];
@@ -178,14 +186,14 @@ paged_decode_attn_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat1
     float mn = m;
 #pragma unroll
     for (int j = 0; j < kPos; ++j)
-      if (g0 + j < p1) mn = fmaxf(mn, sc[j]);
-    const float corr = expf(m - mn);
+      if (use[j]) mn = fmaxf(mn, sc[j]);
+    const float corr = mn == -INFINITY ? 1.f : expf(m - mn);
     l *= corr;
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[i] *= corr;
 #pragma unroll
     for (int j = 0; j < kPos; ++j) {
-      const float pe = g0 + j < p1 ? expf(sc[j] - mn) : 0.f;
+      const float pe = use[j] ? expf(sc[j] - mn) : 0.f;
       const __nv_bfloat162* vb = reinterpret_cast<const __nv_bfloat162*>(&vu[j]);
       const float2 v0 = __bfloat1622float2(vb[0]), v1 = __bfloat1622float2(vb[1]);
       l += pe;
@@ -247,8 +255,9 @@ template <int HPW>
 __global__ void __launch_bounds__((kConsumerWarps + 1) * 32)
 paged_attn_bulk_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_cache,
                        const __nv_bfloat16* __restrict__ v_cache, const int32_t* __restrict__ block_table,
-                       const int32_t* __restrict__ seq_lens, int max_blocks, int block_size, int chunk, float scale,
-                       float* __restrict__ part_ml, float* __restrict__ part_acc, DeviceStatus* st) {
+                       const int32_t* __restrict__ seq_lens, int max_blocks, int num_blocks, int block_size,
+                       int chunk, float scale, float* __restrict__ part_ml, float* __restrict__ part_acc,
+                       DeviceStatus* st) {
   constexpr int NH = kConsumerWarps * HPW;
   constexpr uint32_t kRow = NH * kHeadDim * 2;             // bytes of one position, all heads
   constexpr uint32_t kRun = kStagePos * kRow;              // bytes of one stage of K (or V)
@@ -286,7 +295,7 @@ paged_attn_bulk_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16*
         if (i >= kStages && !mbar_wait(&empty[slot], ((i / kStages) - 1) & 1, abort_flag, st, 410)) break;
         const int p = p0 + i * kStagePos;
         const int blk = block_table[(size_t)b * max_blocks + p / block_size];
-        if (blk < 0) {
+        if (blk < 0 || blk >= num_blocks) {
           record_error(st, DWDP_ERR_DEVICE_BOUNDS, 411, b);
           valid[slot] = 0;
           mbar_arrive(&full[slot]);
@@ -472,13 +481,14 @@ extern "C" int dwdp_add_rmsnorm_launch(void* x, const void* delta, const void* w
 }
 
 extern "C" int dwdp_rope_append_launch(const void* qkv, const void* bias, const int32_t* pos,
-                                       const int32_t* block_table, int B, int max_blocks, int NH, int D,
-                                       int block_size, float theta, void* q_out, void* k_cache, void* v_cache,
-                                       int* status, cudaStream_t stream) {
+                                       const int32_t* block_table, int B, int max_blocks, int num_blocks, int NH,
+                                       int D, int block_size, float theta, void* q_out, void* k_cache,
+                                       void* v_cache, int* status, cudaStream_t stream) {
   if (B <= 0) return DWDP_OK;
   if (D % 2 || D > 1024 || block_size <= 0) return DWDP_ERR_INVALID_ARGUMENT;
   return launch_chained(rope_append_kernel, dim3((unsigned)B, (unsigned)NH), dim3(D / 2), 0, stream, 1u,
-                        (const __nv_bfloat16*)qkv, (const __nv_bfloat16*)bias, pos, block_table, max_blocks, NH, D,
+                        (const __nv_bfloat16*)qkv, (const __nv_bfloat16*)bias, pos, block_table, max_blocks,
+                        num_blocks, NH, D,
                         block_size, theta, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache,
                         reinterpret_cast<DeviceStatus*>(status)) == cudaSuccess
              ? DWDP_OK
@@ -496,8 +506,8 @@ extern "C" size_t dwdp_paged_attention_workspace_bytes_impl(int B, int NH, int s
 template <int HPW>
 static cudaError_t launch_bulk_attn(dim3 grid, cudaStream_t stream, const __nv_bfloat16* q,
                                     const __nv_bfloat16* k, const __nv_bfloat16* v, const int32_t* table,
-                                    const int32_t* lens, int max_blocks, int block_size, int chunk, float scale,
-                                    float* part_ml, float* part_acc, DeviceStatus* st) {
+                                    const int32_t* lens, int max_blocks, int num_blocks, int block_size, int chunk,
+                                    float scale, float* part_ml, float* part_acc, DeviceStatus* st) {
   constexpr size_t smem = bulk_attn_smem<HPW>();
   static bool attr_set = false;
   if (!attr_set) {
@@ -507,14 +517,15 @@ static cudaError_t launch_bulk_attn(dim3 grid, cudaStream_t stream, const __nv_b
     attr_set = true;
   }
   return launch_chained(paged_attn_bulk_kernel<HPW>, grid, dim3((kConsumerWarps + 1) * 32), smem, stream, 1u, q, k, v,
-                        table, lens, max_blocks, block_size, chunk, scale, part_ml, part_acc, st);
+                        table, lens, max_blocks, num_blocks, block_size, chunk, scale, part_ml, part_acc, st);
 }
 
 // splits: context chunks per sequence (per (sequence, head) on the fallback path);
 // chunk = ceil(max_len / splits) positions, rounded up to a whole stage.
 extern "C" int dwdp_paged_attention_launch(const void* q, const void* k_cache, const void* v_cache,
                                            const int32_t* block_table, const int32_t* seq_lens, int B,
-                                           int max_blocks, int NH, int D, int block_size, int max_len, int splits,
+                                           int max_blocks, int num_blocks, int NH, int D, int block_size,
+                                           int max_len, int splits,
                                            float scale, void* workspace, void* out, int* status,
                                            cudaStream_t stream) {
   if (B <= 0) return DWDP_OK;
@@ -532,18 +543,18 @@ extern "C" int dwdp_paged_attention_launch(const void* q, const void* k_cache, c
     const auto* qq = (const __nv_bfloat16*)q;
     const auto* kk = (const __nv_bfloat16*)k_cache;
     const auto* vv = (const __nv_bfloat16*)v_cache;
-    e = NH == 8    ? launch_bulk_attn<1>(grid, stream, qq, kk, vv, block_table, seq_lens, max_blocks, block_size,
-                                         chunk, scale, part_ml, part_acc, st)
-        : NH == 16 ? launch_bulk_attn<2>(grid, stream, qq, kk, vv, block_table, seq_lens, max_blocks, block_size,
-                                         chunk, scale, part_ml, part_acc, st)
-                   : launch_bulk_attn<4>(grid, stream, qq, kk, vv, block_table, seq_lens, max_blocks, block_size,
-                                         chunk, scale, part_ml, part_acc, st);
+    e = NH == 8    ? launch_bulk_attn<1>(grid, stream, qq, kk, vv, block_table, seq_lens, max_blocks, num_blocks,
+                                         block_size, chunk, scale, part_ml, part_acc, st)
+        : NH == 16 ? launch_bulk_attn<2>(grid, stream, qq, kk, vv, block_table, seq_lens, max_blocks, num_blocks,
+                                         block_size, chunk, scale, part_ml, part_acc, st)
+                   : launch_bulk_attn<4>(grid, stream, qq, kk, vv, block_table, seq_lens, max_blocks, num_blocks,
+                                         block_size, chunk, scale, part_ml, part_acc, st);
   } else {
     const int chunk = (max_len + splits - 1) / splits;
     e = launch_chained(paged_decode_attn_kernel, dim3((unsigned)B, (unsigned)NH, (unsigned)splits),
                        dim3(kAttnWarps * 32), 0, stream, 1u, (const __nv_bfloat16*)q, (const __nv_bfloat16*)k_cache,
-                       (const __nv_bfloat16*)v_cache, block_table, seq_lens, max_blocks, NH, block_size, chunk, scale,
-                       part_ml, part_acc);
+                       (const __nv_bfloat16*)v_cache, block_table, seq_lens, max_blocks, num_blocks, NH, block_size,
+                       chunk, scale, part_ml, part_acc, st);
   }
   if (e != cudaSuccess) return DWDP_ERR_CUDA;
   const int BH = B * NH;

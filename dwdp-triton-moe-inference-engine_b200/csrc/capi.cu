@@ -39,10 +39,10 @@ extern "C" int dwdp_merge_launch(const void*, const int64_t*, const void*, int, 
                                  void*, int, int*, cudaStream_t);
 
 extern "C" int dwdp_add_rmsnorm_launch(void*, const void*, const void*, int64_t, int, float, void*, cudaStream_t);
-extern "C" int dwdp_rope_append_launch(const void*, const void*, const int32_t*, const int32_t*, int, int, int, int,
+extern "C" int dwdp_rope_append_launch(const void*, const void*, const int32_t*, const int32_t*, int, int, int, int, int,
                                        int, float, void*, void*, void*, int*, cudaStream_t);
 extern "C" size_t dwdp_paged_attention_workspace_bytes_impl(int, int, int);
-extern "C" int dwdp_paged_attention_launch(const void*, const void*, const void*, const int32_t*, const int32_t*, int,
+extern "C" int dwdp_paged_attention_launch(const void*, const void*, const void*, const int32_t*, const int32_t*, int, int,
                                            int, int, int, int, int, int, float, void*, void*, int*,
                                            cudaStream_t);
 
@@ -370,17 +370,18 @@ extern "C" int dwdp_add_rmsnorm(void* residual, const void* delta, const void* w
 }
 
 extern "C" int dwdp_rope_append_kv(const void* qkv, const void* qkv_bias, const int32_t* positions,
-                                   const int32_t* block_table, int batch, int max_blocks, int num_heads,
-                                   int head_dim, int block_size, float rope_theta, void* q_out, void* k_cache,
-                                   void* v_cache, int* status, void* stream) {
+                                   const int32_t* block_table, int batch, int max_blocks, int num_blocks,
+                                   int num_heads, int head_dim, int block_size, float rope_theta, void* q_out,
+                                   void* k_cache, void* v_cache, int* status, void* stream) {
   g_last_error.clear();
   if (batch < 0 || num_heads <= 0 || head_dim <= 0 || head_dim % 2 || head_dim > 1024 || block_size <= 0 ||
-      max_blocks <= 0)
+      max_blocks <= 0 || num_blocks <= 0)
     return fail(DWDP_ERR_INVALID_ARGUMENT, "rope_append_kv: bad sizes");
   if (batch > 0 && (qkv == nullptr || positions == nullptr || block_table == nullptr || q_out == nullptr ||
                     k_cache == nullptr || v_cache == nullptr))
     return fail(DWDP_ERR_INVALID_ARGUMENT, "rope_append_kv: null pointer");
-  return check(dwdp_rope_append_launch(qkv, qkv_bias, positions, block_table, batch, max_blocks, num_heads, head_dim,
+  return check(dwdp_rope_append_launch(qkv, qkv_bias, positions, block_table, batch, max_blocks, num_blocks,
+                                       num_heads, head_dim,
                                        block_size, rope_theta, q_out, k_cache, v_cache, status, as_stream(stream)),
                "rope_append_kv");
 }
@@ -392,17 +393,18 @@ extern "C" size_t dwdp_paged_attention_workspace_bytes(int batch, int num_heads,
 
 extern "C" int dwdp_paged_attention(const void* q, const void* k_cache, const void* v_cache,
                                     const int32_t* block_table, const int32_t* seq_lens, int batch, int max_blocks,
-                                    int num_heads, int head_dim, int block_size, int max_len, int splits,
-                                    float scale, void* workspace, void* out, int* status, void* stream) {
+                                    int num_blocks, int num_heads, int head_dim, int block_size, int max_len,
+                                    int splits, float scale, void* workspace, void* out, int* status, void* stream) {
   g_last_error.clear();
-  if (batch < 0 || num_heads <= 0 || block_size <= 0 || max_blocks <= 0 || splits <= 0 || max_len <= 0 ||
-      max_len > max_blocks * block_size)
+  if (batch < 0 || num_heads <= 0 || block_size <= 0 || max_blocks <= 0 || num_blocks <= 0 || splits <= 0 ||
+      max_len <= 0 || max_len > max_blocks * block_size)
     return fail(DWDP_ERR_INVALID_ARGUMENT, "paged_attention: bad sizes");
   if (head_dim != 128) return fail(DWDP_ERR_UNSUPPORTED, "paged_attention: head_dim must be 128");
   if (batch > 0 && (q == nullptr || k_cache == nullptr || v_cache == nullptr || block_table == nullptr ||
                     seq_lens == nullptr || workspace == nullptr || out == nullptr))
     return fail(DWDP_ERR_INVALID_ARGUMENT, "paged_attention: null pointer");
-  return check(dwdp_paged_attention_launch(q, k_cache, v_cache, block_table, seq_lens, batch, max_blocks, num_heads,
+  return check(dwdp_paged_attention_launch(q, k_cache, v_cache, block_table, seq_lens, batch, max_blocks, num_blocks,
+                                           num_heads,
                                            head_dim, block_size, max_len, splits, scale, workspace, out,
                                            status, as_stream(stream)),
                "paged_attention");
@@ -419,7 +421,7 @@ extern "C" int dwdp_ep_dispatch(const void* hidden, const int64_t* topk_idx, con
     return fail(DWDP_ERR_CAPACITY, "ep_dispatch: num_tokens * top_k must be <= min(2048, capacity)");
   if (hidden_size <= 0 || hidden_size % 8 || num_experts <= 0)
     return fail(DWDP_ERR_INVALID_ARGUMENT, "ep_dispatch: bad hidden_size / num_experts");
-  if (num_tokens > 0 && (hidden == nullptr || topk_idx == nullptr || topk_weights == nullptr || peers == nullptr))
+  if (peers == nullptr || (num_tokens > 0 && (hidden == nullptr || topk_idx == nullptr || topk_weights == nullptr)))
     return fail(DWDP_ERR_INVALID_ARGUMENT, "ep_dispatch: null pointer");
   return check(dwdp_ep_dispatch_launch(hidden, topk_idx, topk_weights, num_tokens, top_k, num_experts, world, rank,
                                        hidden_size, capacity, peers, status, as_stream(stream)),

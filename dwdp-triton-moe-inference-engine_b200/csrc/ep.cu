@@ -183,7 +183,9 @@ ep_plan_kernel(EpLayout L, int E, int expert_lo, int El, int send_ctas, int64_t*
   if (tid < L.world) {
     if (!ep_wait_geq(arrive + tid, send_ctas)) record_error(st, DWDP_ERR_DEVICE_TIMEOUT, 510, tid);
     __threadfence_system();
-    arrive[tid] = 0;
+    // Subtract this layer's arrivals instead of storing 0: after a timeout, CTAs that arrive
+    // late bring the counter back to 0 rather than satisfying the next layer's wait early.
+    atomicSub(arrive + tid, send_ctas);
     s_rows[tid] = min(ld_acquire_sys(reinterpret_cast<int*>(own + L.recv_count) + tid), L.cap);
   }
   if (tid < El) s_cnt[tid] = 0, s_fill[tid] = 0;
@@ -239,9 +241,10 @@ ep_gather_kernel(EpLayout L, const uint8_t* own, const int* __restrict__ packed_
 }
 
 // weighted[p] -> peers[src].ret_y[slot]; then every CTA raises every source's ret_arrive.
+// The return address comes from a peer's metadata: source and slot are bounds-checked.
 __global__ void __launch_bounds__(kEpThreads)
 ep_return_kernel(EpLayout L, const __nv_bfloat16* __restrict__ weighted, const int* __restrict__ ret_addr,
-                 const int* __restrict__ total, const unsigned long long* __restrict__ peers) {
+                 const int* __restrict__ total, const unsigned long long* __restrict__ peers, DeviceStatus* st) {
   griddep_launch();
   griddep_wait();
   const int lane = threadIdx.x & 31;
@@ -249,6 +252,10 @@ ep_return_kernel(EpLayout L, const __nv_bfloat16* __restrict__ weighted, const i
   for (int p = blockIdx.x * (kEpThreads / 32) + (threadIdx.x >> 5); p < n; p += gridDim.x * (kEpThreads / 32)) {
     const int a = ret_addr[p];
     const int s = a >> 20, slot = a & 0xFFFFF;
+    if (s < 0 || s >= L.world || slot >= L.cap) {
+      if (lane == 0) record_error(st, DWDP_ERR_DEVICE_BOUNDS, 530, a);
+      continue;
+    }
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(peer_base(peers, s) + L.ret_y) + (size_t)slot * L.H;
     warp_copy_row(dst, weighted + (size_t)p * L.H, L.H, lane);
   }
@@ -265,7 +272,7 @@ __global__ void ep_wait_kernel(EpLayout L, uint8_t* own, int expected, DeviceSta
     int* c = reinterpret_cast<int*>(own + L.ret_arrive);
     if (!ep_wait_geq(c, expected)) record_error(st, DWDP_ERR_DEVICE_TIMEOUT, 520, ld_acquire_sys(c));
     __threadfence_system();
-    *c = 0;
+    atomicSub(c, expected);  // late arrivals after a timeout cancel out instead of carrying over
   }
 }
 
@@ -285,8 +292,8 @@ constexpr int kEpReturnCtas = 16;
 extern "C" int dwdp_ep_dispatch_launch(const void* x, const int64_t* topk_idx, const float* topk_w, int T, int K,
                                        int E, int world, int rank, int H, int cap,
                                        const unsigned long long* peers, int* status, cudaStream_t stream) {
-  if (T <= 0) return DWDP_OK;
-  if (T * K > kEpMaxSlots || world > 8 || H % 8) return DWDP_ERR_UNSUPPORTED;
+  // T == 0 still launches: the owners count one arrival per send CTA of every source
+  if (T < 0 || T * K > kEpMaxSlots || world > 8 || H % 8) return DWDP_ERR_UNSUPPORTED;
   const EpLayout L = ep_layout(world, rank, H, cap);
   return launch_chained(ep_send_kernel, dim3(kEpSendCtas), dim3(kEpThreads), 0, stream, 1u,
                         (const __nv_bfloat16*)x, topk_idx, topk_w, T, K, E, L, peers,
@@ -317,7 +324,8 @@ extern "C" int dwdp_ep_combine_launch(void* own, int world, int rank, int H, int
                                       int* status, cudaStream_t stream) {
   const EpLayout L = ep_layout(world, rank, H, cap);
   if (launch_chained(ep_return_kernel, dim3(kEpReturnCtas), dim3(kEpThreads), 0, stream, 1u, L,
-                     (const __nv_bfloat16*)weighted, ret_addr, total, peers) != cudaSuccess)
+                     (const __nv_bfloat16*)weighted, ret_addr, total, peers,
+                     reinterpret_cast<DeviceStatus*>(status)) != cudaSuccess)
     return DWDP_ERR_CUDA;
   return launch_chained(ep_wait_kernel, dim3(1), dim3(32), 0, stream, 1u, L, (uint8_t*)own, world * kEpReturnCtas,
                         reinterpret_cast<DeviceStatus*>(status)) == cudaSuccess

@@ -130,7 +130,7 @@ class ExpertParallelMoE:
         self.ex = exchange
         self.lo, self.hi = lo, hi
         self._routed_group = local_experts.group()
-        self._shared_group = shared_expert.group() if shared_expert is not None else None
+        self._shared_group = shared_expert.group(local_experts.activation_quant) if shared_expert is not None else None
         self._ws: dict[int, dict] = {}
 
     def workspace(self, T: int) -> dict:
@@ -141,7 +141,9 @@ class ExpertParallelMoE:
             raise ValueError(f"EP path takes at most {self.ex.max_tokens} tokens per rank")
         ex, K, E, H, dev = self.ex, self.top_k, self.num_experts, self.hidden_size, self.ex.device
         El = self.local.num_experts
-        rows = ex.world * T * K  # routed rows this rank may receive (every rank runs T tokens)
+        # Rows this rank may receive as an owner: up to `capacity` from every source, whatever
+        # this rank's own T is (ranks may run different token counts, T = 0 included), so the
+        # owner's expert GEMMs are sized for world * capacity rows.
         cap_rows = ex.world * ex.capacity
         Is = self.shared_expert.intermediate_size if self.shared_expert is not None else 0
         parts = ops.moe_shared_parts(T, Is) if self.shared_expert is not None else 0
@@ -160,11 +162,13 @@ class ExpertParallelMoE:
             ret_addr=torch.zeros(cap_rows, dtype=torch.int32, device=dev),
             total=torch.zeros(1, dtype=torch.int32, device=dev),
             packed_hidden=torch.zeros(cap_rows, H, dtype=torch.bfloat16, device=dev),
-            weighted=torch.empty(max(rows, 1), H, dtype=torch.bfloat16, device=dev),
+            weighted=torch.empty(cap_rows, H, dtype=torch.bfloat16, device=dev),
             shared_out=torch.empty(parts, T, H, dtype=torch.bfloat16, device=dev) if parts else None,
             parts=parts,
-            moe_ws=torch.empty(ops.moe_workspace_bytes(T, ex.world * K, El, self.local.intermediate_size, Is),
+            moe_ws=torch.empty(ops.moe_workspace_bytes(cap_rows, 1, El, self.local.intermediate_size, 0),
                                dtype=torch.uint8, device=dev),
+            shared_ws=torch.empty(ops.moe_shared_workspace_bytes(T, H, Is), dtype=torch.uint8, device=dev)
+            if parts else None,
             inv=torch.arange(T * K, dtype=torch.int64, device=dev),
             status=torch.zeros(4, dtype=torch.int32, device=dev),
         )
@@ -178,8 +182,8 @@ class ExpertParallelMoE:
         T = x.shape[0]
         if out is None:
             out = torch.empty_like(x)
-        if T == 0:
-            return out
+        # T == 0 still runs the exchange: this rank owns experts other ranks' tokens may pick,
+        # and every rank's arrival counters must advance once per layer
         self.run(x, self.workspace(T), out)
         return out
 
@@ -202,19 +206,34 @@ class ExpertParallelMoE:
                               ws["packed_src"].data_ptr(), ws["packed_w"].data_ptr(), ws["ret_addr"].data_ptr(),
                               ws["total"].data_ptr(), ws["packed_hidden"].data_ptr(), st, stream)
         _lib.check(rc, "ep_plan")
-        ops.moe_experts(self._routed_group, self._shared_group, ws["packed_hidden"], x, ex.world * K, ws["counts"],
-                        ws["offsets"], ws["packed_w"], r.shared_gate, ws["weighted"], ws["shared_out"],
-                        ws["moe_ws"], ws["status"])
+        # received rows: sized for every source's full capacity (counts/offsets pick the real ones)
+        ops.moe_experts(self._routed_group, None, ws["packed_hidden"], ws["packed_hidden"], 1, ws["counts"],
+                        ws["offsets"], ws["packed_w"], None, ws["weighted"], None, ws["moe_ws"], ws["status"])
         rc = lib.dwdp_ep_combine(ex.buffer.data_ptr(), ex.world, ex.rank, H, ex.capacity, ws["weighted"].data_ptr(),
                                  ws["ret_addr"].data_ptr(), ws["total"].data_ptr(), ex.peers.data_ptr(), st, stream)
         _lib.check(rc, "ep_combine")
-        ops.merge(ex.returned_rows(T * K), ws["inv"], T, K, shared_out=ws["shared_out"],
-                  shared_parts=max(1, ws["parts"]), out=out)
+        if T == 0:
+            return
+        if self.shared_expert is not None:
+            # the shared expert over this rank's own tokens, ungated; the merge applies the gate
+            ops.moe_shared_expert(self._shared_group, x, ws["shared_out"], ws["shared_ws"], ws["status"])
+            gate = r.shared_gate if r.shared_gate is not None else self._ones(T)
+            ops.merge(ex.returned_rows(T * K), ws["inv"], T, K, shared_out=ws["shared_out"],
+                      shared_parts=ws["parts"], out=out, shared_gate=gate)
+        else:
+            ops.merge(ex.returned_rows(T * K), ws["inv"], T, K, out=out)
+
+    def _ones(self, T: int) -> torch.Tensor:
+        ws = self.workspace(T)
+        if "ones" not in ws:
+            ws["ones"] = torch.ones(T, dtype=torch.float32, device=self.ex.device)
+        return ws["ones"]
 
     def read_status(self, T: int) -> tuple[int, ...]:
         return tuple(self.workspace(T)["status"].cpu().tolist())
 
     def kernel_launches(self) -> int:
-        """router, ep_send, ep_plan, ep_gather, expert plan+planes, gate/up, planes, down,
-        ep_return, ep_wait, merge."""
-        return 11
+        """router, ep_send, ep_plan, ep_gather, the received rows' expert GEMMs (plan+planes,
+        gate/up, [planes,] down), ep_return, ep_wait, the shared expert's own GEMMs, merge."""
+        gemm = 3 if self.local.activation_quant == "block128" else 4
+        return 4 + gemm + 2 + (gemm if self.shared_expert is not None else 0) + 1

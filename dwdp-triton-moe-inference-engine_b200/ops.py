@@ -455,7 +455,7 @@ def rope_append_kv(qkv: torch.Tensor, qkv_bias: torch.Tensor | None, positions: 
     if q_out is None:
         q_out = torch.empty(B, NH, D, dtype=torch.bfloat16, device=qkv.device)
     rc = _lib.load().dwdp_rope_append_kv(qkv.data_ptr(), _ptr(qkv_bias), positions.data_ptr(), block_table.data_ptr(),
-                                         B, block_table.shape[-1], NH, D, bs, float(rope_theta), q_out.data_ptr(),
+                                         B, block_table.shape[-1], nb, NH, D, bs, float(rope_theta), q_out.data_ptr(),
                                          k_cache.data_ptr(), v_cache.data_ptr(), _ptr(status), _stream())
     _lib.check(rc, "rope_append_kv")
     return q_out
@@ -498,13 +498,16 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
         raise ValueError("seq_lens and block_table must be int32")
     B, NH, D = q.shape
     bs = k_cache.shape[1]
+    if v_cache.shape != k_cache.shape:
+        raise ValueError("k_cache and v_cache must have the same [num_blocks, block_size, NH, D] shape")
     splits = splits or paged_attention_splits(B, NH, max_len, bs)
     if workspace is None:
         workspace = paged_attention_workspace(B, NH, splits, q.device)
     if out is None:
         out = torch.empty(B, NH, D, dtype=torch.bfloat16, device=q.device)
     rc = _lib.load().dwdp_paged_attention(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(),
-                                          seq_lens.data_ptr(), B, block_table.shape[-1], NH, D, bs, int(max_len),
+                                          seq_lens.data_ptr(), B, block_table.shape[-1], k_cache.shape[0], NH, D, bs,
+                                          int(max_len),
                                           splits, float(scale if scale is not None else D ** -0.5),
                                           workspace.data_ptr(), out.data_ptr(), _ptr(status), _stream())
     _lib.check(rc, "paged_attention")

@@ -292,22 +292,24 @@ int dwdp_add_rmsnorm(void* residual, const void* delta, const void* weight, int6
 /* qkv [batch, 3, num_heads, head_dim] (+ qkv_bias [3, num_heads, head_dim] when given):
  * q_out [batch, num_heads, head_dim] gets q with the rotary embedding at positions[b]
  * (NeoX rotate-half, inv_freq_d = rope_theta^(-2d/head_dim)); the rotated k and v are
- * written into the caches at positions[b]. A negative block id: DWDP_ERR_DEVICE_BOUNDS
- * in *status, the token skipped. */
+ * written into the caches ([num_blocks, block_size, num_heads, head_dim]) at positions[b].
+ * A position outside [0, max_blocks * block_size) or a block id outside [0, num_blocks):
+ * DWDP_ERR_DEVICE_BOUNDS in *status, the token skipped (q_out and the caches untouched). */
 int dwdp_rope_append_kv(const void* qkv, const void* qkv_bias, const int32_t* positions,
-                        const int32_t* block_table, int batch, int max_blocks, int num_heads, int head_dim,
-                        int block_size, float rope_theta, void* q_out, void* k_cache, void* v_cache, int* status,
-                        void* stream);
+                        const int32_t* block_table, int batch, int max_blocks, int num_blocks, int num_heads,
+                        int head_dim, int block_size, float rope_theta, void* q_out, void* k_cache, void* v_cache,
+                        int* status, void* stream);
 size_t dwdp_paged_attention_workspace_bytes(int batch, int num_heads, int splits);
 /* out[b, h] = softmax(scale * q[b, h] . K[b, :seq_lens[b], h]) V[b, :seq_lens[b], h] for one
  * query per sequence. The context is split into `splits` chunks of ceil(max_len / splits)
  * positions per (sequence, head), combined with the log-sum-exp rescaling. head_dim 128;
- * max_len >= every seq_lens[b] and <= max_blocks * block_size. A negative block id or a
- * pipeline wait that runs out: DWDP_ERR_DEVICE_BOUNDS / _TIMEOUT in *status (may be NULL). */
+ * max_len >= every seq_lens[b] and <= max_blocks * block_size. A block id outside
+ * [0, num_blocks) (its positions are skipped) or a pipeline wait that runs out:
+ * DWDP_ERR_DEVICE_BOUNDS / _TIMEOUT in *status (may be NULL). */
 int dwdp_paged_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
-                         const int32_t* seq_lens, int batch, int max_blocks, int num_heads, int head_dim,
-                         int block_size, int max_len, int splits, float scale, void* workspace, void* out,
-                         int* status, void* stream);
+                         const int32_t* seq_lens, int batch, int max_blocks, int num_blocks, int num_heads,
+                         int head_dim, int block_size, int max_len, int splits, float scale, void* workspace,
+                         void* out, int* status, void* stream);
 
 /* ======================================================================== *
  * Expert-parallel decode exchange (replaces the all_to_all_single EP path of
@@ -316,13 +318,16 @@ int dwdp_paged_attention(const void* q, const void* k_cache, const void* v_cache
  * dwdp_ep_buffer_bytes(world, H, capacity) bytes (capacity = T_max * top_k rows), exports
  * it with dwdp_export_ipc_handle and opens the others' with dwdp_ipc_open; `peers` is a
  * DEVICE array of world base addresses (this rank's own buffer at [rank]). Expert e is
- * owned by rank min(e / ceil(E / world), world - 1). All ranks run the same num_tokens
- * and top_k. Per forward, in stream order:
+ * owned by rank min(e / ceil(E / world), world - 1). All ranks use the same top_k and
+ * capacity; each rank's num_tokens may differ (0 <= num_tokens * top_k <= capacity), and
+ * a rank with no tokens still runs every step (the owners count one arrival per send CTA
+ * of every source). Per forward, in stream order:
  *   dwdp_ep_dispatch   rows of every (token, slot) -> the owner's buffer;
  *   dwdp_ep_plan       owner: wait for every rank, counting sort by local expert into
  *                      counts/offsets (local_experts entries, int64), packed_src, packed
  *                      routing weights, return addresses, *total, and the packed rows;
- *   (grouped GEMMs: dwdp_moe_experts with packed_hidden, top_k' = world * top_k)
+ *   (grouped GEMMs over the received rows: dwdp_moe_experts with packed_hidden sized
+ *    for world * capacity rows, num_tokens = world * capacity and top_k = 1)
  *   dwdp_ep_combine    weighted rows back to their source's buffer, then wait for all
  *                      owners; the source's results are then the rows
  *                      [dwdp_ep_ret_offset(), + num_tokens * top_k * H * 2) of its own

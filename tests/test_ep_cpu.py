@@ -61,11 +61,15 @@ def test_decode_pieces_validation_errors(pkg):
     L = pkg._lib
     lib = L.load()
     assert lib.dwdp_add_rmsnorm(None, None, None, 1, 2047, 1e-6, None, None) == L.DWDP_ERR_INVALID_ARGUMENT
-    assert lib.dwdp_rope_append_kv(None, None, None, None, 1, 8, 16, 127, 16, 1e6, None, None, None, None,
+    assert lib.dwdp_rope_append_kv(None, None, None, None, 1, 8, 8, 16, 127, 16, 1e6, None, None, None, None,
                                    None) == L.DWDP_ERR_INVALID_ARGUMENT
-    assert lib.dwdp_paged_attention(None, None, None, None, None, 1, 8, 16, 64, 16, 128, 1, 0.1, None, None,
+    assert lib.dwdp_rope_append_kv(None, None, None, None, 1, 8, 0, 16, 128, 16, 1e6, None, None, None, None,
+                                   None) == L.DWDP_ERR_INVALID_ARGUMENT  # no cache blocks
+    assert lib.dwdp_paged_attention(None, None, None, None, None, 1, 8, 8, 16, 64, 16, 128, 1, 0.1, None, None,
                                     None, None) == L.DWDP_ERR_UNSUPPORTED
-    assert lib.dwdp_paged_attention(None, None, None, None, None, 1, 8, 16, 128, 16, 129, 1, 0.1, None, None,
+    assert lib.dwdp_paged_attention(None, None, None, None, None, 1, 8, 8, 16, 128, 16, 129, 1, 0.1, None, None,
+                                    None, None) == L.DWDP_ERR_INVALID_ARGUMENT
+    assert lib.dwdp_paged_attention(None, None, None, None, None, 1, 8, 0, 16, 128, 16, 128, 1, 0.1, None, None,
                                     None, None) == L.DWDP_ERR_INVALID_ARGUMENT
     assert lib.dwdp_paged_attention_workspace_bytes(4, 16, 8) >= 4 * 16 * 8 * 130 * 4
 

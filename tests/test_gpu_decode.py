@@ -92,6 +92,50 @@ def test_rope_append_kv_bad_block_reports_status(pkg):
     assert int(kc.abs().sum()) == 0
 
 
+@pytest.mark.parametrize("pos,table_row", [(40, [0, 1]), (-1, [0, 1]), (20, [0, 2]), (20, [0, 7])])
+def test_rope_append_kv_out_of_range_reports_status(pkg, pos, table_row):
+    """Positions past the block table (40 >= 2 * 16) or negative, and block ids past the cache
+    (2 and 7 with 2 blocks): recorded in the status word, nothing written."""
+    NH, D, bs = 2, 128, 16
+    table = torch.tensor([table_row], dtype=torch.int32, device=DEV)
+    kc = torch.zeros(2, bs, NH, D, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    q = torch.zeros(1, NH, D, dtype=torch.bfloat16, device=DEV)
+    st = torch.zeros(4, dtype=torch.int32, device=DEV)
+    qkv = torch.randn(1, 3 * NH * D, device=DEV).bfloat16()
+    pkg.ops.rope_append_kv(qkv, None, torch.tensor([pos], dtype=torch.int32, device=DEV), table, kc, vc, 1e6,
+                           q_out=q, status=st)
+    torch.cuda.synchronize()
+    assert int(st[0]) == pkg._lib.DWDP_ERR_DEVICE_BOUNDS
+    assert int(kc.abs().sum()) == 0 and int(vc.abs().sum()) == 0 and int(q.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("NH,bs", [(16, 16), (4, 16), (16, 6)])
+@pytest.mark.parametrize("bad", [-1, 99])
+def test_paged_attention_bad_block_skipped(pkg, NH, bs, bad):
+    """A block id outside [0, num_blocks) on the bulk path (16 heads) and on the per-head
+    fallback (4 heads; block size 6): recorded in the status word, and its positions are left
+    out of the softmax, so the result equals attention over the other positions."""
+    g = torch.Generator().manual_seed(23)
+    D, mb = 128, 4
+    table, kc, vc = _paged(1, NH, D, bs, mb, g)
+    q = torch.randn(1, NH, D, generator=g).bfloat16()
+    n = mb * bs
+    bad_table = table.clone()
+    bad_table[0, 1] = bad
+    st = torch.zeros(4, dtype=torch.int32, device=DEV)
+    out = pkg.ops.paged_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), bad_table.to(DEV),
+                                  torch.tensor([n], dtype=torch.int32, device=DEV), n, status=st)
+    torch.cuda.synchronize()
+    assert int(st[0]) == pkg._lib.DWDP_ERR_DEVICE_BOUNDS
+    keep = torch.ones(n, dtype=torch.bool)
+    keep[bs:2 * bs] = False
+    k = _history(kc, table[0], n)[keep]
+    v = _history(vc, table[0], n)[keep]
+    ref = dor.attention_decode(q[0], k, v, 1 / math.sqrt(D))
+    assert _rel(out[0].cpu(), ref) < BF16_TOL
+
+
 @pytest.mark.parametrize("NH,bs,splits", [(16, 16, 1), (16, 16, None), (16, 16, 37), (8, 16, None),
                                           (32, 16, None), (4, 16, None), (16, 6, None)])
 def test_paged_attention_ragged(pkg, NH, bs, splits):

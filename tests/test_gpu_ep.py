@@ -1,8 +1,9 @@
 """Expert-parallel decode path (token rows over NVLink peer memory) against the layer
-with every expert local. World 1 runs the same kernels on one GPU; world 2 needs two
-GPUs (gpurun --gpus 2). Every result must be bit-identical to the local layer: a row's
-expert arithmetic does not depend on which rows share its tile, and the merge adds the
-k slots in the same order."""
+with every expert local and against the CPU oracle. World 1 runs the same kernels on one
+GPU; world 2 needs two GPUs. Every result must be bit-identical to the local layer (run
+with its shared expert in separate launches, as the EP path runs it): a row's expert
+arithmetic does not depend on which rows share its tile, and the merge adds the k slots
+in the same order. Ranks may run different token counts, none included."""
 from __future__ import annotations
 
 import os
@@ -41,16 +42,22 @@ def _layers(pkg, ep, rank, world, dev, exchange):
     sh.load_expert(0, *shared)
     wr, gate = wr.to(dev), gate.to(dev)
     ref = pkg.MoELayer(wr, full, K, shared_expert=sh, shared_gate_weight=gate)
+    ref.overlap_shared = True  # the shared expert in its own launches, gated by the merge
     epl = ep.ExpertParallelMoE(wr, local, K, exchange, shared_expert=sh, shared_gate_weight=gate)
     return ref, epl
+
+
+# per-step token counts of rank r: equal, then unequal, then one rank with none
+STEPS = [(1, 1), (5, 5), (64, 64), (5, 3), (0, 7), (1, 0)]
 
 
 def _check(pkg, ep, rank, world, dev, exchange):
     ref, epl = _layers(pkg, ep, rank, world, dev, exchange)
     results = []
-    for it, T in enumerate((1, 5, 64, 5, 1)):
+    for it, Ts in enumerate(STEPS):
+        T = Ts[rank % 2]
         x = torch.randn(T, H, generator=torch.Generator().manual_seed(100 * rank + it)).bfloat16().to(dev)
-        y_ref = ref(x)
+        y_ref = ref(x) if T else torch.empty(0, H, dtype=torch.bfloat16, device=dev)
         y = epl(x)
         torch.cuda.synchronize()
         results.append((T, bool(torch.equal(y, y_ref)), epl.read_status(T)[0]))
@@ -85,6 +92,56 @@ def test_ep_world1_matches_local_layer(pkg):
     for T, ok, st in _check(pkg, ep, 0, 1, dev, ex):
         assert st == 0, f"T={T}: status {st}"
         assert ok, f"T={T}: EP output differs from the local layer"
+
+
+def test_ep_world1_matches_oracle(pkg, orc):
+    """The EP layer against the CPU oracle of the reference's EP forward
+    (DWDP/adapters/qwen15_moe.py:164-243: the same routed experts and shared expert)."""
+    ep = pkg.ep
+    dev = torch.device("cuda", 0)
+    ex = ep.EPExchange(1, 0, H, 64, K, dev)
+    ref, epl = _layers(pkg, ep, 0, 1, dev, ex)
+    for T in (1, 13, 64):
+        x = torch.randn(T, H, generator=torch.Generator().manual_seed(T)).bfloat16()
+        y = epl(x.to(dev))
+        torch.cuda.synchronize()
+        assert epl.read_status(T)[0] == 0
+        r = epl.workspace(T)["router"]
+        experts = [tuple(t.cpu() for t in ref.experts.dequantized(e)) for e in range(E)]
+        shared = tuple(t.cpu() for t in ref.shared_expert.dequantized(0))
+        want = orc.moe_forward(x.float(), r.topk_indices.cpu(), r.topk_weights.cpu(), experts, shared=shared,
+                               shared_gate=r.shared_gate.cpu())
+        assert orc.rel_frobenius(y.float().cpu(), want) < 2e-2
+
+
+def test_ep_plan_wait_runs_out(pkg):
+    """A world-2 exchange on one GPU whose second rank never sends: the owner's bounded wait
+    gives up (about a second), records DWDP_ERR_DEVICE_TIMEOUT in the status word and the
+    kernel returns; the context stays usable. Nothing here writes to a peer."""
+    import ctypes
+
+    ep = pkg.ep
+    dev = torch.device("cuda", 0)
+    ex = ep.EPExchange(2, 0, H, 8, K, dev)
+    El = E // 2
+    counts = torch.zeros(El, dtype=torch.int64, device=dev)
+    offsets = torch.zeros(El + 1, dtype=torch.int64, device=dev)
+    cap_rows = 2 * ex.capacity
+    src = torch.zeros(cap_rows, dtype=torch.int32, device=dev)
+    w = torch.zeros(cap_rows, dtype=torch.float32, device=dev)
+    ret = torch.zeros(cap_rows, dtype=torch.int32, device=dev)
+    total = torch.zeros(1, dtype=torch.int32, device=dev)
+    packed = torch.zeros(cap_rows, H, dtype=torch.bfloat16, device=dev)
+    st = torch.zeros(4, dtype=torch.int32, device=dev)
+    lib = pkg._lib.load()
+    rc = lib.dwdp_ep_plan(ex.buffer.data_ptr(), 2, 0, H, ex.capacity, E, 0, El, counts.data_ptr(),
+                          offsets.data_ptr(), src.data_ptr(), w.data_ptr(), ret.data_ptr(), total.data_ptr(),
+                          packed.data_ptr(), st.data_ptr(), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    pkg._lib.check(rc, "ep_plan")
+    torch.cuda.synchronize()
+    assert st.cpu().tolist()[0] == pkg._lib.DWDP_ERR_DEVICE_TIMEOUT
+    assert int(total.item()) == 0
+    assert torch.ones(4, device=dev).sum().item() == 4.0  # the context still runs work
 
 
 def _port() -> int:
