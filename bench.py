@@ -11,9 +11,13 @@ prefetched over NVLink during the current layer (DWDP); the reported time is
 the max over ranks. value = (N * T * L) / step time = MoE-layer tokens/s.
 Rank 0 prints one JSON line.
 
-``--impl reference`` times the reference algorithm's CPU path (the oracle
-restatement of the reference's PyTorch executor, all host threads) on the same
-workload and prints the same metric with ``"impl": "reference"``.
+``--impl reference`` times the reference's OWN PyTorch path on the host cores
+(``DWDPRuntime.build_reference`` of the reference package staged under
+``oracle/_ref`` by ``oracle/stage_reference.sh``, plus its adapter's shared
+expert) on the same workload (L layers x T tokens per step, bf16 weights
+dequantised from per-channel e4m3, all host threads), on rank 0 only, without
+loading this repository's package or library, and prints the same metric with
+``"impl": "reference"``.
 """
 from __future__ import annotations
 
@@ -304,6 +308,106 @@ def cpu_baseline(pkg, layer, T_sample: int, iters: int, device) -> dict:
                       f"CPU {model}", "seconds_per_step": med}
 
 
+# ----------------------------------------------------------------------------- reference arm (CPU)
+REF_DIR = ROOT / "oracle" / "_ref"
+
+
+def _reference_layers(L: int, seed0: int = 1235):
+    """L Qwen-shaped layers for the reference's own runtime, built on the CPU from seeded
+    generators (same shapes and distributions as make_qwen_layer): router W ~ N(0, 1/H),
+    experts and shared expert ~ N(0, 0.02) quantised to e4m3 with per-output-channel scales
+    and run dequantised in bf16 (the reference's FP8 path is CUDA-only), shared gate ~ N(0, 0.02).
+    Nothing here touches this repository's package or library."""
+    from oracle import moe_oracle as orc
+
+    H, E, I, K, Is = QWEN["H"], QWEN["E"], QWEN["I"], QWEN["K"], QWEN["Is"]
+    from DWDP.router.config import MetadataLevel, RouterConfig
+    from DWDP.router.registry import build_router
+    from DWDP.runtime.runtime import DWDPRuntime
+
+    class QwenSwiGLUExpert(torch.nn.Module):
+        """The Qwen expert MLP the reference's executor calls as module(x)."""
+
+        def __init__(self, hidden, inter, g):
+            super().__init__()
+            self.gate_proj = torch.nn.Linear(hidden, inter, bias=False, dtype=torch.bfloat16)
+            self.up_proj = torch.nn.Linear(hidden, inter, bias=False, dtype=torch.bfloat16)
+            self.down_proj = torch.nn.Linear(inter, hidden, bias=False, dtype=torch.bfloat16)
+            with torch.no_grad():
+                for lin in (self.gate_proj, self.up_proj, self.down_proj):
+                    w = torch.randn(lin.weight.shape, generator=g) * 0.02
+                    lin.weight.copy_(orc.dequantize_channel(*orc.quantize_channel(w)).bfloat16())
+
+        def forward(self, x):
+            return self.down_proj(torch.nn.functional.silu(self.gate_proj(x)) * self.up_proj(x))
+
+    layers = []
+    for l in range(L):
+        g = torch.Generator().manual_seed(seed0 + l)
+        router = build_router(RouterConfig(hidden_size=H, num_experts=E, top_k=K,
+                                           metadata_level=MetadataLevel.COUNTS))
+        with torch.no_grad():
+            router.weight.copy_(torch.randn(E, H, generator=g) / H**0.5)
+        router.to(torch.bfloat16)
+        experts = [QwenSwiGLUExpert(H, I, g) for _ in range(E)]
+        rt = DWDPRuntime.build_reference(hidden_size=H, num_experts=E, top_k=K, experts=experts, router=router)
+        shared = QwenSwiGLUExpert(H, Is, g)
+        gate = (torch.randn(H, generator=g) * 0.02).bfloat16()
+        layers.append((rt, shared, gate))
+    return layers
+
+
+def _reference_step(layers, x):
+    """One step through the reference's own PyTorch path: DWDPRuntime.forward (router ->
+    expert-major dispatch -> round-robin schedule -> static planner -> PyTorchExecutor ->
+    PyTorchMerger, DWDP/runtime/runtime.py:189-275) plus the shared expert exactly as the
+    reference's adapter adds it (DWDP/adapters/qwen15_moe.py:302-319)."""
+    for rt, shared, gate in layers:
+        routed = rt(x).hidden_states
+        x = routed + torch.sigmoid(x @ gate.unsqueeze(-1)) * shared(x)
+    return x
+
+
+def reference_available() -> str | None:
+    if not (REF_DIR / "DWDP").is_dir():
+        return "the reference package is not staged under oracle/_ref (run oracle/stage_reference.sh)"
+    return None
+
+
+def run_reference_cpu(T: int, L: int, steps: int, warmup: int, budget_s: float) -> dict:
+    """Times the reference's own runtime on the host cores (all threads): `warmup` untimed
+    steps, then up to `steps` timed steps of L chained layers over T tokens, fewer when the
+    projected time passes `budget_s` (the sample is then stated)."""
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    layers = _reference_layers(L)
+    x = torch.randn(T, QWEN["H"], generator=torch.Generator().manual_seed(4242)).bfloat16()
+    times = []
+    with torch.inference_mode():
+        for _ in range(max(1, warmup)):
+            t0 = time.perf_counter()
+            _reference_step(layers, x)
+            first = time.perf_counter() - t0
+        n = max(1, min(steps, int(budget_s / max(first, 1e-3))))
+        for _ in range(n):
+            t0 = time.perf_counter()
+            _reference_step(layers, x)
+            times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    try:
+        model = next(l.split(":", 1)[1].strip() for l in open("/proc/cpuinfo") if l.startswith("model name"))
+    except (OSError, StopIteration):
+        model = "unknown"
+    return {"value": T * L / med, "unit": "tokens/s", "cores": threads, "kind": "reference",
+            "sample": f"{L} chained layers x {T} tokens per step (the headline workload), median of {n} timed "
+                      f"steps after {max(1, warmup)} untimed; the reference's DWDPRuntime.build_reference PyTorch "
+                      f"path (executor 'pytorch', dispatcher 'expert_major', merger 'pytorch') + its adapter's "
+                      f"shared expert, bf16 weights dequantised from per-channel e4m3; CPU {model}",
+            "seconds_per_step": med, "timed_steps": n}
+
+
 # ----------------------------------------------------------------------------- layer stack (headline)
 class LayerStack:
     """L Qwen-shaped MoE layers with distinct weights, chained (layer l's output
@@ -591,6 +695,41 @@ def main() -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    T, L = args.tokens, args.layers
+    config = {"workload": f"{L} chained qwen1.5-moe-a2.7b-shaped MoE layers, prefill T={T} per GPU",
+              "model": "Qwen1.5-MoE-A2.7B (shape)", "tokens_per_gpu": T, "layers_per_step": L,
+              "hidden": QWEN["H"], "experts": QWEN["E"], "top_k": QWEN["K"],
+              "moe_intermediate": QWEN["I"], "shared_intermediate": QWEN["Is"],
+              "weights": "fp8 e4m3, per-output-channel fp32 scales",
+              "activations": "bf16 in and out; inside the expert GEMMs one e4m3 plane per (token, 128 channels) "
+                             "with fp32 scales, SwiGLU intermediate re-quantised the same way (the reference's "
+                             "FP8 executor scheme)" if ACTIVATION_QUANT == "block128" else "bf16 (hi/lo e4m3 planes)",
+              "l2": "flushed (256 MB write + 256 MB read) before every timed step; weights 554 MB/layer > L2",
+              "parallelism": (f"dwdp{world}: tokens data-parallel, routed experts sharded over {world} GPUs, "
+                              "next layer's remote experts prefetched over NVLink during the current layer")
+              if world > 1 else "single GPU, all experts local"}
+
+    if args.impl == "reference":
+        # The reference's own CPU path, on rank 0 only; it loads nothing of this repository's
+        # package or library (the other ranks exit without work).
+        if rank != 0:
+            return
+        why = reference_available()
+        base = {"impl": "reference", "metric": METRIC, "unit": "tokens/s", "n_gpus": args.gpus,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic", "config": config}
+        if why is not None:
+            print(json.dumps({**base, "unavailable": why}), flush=True)
+            return
+        cb = run_reference_cpu(T, L, args.steps, args.warmup, budget_s=150.0)
+        print(json.dumps({
+            **base, "value": cb["value"], "steps": cb["timed_steps"], "warmup": args.warmup,
+            "ms_per_step": cb["seconds_per_step"] * 1e3,
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
+
     import __graft_entry__
 
     pkg = __graft_entry__.load_package()
@@ -600,34 +739,6 @@ def main() -> None:
         import torch.distributed as dist
 
         dist.init_process_group("nccl", device_id=device)
-    T, L = args.tokens, args.layers
-    config = {"workload": f"{L} chained qwen1.5-moe-a2.7b-shaped MoE layers, prefill T={T} per GPU",
-              "model": "Qwen1.5-MoE-A2.7B (shape)", "tokens_per_gpu": T, "layers_per_step": L,
-              "hidden": QWEN["H"], "experts": QWEN["E"], "top_k": QWEN["K"],
-              "moe_intermediate": QWEN["I"], "shared_intermediate": QWEN["Is"],
-              "weights": "fp8 e4m3, per-output-channel fp32 scales", "activations": "bf16",
-              "l2": "flushed (256 MB write + 256 MB read) before every timed step; weights 554 MB/layer > L2",
-              "parallelism": (f"dwdp{world}: tokens data-parallel, routed experts sharded over {world} GPUs, "
-                              "next layer's remote experts prefetched over NVLink during the current layer")
-              if world > 1 else "single GPU, all experts local"}
-
-    if args.impl == "reference":
-        if rank == 0:
-            layer = make_qwen_layer(pkg, device)
-            iters = max(args.steps // 5, 2)
-            cb = cpu_baseline(pkg, layer, args.cpu_sample, iters, device)
-            print(json.dumps({
-                "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s",
-                "n_gpus": args.gpus, "steps": iters, "warmup": 1,
-                "ms_per_step": cb["seconds_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
-                "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
-                "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            }), flush=True)
-        if world > 1:
-            torch.distributed.barrier()
-            torch.distributed.destroy_process_group()
-        return
 
     flush = L2Flusher(device)
     if args.workload == "attention":
@@ -705,7 +816,10 @@ def main() -> None:
 
     cb = None
     if rank == 0 and world == 1:
-        cb = cpu_baseline(pkg, lay0, args.cpu_sample, 3, device)
+        if reference_available() is None:  # the reference's own runtime, one layer at the headline T
+            cb = run_reference_cpu(T, 1, 3, 1, budget_s=20.0)
+        else:
+            cb = cpu_baseline(pkg, lay0, args.cpu_sample, 3, device)
         cb = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
     if rank == 0:
         print(json.dumps({
