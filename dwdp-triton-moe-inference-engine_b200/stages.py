@@ -26,8 +26,11 @@ import torch
 from torch import nn
 
 from . import _lib, ops
-from .plans import (CommunicationPlan, DispatchMetadata, DispatchPlan, ExecutionPlan, ExecutorOutput,
-                    ExpertAssignments, MergerOutput, RouterOutput, RoutingMetadata)
+from .plans import (EXECUTION_STATISTICS_FIELDS, SCHEDULER_STATISTICS_FIELDS, CommunicationPlan,
+                    DependencyMetadata, DispatchMetadata, DispatchPlan, ExecutionMetadata, ExecutionPlan,
+                    ExecutorOutput, ExpertAssignments, LazyStatistics, MergeMetadata, MergerOutput,
+                    MergeStatistics, OutputMetadata, RouterOutput, RoutingMetadata, SynchronizationMetadata,
+                    TimingMetadata, WorkspaceMetadata)
 from .weights import ExpertWeightStore
 
 # ----------------------------------------------------------------------------- registries
@@ -270,12 +273,30 @@ class B200RoundRobinScheduler(nn.Module):
     def forward(self, dispatch_plan: DispatchPlan, workspace=None) -> ExecutionPlan:
         md = dispatch_plan.metadata
         r = ops.schedule(md.expert_counts, md.expert_offsets, self.config.stream_count)
+        dev = r.expert_queue.device
+        counts, policy = md.expert_counts, self.config.scheduling_policy
+
+        def stats() -> dict:  # DWDP/scheduler/policies/round_robin.py _build_statistics, read on demand
+            c = counts.cpu()
+            active = c[c > 0]
+            n_act = int(active.numel())
+            return dict(num_experts=int(c.numel()), num_active_experts=n_act,
+                        num_empty_experts=int(c.numel()) - n_act, num_execution_batches=n_act,
+                        num_assignments=md.num_assignments,
+                        max_tokens_per_expert=int(active.max()) if n_act else 0,
+                        min_tokens_per_active_expert=int(active.min()) if n_act else 0, scheduling_policy=policy)
+
+        empty = torch.empty(0, dtype=torch.int64, device=dev)
         return ExecutionPlan(execution_order=r.execution_priority, expert_queue=r.expert_queue,
                              expert_starts=r.expert_starts, expert_ends=r.expert_ends,
                              expert_counts=r.expert_counts, execution_priority=r.execution_priority,
-                             stream_assignments=r.stream_assignments, num_active=r.num_active,
-                             scheduling_policy=self.config.scheduling_policy,
-                             deterministic=self.config.deterministic)
+                             stream_assignments=r.stream_assignments, batches=(),
+                             synchronization=SynchronizationMetadata(
+                                 barrier_after_batch=torch.empty(0, dtype=torch.bool, device=dev)),
+                             dependencies=DependencyMetadata(dependency_src=empty, dependency_dst=empty),
+                             statistics=LazyStatistics(stats, SCHEDULER_STATISTICS_FIELDS),
+                             scheduling_policy=policy, deterministic=self.config.deterministic,
+                             num_active=r.num_active)
 
 
 class StaticCommunicationPlanner(nn.Module):
@@ -387,10 +408,33 @@ class B200Executor(nn.Module):
         ops.moe_experts(self._group, None, packed, x, K, md.expert_counts, md.expert_offsets, w, None,
                         weighted, None, self._ws[key],
                         packed_token_indices=dispatch_plan.assignments.packed_token_indices)
-        return ExecutorOutput(packed_expert_outputs=None, weighted_expert_outputs=weighted,
-                              backend=self.config.backend, deterministic=True,
-                              inverse_permutation=md.inverse_permutation, token_shape=tuple(md.token_shape),
-                              top_k=K)
+        asg = dispatch_plan.assignments
+        counts, E = md.expert_counts, self.store.num_experts
+
+        def stats() -> dict:  # DWDP/executor/outputs.py ExecutionStatistics, read on demand
+            n = int((counts > 0).sum())
+            return dict(num_executed_experts=n, num_skipped_experts=E - n, num_input_tokens=T,
+                        num_assignments=md.num_assignments, hidden_size=H, output_size=H,
+                        backend=self.config.backend)
+
+        cp = communication_plan
+        return ExecutorOutput(
+            packed_expert_outputs=None, weighted_expert_outputs=weighted, expert_outputs=(),
+            output_metadata=OutputMetadata(
+                packed_token_indices=asg.packed_token_indices, packed_expert_ids=asg.expert_ids,
+                packed_routing_weights=asg.packed_routing_weights, token_permutation=md.token_permutation,
+                inverse_permutation=md.inverse_permutation, token_shape=tuple(md.token_shape), top_k=K),
+            execution_metadata=ExecutionMetadata(
+                execution_order=execution_plan.execution_order, expert_queue=execution_plan.expert_queue,
+                expert_starts=execution_plan.expert_starts, expert_ends=execution_plan.expert_ends,
+                stream_assignments=execution_plan.stream_assignments,
+                communication_remote_expert_ids=cp.remote_expert_ids if cp is not None
+                else torch.empty(0, dtype=torch.int64, device=x.device),
+                communication_policy=cp.planner_policy if cp is not None else "static",
+                scheduling_policy=execution_plan.scheduling_policy),
+            statistics=LazyStatistics(stats, EXECUTION_STATISTICS_FIELDS), timing=TimingMetadata(),
+            workspace=WorkspaceMetadata(used_workspace=True, workspace_bytes=int(self._ws[key].numel())),
+            backend=self.config.backend, deterministic=True)
 
 
 # ----------------------------------------------------------------------------- merger
@@ -410,14 +454,24 @@ class B200Merger(nn.Module):
             src = executor_output.weighted_expert_outputs
             if src is None:
                 raise ValueError("executor did not provide weighted expert outputs")
+            om = executor_output.output_metadata  # the reference's ExecutorOutput carries the same
             T = 1
-            for s in executor_output.token_shape:
+            for s in om.token_shape:
                 T *= s
-            out = ops.merge(src, executor_output.inverse_permutation, T, executor_output.top_k,
+            out = ops.merge(src, om.inverse_permutation, T, om.top_k,
                             out_dtype=getattr(self.config, "out_dtype", torch.bfloat16))
         H = out.shape[-1]
-        return MergerOutput(hidden_states=out.reshape(*executor_output.token_shape, H).contiguous(),
-                            backend=self.config.backend, deterministic=True)
+        om = executor_output.output_metadata
+        T = out.shape[0]
+        K = om.top_k
+        return MergerOutput(
+            hidden_states=out.reshape(*om.token_shape, H).contiguous(),
+            metadata=MergeMetadata(token_shape=tuple(om.token_shape), assignment_shape=(T, K),
+                                   inverse_permutation=om.inverse_permutation, top_k=K, deterministic=True),
+            statistics=MergeStatistics(num_tokens=T, num_assignments=T * K, top_k=K, output_size=H,
+                                       used_weighted_executor_outputs=True, backend=self.config.backend),
+            timing=TimingMetadata(), workspace=WorkspaceMetadata(used_workspace=False, workspace_bytes=0),
+            backend=self.config.backend, deterministic=True)
 
 
 # ----------------------------------------------------------------------------- runtime
