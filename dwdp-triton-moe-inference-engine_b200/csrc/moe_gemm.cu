@@ -590,8 +590,12 @@ struct CfgP {
   static constexpr int EPI_WARPS = 4 * CHUNKS;
   static constexpr int EPI_THREADS = EPI_WARPS * 32;
   static constexpr int THREADS = (2 + EPI_WARPS) * 32;
-  // the register file split evenly over the threads (8-register granularity), at most 168
-  static constexpr int MAXREG = 65536 / THREADS / 8 * 8 > 168 ? 168 : 65536 / THREADS / 8 * 8;
+  // Registers per thread: each of the SM's four sub-partitions holds 16384 registers and
+  // receives every fourth warp, so the fullest one (ceil(warps / 4) warps) sets the limit
+  // (8-register granularity); at most 168.
+  static constexpr int WARPS = THREADS / 32;
+  static constexpr int REG_FIT = 16384 / (((WARPS + 3) / 4) * 32) / 8 * 8;
+  static constexpr int MAXREG = REG_FIT > 168 ? 168 : REG_FIT;
   static constexpr bool QOUT = MODE == 0 && PLANES == 1;   // gate/up writes e4m3 rows + scales
   static constexpr int STAGING = QOUT ? BNT * BM : 0;      // e4m3 [tokens][128 features]
   static constexpr int SCL = EPI_WARPS * 2 * NMAT * 32 * 4;  // per-warp factor broadcast buffers
@@ -842,8 +846,7 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
       if constexpr (MODE == 0) {
         if constexpr (C::QOUT) {
           // h per the reference executor's bf16 arithmetic, then its (token, 128) amax
-          __nv_bfloat162 hp[16];  // h of tokens t0 + j, exact in bf16
-          float hq[32];
+          __nv_bfloat162 hp[16];  // h of tokens t0 + j, exact in bf16 (the accumulators die here)
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const float gb = bf16_round(acc[0][j] * s_row[0]);
@@ -851,7 +854,13 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
             const float sg = bf16_round(1.0f / (1.0f + expf(-gb)));
             const float h = j < ntk ? bf16_round(bf16_round(gb * sg) * ub) : 0.f;
             if (j & 1) hp[j >> 1].y = __float2bfloat16_rn(h); else hp[j >> 1].x = __float2bfloat16_rn(h);
-            hq[j] = fabsf(h);
+          }
+          float hq[32];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float2 f = __bfloat1622float2(hp[j]);
+            hq[2 * j] = fabsf(f.x);
+            hq[2 * j + 1] = fabsf(f.y);
           }
           const float wmax = warp_transpose_max(hq, lane);  // this warp's rows, token t0 + lane
           sRed[quad * BNT + t0 + lane] = wmax;

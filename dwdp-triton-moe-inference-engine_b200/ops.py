@@ -93,6 +93,8 @@ def router_topk(
             shared_gate=(torch.empty(T, dtype=torch.float32, device=dev)
                          if shared_gate_weight is not None else None),
         )
+    if T == 0:  # nothing to route (empty tensors have no data pointer to pass)
+        return out
     b = None if bias is None else bias.float().contiguous()
     rc = _lib.load().dwdp_router_topk(
         x.data_ptr(), dtype_code(x.dtype), w.data_ptr(), dtype_code(w.dtype), _ptr(b),
