@@ -18,11 +18,13 @@ Weights are imported once per block (lazily, on the block's first forward or on
 ``adapter.prepare()``): bf16/fp32 experts are quantised to e4m3 with per-output-channel
 (or 128x128 block) scales, or kept bf16; experts that are already e4m3 with their scale
 tensors (``weight_scale`` / ``weight_scale_inv`` attributes, per output channel or per
-128x128 block) are imported from those (``import_fp8_expert``). Routing follows the
-replaced module: ``norm_topk_prob`` true gives the softmax over the k selected;
-false gives the selected experts' probabilities under the softmax over all experts
-(what transformers computes; the reference's own routing always takes the softmax
-over the k selected, available here as ``routing="reference"``).
+128x128 block) are imported from those (``import_fp8_expert``). Routing defaults to the
+reference's (``routing="reference"``, DWDP/router/kernels/fused.py:25-35): the softmax
+over the k selected, whatever the replaced module's ``norm_topk_prob`` says, so a block
+swapped in for the reference's ``DWDPMoEBlock`` gives the reference's outputs.
+``routing="hf"`` follows the replaced transformers module instead: ``norm_topk_prob``
+true gives the softmax over the k selected; false gives the selected experts'
+probabilities under the softmax over all experts (what transformers computes).
 
 With ``world_size > 1`` (one process per GPU, ``torch.distributed`` initialised) every block
 holds only its rank's shard of the experts and runs the reference's hybrid
@@ -333,7 +335,7 @@ class B200MoEBlock(nn.Module):
     is a contiguous bf16 CUDA tensor."""
 
     def __init__(self, spec: MoELayerSpec, *, weight_dtype: torch.dtype = torch.float8_e4m3fn,
-                 scale_mode: int = _lib.SCALE_CHANNEL, routing: str = "hf",
+                 scale_mode: int = _lib.SCALE_CHANNEL, routing: str = "reference",
                  parallel: ParallelContext | None = None) -> None:
         super().__init__()
         if routing not in ("hf", "reference"):
@@ -426,7 +428,7 @@ class Qwen15MoEAdapter:
     (DWDP/adapters/qwen15_moe.py:434-580)."""
 
     def __init__(self, model: nn.Module, *, weight_dtype: torch.dtype = torch.float8_e4m3fn,
-                 scale_mode: int = _lib.SCALE_CHANNEL, routing: str = "hf", world_size: int = 1, rank: int = 0,
+                 scale_mode: int = _lib.SCALE_CHANNEL, routing: str = "reference", world_size: int = 1, rank: int = 0,
                  ep_batch_size_threshold: int = 64, group=None) -> None:
         self.model = model
         self.parallel = (ParallelContext(world_size, rank, ep_batch_size_threshold=ep_batch_size_threshold,

@@ -1,7 +1,7 @@
 """DWDP on 2+ GPUs: experts sharded across ranks, remote experts prefetched over
 NVLink (CUDA IPC + copy engine) into staging, then the same grouped GEMM. Each
 rank's output must be bit-identical to the layer run with every expert local.
-Runs only where at least two GPUs are visible (gpurun --gpus 2)."""
+Runs only where at least two GPUs are visible."""
 import os
 import socket
 

@@ -69,7 +69,7 @@ def _clear_tokens(blk, x, gap=2e-2):
 
 def _block_pair(pkg, model, layer, weight_dtype):
     spec = [s for s in pkg.hf_adapter.discover_moe_layers(model) if s.name == f"model.layers.{layer}.mlp"][0]
-    ours = pkg.hf_adapter.B200MoEBlock(spec, weight_dtype=weight_dtype)
+    ours = pkg.hf_adapter.B200MoEBlock(spec, weight_dtype=weight_dtype, routing="hf")  # vs transformers
     ours.prepare()
     return spec.module, ours
 
@@ -120,7 +120,7 @@ def test_patched_model_greedy_tokens_match_transformers(pkg):
     ids = torch.randint(0, 128, (2, 24), generator=torch.Generator().manual_seed(1)).to(DEV)
     with torch.no_grad():
         ref = model(ids).logits.float()
-    ad = pkg.hf_adapter.Qwen15MoEAdapter(model, weight_dtype=torch.bfloat16)
+    ad = pkg.hf_adapter.Qwen15MoEAdapter(model, weight_dtype=torch.bfloat16, routing="hf")
     assert ad.patch_model() == 2
     with torch.no_grad():
         out = model(ids).logits.float()

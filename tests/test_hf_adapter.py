@@ -93,6 +93,10 @@ def test_routing_mode_follows_norm_topk_prob(pkg):
         ad = pkg.hf_adapter.Qwen15MoEAdapter(model, routing=routing)
         ad.patch_model()
         assert all(b.renormalize == want for b in ad.blocks)
+    # the default is the reference's routing (softmax over the k selected), whatever the model says
+    ad = pkg.hf_adapter.Qwen15MoEAdapter(_hf_tiny(norm_topk_prob=False))
+    ad.patch_model()
+    assert ad.routing == "reference" and all(b.renormalize == 1 for b in ad.blocks)
 
 
 def test_cpu_forward_fails_loudly(pkg):
