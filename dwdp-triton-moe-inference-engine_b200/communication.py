@@ -142,71 +142,184 @@ class TransferScheduler:
 class CommunicationEngine:
     """Expert-slab prefetch engine (communication_engine.cpp; bindings.cpp:39-60).
 
-    ``initialize(slot_bytes, num_slots, num_buffers)`` allocates the staging
-    buffers; ``register_expert`` / ``register_ipc_expert`` / ``register_peer_expert``
-    declare local and remote slabs; ``prefetch(ids, buffer)`` copies the remote
-    ones into staging on the engine's greatest-priority stream; ``wait(buffer)``
-    orders the current torch stream after those copies."""
+    Two ways to drive it:
+
+    * the reference's surface (``CommunicationEngine(device_id)``, bindings.cpp:39-60):
+      ``initialize(staging_bytes)``, ``register_expert(id, ptr, size)`` /
+      ``register_ipc_expert(id, handle, size)``, ``prefetch(id)`` (copy a remote expert
+      into the NEXT staging buffer), ``wait(id)`` (order the current stream after that
+      copy), ``swap_buffers()`` (the next buffer becomes current, after the compute that
+      read the current one was queued), ``is_resident(id)``, ``get_resident_pointer(id)``,
+      ``get_weight(id)``, ``release(id)``, ``initialized()``, ``shutdown()``. Staging is
+      two buffers with one fixed slot of ``staging_bytes`` per registered remote expert,
+      created on the first prefetch (the reference's buffers hold one expert at a time);
+    * whole layers at once, as the DWDP path uses it: ``initialize(slot_bytes, num_slots,
+      num_buffers)``, ``prefetch_into(ids, buffer)`` copies every listed remote expert
+      into ``buffer`` on the engine's greatest-priority copy streams, ``wait_buffer(buffer)``
+      orders the current torch stream after those copies."""
 
     def __init__(self, device_id: int = 0) -> None:
         self.device_id = device_id
         self._h = None
+        self._pending: list[tuple] | None = None  # registrations made before a deferred create
+        self._slot_bytes = 0
+        self.num_buffers = 0
+        self._current = 0
+        self._where: dict[int, int] = {}  # remote expert -> staging buffer of its last prefetch
+        self._local: set[int] = set()
 
-    def initialize(self, slot_bytes: int, num_slots: int, num_buffers: int = 2) -> None:
-        if self._h is not None:
+    def initialize(self, staging_bytes: int, num_slots: int | None = None, num_buffers: int = 2) -> None:
+        if self.initialized():
             raise RuntimeError("engine already initialized")
+        if num_slots is None:  # the reference's form: staging created once the experts are known
+            if staging_bytes <= 0:
+                raise ValueError("staging_bytes must be > 0")
+            self._pending = []
+            self._slot_bytes = int(staging_bytes)
+            self.num_buffers = 2
+            return
         h = ctypes.c_void_p()
-        _chk(_lib.load().dwdp_engine_create(self.device_id, slot_bytes, num_slots, num_buffers, ctypes.byref(h)),
-             "engine_create")
+        self._slot_bytes = int(staging_bytes)
+        _chk(_lib.load().dwdp_engine_create(self.device_id, self._slot_bytes, num_slots, num_buffers,
+                                            ctypes.byref(h)), "engine_create")
         self._h = h
         self.num_buffers = num_buffers
 
     def initialized(self) -> bool:
-        return self._h is not None
+        return self._h is not None or self._pending is not None
 
     def _eng(self):
+        if self._pending is not None:  # first use of a reference-form engine: create, replay
+            pending, self._pending = self._pending, None
+            n_remote = sum(1 for p in pending if p[0] != "local")
+            h = ctypes.c_void_p()
+            _chk(_lib.load().dwdp_engine_create(self.device_id, self._slot_bytes, max(1, n_remote), 2,
+                                                ctypes.byref(h)), "engine_create")
+            self._h = h
+            for kind, *args in pending:
+                getattr(self, "_register_" + kind)(*args)
         if self._h is None:
             raise RuntimeError("communication engine is not initialized")
         return self._h
 
+    def _register_local(self, expert_id: int, ptr: int, size_bytes: int) -> None:
+        _chk(_lib.load().dwdp_engine_register_local(self._h, expert_id, ptr, size_bytes), "register_expert")
+        self._local.add(expert_id)
+
+    def _register_ipc(self, expert_id: int, handle: bytes, off: int, size_bytes: int, owner_device: int) -> None:
+        _chk(_lib.load().dwdp_engine_register_ipc(self._h, expert_id, handle, off, size_bytes, owner_device),
+             "register_ipc_expert")
+        self._local.discard(expert_id)
+
+    def _register_peer(self, expert_id: int, ptr: int, size_bytes: int, owner_device: int) -> None:
+        _chk(_lib.load().dwdp_engine_register_peer(self._h, expert_id, ptr, size_bytes, owner_device),
+             "register_peer_expert")
+        self._local.discard(expert_id)
+
+    def _register(self, kind: str, *args) -> None:
+        if self._pending is not None:
+            if kind != "local" and args[-2] > self._slot_bytes:  # (..., size_bytes, owner_device)
+                raise ValueError("expert exceeds the staging capacity")
+            self._pending.append((kind, *args))
+            if kind == "local":
+                self._local.add(args[0])
+            return
+        self._eng()
+        getattr(self, "_register_" + kind)(*args)
+
     def register_expert(self, expert_id: int, ptr: int, size_bytes: int) -> None:
-        _chk(_lib.load().dwdp_engine_register_local(self._eng(), expert_id, ptr, size_bytes), "register_expert")
+        """A local expert (the reference's register_expert): used in place, never copied."""
+        self._register("local", expert_id, int(ptr), int(size_bytes))
 
     def register_ipc_expert(self, expert_id: int, handle_blob: bytes, size_bytes: int, owner_device: int = -1,
                             extra_offset: int = 0) -> None:
         handle, off = split_ipc_handle(handle_blob)
-        _chk(_lib.load().dwdp_engine_register_ipc(self._eng(), expert_id, handle, off + extra_offset, size_bytes,
-                                                  owner_device), "register_ipc_expert")
+        self._register("ipc", expert_id, handle, off + extra_offset, int(size_bytes), owner_device)
 
     def register_peer_expert(self, expert_id: int, ptr: int, size_bytes: int, owner_device: int) -> None:
-        _chk(_lib.load().dwdp_engine_register_peer(self._eng(), expert_id, ptr, size_bytes, owner_device),
-             "register_peer_expert")
+        self._register("peer", expert_id, int(ptr), int(size_bytes), owner_device)
 
-    def prefetch(self, expert_ids, buffer: int = 0, after_current_stream: bool = True) -> None:
+    # ------------------------------------------------------------------ whole-layer form
+    def prefetch_into(self, expert_ids, buffer: int = 0, after_current_stream: bool = True) -> None:
         ids = [int(expert_ids)] if isinstance(expert_ids, int) else [int(e) for e in expert_ids]
         arr = (ctypes.c_int * max(1, len(ids)))(*ids)
         after = torch.cuda.current_stream(self.device_id).cuda_stream if after_current_stream else None
         _chk(_lib.load().dwdp_engine_prefetch(self._eng(), arr, len(ids), buffer, after), "prefetch")
+        for e in ids:
+            if e not in self._local:
+                self._where[e] = buffer
 
-    def wait(self, buffer: int = 0, stream: torch.cuda.Stream | None = None) -> None:
+    def wait_buffer(self, buffer: int = 0, stream: torch.cuda.Stream | None = None) -> None:
         s = (stream or torch.cuda.current_stream(self.device_id)).cuda_stream
         _chk(_lib.load().dwdp_engine_wait(self._eng(), buffer, s), "wait")
 
-    def get_resident_pointer(self, expert_id: int, buffer: int = 0) -> int:
+    # ------------------------------------------------------------------ the reference's form
+    @property
+    def current_buffer(self) -> int:
+        return self._current
+
+    @property
+    def next_buffer(self) -> int:
+        return (self._current + 1) % max(1, self.num_buffers)
+
+    def prefetch(self, expert_id: int) -> None:
+        """Copy a remote expert into the next staging buffer (after the work queued on the
+        current stream); local experts need no copy (communication_engine.cpp:85-91)."""
+        if int(expert_id) in self._local:
+            return
+        self.prefetch_into([int(expert_id)], self.next_buffer)
+
+    def wait(self, expert_id: int) -> None:
+        """Order the current stream after the copy of ``expert_id`` (communication_engine.cpp:93-96)."""
+        e = int(expert_id)
+        if e in self._local:
+            return
+        if e not in self._where:
+            raise RuntimeError(f"expert {e} was never prefetched")
+        self.wait_buffer(self._where[e])
+
+    def swap_buffers(self) -> None:
+        """The next buffer becomes current; what the old current buffer held is no longer
+        resident (communication_engine.cpp:128-135). Call it after the compute that read the
+        current buffer has been queued."""
+        self._eng()
+        old = self._current
+        self._current = self.next_buffer
+        self._where = {e: b for e, b in self._where.items() if b != old}
+
+    def is_resident(self, expert_id: int) -> bool:
+        """Local, or staged in the current buffer (communication_engine.cpp:102-105)."""
+        e = int(expert_id)
+        return e in self._local or self._where.get(e) == self._current
+
+    def get_resident_pointer(self, expert_id: int, buffer: int | None = None) -> int:
+        """Device pointer of the usable copy: the local slab, or the staged copy in the current
+        buffer (or in ``buffer``). The reference's form waits for the copy on the current
+        stream and refuses an expert staged only in the next buffer (communication_engine.cpp:107-126)."""
+        e = int(expert_id)
+        if buffer is None and e not in self._local:
+            if self._where.get(e) == self.next_buffer:
+                raise RuntimeError("expert is resident in the next buffer; call swap_buffers after prior compute")
+            if e not in self._where:
+                raise RuntimeError(f"expert {e} is not resident")
+            self.wait(e)
+        b = self._current if buffer is None else buffer
         out = ctypes.c_void_p()
-        _chk(_lib.load().dwdp_engine_resident_pointer(self._eng(), expert_id, buffer, ctypes.byref(out)),
+        _chk(_lib.load().dwdp_engine_resident_pointer(self._eng(), e, b, ctypes.byref(out)),
              "get_resident_pointer")
         return int(out.value or 0)
 
     getResidentPointer = get_resident_pointer
 
+    def get_weight(self, expert_id: int) -> int:
+        """Device pointer of the expert's weights as usable now (the reference's get_weight):
+        the local slab, or the staged copy of a remote expert in the current buffer."""
+        return self.get_resident_pointer(expert_id)
+
     def is_remote(self, expert_id: int) -> bool:
         out = ctypes.c_int(0)
         _chk(_lib.load().dwdp_engine_is_remote(self._eng(), expert_id, ctypes.byref(out)), "is_remote")
         return bool(out.value)
-
-    def is_resident(self, expert_id: int) -> bool:
-        return not self.is_remote(expert_id)
 
     def release(self, expert_id: int) -> None:
         _chk(_lib.load().dwdp_engine_release(self._eng(), expert_id), "release")

@@ -157,14 +157,14 @@ def measure_link(store, experts_per_sample: tuple[int, ...] = (1, 4, 8), repeats
     for n in experts_per_sample:
         ids = store.remote[:n]
         for _ in range(2):
-            store.engine.prefetch(ids, 0)
-            store.engine.wait(0)
+            store.engine.prefetch_into(ids, 0)
+            store.engine.wait_buffer(0)
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(repeats):
-            store.engine.prefetch(ids, 0)
-            store.engine.wait(0)
+            store.engine.prefetch_into(ids, 0)
+            store.engine.wait_buffer(0)
         b.record()
         torch.cuda.synchronize()
         samples.append((n, a.elapsed_time(b) * 1e3 / repeats))

@@ -146,10 +146,10 @@ class ShardedExpertStore:
     def prefetch(self, buffer: int = 0) -> None:
         """Copy every remote expert into ``buffer`` (after the work already queued
         on the current stream), on the engine's copy stream."""
-        self.engine.prefetch(self.remote, buffer)
+        self.engine.prefetch_into(self.remote, buffer)
 
     def wait(self, buffer: int = 0) -> None:
-        self.engine.wait(buffer)
+        self.engine.wait_buffer(buffer)
 
     def select_buffer(self, buffer: int) -> None:
         self.buffer = buffer

@@ -138,3 +138,22 @@ def test_policy_table(pkg):
     assert p.decide(owner_gpu=3, peer_access=True) == c.CommunicationPath.P2P
     assert p.decide(owner_gpu=3, peer_access=False) == c.CommunicationPath.COPY
     assert p.decide(owner_gpu=0) == c.CommunicationPath.COPY
+
+
+def test_engine_reference_surface_bookkeeping(pkg):
+    """The reference's CommunicationEngine surface before any device work: initialize(staging_bytes)
+    defers the staging allocation until the experts are known; local experts are resident and
+    need neither a copy nor a wait; an oversized remote expert is refused."""
+    eng = pkg.communication.CommunicationEngine(0)
+    assert not eng.initialized()
+    eng.initialize(1 << 20)
+    assert eng.initialized()
+    eng.register_expert(3, 0x1000, 4096)
+    assert eng.is_resident(3)
+    eng.prefetch(3)  # local: nothing to copy
+    eng.wait(3)
+    assert eng.current_buffer == 0 and eng.next_buffer == 1
+    with pytest.raises(ValueError):
+        eng.register_peer_expert(4, 0x2000, 2 << 20, 1)
+    with pytest.raises(RuntimeError):
+        eng.wait(5)  # never prefetched

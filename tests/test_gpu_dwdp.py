@@ -80,3 +80,37 @@ def test_dwdp_sharded_layer_matches_local():
     for rank, ok, copied, remote in res:
         assert ok is True, f"rank {rank}: {ok}"
         assert copied == 3 * remote  # three prefetches of every remote expert
+
+
+def test_engine_reference_surface_single_gpu(pkg):
+    """The reference's engine calls on one GPU (a same-device "peer" stands in for a remote
+    owner): prefetch(id) stages into the next buffer, which is not resident until
+    swap_buffers(); then get_weight(id) is a staged copy holding the owner's bytes."""
+    import ctypes
+
+    dev = torch.device("cuda", 0)
+    nbytes = 3 << 20
+    local = torch.arange(nbytes, dtype=torch.int64, device=dev).to(torch.uint8)
+    remote = (torch.arange(nbytes, dtype=torch.int64, device=dev) * 7 + 3).to(torch.uint8)
+    eng = pkg.communication.CommunicationEngine(0)
+    eng.initialize(4 << 20)
+    eng.register_expert(0, local.data_ptr(), nbytes)
+    eng.register_peer_expert(1, remote.data_ptr(), nbytes, 0)
+    assert eng.get_weight(0) == local.data_ptr()
+    assert not eng.is_resident(1)
+    eng.prefetch(1)
+    assert not eng.is_resident(1)
+    with pytest.raises(RuntimeError):
+        eng.get_resident_pointer(1)  # staged in the next buffer only
+    eng.swap_buffers()
+    assert eng.is_resident(1)
+    ptr = eng.get_weight(1)
+    assert ptr not in (0, remote.data_ptr())
+    torch.cuda.synchronize()
+    host = torch.empty(nbytes, dtype=torch.uint8)
+    cudart = ctypes.CDLL("libcudart.so.12")
+    assert cudart.cudaMemcpy(ctypes.c_void_p(host.data_ptr()), ctypes.c_void_p(ptr), ctypes.c_size_t(nbytes), 2) == 0
+    assert torch.equal(host, remote.cpu())
+    eng.swap_buffers()
+    assert not eng.is_resident(1)
+    eng.shutdown()
