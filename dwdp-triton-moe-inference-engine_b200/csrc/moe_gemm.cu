@@ -585,7 +585,10 @@ struct CfgP {
   static constexpr int SLOT = NMAT * NCOL;                // TMEM columns per K-block slot
   static constexpr int NSLOT = 512 / SLOT > 4 ? 4 : 512 / SLOT;
   static constexpr int TMEM_COLS = NSLOT * SLOT <= 256 ? 256 : 512;
-  static constexpr int TOKW = 32 / PLANES;                // tokens per epilogue warp (32 TMEM columns)
+  // tokens per epilogue warp: 16 (sixteen epilogue warps, four per SM sub-partition, to hide
+  // the TMEM-load latency) unless that would take more than 32 warps (128-token tiles)
+  static constexpr int TOKW = (PLANES == 1 && BNT == 128) ? 32 : 16;
+  static constexpr int TCOL = PLANES * TOKW;               // TMEM columns per warp and matrix
   static constexpr int CHUNKS = BNT / TOKW;
   static constexpr int EPI_WARPS = 4 * CHUNKS;
   static constexpr int EPI_THREADS = EPI_WARPS * 32;
@@ -608,6 +611,25 @@ struct CfgP {
 };
 
 __device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// (a0, a1) += (v0, v1) * (f0, f1) as one packed fp32x2 FMA (round to nearest).
+__device__ __forceinline__ void ffma2(float& a0, float& a1, float v0, float v1, float f0, float f1) {
+  asm("{\n\t.reg .b64 va, vf, vc;\n\t"
+      "mov.b64 va, {%2, %3};\n\t"
+      "mov.b64 vf, {%4, %5};\n\t"
+      "mov.b64 vc, {%0, %1};\n\t"
+      "fma.rn.f32x2 vc, va, vf, vc;\n\t"
+      "mov.b64 {%0, %1}, vc;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(v0), "f"(v1), "f"(f0), "f"(f1));
+}
+
+// TMEM columns of this thread's lane, N = 16 or 32.
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, float (&v)[N]) {
+  if constexpr (N == 16) tmem_ld16(taddr, v);
+  else tmem_ld32(taddr, v);
+}
 
 // Lane l ends with max over the warp's 32 lanes of v[l] (31 shuffles): at each step a
 // lane keeps the half of its array whose index bit matches its own lane bit and
@@ -742,11 +764,9 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
     const int t0 = chunk * C::TOKW;        // first token of this warp inside the tile
     float* my_scl = sScl + ew * 2 * C::NMAT * 32;
     uint32_t kc = 0;
-    WorkItem wn = p.items[blockIdx.x];
     bool ok = true;
     for (int item = blockIdx.x; item < n_items && !s_abort && ok; item += gridDim.x) {
-      const WorkItem wi = wn;
-      if (item + (int)gridDim.x < p.cap) wn = p.items[item + gridDim.x];
+      const WorkItem wi = p.items[item];  // loaded per item: no registers held across the K loop
       const GroupParams& g = p.g[wi.group];
       const int nm = min(wi.nmat, C::NMAT);
       const int ntk = min(C::TOKW, wi.nrows - t0);  // tokens of this warp (<= 0: none)
@@ -799,30 +819,57 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
         tc_fence_after();
         if (ntk > 0) {
           const uint32_t t_acc = tmem_base + slot * C::SLOT + PLANES * t0 + ((uint32_t)(quad * 32) << 16);
+          if constexpr (C::NMAT * C::TCOL <= 32) {
+            // every matrix's columns in flight at once, one wait
+            float v[C::NMAT][C::TCOL];
 #pragma unroll
-          for (int m = 0; m < C::NMAT; ++m) {
-            if (m < nm) {
+            for (int m = 0; m < C::NMAT; ++m)
+              if (m < nm) tmem_ld<C::TCOL>(t_acc + m * C::NCOL, v[m]);
+            tmem_ld_wait();
 #pragma unroll
-              for (int hf = 0; hf < 2; ++hf) {  // 16 TMEM columns at a time keeps registers in budget
-                float v[16];
-                tmem_ld16(t_acc + m * C::NCOL + 16 * hf, v);
-                tmem_ld_wait();
+            for (int m = 0; m < C::NMAT; ++m) {
+              if (m < nm) {
                 if constexpr (PLANES == 1) {
-                  const float4* f4 = reinterpret_cast<const float4*>(fac + m * 32 + 16 * hf);
+                  const float4* f4 = reinterpret_cast<const float4*>(fac + m * 32);
 #pragma unroll
-                  for (int q = 0; q < 4; ++q) {
+                  for (int q = 0; q < C::TOKW / 4; ++q) {
                     const float4 f = f4[q];
-                    float* a4 = &acc[m][16 * hf + 4 * q];
-                    a4[0] = fmaf(v[4 * q + 0], f.x, a4[0]);
-                    a4[1] = fmaf(v[4 * q + 1], f.y, a4[1]);
-                    a4[2] = fmaf(v[4 * q + 2], f.z, a4[2]);
-                    a4[3] = fmaf(v[4 * q + 3], f.w, a4[3]);
+                    ffma2(acc[m][4 * q], acc[m][4 * q + 1], v[m][4 * q], v[m][4 * q + 1], f.x, f.y);
+                    ffma2(acc[m][4 * q + 2], acc[m][4 * q + 3], v[m][4 * q + 2], v[m][4 * q + 3], f.z, f.w);
                   }
                 } else {
 #pragma unroll
-                  for (int j = 0; j < 8; ++j)
-                    acc[m][8 * hf + j] =
-                        fmaf(v[2 * j] + v[2 * j + 1] * (1.0f / kLoPlaneGain), sw_cur[m], acc[m][8 * hf + j]);
+                  for (int j = 0; j < C::TOKW; ++j)
+                    acc[m][j] = fmaf(v[m][2 * j] + v[m][2 * j + 1] * (1.0f / kLoPlaneGain), sw_cur[m], acc[m][j]);
+                }
+              }
+            }
+          } else {
+            // more columns than registers allow at once: 16 TMEM columns at a time
+            constexpr int TPH = 16 / PLANES;  // tokens per 16 columns
+#pragma unroll
+            for (int m = 0; m < C::NMAT; ++m) {
+              if (m < nm) {
+#pragma unroll
+                for (int hf = 0; hf < C::TCOL / 16; ++hf) {
+                  float v[16];
+                  tmem_ld16(t_acc + m * C::NCOL + 16 * hf, v);
+                  tmem_ld_wait();
+                  if constexpr (PLANES == 1) {
+                    const float4* f4 = reinterpret_cast<const float4*>(fac + m * 32 + 16 * hf);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                      const float4 f = f4[q];
+                      float* a4 = &acc[m][16 * hf + 4 * q];
+                      ffma2(a4[0], a4[1], v[4 * q], v[4 * q + 1], f.x, f.y);
+                      ffma2(a4[2], a4[3], v[4 * q + 2], v[4 * q + 3], f.z, f.w);
+                    }
+                  } else {
+#pragma unroll
+                    for (int j = 0; j < TPH; ++j)
+                      acc[m][TPH * hf + j] =
+                          fmaf(v[2 * j] + v[2 * j + 1] * (1.0f / kLoPlaneGain), sw_cur[m], acc[m][TPH * hf + j]);
+                  }
                 }
               }
             }
@@ -846,35 +893,38 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
       if constexpr (MODE == 0) {
         if constexpr (C::QOUT) {
           // h per the reference executor's bf16 arithmetic, then its (token, 128) amax
-          __nv_bfloat162 hp[16];  // h of tokens t0 + j, exact in bf16 (the accumulators die here)
+          __nv_bfloat162 hp[C::TOKW / 2];  // h of tokens t0 + j, exact in bf16 (the accumulators die here)
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
+          for (int j = 0; j < C::TOKW; ++j) {
             const float gb = bf16_round(acc[0][j] * s_row[0]);
             const float ub = bf16_round(acc[1][j] * s_row[1]);
             const float sg = bf16_round(1.0f / (1.0f + expf(-gb)));
             const float h = j < ntk ? bf16_round(bf16_round(gb * sg) * ub) : 0.f;
             if (j & 1) hp[j >> 1].y = __float2bfloat16_rn(h); else hp[j >> 1].x = __float2bfloat16_rn(h);
           }
-          float hq[32];
+          float hq[32];  // |h| of tokens t0 + j (zero past TOKW)
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const float2 f = __bfloat1622float2(hp[j]);
+            const float2 f = j < C::TOKW / 2 ? __bfloat1622float2(hp[j]) : make_float2(0.f, 0.f);
             hq[2 * j] = fabsf(f.x);
             hq[2 * j + 1] = fabsf(f.y);
           }
           const float wmax = warp_transpose_max(hq, lane);  // this warp's rows, token t0 + lane
-          sRed[quad * BNT + t0 + lane] = wmax;
+          if (lane < C::TOKW) sRed[quad * BNT + t0 + lane] = wmax;
           named_bar_sync(3, C::EPI_THREADS);
-          float tmax = sRed[t0 + lane];
+          float tmax = 0.f;
+          if (lane < C::TOKW) {
+            tmax = sRed[t0 + lane];
 #pragma unroll
-          for (int q = 1; q < 4; ++q) tmax = fmaxf(tmax, sRed[q * BNT + t0 + lane]);
+            for (int q = 1; q < 4; ++q) tmax = fmaxf(tmax, sRed[q * BNT + t0 + lane]);
+          }
           const float tsc = __fdiv_rn(fmaxf(tmax, 1e-5f), 448.0f);
           my_scl[lane] = tsc;
           __syncwarp();
           if (quad == 0 && lane < ntk)
             g.out_scale[(size_t)wi.rb * g.os_ld + wi.row0 + t0 + lane] = tsc;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
+          for (int j = 0; j < C::TOKW; ++j) {
             if (j < ntk) {
               const float hvj = __bfloat162float((j & 1) ? hp[j >> 1].y : hp[j >> 1].x);
               const float q = __fdiv_rn(hvj, my_scl[j]);
