@@ -601,7 +601,10 @@ struct CfgP {
   static constexpr int MAXREG = REG_FIT > 168 ? 168 : REG_FIT;
   static constexpr bool QOUT = MODE == 0 && PLANES == 1;   // gate/up writes e4m3 rows + scales
   static constexpr int STAGING = QOUT ? BNT * BM : 0;      // e4m3 [tokens][128 features]
-  static constexpr int SCL = EPI_WARPS * 2 * NMAT * 32 * 4;  // per-warp factor broadcast buffers
+  // per-warp ring of K-block scales (RING blocks of [32 token scales | NMAT weight-block scales]),
+  // filled DIST blocks ahead with asynchronous copies
+  static constexpr int RING = 4, DIST = 3, RSTRIDE = 32 + NMAT;
+  static constexpr int SCL = EPI_WARPS * RING * RSTRIDE * 4;
   static constexpr int RED = QOUT ? 4 * BNT * 4 : 0;       // per-quadrant token amax
   static constexpr int FIXED = STAGING + SCL + RED + 1024 /*align*/ + 512 /*barriers*/;
   static constexpr int S = (227 * 1024 - FIXED) / (W_STAGE_BYTES + B_TILE);
@@ -657,8 +660,8 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
   uint8_t* sB = smem;
   uint8_t* sW = sB + C::S * C::B_TILE;
   uint8_t* sQ = sW + C::S * C::W_STAGE_BYTES;                                  // [BNT][128] e4m3
-  float* sScl = reinterpret_cast<float*>(sQ + C::STAGING);                     // [EPI_WARPS][2][NMAT][32]
-  float* sRed = sScl + C::EPI_WARPS * 2 * C::NMAT * 32;                        // [4][BNT]
+  float* sScl = reinterpret_cast<float*>(sQ + C::STAGING);                     // [EPI_WARPS][RING][RSTRIDE]
+  float* sRed = sScl + C::EPI_WARPS * C::RING * C::RSTRIDE;                    // [4][BNT]
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sRed) + C::RED);
   uint64_t* ld_full = bars;
   uint64_t* ld_empty = ld_full + C::S;
@@ -762,7 +765,7 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
     const int chunk = ew >> 2;
     const int lrow = quad * 32 + lane;     // weight row inside the 128-row block
     const int t0 = chunk * C::TOKW;        // first token of this warp inside the tile
-    float* my_scl = sScl + ew * 2 * C::NMAT * 32;
+    float* my_scl = sScl + ew * C::RING * C::RSTRIDE;  // this warp's scale ring
     uint32_t kc = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < n_items && !s_abort && ok; item += gridDim.x) {
@@ -783,36 +786,44 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
 #pragma unroll
         for (int j = 0; j < C::TOKW; ++j) acc[m][j] = 0.f;
       // scale of this lane's token at K block kb (PLANES = 1), prefetched one block ahead
-      auto load_sx = [&](int kb) -> float {
+      // K-block kb's scales -> ring slot kb % RING: lane t the scale of token t0 + t (zero past the
+      // tile), lanes m < nm the block scale of matrix m (block-scaled weights)
+      auto issue = [&](int kb) {
+        float* rs = my_scl + (kb % C::RING) * C::RSTRIDE;
         if constexpr (PLANES == 1) {
-          return lane < ntk ? g.x_scale[(size_t)kb * g.xs_ld + wi.row0 + t0 + lane] : 0.f;
-        } else {
-          return 0.f;
+          const int t = lane < ntk ? lane : 0;
+          cp_async4(rs + lane, g.x_scale + (size_t)kb * g.xs_ld + wi.row0 + t0 + t, lane < ntk ? 4u : 0u);
         }
+        if (block_w && lane < nm) cp_async4(rs + 32 + lane, wsc + wsc_index(lane, kb), 4u);
+        cp_async_commit();
       };
-      auto load_sw = [&](int m, int kb) -> float {
-        return (block_w && m < nm) ? wsc[wsc_index(m, kb)] : 1.0f;
-      };
-      float sx_next = ntk > 0 ? load_sx(wi.kb_begin) : 0.f;
-      float sw_next[C::NMAT];
+      if (ntk > 0) {
 #pragma unroll
-      for (int m = 0; m < C::NMAT; ++m) sw_next[m] = ntk > 0 ? load_sw(m, wi.kb_begin) : 1.f;
+        for (int d = 0; d < C::DIST; ++d) {
+          if (wi.kb_begin + d < wi.kb_end) issue(wi.kb_begin + d);
+          else cp_async_commit();
+        }
+      }
+      // per-row weight scales (CHANNEL / TENSOR), applied after the K loop, loaded now
+      const int feat = wi.rb * BM + lrow;
+      float s_row[C::NMAT];
+#pragma unroll
+      for (int m = 0; m < C::NMAT; ++m) {
+        s_row[m] = 1.0f;
+        if (per_row_scales(g.scale_mode) && m < nm)
+          s_row[m] = MODE == 0 ? wsc[m * g.R + feat] : wsc[feat + m * BM];
+      }
       for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++kc) {
         const int slot = kc % C::NSLOT;
-        const float sx_cur = sx_next;
+        const float* rs = my_scl + (kb % C::RING) * C::RSTRIDE;
         float sw_cur[C::NMAT];
 #pragma unroll
-        for (int m = 0; m < C::NMAT; ++m) sw_cur[m] = sw_next[m];
-        if (ntk > 0 && kb + 1 < wi.kb_end) {  // next block's scales load while this one waits
-          sx_next = load_sx(kb + 1);
+        for (int m = 0; m < C::NMAT; ++m) sw_cur[m] = 1.0f;
+        if (ntk > 0) {
+          cp_async_wait<C::DIST - 1>();  // this lane's copies of block kb have landed
+          __syncwarp();                  // ... and every lane's are visible
 #pragma unroll
-          for (int m = 0; m < C::NMAT; ++m) sw_next[m] = load_sw(m, kb + 1);
-        }
-        // PLANES = 1: this lane's token factor sx * sw per matrix, broadcast through shared memory
-        float* fac = my_scl + (kb & 1) * C::NMAT * 32;
-        if constexpr (PLANES == 1) {
-#pragma unroll
-          for (int m = 0; m < C::NMAT; ++m) fac[m * 32 + lane] = sx_cur * sw_cur[m];
+          for (int m = 0; m < C::NMAT; ++m) sw_cur[m] = (block_w && m < nm) ? rs[32 + m] : 1.0f;
         }
         __syncwarp();
         if (!mbar_wait(&acc_full[slot], (kc / C::NSLOT) & 1, &s_abort, st, 44 + 8 * MODE)) { ok = false; break; }
@@ -830,10 +841,11 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
             for (int m = 0; m < C::NMAT; ++m) {
               if (m < nm) {
                 if constexpr (PLANES == 1) {
-                  const float4* f4 = reinterpret_cast<const float4*>(fac + m * 32);
+                  const float4* f4 = reinterpret_cast<const float4*>(rs);
 #pragma unroll
                   for (int q = 0; q < C::TOKW / 4; ++q) {
-                    const float4 f = f4[q];
+                    float4 f = f4[q];
+                    if (block_w) f = make_float4(f.x * sw_cur[m], f.y * sw_cur[m], f.z * sw_cur[m], f.w * sw_cur[m]);
                     ffma2(acc[m][4 * q], acc[m][4 * q + 1], v[m][4 * q], v[m][4 * q + 1], f.x, f.y);
                     ffma2(acc[m][4 * q + 2], acc[m][4 * q + 3], v[m][4 * q + 2], v[m][4 * q + 3], f.z, f.w);
                   }
@@ -856,10 +868,11 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
                   tmem_ld16(t_acc + m * C::NCOL + 16 * hf, v);
                   tmem_ld_wait();
                   if constexpr (PLANES == 1) {
-                    const float4* f4 = reinterpret_cast<const float4*>(fac + m * 32 + 16 * hf);
+                    const float4* f4 = reinterpret_cast<const float4*>(rs + 16 * hf);
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
-                      const float4 f = f4[q];
+                      float4 f = f4[q];
+                      if (block_w) f = make_float4(f.x * sw_cur[m], f.y * sw_cur[m], f.z * sw_cur[m], f.w * sw_cur[m]);
                       float* a4 = &acc[m][16 * hf + 4 * q];
                       ffma2(a4[0], a4[1], v[4 * q], v[4 * q + 1], f.x, f.y);
                       ffma2(a4[2], a4[3], v[4 * q + 2], v[4 * q + 3], f.z, f.w);
@@ -876,20 +889,18 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
           }
         }
         tc_fence_before();
-        __syncwarp();
+        __syncwarp();  // every lane is done with ring slot kb % RING and with the TMEM slot
         if (lane == 0) mbar_arrive(&acc_empty[slot]);
+        if (ntk > 0) {
+          if (kb + C::DIST < wi.kb_end) issue(kb + C::DIST);
+          else cp_async_commit();
+        }
       }
       if (!ok) break;
+      cp_async_wait<0>();
 
       // ---------------- item epilogue: per-row scales, SwiGLU / routing weight, stores
-      const int feat = wi.rb * BM + lrow;
-      float s_row[C::NMAT];
-#pragma unroll
-      for (int m = 0; m < C::NMAT; ++m) {
-        s_row[m] = 1.0f;
-        if (per_row_scales(g.scale_mode) && m < nm)
-          s_row[m] = MODE == 0 ? wsc[m * g.R + feat] : wsc[feat + m * BM];
-      }
+      __syncwarp();
       if constexpr (MODE == 0) {
         if constexpr (C::QOUT) {
           // h per the reference executor's bf16 arithmetic, then its (token, 128) amax
