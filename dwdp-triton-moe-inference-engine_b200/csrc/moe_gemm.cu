@@ -603,7 +603,10 @@ struct CfgP {
   static constexpr int STAGING = QOUT ? BNT * BM : 0;      // e4m3 [tokens][128 features]
   // per-warp ring of K-block scales (RING blocks of [32 token scales | NMAT weight-block scales]),
   // filled DIST blocks ahead with asynchronous copies
-  static constexpr int RING = 4, DIST = 3, RSTRIDE = 32 + NMAT;
+  // (a slot is 36 floats so that every slot starts on a 16-byte boundary: the token scales
+  // are read as float4)
+  static constexpr int RING = 4, DIST = 3, RSTRIDE = 36;
+  static_assert(NMAT <= RSTRIDE - 32, "weight-block scales must fit the slot padding");
   static constexpr int SCL = EPI_WARPS * RING * RSTRIDE * 4;
   static constexpr int RED = QOUT ? 4 * BNT * 4 : 0;       // per-quadrant token amax
   static constexpr int FIXED = STAGING + SCL + RED + 1024 /*align*/ + 512 /*barriers*/;
