@@ -46,11 +46,17 @@ ACTIVATION_QUANT = "block128"
 
 
 def _peaks() -> dict:
+    """Roofline denominators: measured HBM copy bandwidth and cuBLAS bf16 burst rate from
+    MEASURED_PEAKS.json (else the pool's fallback figures). MEASURED_PEAKS has no FP8 figure;
+    the FP8 dense peak used is 2x the measured bf16 burst (B200's dense FP8:bf16 ratio is 2:1)."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+        hbm, bf16, src = d["hbm_gbs"], d["bf16_tflops"], "measured"
+    else:
+        hbm, bf16, src = 6650.0, 1590.0, "fallback"
+    return {"hbm_gbs": hbm, "bf16_tflops": bf16, "fp8_tflops": 2.0 * bf16, "source": src,
+            "fp8_source": f"2 x the {src} bf16 dense burst ({bf16:.1f} TF/s); HBM {src} copy bandwidth"}
 
 
 # ----------------------------------------------------------------------------- setup
@@ -95,9 +101,9 @@ def make_qwen_layer(pkg, device, seed: int = 1235, *, rank: int = 0, world: int 
                         activation_quant=activation_quant or ACTIVATION_QUANT)
 
 
-def make_inputs(T: int, device, seed: int) -> torch.Tensor:
+def make_inputs(T: int, device, seed: int, H: int | None = None) -> torch.Tensor:
     g = torch.Generator(device=device).manual_seed(seed)
-    return torch.randn(T, QWEN["H"], generator=g, device=device).bfloat16()
+    return torch.randn(T, H or QWEN["H"], generator=g, device=device).bfloat16()
 
 
 class L2Flusher:
@@ -226,18 +232,33 @@ def expert_bytes(layer, counts: torch.Tensor, T: int) -> int:
     experts and the shared expert, packed activations in, weighted rows out."""
     active = int((counts > 0).sum().item())
     H, K = layer.hidden_size, layer.top_k
-    b = active * layer.experts.nbytes_per_expert() + layer.shared_expert.nbytes_per_expert()
-    b += (T * K + T) * H * 2 * 2
+    b = active * layer.experts.nbytes_per_expert()
+    if layer.shared_expert is not None:
+        b += layer.shared_expert.nbytes_per_expert() + T * H * 2 * 2
+    b += T * K * H * 2 * 2
     return b
 
 
+def algo_layer_bytes(layer, expert_b: int, T: int) -> int:
+    """Whole-layer algorithmic bytes: the expert launches' bytes plus the router weight, the
+    routing indices and weights, and the layer's input read and output write."""
+    K, H = layer.top_k, layer.hidden_size
+    return expert_b + layer.router_weight.numel() * layer.router_weight.element_size() + T * K * (8 + 4) + T * H * 2 * 2
+
+
+# DRAM bytes (read + write) of the expert launches of one Qwen-shaped layer, per (T, activation
+# mode), from one ncu capture of bench's layer (profiles/). None where no capture was made.
+TRAFFIC_PER_LAYER: dict = {}
+
+
 def expert_flops(layer, T: int) -> int:
-    H, I, K, Is = layer.hidden_size, layer.experts.intermediate_size, layer.top_k, layer.shared_expert.intermediate_size
+    H, I, K = layer.hidden_size, layer.experts.intermediate_size, layer.top_k
+    Is = layer.shared_expert.intermediate_size if layer.shared_expert is not None else 0
     return 2 * T * K * 3 * H * I + 2 * T * 3 * H * Is
 
 
 def run_point(pkg, layer, T: int, steps: int, warmup: int, flush, device, rank: int, world: int):
-    x = make_inputs(T, device, seed=4242 + 7919 * rank + T)
+    x = make_inputs(T, device, seed=4242 + 7919 * rank + T, H=layer.hidden_size)
     out = torch.empty(T, layer.hidden_size, dtype=torch.bfloat16, device=device)
     ws = layer.workspace(T)
     stream = torch.cuda.Stream(device)
@@ -645,6 +666,83 @@ def decode_step_bench(pkg, device, batches: list[int], steps: int, warmup: int, 
             "peak_source": peaks["source"]}
 
 
+# ----------------------------------------------------------------------------- other BASELINE shapes
+SHAPES = {
+    # Mixtral-8x7B, 128x128 block scales, Zipf(1.2)-skewed routing
+    "mixtral": dict(H=4096, E=8, I=14336, K=2, Is=0, prefill=8192, decode=[128], zipf=True,
+                    model="Mixtral-8x7B (shape)"),
+    # DeepSeek-V3, 256 experts, top-8, one shared expert, 128x128 block scales
+    "deepseek": dict(H=7168, E=256, I=2048, K=8, Is=2048, prefill=4096, decode=[16, 256], zipf=False,
+                     model="DeepSeek-V3 (shape)"),
+}
+
+
+def make_shape_layer(pkg, device, shape: dict, seed: int = 1240):
+    """Random-init layer of a BASELINE shape: router W ~ N(0, 1/H) (+ a Zipf(1.2) expert bias
+    for Mixtral: bias_e = -1.2 ln(rank_e + 1)), experts ~ N(0, 0.02) in e4m3 with 128x128 block
+    scales, bench's activation quantisation, shared expert with a sigmoid gate where the
+    shape has one. Weights are generated one expert at a time on the device."""
+    H, E, I, K, Is = shape["H"], shape["E"], shape["I"], shape["K"], shape["Is"]
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def store(n, inter):
+        st = pkg.ExpertWeightStore(n, H, inter, weight_dtype=torch.float8_e4m3fn,
+                                   scale_mode=pkg._lib.SCALE_BLOCK128, device=device,
+                                   activation_quant=ACTIVATION_QUANT)
+        for e in range(n):
+            st.load_expert(e, torch.randn(inter, H, generator=g, device=device) * 0.02,
+                           torch.randn(inter, H, generator=g, device=device) * 0.02,
+                           torch.randn(H, inter, generator=g, device=device) * 0.02)
+        return st
+
+    wr = (torch.randn(E, H, generator=g, device=device) / H**0.5).bfloat16()
+    bias = None
+    if shape["zipf"]:
+        rank = torch.randperm(E, generator=torch.Generator().manual_seed(seed))
+        bias = (-1.2 * torch.log(rank.float() + 1.0)).to(device)
+    shared = store(1, Is) if Is else None
+    gate = (torch.randn(H, generator=g, device=device) * 0.02).bfloat16() if Is else None
+    return pkg.MoELayer(wr, store(E, I), K, shared_expert=shared, shared_gate_weight=gate, router_bias=bias,
+                        activation_quant=ACTIVATION_QUANT)
+
+
+def shape_bench(pkg, device, name: str, steps: int, warmup: int, flush) -> dict:
+    """One layer of a BASELINE shape at its prefill and decode batch sizes, graph-replayed,
+    L2 flushed before every timed replay: tokens/s, the expert GEMMs' useful FP8 rate against
+    the FP8 peak and their bytes against measured HBM."""
+    shape = SHAPES[name]
+    peaks = _peaks()
+    layer = make_shape_layer(pkg, device, shape)
+    points = []
+    for T in [shape["prefill"]] + shape["decode"]:
+        pt = run_point(pkg, layer, T, steps, warmup, flush, device, 0, 1)
+        lm, em = statistics.mean(pt["layer_ms"]), statistics.mean(pt["experts_ms"])
+        tf = pt["flops"] / (em / 1e3) / 1e12
+        gbs = pt["bytes"] / (em / 1e3) / 1e9
+        points.append({"T": T, "layer_us": lm * 1e3, "tokens_per_s": T / (lm / 1e3), "experts_us": em * 1e3,
+                       "active_experts": pt["active_experts"], "expert_tflops": tf,
+                       "frac_fp8_peak": tf / peaks["fp8_tflops"], "expert_bytes": pt["bytes"], "hbm_gbs": gbs,
+                       "frac_hbm": gbs / peaks["hbm_gbs"],
+                       "bound": "tensor" if T == shape["prefill"] else "hbm"})
+        del pt
+    extra = {}
+    if shape["zipf"]:
+        xs = make_inputs(8192, device, seed=77, H=shape["H"])
+        res = pkg.ops.router_topk(xs, layer.router_weight, shape["K"], bias=layer.router_bias)
+        load = torch.bincount(res.topk_indices.reshape(-1), minlength=shape["E"]).float().cpu()
+        srt = load.sort(descending=True).values.clamp_min(1.0)
+        lr = torch.log(torch.arange(1, shape["E"] + 1).float())
+        ll = torch.log(srt)
+        extra["zipf_loglog_slope"] = float(((lr - lr.mean()) * (ll - ll.mean())).sum() / ((lr - lr.mean()) ** 2).sum())
+        extra["expert_load"] = load.tolist()
+    return {"workload": name, "model": shape["model"], "hidden": shape["H"], "experts": shape["E"],
+            "moe_intermediate": shape["I"], "top_k": shape["K"], "shared_intermediate": shape["Is"],
+            "weights": "fp8 e4m3, 128x128 block scales", "activations": ACTIVATION_QUANT, "points": points,
+            "fp8_peak_tflops": peaks["fp8_tflops"], "hbm_peak_gbs": peaks["hbm_gbs"],
+            "peak_source": peaks["fp8_source"],
+            "l2": "flushed (256 MB write + 256 MB read) before every timed replay", **extra}
+
+
 def attention_bench(pkg, device, batches: list[int], steps: int, warmup: int, flush) -> dict:
     """paged_attention alone (16 heads of 128, block_size 16, every sequence at context 2048,
     pages in a random order): the kernel pair's time and its HBM roofline per batch size."""
@@ -687,7 +785,8 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=256)
-    ap.add_argument("--workload", default="moe_layers", choices=["moe_layers", "decode_step", "attention"])
+    ap.add_argument("--workload", default="moe_layers",
+                    choices=["moe_layers", "decode_step", "attention", "mixtral", "deepseek"])
     ap.add_argument("--batch", default="1,8,64", help="decode_step batch sizes")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -746,6 +845,13 @@ def main() -> None:
         print(json.dumps({"metric": "paged attention HBM GB/s", "unit": "GB/s", "steps": args.steps,
                           "warmup": args.warmup, **res}), flush=True)
         return
+    if args.workload in SHAPES:
+        res = shape_bench(pkg, device, args.workload, args.steps, args.warmup, flush)
+        p0 = res["points"][0]
+        print(json.dumps({"metric": f"MoE-layer tokens/s ({res['model']})", "value": p0["tokens_per_s"],
+                          "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                          "higher_is_better": True, "dtype": "fp8_e4m3", "data": "synthetic", **res}), flush=True)
+        return
     if args.workload == "decode_step":
         res = decode_step_bench(pkg, device, [int(b) for b in args.batch.split(",")], args.steps, args.warmup, flush)
         if rank == 0:
@@ -776,13 +882,18 @@ def main() -> None:
     pt = run_point(pkg, lay0, T, args.steps, args.warmup, flush, device, rank, world)
     exp_ms = statistics.mean(pt["experts_ms"])
     ach = pt["flops"] / (exp_ms / 1e3) / 1e12
-    roof = {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-            "frac": ach / peaks["bf16_tflops"], "traffic": None,
-            "kernel": "grouped expert GEMMs of one layer (plan+planes, gate/up, planes, down launches): "
-                      "tcgen05 kind::f8f6f4 on e4m3 weights x hi/lo e4m3 activation planes",
-            "peak_source": peaks["source"] + " bf16 dense (burst); useful FLOPs, the hi/lo planes run "
-                           "2 e4m3 MMA columns per token so the e4m3 pipe is held to the bf16 rate",
-            "e4m3_pipe_tflops": 2 * ach,
+    hilo = lay0.activation_quant != "block128"
+    roof = {"bound": "tensor", "achieved": ach, "peak": peaks["fp8_tflops"], "unit": "TFLOP/s",
+            "frac": ach / peaks["fp8_tflops"], "traffic": TRAFFIC_PER_LAYER.get((T, lay0.activation_quant)),
+            "kernel": "grouped expert GEMMs of one layer (plan + activation quantisation, gate/up + SwiGLU + "
+                      "re-quantisation, down + routing weight): tcgen05 kind::f8f6f4 on e4m3 weights x "
+                      + ("hi/lo e4m3 activation planes" if hilo else
+                         "one e4m3 activation plane per (token, 128) with per-K-block fp32 promotion"),
+            "peak_source": peaks["fp8_source"] + "; achieved counts useful FLOPs "
+                           "(2*T*K*3*H*I + 2*T*3*H*Is) over the CUDA-event time of the expert launches",
+            "executed_tflops": (2 if hilo else 1) * ach,
+            "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of the expert launches of one "
+                            "layer at this T from one ncu capture (profiles/)",
             "layer_us": statistics.mean(pt["layer_ms"]) * 1e3, "experts_us": exp_ms * 1e3}
 
     sweep = []
@@ -791,9 +902,11 @@ def main() -> None:
             p2 = run_point(pkg, lay0, Ts, args.steps, args.warmup, flush, device, rank, world)
             lm, em = statistics.mean(p2["layer_ms"]), statistics.mean(p2["experts_ms"])
             gbs = p2["bytes"] / (em / 1e3) / 1e9
+            lb = algo_layer_bytes(lay0, p2["bytes"], Ts)
             sweep.append({"T": Ts, "layer_us": lm * 1e3, "tokens_per_s": Ts / (lm / 1e3),
                           "experts_us": em * 1e3, "active_experts": p2["active_experts"],
-                          "expert_bytes": p2["bytes"], "hbm_gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"]})
+                          "expert_bytes": p2["bytes"], "hbm_gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"],
+                          "layer_bytes": lb, "layer_hbm_frac": lb / (lm / 1e3) / 1e9 / peaks["hbm_gbs"]})
 
     # end to end: pinned host input -> L layers -> pinned host output, every step
     x_host = stack.x0.cpu().pin_memory()

@@ -19,7 +19,7 @@ LIB_NAME = "libdwdp_b200.so"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", f"-I{INCLUDE}",
-          "--expt-relaxed-constexpr"]
+          "--expt-relaxed-constexpr"] + os.environ.get("DWDP_NVCC_FLAGS", "").split()  # e.g. a diagnostic -D
 
 
 def _sources() -> list[pathlib.Path]:

@@ -616,6 +616,24 @@ struct CfgP {
   static_assert(NSLOT >= 2, "need at least two TMEM slots");
 };
 
+#ifdef DWDP_PROFILE_ROLES
+// Diagnostic build only: cycles each role of moe_gemm_f8p_kernel spends per activity, in
+// g_role_cycles[cta][32 * MODE + slot] (producer 0-1, MMA issuer 2-4, epilogue warp 2: 5-10).
+#define RP_TIMED(slot, call) ([&]() { const long long t_ = clock64(); const bool r_ = (call); \
+    rp_[slot] += (unsigned long long)(clock64() - t_); return r_; }())
+#define RP_BEGIN unsigned long long rp_[16] = {}; const long long rp0_ = clock64();
+#define RP_MARK long long rpm_ = clock64();
+#define RP_ADD(slot) { const long long n_ = clock64(); rp_[slot] += (unsigned long long)(n_ - rpm_); rpm_ = n_; }
+#define RP_END(total, lo, hi) { rp_[total] = (unsigned long long)(clock64() - rp0_); \
+    for (int q_ = lo; q_ <= hi; ++q_) g_role_cycles[blockIdx.x][32 * MODE + q_] = rp_[q_]; }
+#else
+#define RP_TIMED(slot, call) (call)
+#define RP_BEGIN
+#define RP_MARK
+#define RP_ADD(slot)
+#define RP_END(total, lo, hi)
+#endif
+
 __device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
 // (a0, a1) += (v0, v1) * (f0, f1) as one packed fp32x2 FMA (round to nearest).
@@ -708,6 +726,7 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
+      RP_BEGIN
       uint32_t it = 0;
       WorkItem wn = p.items[blockIdx.x];
       for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
@@ -719,7 +738,7 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
         const int nm = min(wi.nmat, C::NMAT);
         for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
           const int s = it % C::S;
-          if (!mbar_wait(&ld_empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 41 + 8 * MODE)) break;
+          if (!RP_TIMED(0, mbar_wait(&ld_empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 41 + 8 * MODE))) break;
           mbar_arrive_expect_tx(&ld_full[s], (uint32_t)(nm * kW8TileBytes) + b_bytes);
           for (int m = 0; m < nm; ++m)
             bulk_g2s(sW + s * C::W_STAGE_BYTES + m * kW8TileBytes,
@@ -727,10 +746,12 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
           tma_load_2d(sB + s * C::B_TILE, &g.tmap_b, kb * BK8, PLANES * wi.row0, &ld_full[s]);
         }
       }
+      RP_END(1, 0, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
+      RP_BEGIN
       uint32_t it = 0, kc = 0;
       WorkItem wn = p.items[blockIdx.x];
       bool ok = true;
@@ -743,8 +764,8 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
         for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it, ++kc) {
           const int s = it % C::S;
           const int slot = kc % C::NSLOT;
-          if (!mbar_wait(&acc_empty[slot], ((kc / C::NSLOT) & 1) ^ 1, &s_abort, st, 42 + 8 * MODE)) { ok = false; break; }
-          if (!mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 43 + 8 * MODE)) { ok = false; break; }
+          if (!RP_TIMED(2, mbar_wait(&acc_empty[slot], ((kc / C::NSLOT) & 1) ^ 1, &s_abort, st, 42 + 8 * MODE))) { ok = false; break; }
+          if (!RP_TIMED(3, mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 43 + 8 * MODE))) { ok = false; break; }
           tc_fence_after();
           // a K step of 32 e4m3 (32 bytes) is +2 in the encoded start address
           const uint64_t b_desc0 = smem_desc_sw128(smem_u32(sB + s * C::B_TILE));
@@ -760,6 +781,7 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
           mma_commit(&acc_full[slot]);
         }
       }
+      RP_END(4, 2, 4)
     }
   } else {
     // ------------------------------------------------------------ epilogue (promotion)
@@ -771,7 +793,9 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
     float* my_scl = sScl + ew * C::RING * C::RSTRIDE;  // this warp's scale ring
     uint32_t kc = 0;
     bool ok = true;
+    RP_BEGIN
     for (int item = blockIdx.x; item < n_items && !s_abort && ok; item += gridDim.x) {
+      RP_MARK
       const WorkItem wi = p.items[item];  // loaded per item: no registers held across the K loop
       const GroupParams& g = p.g[wi.group];
       const int nm = min(wi.nmat, C::NMAT);
@@ -823,13 +847,16 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
 #pragma unroll
         for (int m = 0; m < C::NMAT; ++m) sw_cur[m] = 1.0f;
         if (ntk > 0) {
+          RP_ADD(10)
           cp_async_wait<C::DIST - 1>();  // this lane's copies of block kb have landed
           __syncwarp();                  // ... and every lane's are visible
 #pragma unroll
           for (int m = 0; m < C::NMAT; ++m) sw_cur[m] = (block_w && m < nm) ? rs[32 + m] : 1.0f;
         }
         __syncwarp();
+        RP_ADD(6)
         if (!mbar_wait(&acc_full[slot], (kc / C::NSLOT) & 1, &s_abort, st, 44 + 8 * MODE)) { ok = false; break; }
+        RP_ADD(5)
         tc_fence_after();
         if (ntk > 0) {
           const uint32_t t_acc = tmem_base + slot * C::SLOT + PLANES * t0 + ((uint32_t)(quad * 32) << 16);
@@ -891,6 +918,7 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
             }
           }
         }
+        RP_ADD(7)
         tc_fence_before();
         __syncwarp();  // every lane is done with ring slot kb % RING and with the TMEM slot
         if (lane == 0) mbar_arrive(&acc_empty[slot]);
@@ -903,6 +931,7 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
       cp_async_wait<0>();
 
       // ---------------- item epilogue: per-row scales, SwiGLU / routing weight, stores
+      RP_ADD(10)
       __syncwarp();
       if constexpr (MODE == 0) {
         if constexpr (C::QOUT) {
@@ -981,7 +1010,11 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
           }
         }
       }
+      RP_ADD(8)
     }
+#ifdef DWDP_PROFILE_ROLES
+    if (warp == 2 && lane == 0) RP_END(9, 5, 10)
+#endif
   }
 
   tc_fence_before();
