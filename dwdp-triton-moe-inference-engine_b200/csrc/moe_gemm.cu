@@ -648,6 +648,17 @@ __device__ __forceinline__ void ffma2(float& a0, float& a1, float v0, float v1, 
       : "f"(v0), "f"(v1), "f"(f0), "f"(f1));
 }
 
+// acc += v * f for a pair of tokens: one packed fp32x2 FMA in the DWDP_FFMA2 build, two
+// scalar FMAs otherwise (the packing moves can cost more than the FMA they save).
+__device__ __forceinline__ void fma_pair(float& a0, float& a1, float v0, float v1, float f0, float f1) {
+#ifdef DWDP_FFMA2
+  ffma2(a0, a1, v0, v1, f0, f1);
+#else
+  a0 = fmaf(v0, f0, a0);
+  a1 = fmaf(v1, f1, a1);
+#endif
+}
+
 // TMEM columns of this thread's lane, N = 16 or 32.
 template <int N>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, float (&v)[N]) {
@@ -872,12 +883,21 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
               if (m < nm) {
                 if constexpr (PLANES == 1) {
                   const float4* f4 = reinterpret_cast<const float4*>(rs);
+                  if (block_w) {
 #pragma unroll
-                  for (int q = 0; q < C::TOKW / 4; ++q) {
-                    float4 f = f4[q];
-                    if (block_w) f = make_float4(f.x * sw_cur[m], f.y * sw_cur[m], f.z * sw_cur[m], f.w * sw_cur[m]);
-                    ffma2(acc[m][4 * q], acc[m][4 * q + 1], v[m][4 * q], v[m][4 * q + 1], f.x, f.y);
-                    ffma2(acc[m][4 * q + 2], acc[m][4 * q + 3], v[m][4 * q + 2], v[m][4 * q + 3], f.z, f.w);
+                    for (int q = 0; q < C::TOKW / 4; ++q) {
+                      float4 f = f4[q];
+                      const float w = sw_cur[m];
+                      fma_pair(acc[m][4 * q], acc[m][4 * q + 1], v[m][4 * q], v[m][4 * q + 1], f.x * w, f.y * w);
+                      fma_pair(acc[m][4 * q + 2], acc[m][4 * q + 3], v[m][4 * q + 2], v[m][4 * q + 3], f.z * w, f.w * w);
+                    }
+                  } else {
+#pragma unroll
+                    for (int q = 0; q < C::TOKW / 4; ++q) {
+                      const float4 f = f4[q];
+                      fma_pair(acc[m][4 * q], acc[m][4 * q + 1], v[m][4 * q], v[m][4 * q + 1], f.x, f.y);
+                      fma_pair(acc[m][4 * q + 2], acc[m][4 * q + 3], v[m][4 * q + 2], v[m][4 * q + 3], f.z, f.w);
+                    }
                   }
                 } else {
 #pragma unroll
@@ -899,13 +919,14 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
                   tmem_ld_wait();
                   if constexpr (PLANES == 1) {
                     const float4* f4 = reinterpret_cast<const float4*>(rs + 16 * hf);
+                    const float w = block_w ? sw_cur[m] : 1.0f;
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                       float4 f = f4[q];
-                      if (block_w) f = make_float4(f.x * sw_cur[m], f.y * sw_cur[m], f.z * sw_cur[m], f.w * sw_cur[m]);
+                      if (block_w) f = make_float4(f.x * w, f.y * w, f.z * w, f.w * w);
                       float* a4 = &acc[m][16 * hf + 4 * q];
-                      ffma2(a4[0], a4[1], v[4 * q], v[4 * q + 1], f.x, f.y);
-                      ffma2(a4[2], a4[3], v[4 * q + 2], v[4 * q + 3], f.z, f.w);
+                      fma_pair(a4[0], a4[1], v[4 * q], v[4 * q + 1], f.x, f.y);
+                      fma_pair(a4[2], a4[3], v[4 * q + 2], v[4 * q + 3], f.z, f.w);
                     }
                   } else {
 #pragma unroll
@@ -941,7 +962,7 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
           for (int j = 0; j < C::TOKW; ++j) {
             const float gb = bf16_round(acc[0][j] * s_row[0]);
             const float ub = bf16_round(acc[1][j] * s_row[1]);
-            const float sg = bf16_round(1.0f / (1.0f + expf(-gb)));
+            const float sg = bf16_round(__fdividef(1.0f, 1.0f + __expf(-gb)));
             const float h = j < ntk ? bf16_round(bf16_round(gb * sg) * ub) : 0.f;
             if (j & 1) hp[j >> 1].y = __float2bfloat16_rn(h); else hp[j >> 1].x = __float2bfloat16_rn(h);
           }
@@ -962,7 +983,7 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
             for (int q = 1; q < 4; ++q) tmax = fmaxf(tmax, sRed[q * BNT + t0 + lane]);
           }
           const float tsc = __fdiv_rn(fmaxf(tmax, 1e-5f), 448.0f);
-          my_scl[lane] = tsc;
+          my_scl[lane] = __frcp_rn(tsc);  // quantise by multiplying with the reciprocal
           __syncwarp();
           if (quad == 0 && lane < ntk)
             g.out_scale[(size_t)wi.rb * g.os_ld + wi.row0 + t0 + lane] = tsc;
@@ -970,7 +991,7 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
           for (int j = 0; j < C::TOKW; ++j) {
             if (j < ntk) {
               const float hvj = __bfloat162float((j & 1) ? hp[j >> 1].y : hp[j >> 1].x);
-              const float q = __fdiv_rn(hvj, my_scl[j]);
+              const float q = hvj * my_scl[j];
               sQ[(t0 + j) * BM + lrow] = (uint8_t)__nv_cvt_float_to_fp8(q, __NV_SATFINITE, __NV_E4M3);
             }
           }
