@@ -651,7 +651,9 @@ __device__ __forceinline__ void ffma2(float& a0, float& a1, float v0, float v1, 
 // acc += v * f for a pair of tokens: one packed fp32x2 FMA in the DWDP_FFMA2 build, two
 // scalar FMAs otherwise (the packing moves can cost more than the FMA they save).
 __device__ __forceinline__ void fma_pair(float& a0, float& a1, float v0, float v1, float f0, float f1) {
-#ifdef DWDP_FFMA2
+#if defined(DWDP_DIAG_NO_FMA)
+  a0 += v0; (void)a1; (void)v1; (void)f0; (void)f1;
+#elif defined(DWDP_FFMA2)
   ffma2(a0, a1, v0, v1, f0, f1);
 #else
   a0 = fmaf(v0, f0, a0);
@@ -876,7 +878,11 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
             float v[C::NMAT][C::TCOL];
 #pragma unroll
             for (int m = 0; m < C::NMAT; ++m)
+#ifdef DWDP_DIAG_NO_TMEM
+              for (int j = 0; j < C::TCOL; ++j) v[m][j] = (float)j;
+#else
               if (m < nm) tmem_ld<C::TCOL>(t_acc + m * C::NCOL, v[m]);
+#endif
             tmem_ld_wait();
 #pragma unroll
             for (int m = 0; m < C::NMAT; ++m) {
@@ -915,7 +921,11 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
 #pragma unroll
                 for (int hf = 0; hf < C::TCOL / 16; ++hf) {
                   float v[16];
+#ifdef DWDP_DIAG_NO_TMEM
+                  for (int j = 0; j < 16; ++j) v[j] = (float)j;
+#else
                   tmem_ld16(t_acc + m * C::NCOL + 16 * hf, v);
+#endif
                   tmem_ld_wait();
                   if constexpr (PLANES == 1) {
                     const float4* f4 = reinterpret_cast<const float4*>(rs + 16 * hf);
@@ -955,7 +965,11 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
       RP_ADD(10)
       __syncwarp();
       if constexpr (MODE == 0) {
+#ifdef DWDP_DIAG_NO_QOUT
+        if constexpr (false) {
+#else
         if constexpr (C::QOUT) {
+#endif
           // h per the reference executor's bf16 arithmetic, then its (token, 128) amax
           __nv_bfloat162 hp[C::TOKW / 2];  // h of tokens t0 + j, exact in bf16 (the accumulators die here)
 #pragma unroll
