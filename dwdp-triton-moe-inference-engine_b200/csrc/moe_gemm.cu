@@ -585,9 +585,11 @@ struct CfgP {
   static constexpr int SLOT = NMAT * NCOL;                // TMEM columns per K-block slot
   static constexpr int NSLOT = 512 / SLOT > 4 ? 4 : 512 / SLOT;
   static constexpr int TMEM_COLS = NSLOT * SLOT <= 256 ? 256 : 512;
-  // tokens per epilogue warp: 16 (sixteen epilogue warps, four per SM sub-partition, to hide
-  // the TMEM-load latency) unless that would take more than 32 warps (128-token tiles)
-  static constexpr int TOKW = (PLANES == 1 && BNT == 128) ? 32 : 16;
+  // Tokens per epilogue warp: 32 with one activation plane (eight epilogue warps for 64-token
+  // tiles, so each thread has 168 registers and the promoted accumulators never spill: with
+  // sixteen warps the 96-register budget spilled them and every K block paid local-memory
+  // round trips), 16 with hi/lo planes (two TMEM columns per token).
+  static constexpr int TOKW = PLANES == 1 ? 32 : 16;
   static constexpr int TCOL = PLANES * TOKW;               // TMEM columns per warp and matrix
   static constexpr int CHUNKS = BNT / TOKW;
   static constexpr int EPI_WARPS = 4 * CHUNKS;
@@ -599,6 +601,9 @@ struct CfgP {
   static constexpr int WARPS = THREADS / 32;
   static constexpr int REG_FIT = 16384 / (((WARPS + 3) / 4) * 32) / 8 * 8;
   static constexpr int MAXREG = REG_FIT > 168 ? 168 : REG_FIT;
+  // every matrix's TMEM columns of a K block loaded at once when accumulators + loaded columns
+  // leave ~40 registers for the rest; else 16 columns at a time
+  static constexpr bool ALL_AT_ONCE = NMAT * (TOKW + TCOL) + 40 <= MAXREG;
   static constexpr bool QOUT = MODE == 0 && PLANES == 1;   // gate/up writes e4m3 rows + scales
   static constexpr int STAGING = QOUT ? BNT * BM : 0;      // e4m3 [tokens][128 features]
   // per-warp ring of K-block scales (RING blocks of [32 token scales | NMAT weight-block scales]),
@@ -873,7 +878,7 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
         tc_fence_after();
         if (ntk > 0) {
           const uint32_t t_acc = tmem_base + slot * C::SLOT + PLANES * t0 + ((uint32_t)(quad * 32) << 16);
-          if constexpr (C::NMAT * C::TCOL <= 32) {
+          if constexpr (C::ALL_AT_ONCE) {
             // every matrix's columns in flight at once, one wait
             float v[C::NMAT][C::TCOL];
 #pragma unroll
@@ -934,9 +939,9 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
                     for (int q = 0; q < 4; ++q) {
                       float4 f = f4[q];
                       if (block_w) f = make_float4(f.x * w, f.y * w, f.z * w, f.w * w);
-                      float* a4 = &acc[m][16 * hf + 4 * q];
-                      fma_pair(a4[0], a4[1], v[4 * q], v[4 * q + 1], f.x, f.y);
-                      fma_pair(a4[2], a4[3], v[4 * q + 2], v[4 * q + 3], f.z, f.w);
+                      const int j = 16 * hf + 4 * q;
+                      fma_pair(acc[m][j], acc[m][j + 1], v[4 * q], v[4 * q + 1], f.x, f.y);
+                      fma_pair(acc[m][j + 2], acc[m][j + 3], v[4 * q + 2], v[4 * q + 3], f.z, f.w);
                     }
                   } else {
 #pragma unroll
@@ -1750,11 +1755,11 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   const int planes = act_blk ? 1 : 2;  // e4m3 activation planes (fp8 paths)
   const int bk = fp8 ? BK8 : BK;
   const int64_t N = shared_only ? 0 : T * K;  // routed rows
-  // Token tiles. hi/lo: 64 (128-token tiles, half the weight traffic per FLOP but one TMEM
-  // accumulator buffer for gate/up and a 3-deep ring, measured slower on the Qwen shape).
-  // One plane: 128 once experts average 96+ rows (the MMA then carries 128 useful columns,
-  // the per-stage activation bytes of the hi/lo 64-token tile). DWDP_WIDE_TILES=0|1 forces.
-  bool wide = act_blk && N >= 96LL * E;
+  // Token tiles: 64. 128-token tiles halve the weight traffic per FLOP, but measured slower:
+  // hi/lo keeps one TMEM accumulator buffer for gate/up and a 3-deep ring; one plane needs
+  // sixteen promotion warps whose 96-register budget spills the accumulators.
+  // DWDP_WIDE_TILES=1 selects them for tuning.
+  bool wide = false;
   if (const char* v = getenv("DWDP_WIDE_TILES"))  // tuning override
     wide = (hilo_native || act_blk) && v[0] == '1';
   const int bn = fp8 ? (wide ? 128 : BN8) : BN_MAX;
