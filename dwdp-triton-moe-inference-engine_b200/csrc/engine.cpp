@@ -341,15 +341,29 @@ extern "C" int dwdp_engine_prefetch(dwdp_engine* eng, const int* expert_ids, int
     if (it == eng->experts.end()) return fail(DWDP_ERR_NOT_FOUND, "prefetch: unknown expert " + std::to_string(expert_ids[i]));
     if (it->second.remote) todo.push_back(&it->second);
   }
+  // Copies start at a device-dependent expert so that ranks do not all read the same peer
+  // first. With DWDP_PREFETCH_SLICE_MB = s > 0 every expert moves as s-MiB slices dealt
+  // round-robin over the copy streams (the reference's 2 MiB slices, buffers.cu:94-134);
+  // by default each expert is one copy.
+  static const size_t slice = [] {
+    const char* v = getenv("DWDP_PREFETCH_SLICE_MB");
+    return v != nullptr ? (size_t)atoi(v) << 20 : (size_t)0;
+  }();
   const size_t rot = todo.empty() ? 0 : (size_t)eng->device % todo.size();  // spread peer load across ranks
+  size_t k = 0;  // copy counter: picks the stream
   for (size_t j = 0; j < todo.size(); ++j) {
     const EngineExpert* x = todo[(j + rot) % todo.size()];
-    void* dst = static_cast<char*>(eng->buffers[buffer]) + (size_t)x->slot * eng->slot_bytes;
-    e = cudaMemcpyAsync(dst, x->src, x->bytes, cudaMemcpyDeviceToDevice,
-                        eng->copy_streams[j % eng->copy_streams.size()]);
-    if (e != cudaSuccess) return set_error("cudaMemcpyAsync(prefetch)", e);
+    char* dst = static_cast<char*>(eng->buffers[buffer]) + (size_t)x->slot * eng->slot_bytes;
+    const char* src = static_cast<const char*>(x->src);
+    const size_t step = slice > 0 ? slice : x->bytes;
+    for (size_t off = 0; off < x->bytes; off += step, ++k) {
+      const size_t n = std::min(step, x->bytes - off);
+      e = cudaMemcpyAsync(dst + off, src + off, n, cudaMemcpyDeviceToDevice,
+                          eng->copy_streams[k % eng->copy_streams.size()]);
+      if (e != cudaSuccess) return set_error("cudaMemcpyAsync(prefetch)", e);
+      eng->copies_issued += 1;
+    }
     eng->bytes_copied += x->bytes;
-    eng->copies_issued += 1;
   }
   // join the copy streams into stream 0, then one event marks the buffer ready
   for (size_t i = 1; i < eng->copy_streams.size(); ++i) {
