@@ -84,6 +84,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p],
     ),
     "dwdp_dispatch_noalloc_max_scratch_bytes": (c_size_t, []),
+    "dwdp_route_dispatch_small": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_float, c_int, c_float]
+        + [c_void_p] * 16
+    ),
     "dwdp_quantize_activations_blockwise": (
         c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p]
     ),

@@ -21,6 +21,10 @@ extern "C" size_t dwdp_dispatch_noalloc_max_scratch_bytes(void);
 extern "C" int dwdp_gather_rows_launch(const void*, const int64_t*, int64_t, int, int64_t, void*, int*,
                                        cudaStream_t);
 extern "C" size_t dwdp_dispatch_scratch_bytes(int64_t, int, int);
+extern "C" int dwdp_route_dispatch_small_launch(const void*, const void*, const float*, const void*, int64_t, int,
+                                                int, int, float, int, float, float*, float*, float*, int64_t*,
+                                                float*, float*, int64_t*, int64_t*, int64_t*, int64_t*, int64_t*,
+                                                int64_t*, float*, int*, int*, cudaStream_t);
 extern "C" int dwdp_quantize_activations_launch(const void*, int64_t, const int64_t*, int64_t, int, void*, float*,
                                                 int, int*, cudaStream_t);
 extern "C" int dwdp_schedule_launch(const int64_t*, const int64_t*, int, int, int64_t*, int64_t*,
@@ -182,6 +186,29 @@ extern "C" int dwdp_gather_rows(const void* hidden, const int64_t* token_index, 
   return check(dwdp_gather_rows_launch(hidden, token_index, num_rows, hidden_size, num_tokens, packed, status,
                                        as_stream(stream)),
                "gather_rows");
+}
+
+extern "C" int dwdp_route_dispatch_small(const void* hidden, const void* weight, const float* bias,
+                                         const void* shared_gate_weight, int64_t num_tokens, int hidden_size,
+                                         int num_experts, int top_k, float score_scale, int renormalize, float eps,
+                                         float* logits, float* gate_logit, float* probs, int64_t* topk_idx,
+                                         float* topk_weights, float* shared_gate, int64_t* counts, int64_t* offsets,
+                                         int64_t* perm, int64_t* inv, int64_t* ids, int64_t* tok,
+                                         float* packed_weights, int* ticket, int* status, void* stream) {
+  g_last_error.clear();
+  if (num_tokens <= 0 || top_k <= 0 || num_tokens * top_k > 256 || num_experts <= 0 || num_experts > 256 ||
+      top_k > 16 || top_k > num_experts || hidden_size <= 0 || hidden_size % 8 != 0)
+    return fail(DWDP_ERR_UNSUPPORTED, "route_dispatch_small: needs 0 < T*K <= 256, E <= 256, K <= 16, H %% 8 == 0");
+  if (hidden == nullptr || weight == nullptr || logits == nullptr || topk_idx == nullptr ||
+      topk_weights == nullptr || counts == nullptr || offsets == nullptr || perm == nullptr || inv == nullptr ||
+      ids == nullptr || tok == nullptr || packed_weights == nullptr || ticket == nullptr)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "route_dispatch_small: null pointer");
+  if (renormalize < 0 || renormalize > 2) return fail(DWDP_ERR_INVALID_ARGUMENT, "route_dispatch_small: bad renormalize");
+  return check(dwdp_route_dispatch_small_launch(hidden, weight, bias, shared_gate_weight, num_tokens, hidden_size,
+                                                num_experts, top_k, score_scale, renormalize, eps, logits, gate_logit,
+                                                probs, topk_idx, topk_weights, shared_gate, counts, offsets, perm, inv,
+                                                ids, tok, packed_weights, ticket, status, as_stream(stream)),
+               "route_dispatch_small");
 }
 
 extern "C" int dwdp_quantize_activations_blockwise(const void* src, int64_t src_rows, const int64_t* row_index,

@@ -418,6 +418,158 @@ router_topk_kernel(const float* __restrict__ logits, int T, int E, int K, int re
   topk_warp(logits + (int64_t)t * E, E, K, renorm, eps, t, probs, idx_out, w_out);
 }
 
+
+// ---------------------------------------------------------------------------
+// Decode-sized batches (T * K <= 256, E <= 256, bf16): router AND dispatch in ONE
+// launch. CTA e < E computes expert e's logits for every token (its 2-byte weight row
+// is read once, each of the 256 threads holding 8 elements of it); CTA E computes the
+// shared gate's logit. The last CTA to finish (a ticket counter in device memory,
+// reset by that CTA for the next launch) runs top-k / softmax / renormalisation per
+// token (one warp per token) and the stable counting sort of the T * K assignments:
+// dest[i] = offsets[e_i] + #{j < i : e_j == e_i}, the reference counting scatter
+// (DWDP/dispatcher/kernels/reference.py:163-257). With one expert row per CTA the
+// router's weight stream spreads over E SMs instead of one cluster.
+// ---------------------------------------------------------------------------
+constexpr int kRdThreads = 256;
+constexpr int kRdMaxN = 256;  // assignments
+
+__global__ void __launch_bounds__(kRdThreads)
+route_dispatch_small_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                            const float* __restrict__ bias, const __nv_bfloat16* __restrict__ gate_w, int T,
+                            int H, int E, int K, float score_scale, int renorm, float eps,
+                            float* __restrict__ logits, float* __restrict__ gate_logit, float* __restrict__ probs,
+                            int64_t* __restrict__ idx_out, float* __restrict__ w_out,
+                            float* __restrict__ shared_gate, int64_t* __restrict__ counts,
+                            int64_t* __restrict__ offsets, int64_t* __restrict__ perm, int64_t* __restrict__ inv,
+                            int64_t* __restrict__ ids, int64_t* __restrict__ tok, float* __restrict__ packed_w,
+                            int* __restrict__ ticket, DeviceStatus* st) {
+  griddep_launch();
+  griddep_wait();
+  __shared__ float s_part[kRdThreads / 32][64];
+  __shared__ int s_last;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int row = blockIdx.x;  // expert row, or E for the shared gate
+  const __nv_bfloat16* wr = row < E ? w + (int64_t)row * H : gate_w;
+  // ---- 1. logits of this row for every token (tokens in chunks of 32)
+  for (int t0 = 0; t0 < T; t0 += 32) {
+    const int nt = min(32, T - t0);
+    float part[32];
+#pragma unroll
+    for (int t = 0; t < 32; ++t) part[t] = 0.f;
+    for (int c = tid * 8; c < H; c += kRdThreads * 8) {
+      float wv[8];
+      load8(wr + c, wv);
+#pragma unroll
+      for (int t = 0; t < 32; ++t) {
+        if (t < nt) {
+          float xv[8];
+          load8(x + (int64_t)(t0 + t) * H + c, xv);
+          float s = part[t];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) s = fmaf(xv[q], wv[q], s);
+          part[t] = s;
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < 32; ++t) {
+      if (t < nt) {
+        float v = part[t];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0) s_part[warp][t] = v;
+      }
+    }
+    __syncthreads();
+    if (tid < nt) {
+      float v = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < kRdThreads / 32; ++ww) v += s_part[ww][tid];
+      if (row < E) {
+        if (bias != nullptr) v += bias[row];
+        logits[(int64_t)(t0 + tid) * E + row] = v * score_scale;
+      } else {
+        gate_logit[t0 + tid] = v;
+      }
+    }
+    __syncthreads();
+  }
+  // ---- 2. the last CTA to finish routes and dispatches
+  __threadfence();
+  if (tid == 0) {
+    const int done = atomicAdd(ticket, 1);
+    s_last = done == (int)gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (tid == 0) *ticket = 0;  // ready for the next launch
+  // top-k / softmax / renormalisation, one warp per token, on the logits the other CTAs wrote
+  __shared__ float s_lg[kRdThreads / 32][256];
+  for (int t = warp; t < T; t += kRdThreads / 32) {
+    for (int e = lane; e < E; e += 32) s_lg[warp][e] = __ldcg(logits + (int64_t)t * E + e);
+    __syncwarp();
+    topk_warp(s_lg[warp], E, K, renorm, eps, t, probs, idx_out, w_out);
+    if (lane == 0 && gate_w != nullptr) shared_gate[t] = 1.0f / (1.0f + expf(-__ldcg(gate_logit + t)));
+    __syncwarp();
+  }
+  __syncthreads();
+  // stable counting sort of the N = T * K assignments (token-major order i = t * K + k)
+  __shared__ int s_e[kRdMaxN];
+  __shared__ int s_cnt[256];
+  __shared__ int s_off[257];
+  const int N = T * K;
+  for (int e = tid; e < E; e += kRdThreads) s_cnt[e] = 0;
+  __syncthreads();
+  int my_e = -1;
+  if (tid < N) {
+    my_e = (int)__ldcg(idx_out + tid);
+    s_e[tid] = my_e;
+    if (my_e >= 0 && my_e < E) atomicAdd(&s_cnt[my_e], 1);
+    else record_error(st, DWDP_ERR_DEVICE_BOUNDS, 102, tid);
+  }
+  __syncthreads();
+  if (warp == 0) {  // exclusive scan over E <= 256 experts: 8 per lane, then across lanes
+    int loc[8], sum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int e = lane * 8 + j;
+      loc[j] = e < E ? s_cnt[e] : 0;
+      sum += loc[j];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += v;
+    }
+    int run = incl - sum;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int e = lane * 8 + j;
+      if (e < E) s_off[e] = run;
+      run += loc[j];
+    }
+    if (lane == 31) s_off[E] = incl;
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += kRdThreads) {
+    counts[e] = s_cnt[e];
+    offsets[e] = s_off[e];
+  }
+  if (tid == 0) offsets[E] = s_off[E];
+  if (tid < N && my_e >= 0 && my_e < E) {
+    int rank = 0;
+    for (int j = 0; j < tid; ++j) rank += s_e[j] == my_e;
+    const int d = s_off[my_e] + rank;
+    perm[d] = tid;
+    inv[tid] = d;
+    ids[d] = my_e;
+    tok[d] = tid / K;
+    packed_w[d] = __ldcg(w_out + tid);
+  }
+}
+
 }  // namespace dwdp
 
 using namespace dwdp;
@@ -502,4 +654,26 @@ extern "C" int dwdp_router_launch(const void* hidden, int hidden_dtype, const vo
                      shared_gate_weight ? shared_gate : (float*)nullptr) != cudaSuccess)
     return DWDP_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;
+}
+
+// Router + dispatch in one launch for decode-sized batches (see route_dispatch_small_kernel).
+// Returns DWDP_ERR_UNSUPPORTED outside its range (the caller then launches the two stages).
+extern "C" int dwdp_route_dispatch_small_launch(const void* hidden, const void* weight, const float* bias,
+                                                const void* shared_gate_weight, int64_t T, int H, int E, int K,
+                                                float score_scale, int renorm, float eps, float* logits,
+                                                float* gate_logit, float* probs, int64_t* idx, float* topk_w,
+                                                float* shared_gate, int64_t* counts, int64_t* offsets,
+                                                int64_t* perm, int64_t* inv, int64_t* ids, int64_t* tok,
+                                                float* packed_w, int* ticket, int* status, cudaStream_t stream) {
+  if (T <= 0 || T * K > kRdMaxN || E > 256 || K > 16 || K > E || H % 8 != 0) return DWDP_ERR_UNSUPPORTED;
+  if (shared_gate_weight != nullptr && (gate_logit == nullptr || shared_gate == nullptr))
+    return DWDP_ERR_INVALID_ARGUMENT;
+  const int rows = E + (shared_gate_weight != nullptr ? 1 : 0);
+  return launch_chained(route_dispatch_small_kernel, dim3((unsigned)rows), dim3(kRdThreads), 0, stream, 1u,
+                        (const __nv_bfloat16*)hidden, (const __nv_bfloat16*)weight, bias,
+                        (const __nv_bfloat16*)shared_gate_weight, (int)T, H, E, K, score_scale, renorm, eps, logits,
+                        gate_logit, probs, idx, topk_w, shared_gate, counts, offsets, perm, inv, ids, tok, packed_w,
+                        ticket, reinterpret_cast<DeviceStatus*>(status)) == cudaSuccess
+             ? DWDP_OK
+             : DWDP_ERR_CUDA;
 }

@@ -33,6 +33,8 @@ class LayerWorkspace:
     status: torch.Tensor
     shared_ws: torch.Tensor | None = None        # the shared expert's own launches (side stream)
     side: torch.cuda.Stream | None = None
+    ticket: torch.Tensor | None = None           # one-launch router + dispatch (decode sizes)
+    gate_logit: torch.Tensor | None = None
 
 
 class MoELayer:
@@ -84,6 +86,8 @@ class MoELayer:
         # GEMMs each size their grid to every SM, so concurrent launches queue behind each
         # other, and the cross-stream join breaks the programmatic-launch chain): off by default.
         self.overlap_shared = False
+        # decode sizes (T * top_k <= 256, bf16 router): router and dispatch in one launch
+        self.fused_routing = True
         self.refresh_handles()
 
     def refresh_handles(self) -> None:
@@ -137,6 +141,8 @@ class MoELayer:
             shared_ws=torch.empty(ops.moe_shared_workspace_bytes(T, H, Is), dtype=torch.uint8, device=dev)
             if has_shared else None,
             side=torch.cuda.Stream(device=dev) if has_shared else None,
+            ticket=torch.zeros(1, dtype=torch.int32, device=dev),
+            gate_logit=torch.empty(max(T, 1), dtype=torch.float32, device=dev),
         )
         self._ws[num_tokens] = ws
         return ws
@@ -171,15 +177,21 @@ class MoELayer:
         if overlap:
             self._start_shared(x, ws)
         gate_w = self.shared_gate_weight if self.shared_expert is not None else None
-        ops.router_topk(
-            x, self.router_weight, K, bias=self.router_bias, shared_gate_weight=gate_w,
-            score_scale=self.score_scale, renormalize=self.renormalize, eps=self.eps, out=ws.router,
-        )
-        # the expert kernels read routed rows through packed_token_indices: no gathered copy
-        ops.dispatch(
-            ws.router.topk_indices, ws.router.topk_weights, self.num_experts,
-            scratch=ws.dispatch_scratch, out=ws.dispatch, status=ws.status,
-        )
+        if self.fused_routing and ops.route_dispatch_small_fits(T, K, self.num_experts, x, self.router_weight):
+            # decode sizes: router and dispatch in one launch
+            ops.route_dispatch_small(x, self.router_weight, K, ws.router, ws.dispatch, ws.ticket, ws.gate_logit,
+                                     bias=self.router_bias, shared_gate_weight=gate_w, score_scale=self.score_scale,
+                                     renormalize=self.renormalize, eps=self.eps, status=ws.status)
+        else:
+            ops.router_topk(
+                x, self.router_weight, K, bias=self.router_bias, shared_gate_weight=gate_w,
+                score_scale=self.score_scale, renormalize=self.renormalize, eps=self.eps, out=ws.router,
+            )
+            # the expert kernels read routed rows through packed_token_indices: no gathered copy
+            ops.dispatch(
+                ws.router.topk_indices, ws.router.topk_weights, self.num_experts,
+                scratch=ws.dispatch_scratch, out=ws.dispatch, status=ws.status,
+            )
         self._routed(x, ws, with_shared=not overlap)
         if overlap:
             torch.cuda.current_stream().wait_stream(ws.side)
@@ -223,6 +235,9 @@ class MoELayer:
         planes,] down GEMM, merge."""
         router = 1 if self.router_weight.dtype == torch.bfloat16 and self.num_experts <= 256 else 2
         dispatch = 1 if num_tokens * self.top_k <= 256 else 2
+        if (self.fused_routing and self.router_weight.dtype == torch.bfloat16 and self.num_experts <= 256
+                and 0 < num_tokens * self.top_k <= 256):
+            router, dispatch = 1, 0
         # e4m3 hi/lo: plan(+planes), gate/up, planes, down; e4m3 block128: the gate/up epilogue
         # writes the intermediate's e4m3 rows, so no launch between the GEMMs; bf16: row gather
         fp8 = self.experts.weight_dtype == torch.float8_e4m3fn

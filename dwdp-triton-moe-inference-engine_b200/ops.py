@@ -227,6 +227,45 @@ def quantize_activations_blockwise(
     return q, sc
 
 
+def route_dispatch_small_fits(num_tokens: int, top_k: int, num_experts: int, hidden: torch.Tensor,
+                              weight: torch.Tensor) -> bool:
+    """Whether :func:`route_dispatch_small` covers this call (bf16, 0 < T*K <= 256, E <= 256)."""
+    return (hidden.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and 0 < num_tokens * top_k <= 256
+            and num_experts <= 256 and top_k <= 16 and hidden.shape[-1] % 8 == 0)
+
+
+def route_dispatch_small(hidden: torch.Tensor, weight: torch.Tensor, top_k: int, router: RouterResult,
+                         disp: DispatchResult, ticket: torch.Tensor, gate_logit: torch.Tensor | None = None, *,
+                         bias: torch.Tensor | None = None, shared_gate_weight: torch.Tensor | None = None,
+                         score_scale: float = 1.0, renormalize: int | bool = True, eps: float = 1e-9,
+                         status: torch.Tensor | None = None) -> None:
+    """:func:`router_topk` then :func:`dispatch` (fp32 routing weights, no row gather) in ONE
+    launch for decode-sized batches, into the given result holders. ``ticket`` is one int32 of
+    device memory, zero before the first call (the kernel leaves it at zero)."""
+    _require_cuda(hidden, weight, ticket, bias, shared_gate_weight)
+    H = hidden.shape[-1]
+    x = hidden.reshape(-1, H).contiguous()
+    T = x.shape[0]
+    E = weight.shape[0]
+    if not route_dispatch_small_fits(T, top_k, E, x, weight):
+        raise ValueError("route_dispatch_small needs bf16, 0 < T * K <= 256, E <= 256, K <= 16")
+    if disp.packed_routing_weights.dtype != torch.float32:
+        raise ValueError("route_dispatch_small writes fp32 packed routing weights")
+    gw = shared_gate_weight.reshape(-1).to(weight.dtype).contiguous() if shared_gate_weight is not None else None
+    if gw is not None and (gate_logit is None or router.shared_gate is None):
+        raise ValueError("a shared gate weight needs gate_logit scratch and a shared_gate output")
+    b = None if bias is None else bias.float().contiguous()
+    rc = _lib.load().dwdp_route_dispatch_small(
+        x.data_ptr(), weight.contiguous().data_ptr(), _ptr(b), _ptr(gw), T, H, E, top_k, float(score_scale),
+        int(renormalize), float(eps), router.router_logits.data_ptr(), _ptr(gate_logit),
+        _ptr(router.routing_probabilities), router.topk_indices.data_ptr(), router.topk_weights.data_ptr(),
+        _ptr(router.shared_gate), disp.expert_counts.data_ptr(), disp.expert_offsets.data_ptr(),
+        disp.token_permutation.data_ptr(), disp.inverse_permutation.data_ptr(), disp.packed_expert_ids.data_ptr(),
+        disp.packed_token_indices.data_ptr(), disp.packed_routing_weights.data_ptr(), ticket.data_ptr(),
+        _ptr(status), _stream())
+    _lib.check(rc, "route_dispatch_small")
+
+
 # --------------------------------------------------------------------------- schedule
 @dataclass
 class ScheduleResult:

@@ -154,6 +154,28 @@ int dwdp_quantize_activations_blockwise(const void* src, int64_t src_rows, const
                                         int* status, void* stream);
 
 /* ======================================================================== *
+ * Router + dispatch in ONE launch for decode-sized batches: dwdp_router_topk
+ * followed by dwdp_dispatch (fp32 routing weights, no row gather) with the same
+ * outputs and meaning, for bf16 hidden and weights, 0 < T * K <= 256, E <= 256,
+ * K <= 16. One CTA per expert row (and one for the shared gate) computes that
+ * row's logits for every token; the last CTA to finish routes every token and
+ * sorts the T * K assignments (the reference counting scatter,
+ * DWDP/dispatcher/kernels/reference.py:163-257, after DWDP/router/kernels/fused.py:8-42).
+ *   gate_logit [T] f32 scratch (needed with a shared gate weight);
+ *   ticket: one int32 of device memory, zero before the first call; the kernel
+ *   returns it to zero, so a stream's consecutive calls may share it (calls that
+ *   overlap on the GPU must not).
+ * Outside that range: DWDP_ERR_UNSUPPORTED (use the two stages).
+ * ======================================================================== */
+int dwdp_route_dispatch_small(const void* hidden, const void* weight, const float* bias,
+                              const void* shared_gate_weight, int64_t num_tokens, int hidden_size, int num_experts,
+                              int top_k, float score_scale, int renormalize, float eps, float* logits,
+                              float* gate_logit, float* probs, int64_t* topk_idx, float* topk_weights,
+                              float* shared_gate, int64_t* counts, int64_t* offsets, int64_t* perm, int64_t* inv,
+                              int64_t* ids, int64_t* tok, float* packed_weights, int* ticket, int* status,
+                              void* stream);
+
+/* ======================================================================== *
  * Round-robin schedule over active experts in ascending id
  * (build_round_robin_schedule, round_robin.py:8-80), padded to E entries:
  * rows [0, num_active) hold the reference values, the rest are -1.

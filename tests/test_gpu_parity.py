@@ -466,3 +466,60 @@ def test_moe_experts_repeated_expert_block128(pkg, orc, mode):
     experts = [tuple(t.cpu() for t in layer.experts.dequantized(e)) for e in range(layer.num_experts)]
     ref = orc.moe_forward(x.float(), ids, wts, experts, act_quant="block128")
     assert orc.rel_frobenius(y.cpu(), ref) < FP8_TOL
+
+
+@pytest.mark.parametrize("T,E,K,H,gate,renorm", [(1, 60, 4, 2048, True, 1), (8, 60, 4, 2048, True, 1),
+                                                 (64, 60, 4, 2048, True, 1), (16, 256, 8, 512, False, 1),
+                                                 (5, 8, 2, 256, True, 2), (3, 8, 1, 128, False, 0)])
+def test_route_dispatch_small(pkg, orc, T, E, K, H, gate, renorm):
+    """Router + dispatch in one launch (decode sizes): logits within 1e-5 of the oracle, top-k
+    / weights exactly the oracle's on the kernel's own logits, and every dispatch array
+    bit-exact with the oracle's counting scatter; two calls in a row (the ticket returns to 0)."""
+    g = torch.Generator().manual_seed(T * 31 + E)
+    x = torch.randn(T, H, generator=g).bfloat16()
+    W = (torch.randn(E, H, generator=g) / H**0.5).bfloat16()
+    gw = (torch.randn(H, generator=g) * 0.02).bfloat16() if gate else None
+    bias = (torch.randn(E, generator=g) * 0.1) if not gate else None
+    dev = torch.device(DEV)
+    N = T * K
+    ticket = torch.zeros(1, dtype=torch.int32, device=dev)
+    gl = torch.empty(T, dtype=torch.float32, device=dev)
+    for rep in range(2):
+        r = pkg.ops.RouterResult(
+            router_logits=torch.empty(T, E, device=dev), routing_probabilities=torch.empty(T, K, device=dev),
+            topk_indices=torch.empty(T, K, dtype=torch.int64, device=dev), topk_weights=torch.empty(T, K, device=dev),
+            shared_gate=torch.empty(T, device=dev) if gate else None)
+        i64 = lambda n: torch.full((n,), -7, dtype=torch.int64, device=dev)  # noqa: E731
+        d = pkg.ops.DispatchResult(expert_counts=i64(E), expert_offsets=i64(E + 1), token_permutation=i64(N),
+                                   inverse_permutation=i64(N), packed_expert_ids=i64(N), packed_token_indices=i64(N),
+                                   packed_routing_weights=torch.empty(N, device=dev), packed_hidden=None)
+        st = torch.zeros(4, dtype=torch.int32, device=dev)
+        pkg.ops.route_dispatch_small(x.to(dev), W.to(dev), K, r, d, ticket, gl,
+                                     bias=bias.to(dev) if bias is not None else None,
+                                     shared_gate_weight=gw.to(dev) if gw is not None else None,
+                                     renormalize=renorm, status=st)
+        torch.cuda.synchronize()
+        assert int(ticket.item()) == 0 and st.cpu().tolist()[0] == 0
+        lg = r.router_logits.cpu()
+        torch.testing.assert_close(lg, orc.router_logits(x, W, bias), rtol=1e-5, atol=1e-5)
+        if renorm != 2:
+            probs, idx, wts = orc.topk_routing(lg, K, renormalize=bool(renorm))
+            assert torch.equal(r.topk_indices.cpu(), idx)
+            torch.testing.assert_close(r.topk_weights.cpu(), wts, rtol=1e-6, atol=1e-6)
+        # the two-stage path on the same logits gives the same routing
+        ref = pkg.ops.router_topk(x.to(dev), W.to(dev), K, bias=bias.to(dev) if bias is not None else None,
+                                  shared_gate_weight=gw.to(dev) if gw is not None else None, renormalize=renorm)
+        same = (torch.sort(ref.topk_indices.cpu(), 1).values == torch.sort(r.topk_indices.cpu(), 1).values).all(1)
+        assert same.float().mean() > 0.9
+        if gate:
+            torch.testing.assert_close(r.shared_gate.cpu(), torch.sigmoid(x.float() @ gw.float()), rtol=1e-5, atol=1e-6)
+        plan = orc.counting_scatter(r.topk_indices.reshape(-1).cpu().numpy(),
+                                    r.topk_weights.reshape(-1).cpu().numpy(), E, K)
+        assert np.array_equal(d.expert_counts.cpu().numpy(), plan["counts"])
+        assert np.array_equal(d.expert_offsets.cpu().numpy(), plan["offsets"])
+        assert np.array_equal(d.token_permutation.cpu().numpy(), plan["perm"])
+        assert np.array_equal(d.inverse_permutation.cpu().numpy(), plan["inv"])
+        assert np.array_equal(d.packed_expert_ids.cpu().numpy(), plan["ids"])
+        assert np.array_equal(d.packed_token_indices.cpu().numpy(), plan["tok"])
+        assert np.array_equal(d.packed_routing_weights.cpu().numpy().view(np.uint32),
+                              plan["weights"].astype(np.float32).view(np.uint32))
