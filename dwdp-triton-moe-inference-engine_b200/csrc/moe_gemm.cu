@@ -589,7 +589,11 @@ struct CfgP {
   // tiles, so each thread has 168 registers and the promoted accumulators never spill: with
   // sixteen warps the 96-register budget spilled them and every K block paid local-memory
   // round trips), 16 with hi/lo planes (two TMEM columns per token).
+#ifdef DWDP_TOKW16
+  static constexpr int TOKW = 16;
+#else
   static constexpr int TOKW = PLANES == 1 ? 32 : 16;
+#endif
   static constexpr int TCOL = PLANES * TOKW;               // TMEM columns per warp and matrix
   static constexpr int CHUNKS = BNT / TOKW;
   static constexpr int EPI_WARPS = 4 * CHUNKS;
@@ -890,32 +894,43 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
 #endif
             tmem_ld_wait();
 #pragma unroll
-            for (int m = 0; m < C::NMAT; ++m) {
-              if (m < nm) {
-                if constexpr (PLANES == 1) {
-                  const float4* f4 = reinterpret_cast<const float4*>(rs);
-                  if (block_w) {
+            if constexpr (PLANES == 1) {
+              // each float4 of token factors serves every matrix
+              const float4* f4 = reinterpret_cast<const float4*>(rs);
+              if (block_w) {
 #pragma unroll
-                    for (int q = 0; q < C::TOKW / 4; ++q) {
-                      float4 f = f4[q];
+                for (int q = 0; q < C::TOKW / 4; ++q) {
+                  const float4 f = f4[q];
+#pragma unroll
+                  for (int m = 0; m < C::NMAT; ++m) {
+                    if (m < nm) {
                       const float w = sw_cur[m];
                       fma_pair(acc[m][4 * q], acc[m][4 * q + 1], v[m][4 * q], v[m][4 * q + 1], f.x * w, f.y * w);
-                      fma_pair(acc[m][4 * q + 2], acc[m][4 * q + 3], v[m][4 * q + 2], v[m][4 * q + 3], f.z * w, f.w * w);
+                      fma_pair(acc[m][4 * q + 2], acc[m][4 * q + 3], v[m][4 * q + 2], v[m][4 * q + 3], f.z * w,
+                               f.w * w);
                     }
-                  } else {
+                  }
+                }
+              } else {
 #pragma unroll
-                    for (int q = 0; q < C::TOKW / 4; ++q) {
-                      const float4 f = f4[q];
+                for (int q = 0; q < C::TOKW / 4; ++q) {
+                  const float4 f = f4[q];
+#pragma unroll
+                  for (int m = 0; m < C::NMAT; ++m) {
+                    if (m < nm) {
                       fma_pair(acc[m][4 * q], acc[m][4 * q + 1], v[m][4 * q], v[m][4 * q + 1], f.x, f.y);
                       fma_pair(acc[m][4 * q + 2], acc[m][4 * q + 3], v[m][4 * q + 2], v[m][4 * q + 3], f.z, f.w);
                     }
                   }
-                } else {
+                }
+              }
+            } else {
+#pragma unroll
+              for (int m = 0; m < C::NMAT; ++m)
+                if (m < nm)
 #pragma unroll
                   for (int j = 0; j < C::TOKW; ++j)
                     acc[m][j] = fmaf(v[m][2 * j] + v[m][2 * j + 1] * (1.0f / kLoPlaneGain), sw_cur[m], acc[m][j]);
-                }
-              }
             }
           } else {
             // more columns than registers allow at once: 16 TMEM columns at a time
