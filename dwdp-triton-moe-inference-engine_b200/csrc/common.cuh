@@ -102,6 +102,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   return false;
 }
 
+// As mbar_wait, backing off with a short sleep between polls: for the many warps that wait
+// on one barrier (epilogue warps), so that their polling does not take issue slots from the
+// warps doing the work.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                  DeviceStatus* st, int where) {
+  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023u) == 1023u && *abort_flag) return false;
+    __nanosleep(64);
+  }
+  *abort_flag = 1;
+  record_error(st, DWDP_ERR_DEVICE_TIMEOUT, where, (int)parity);
+  return false;
+}
+
 // ---------------------------------------------------------------------------
 // Bulk (non-tensor) and tensor (TMA) copies global -> shared::cta, completion
 // tracked by an mbarrier transaction count. No multicast anywhere.

@@ -877,7 +877,11 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
         }
         __syncwarp();
         RP_ADD(6)
+#ifdef DWDP_EPI_SPIN
         if (!mbar_wait(&acc_full[slot], (kc / C::NSLOT) & 1, &s_abort, st, 44 + 8 * MODE)) { ok = false; break; }
+#else
+        if (!mbar_wait_backoff(&acc_full[slot], (kc / C::NSLOT) & 1, &s_abort, st, 44 + 8 * MODE)) { ok = false; break; }
+#endif
         RP_ADD(5)
         tc_fence_after();
         if (ntk > 0) {
