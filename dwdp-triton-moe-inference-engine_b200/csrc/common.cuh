@@ -102,15 +102,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   return false;
 }
 
-// As mbar_wait, backing off with a short sleep between polls: for the many warps that wait
-// on one barrier (epilogue warps), so that their polling does not take issue slots from the
-// warps doing the work.
+// try_wait with a suspend-time hint: the thread is parked by the hardware until the phase
+// completes or about 20 us pass, instead of re-polling (polling threads take issue slots
+// from the warps doing the work).
+constexpr uint32_t kSuspendNs = 20000;
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait built on the suspending try_wait: at most 2^17 tries of <= 20 us (a few
+// seconds), the abort flag checked every 64 tries.
 __device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                                   DeviceStatus* st, int where) {
-  for (uint32_t i = 0; i < kMaxPolls; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 1023u) == 1023u && *abort_flag) return false;
-    __nanosleep(64);
+  for (uint32_t i = 0; i < (1u << 17); ++i) {
+    if (mbar_try_wait_suspend(bar, parity)) return true;
+    if ((i & 63u) == 63u && *abort_flag) return false;
   }
   *abort_flag = 1;
   record_error(st, DWDP_ERR_DEVICE_TIMEOUT, where, (int)parity);

@@ -643,6 +643,13 @@ struct CfgP {
 #define RP_END(total, lo, hi)
 #endif
 
+// The f8p kernel's pipeline waits park the waiting thread in hardware (DWDP_SPIN_WAITS: poll).
+#ifdef DWDP_SPIN_WAITS
+#define MBAR_WAIT_P mbar_wait
+#else
+#define MBAR_WAIT_P mbar_wait_backoff
+#endif
+
 __device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
 // (a0, a1) += (v0, v1) * (f0, f1) as one packed fp32x2 FMA (round to nearest).
@@ -760,7 +767,7 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
         const int nm = min(wi.nmat, C::NMAT);
         for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
           const int s = it % C::S;
-          if (!RP_TIMED(0, mbar_wait(&ld_empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 41 + 8 * MODE))) break;
+          if (!RP_TIMED(0, MBAR_WAIT_P(&ld_empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 41 + 8 * MODE))) break;
           mbar_arrive_expect_tx(&ld_full[s], (uint32_t)(nm * kW8TileBytes) + b_bytes);
           for (int m = 0; m < nm; ++m)
             bulk_g2s(sW + s * C::W_STAGE_BYTES + m * kW8TileBytes,
@@ -786,8 +793,8 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
         for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it, ++kc) {
           const int s = it % C::S;
           const int slot = kc % C::NSLOT;
-          if (!RP_TIMED(2, mbar_wait(&acc_empty[slot], ((kc / C::NSLOT) & 1) ^ 1, &s_abort, st, 42 + 8 * MODE))) { ok = false; break; }
-          if (!RP_TIMED(3, mbar_wait(&ld_full[s], (it / C::S) & 1, &s_abort, st, 43 + 8 * MODE))) { ok = false; break; }
+          if (!RP_TIMED(2, MBAR_WAIT_P(&acc_empty[slot], ((kc / C::NSLOT) & 1) ^ 1, &s_abort, st, 42 + 8 * MODE))) { ok = false; break; }
+          if (!RP_TIMED(3, MBAR_WAIT_P(&ld_full[s], (it / C::S) & 1, &s_abort, st, 43 + 8 * MODE))) { ok = false; break; }
           tc_fence_after();
           // a K step of 32 e4m3 (32 bytes) is +2 in the encoded start address
           const uint64_t b_desc0 = smem_desc_sw128(smem_u32(sB + s * C::B_TILE));
@@ -877,11 +884,7 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
         }
         __syncwarp();
         RP_ADD(6)
-#ifdef DWDP_EPI_SPIN
-        if (!mbar_wait(&acc_full[slot], (kc / C::NSLOT) & 1, &s_abort, st, 44 + 8 * MODE)) { ok = false; break; }
-#else
-        if (!mbar_wait_backoff(&acc_full[slot], (kc / C::NSLOT) & 1, &s_abort, st, 44 + 8 * MODE)) { ok = false; break; }
-#endif
+        if (!MBAR_WAIT_P(&acc_full[slot], (kc / C::NSLOT) & 1, &s_abort, st, 44 + 8 * MODE)) { ok = false; break; }
         RP_ADD(5)
         tc_fence_after();
         if (ntk > 0) {
