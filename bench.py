@@ -39,10 +39,13 @@ sys.path.insert(0, str(ROOT))
 METRIC = "MoE-layer tokens/s (Qwen1.5-MoE-A2.7B shape)"
 QWEN = dict(H=2048, E=60, I=1408, K=4, Is=5632)
 DECODE_SWEEP = [1, 8, 32, 64]
-# The FP8 computation bench.py times: activations quantised to one e4m3 plane per
-# (token, 128 channels) and the SwiGLU intermediate re-quantised the same way, the
-# reference's FP8 executor math (DWDP/executor/fp8.py:86-115, triton_tma.py:185-207).
-ACTIVATION_QUANT = "block128"
+# The headline's activation mode: each activation row as two e4m3 planes (hi + lo/16, about
+# bf16 accuracy), the layer's fastest mode. The reference's FP8 executor scheme (one e4m3
+# plane per (token, 128 channels), the SwiGLU intermediate re-quantised the same way:
+# DWDP/executor/fp8.py:86-115, triton_tma.py:185-207) is timed beside it at the same T
+# (`modes` in the JSON line).
+ACTIVATION_QUANT = "hilo"
+SIDE_MODES = ["block128"]
 
 
 def _peaks() -> dict:
@@ -786,7 +789,9 @@ def main() -> None:
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=256)
     ap.add_argument("--workload", default="moe_layers",
-                    choices=["moe_layers", "decode_step", "attention", "mixtral", "deepseek"])
+                    choices=["moe_layers", "decode_step", "attention", "mixtral", "deepseek", "layer"])
+    ap.add_argument("--activation", default=None, choices=["hilo", "block128"],
+                    help="activation mode of --workload layer (default: the headline's)")
     ap.add_argument("--batch", default="1,8,64", help="decode_step batch sizes")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -802,7 +807,9 @@ def main() -> None:
               "weights": "fp8 e4m3, per-output-channel fp32 scales",
               "activations": "bf16 in and out; inside the expert GEMMs one e4m3 plane per (token, 128 channels) "
                              "with fp32 scales, SwiGLU intermediate re-quantised the same way (the reference's "
-                             "FP8 executor scheme)" if ACTIVATION_QUANT == "block128" else "bf16 (hi/lo e4m3 planes)",
+                             "FP8 executor scheme)" if ACTIVATION_QUANT == "block128" else
+                             "bf16 in and out; inside the expert GEMMs each activation row is two e4m3 planes "
+                             "(hi, lo = residual x 16) with one fp32 scale per row, SwiGLU intermediate the same",
               "l2": "flushed (256 MB write + 256 MB read) before every timed step; weights 554 MB/layer > L2",
               "parallelism": (f"dwdp{world}: tokens data-parallel, routed experts sharded over {world} GPUs, "
                               "next layer's remote experts prefetched over NVLink during the current layer")
@@ -844,6 +851,21 @@ def main() -> None:
         res = attention_bench(pkg, device, [int(b) for b in args.batch.split(",")], args.steps, args.warmup, flush)
         print(json.dumps({"metric": "paged attention HBM GB/s", "unit": "GB/s", "steps": args.steps,
                           "warmup": args.warmup, **res}), flush=True)
+        return
+    if args.workload == "layer":
+        # one Qwen-shaped layer, `warmup` untimed forwards then `steps` more: the small, fixed
+        # launch sequence the ncu captures under profiles/ are taken on
+        lay = make_qwen_layer(pkg, device, activation_quant=args.activation or ACTIVATION_QUANT)
+        x = make_inputs(T, device, 7)
+        for _ in range(args.warmup + args.steps):
+            lay.forward(x)
+        torch.cuda.synchronize()
+        st = lay.read_status(T)
+        print(json.dumps({"workload": "layer", "T": T, "activation": lay.activation_quant,
+                          "launches_per_forward": lay.kernel_launches(T), "forwards": args.warmup + args.steps,
+                          "status": list(st)}), flush=True)
+        if st[0] != 0:
+            raise SystemExit(f"device status {st}")
         return
     if args.workload in SHAPES:
         res = shape_bench(pkg, device, args.workload, args.steps, args.warmup, flush)
@@ -892,9 +914,28 @@ def main() -> None:
             "peak_source": peaks["fp8_source"] + "; achieved counts useful FLOPs "
                            "(2*T*K*3*H*I + 2*T*3*H*Is) over the CUDA-event time of the expert launches",
             "executed_tflops": (2 if hilo else 1) * ach,
+            "executed_frac": (2 if hilo else 1) * ach / peaks["fp8_tflops"],
             "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of the expert launches of one "
                             "layer at this T from one ncu capture (profiles/)",
             "layer_us": statistics.mean(pt["layer_ms"]) * 1e3, "experts_us": exp_ms * 1e3}
+
+    # the other activation modes, same weights' shape and T, one layer (single-layer graph)
+    modes = {}
+    if not args.no_sweep and world == 1:
+        for mode in SIDE_MODES:
+            lay_m = make_qwen_layer(pkg, device, activation_quant=mode)
+            pm = run_point(pkg, lay_m, T, args.steps, args.warmup, flush, device, rank, world)
+            em, lm = statistics.mean(pm["experts_ms"]), statistics.mean(pm["layer_ms"])
+            a_m = pm["flops"] / (em / 1e3) / 1e12
+            modes[mode] = {"T": T, "layer_us": lm * 1e3, "tokens_per_s_one_layer": T / (lm / 1e3),
+                           "experts_us": em * 1e3, "achieved_tflops": a_m,
+                           "frac_of_fp8_peak": a_m / peaks["fp8_tflops"],
+                           "traffic": TRAFFIC_PER_LAYER.get((T, mode))}
+            del lay_m
+        modes[ACTIVATION_QUANT] = {"T": T, "layer_us": roof["layer_us"],
+                                   "tokens_per_s_one_layer": T / (roof["layer_us"] / 1e6),
+                                   "experts_us": roof["experts_us"], "achieved_tflops": ach,
+                                   "frac_of_fp8_peak": roof["frac"], "traffic": roof["traffic"]}
 
     sweep = []
     if not args.no_sweep and world == 1:
@@ -945,7 +986,7 @@ def main() -> None:
                     "note": "every step copies its input from pinned host memory and its output back; the "
                             "copies of neighbouring steps overlap compute (double-buffered, two copy streams); "
                             "no L2 flush: each step streams 2.2 GB of weights"},
-            "gpu_launches": sum(l.kernel_launches(T) for l in stack.layers) * args.steps, "nvlink": nvlink, "sweep": sweep,
+            "gpu_launches": sum(l.kernel_launches(T) for l in stack.layers) * args.steps, "nvlink": nvlink, "modes": modes, "sweep": sweep,
         }), flush=True)
     if world > 1:
         torch.distributed.barrier()

@@ -610,11 +610,14 @@ struct CfgP {
   static constexpr bool ALL_AT_ONCE = NMAT * (TOKW + TCOL) + 40 <= MAXREG;
   static constexpr bool QOUT = MODE == 0 && PLANES == 1;   // gate/up writes e4m3 rows + scales
   static constexpr int STAGING = QOUT ? BNT * BM : 0;      // e4m3 [tokens][128 features]
-  // per-warp ring of K-block scales (RING blocks of [32 token scales | NMAT weight-block scales]),
-  // filled DIST blocks ahead with asynchronous copies
-  // (a slot is 36 floats so that every slot starts on a 16-byte boundary: the token scales
-  // are read as float4)
-  static constexpr int RING = 4, DIST = 3, RSTRIDE = 36;
+  // per-warp ring of K-block scales, filled DIST blocks ahead with asynchronous copies. A slot
+  // holds [32 token scales | 4: NMAT weight-block scales | NMAT x 32 promotion factors]: with
+  // one activation plane and block-scaled weights each lane writes its token's factor
+  // s_x[t] * s_w[m] once per K block, so the promotion is one FMA per element (every slot
+  // starts on a 16-byte boundary: the factors are read as float4).
+  static constexpr int FAC = 36;                            // offset of the factors in a slot
+  static constexpr int RING = 4, DIST = 3, RSTRIDE = PLANES == 1 ? FAC + NMAT * 32 : 36;
+  static_assert(RSTRIDE % 4 == 0, "ring slots must stay 16-byte aligned");
   static_assert(NMAT <= RSTRIDE - 32, "weight-block scales must fit the slot padding");
   static constexpr int SCL = EPI_WARPS * RING * RSTRIDE * 4;
   static constexpr int RED = QOUT ? 4 * BNT * 4 : 0;       // per-quadrant token amax
@@ -664,12 +667,12 @@ __device__ __forceinline__ void ffma2(float& a0, float& a1, float v0, float v1, 
       : "f"(v0), "f"(v1), "f"(f0), "f"(f1));
 }
 
-// acc += v * f for a pair of tokens: one packed fp32x2 FMA in the DWDP_FFMA2 build, two
-// scalar FMAs otherwise (the packing moves can cost more than the FMA they save).
+// acc += v * f for a pair of tokens: one packed fp32x2 FMA (measured 4 % faster on the
+// gate/up promotion than two scalar FMAs); DWDP_SCALAR_FMA builds the scalar pair.
 __device__ __forceinline__ void fma_pair(float& a0, float& a1, float v0, float v1, float f0, float f1) {
 #if defined(DWDP_DIAG_NO_FMA)
   a0 += v0; (void)a1; (void)v1; (void)f0; (void)f1;
-#elif defined(DWDP_FFMA2)
+#elif !defined(DWDP_SCALAR_FMA)
   ffma2(a0, a1, v0, v1, f0, f1);
 #else
   a0 = fmaf(v0, f0, a0);
@@ -881,6 +884,16 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
           __syncwarp();                  // ... and every lane's are visible
 #pragma unroll
           for (int m = 0; m < C::NMAT; ++m) sw_cur[m] = (block_w && m < nm) ? rs[32 + m] : 1.0f;
+          if constexpr (PLANES == 1) {
+            if (block_w) {
+              // lane t: the promotion factors of token t0 + t for every matrix
+              float* fw = my_scl + (kb % C::RING) * C::RSTRIDE + C::FAC;
+              const float sx = rs[lane];
+#pragma unroll
+              for (int m = 0; m < C::NMAT; ++m) fw[m * 32 + lane] = sx * sw_cur[m];
+              __syncwarp();
+            }
+          }
         }
         __syncwarp();
         RP_ADD(6)
@@ -902,19 +915,18 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
             tmem_ld_wait();
 #pragma unroll
             if constexpr (PLANES == 1) {
-              // each float4 of token factors serves every matrix
+              // each float4 of token scales serves every matrix
               const float4* f4 = reinterpret_cast<const float4*>(rs);
               if (block_w) {
 #pragma unroll
-                for (int q = 0; q < C::TOKW / 4; ++q) {
-                  const float4 f = f4[q];
+                for (int m = 0; m < C::NMAT; ++m) {
+                  if (m < nm) {
+                    const float4* fm = reinterpret_cast<const float4*>(rs + C::FAC + m * 32);
 #pragma unroll
-                  for (int m = 0; m < C::NMAT; ++m) {
-                    if (m < nm) {
-                      const float w = sw_cur[m];
-                      fma_pair(acc[m][4 * q], acc[m][4 * q + 1], v[m][4 * q], v[m][4 * q + 1], f.x * w, f.y * w);
-                      fma_pair(acc[m][4 * q + 2], acc[m][4 * q + 3], v[m][4 * q + 2], v[m][4 * q + 3], f.z * w,
-                               f.w * w);
+                    for (int q = 0; q < C::TOKW / 4; ++q) {
+                      const float4 f = fm[q];
+                      fma_pair(acc[m][4 * q], acc[m][4 * q + 1], v[m][4 * q], v[m][4 * q + 1], f.x, f.y);
+                      fma_pair(acc[m][4 * q + 2], acc[m][4 * q + 3], v[m][4 * q + 2], v[m][4 * q + 3], f.z, f.w);
                     }
                   }
                 }
@@ -955,12 +967,11 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
 #endif
                   tmem_ld_wait();
                   if constexpr (PLANES == 1) {
-                    const float4* f4 = reinterpret_cast<const float4*>(rs + 16 * hf);
-                    const float w = block_w ? sw_cur[m] : 1.0f;
+                    const float4* f4 =
+                        reinterpret_cast<const float4*>(rs + (block_w ? C::FAC + m * 32 : 0) + 16 * hf);
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
-                      float4 f = f4[q];
-                      if (block_w) f = make_float4(f.x * w, f.y * w, f.z * w, f.w * w);
+                      const float4 f = f4[q];
                       const int j = 16 * hf + 4 * q;
                       fma_pair(acc[m][j], acc[m][j + 1], v[4 * q], v[4 * q + 1], f.x, f.y);
                       fma_pair(acc[m][j + 2], acc[m][j + 3], v[4 * q + 2], v[4 * q + 3], f.z, f.w);
