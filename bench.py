@@ -449,11 +449,14 @@ class LayerStack:
         if self.sharded:
             self.layers[0].experts.prefetch(0)
 
-    def step(self, x: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    def step(self, x: torch.Tensor | None = None, out: torch.Tensor | None = None,
+             prefetch: bool = True) -> torch.Tensor:
+        """L layers; with `prefetch` (the DWDP step) layer l+1's remote experts are copied
+        while layer l computes. prefetch=False reads whatever staging holds (compute alone)."""
         x = self.x0 if x is None else x
         L = len(self.layers)
         for l, lay in enumerate(self.layers):
-            if self.sharded:
+            if self.sharded and prefetch:
                 self.layers[(l + 1) % L].experts.prefetch(0)  # overlaps layer l's kernels
                 lay.experts.wait(0)
             dst = out if (out is not None and l == L - 1) else self.outs[l % 2]
@@ -466,6 +469,47 @@ class LayerStack:
 
 
 # ----------------------------------------------------------------------------- DWDP transfer comparison
+def _timed_max(fn, n: int, device) -> float:
+    """ms per call of fn on the device (CUDA events around n calls after two warm-up calls,
+    barrier before), max over ranks."""
+    import torch.distributed as dist
+
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(n):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) / n], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def step_breakdown(stack, steps: int, device) -> dict:
+    """Per-N anatomy of a DWDP step (max over ranks): the L layers' prefetch copies alone,
+    the L layers' compute alone (staging already filled), and both overlapped (the step)."""
+    n = max(3, min(steps, 10))
+
+    def copies():
+        for lay in stack.layers:
+            lay.experts.prefetch(0)
+        for lay in stack.layers:
+            lay.experts.wait(0)
+
+    copies_ms = _timed_max(copies, n, device)
+    compute_ms = _timed_max(lambda: stack.step(prefetch=False), n, device)
+    both_ms = _timed_max(stack.step, n, device)
+    rb = stack.remote_bytes_per_step()
+    return {"copies_alone_ms": copies_ms, "compute_alone_ms": compute_ms, "overlapped_ms": both_ms,
+            "copies_alone_gbs": rb / (copies_ms / 1e3) / 1e9,
+            "hidden_fraction_of_copies": max(0.0, min(1.0, (compute_ms + copies_ms - both_ms) / copies_ms)),
+            "slowdown_of_compute": both_ms / compute_ms - 1.0}
+
+
 def transfer_comparison(store, world: int, steps: int, device) -> dict:
     """One layer's remote experts moved two ways, nothing else running, max over ranks:
     the engine's peer copies into staging (the DWDP path) and an NCCL all-gather of
@@ -496,6 +540,13 @@ def transfer_comparison(store, world: int, steps: int, device) -> dict:
         store.wait(0)
 
     p2p_ms = timed(p2p, n)
+    # the same copies by SMs (one copy kernel, peer loads, local stores) instead of copy engines
+    sm = {}
+    for ctas in (148, 32):
+        store.engine.set_copy_mode("sm", ctas)
+        ms = timed(p2p, n)
+        sm[f"ctas_{ctas}"] = {"ms_per_layer": ms, "gbs": recv / (ms / 1e3) / 1e9}
+    store.engine.set_copy_mode("engine")
     shard = store.local.slabs.view(-1)
     per_rank = -(-store.num_experts // world) * store.slab_bytes  # every rank's shard padded to ceil(E/G)
     src = torch.zeros(per_rank, dtype=torch.uint8, device=device)
@@ -517,6 +568,7 @@ def transfer_comparison(store, world: int, steps: int, device) -> dict:
     except Exception as exc:  # the model is a report, never a reason to lose the bench line
         model = {"error": repr(exc)}
     return {"cost_model": model, "p2p_prefetch_ms_per_layer": p2p_ms, "p2p_prefetch_gbs": recv / (p2p_ms / 1e3) / 1e9,
+            "sm_copy": sm,
             "nccl_all_gather_ms_per_layer": ag_ms, "nccl_all_gather_gbs": ag_recv / (ag_ms / 1e3) / 1e9,
             "bytes_received_per_gpu": {"p2p": recv, "nccl": ag_recv}}
 
@@ -966,6 +1018,7 @@ def main() -> None:
                   "prefetch_gbs_lower_bound": rb / (ms_per_step / 1e3) / 1e9,
                   "note": "copies overlap compute; GB/s is remote bytes / step time (a lower bound on link rate)"}
         nvlink.update(transfer_comparison(stack.layers[0].experts, world, args.steps, device))
+        nvlink["step_breakdown"] = step_breakdown(stack, args.steps, device)
         nvlink["ep_decode"] = ep_decode_comparison(pkg, stack.layers[0], world, rank, args.steps, device)
 
     cb = None

@@ -164,6 +164,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dwdp_engine_synchronize": (c_int, [c_void_p]),
     "dwdp_engine_stats": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_ulonglong),
                                   ctypes.POINTER(ctypes.c_ulonglong), ctypes.POINTER(c_void_p)]),
+    "dwdp_engine_set_copy_mode": (c_int, [c_void_p, c_int, c_int]),
+    "dwdp_peer_copy_sm": (c_int, [c_void_p, c_int, c_void_p]),
     "dwdp_policy_decide": (c_int, [c_int, c_int, c_int, c_int, c_int]),
     "dwdp_sched_create": (c_int, [ctypes.POINTER(c_void_p)]),
     "dwdp_sched_destroy": (c_int, [c_void_p]),

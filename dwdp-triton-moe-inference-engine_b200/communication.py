@@ -321,6 +321,15 @@ class CommunicationEngine:
         _chk(_lib.load().dwdp_engine_is_remote(self._eng(), expert_id, ctypes.byref(out)), "is_remote")
         return bool(out.value)
 
+    def set_copy_mode(self, mode: str = "engine", ctas: int = 148) -> None:
+        """How prefetches move bytes: ``"engine"`` (cudaMemcpyAsync on the copy engines, the
+        default and the reference's mechanism) or ``"sm"`` (one copy kernel of ``ctas`` CTAs
+        loading the peer's slabs: faster alone, but it competes with the GEMMs for SMs)."""
+        code = {"engine": 0, "sm": 1}.get(mode)
+        if code is None:
+            raise ValueError(f"copy mode must be 'engine' or 'sm', got {mode!r}")
+        _chk(_lib.load().dwdp_engine_set_copy_mode(self._eng(), code, int(ctas)), "set_copy_mode")
+
     def release(self, expert_id: int) -> None:
         _chk(_lib.load().dwdp_engine_release(self._eng(), expert_id), "release")
 

@@ -77,6 +77,8 @@ struct dwdp_engine {
   int next_slot = 0;
   unsigned long long bytes_copied = 0;
   unsigned long long copies_issued = 0;
+  int copy_mode = DWDP_COPY_ENGINE;  // DWDP_COPY_SM: one SM copy kernel per prefetch
+  int copy_ctas = 148;
   std::mutex mu;
 };
 
@@ -350,6 +352,27 @@ extern "C" int dwdp_engine_prefetch(dwdp_engine* eng, const int* expert_ids, int
     return v != nullptr ? (size_t)atoi(v) << 20 : (size_t)0;
   }();
   const size_t rot = todo.empty() ? 0 : (size_t)eng->device % todo.size();  // spread peer load across ranks
+  if (eng->copy_mode == DWDP_COPY_SM) {
+    // SM copies: the listed experts in kernels of up to DWDP_COPY_LIST_MAX copies on stream 0
+    dwdp_copy_list list;
+    list.n = 0;
+    for (size_t j = 0; j <= todo.size(); ++j) {
+      if (list.n == DWDP_COPY_LIST_MAX || (j == todo.size() && list.n > 0)) {
+        const int rc = dwdp_peer_copy_sm(&list, eng->copy_ctas, eng->copy_streams[0]);
+        if (rc != DWDP_OK) return fail(rc, "prefetch: SM copy launch failed");
+        eng->copies_issued += 1;
+        list.n = 0;
+      }
+      if (j == todo.size()) break;
+      const EngineExpert* x = todo[(j + rot) % todo.size()];
+      list.src[list.n] = x->src;
+      list.dst[list.n] = static_cast<char*>(eng->buffers[buffer]) + (size_t)x->slot * eng->slot_bytes;
+      list.bytes[list.n] = x->bytes;
+      ++list.n;
+      eng->bytes_copied += x->bytes;
+    }
+    todo.clear();
+  }
   size_t k = 0;  // copy counter: picks the stream
   for (size_t j = 0; j < todo.size(); ++j) {
     const EngineExpert* x = todo[(j + rot) % todo.size()];
@@ -373,6 +396,15 @@ extern "C" int dwdp_engine_prefetch(dwdp_engine* eng, const int* expert_ids, int
   e = cudaEventRecord(eng->ready[buffer], eng->copy_streams[0]);
   if (e != cudaSuccess) return set_error("cudaEventRecord", e);
   eng->buffer_valid[buffer] = 1;
+  return DWDP_OK;
+}
+
+extern "C" int dwdp_engine_set_copy_mode(dwdp_engine* eng, int mode, int ctas) {
+  if (eng == nullptr || (mode != DWDP_COPY_ENGINE && mode != DWDP_COPY_SM) || ctas <= 0)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "set_copy_mode: bad argument");
+  std::lock_guard<std::mutex> lock(eng->mu);
+  eng->copy_mode = mode;
+  eng->copy_ctas = ctas;
   return DWDP_OK;
 }
 

@@ -407,6 +407,25 @@ int dwdp_engine_synchronize(dwdp_engine* engine);
 int dwdp_engine_stats(dwdp_engine* engine, unsigned long long* bytes_copied,
                       unsigned long long* copies_issued, void** copy_stream);
 
+/* Copy mechanism of dwdp_engine_prefetch: DWDP_COPY_ENGINE (default) issues one
+ * cudaMemcpyAsync per expert (or per slice) on the engine's copy streams, as the
+ * reference's buffers.cu did; DWDP_COPY_SM launches dwdp_peer_copy_sm with `ctas`
+ * CTAs on copy stream 0 (SMs load the peer's slab and store it locally). */
+#define DWDP_COPY_ENGINE 0
+#define DWDP_COPY_SM 1
+int dwdp_engine_set_copy_mode(dwdp_engine* engine, int mode, int ctas);
+
+/* Up to DWDP_COPY_LIST_MAX copies for one dwdp_peer_copy_sm launch (passed by value
+ * as a kernel parameter). Every pointer 16-byte aligned. */
+#define DWDP_COPY_LIST_MAX 64
+typedef struct dwdp_copy_list {
+  int n;
+  const void* src[DWDP_COPY_LIST_MAX];
+  void* dst[DWDP_COPY_LIST_MAX];
+  size_t bytes[DWDP_COPY_LIST_MAX];
+} dwdp_copy_list;
+int dwdp_peer_copy_sm(const dwdp_copy_list* list, int ctas, void* stream);
+
 /* CommunicationPolicy.decide (communication_policy.cpp:5-17); CommunicationPath codes. */
 #define DWDP_PATH_LOCAL 0
 #define DWDP_PATH_P2P 1

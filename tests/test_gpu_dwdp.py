@@ -48,7 +48,8 @@ def _worker(rank, world, port, q):
         x = torch.randn(200, H, generator=torch.Generator().manual_seed(100 + rank)).bfloat16().to(dev)
         ref = pkg.MoELayer(wr, full, K)(x)
         outs = []
-        for buf in (0, 1, 0):
+        for i, buf in enumerate((0, 1, 0)):
+            shard.engine.set_copy_mode("sm" if i == 1 else "engine", 64)  # both copy mechanisms
             shard.prefetch(buf)
             shard.wait(buf)
             shard.select_buffer(buf)
@@ -114,3 +115,33 @@ def test_engine_reference_surface_single_gpu(pkg):
     eng.swap_buffers()
     assert not eng.is_resident(1)
     eng.shutdown()
+
+
+def test_engine_sm_copy_mode_single_gpu(pkg):
+    """DWDP_COPY_SM: the prefetch copies run as one SM kernel; every byte staged, ragged sizes
+    (not a multiple of 16 bytes) included, for several experts and CTA counts."""
+    import ctypes
+
+    dev = torch.device("cuda", 0)
+    sizes = [(1 << 20) + 5, 3 << 20, 4096 + 16, 7]
+    srcs = [((torch.arange(n, dtype=torch.int64, device=dev) * (3 + i) + i) % 251).to(torch.uint8)
+            for i, n in enumerate(sizes)]
+    cudart = ctypes.CDLL("libcudart.so.12")
+    for ctas in (1, 148):
+        eng = pkg.communication.CommunicationEngine(0)
+        eng.initialize(4 << 20)
+        for i, (n, t) in enumerate(zip(sizes, srcs)):
+            eng.register_peer_expert(i, t.data_ptr(), n, 0)
+        eng.set_copy_mode("sm", ctas)
+        for i in range(len(sizes)):
+            eng.prefetch(i)
+        eng.swap_buffers()
+        torch.cuda.synchronize()
+        for i, (n, t) in enumerate(zip(sizes, srcs)):
+            host = torch.empty(n, dtype=torch.uint8)
+            assert cudart.cudaMemcpy(ctypes.c_void_p(host.data_ptr()), ctypes.c_void_p(eng.get_weight(i)),
+                                     ctypes.c_size_t(n), 2) == 0
+            assert torch.equal(host, t.cpu()), (ctas, i)
+        with pytest.raises(ValueError):
+            eng.set_copy_mode("dma")
+        eng.shutdown()
