@@ -249,9 +249,9 @@ def algo_layer_bytes(layer, expert_b: int, T: int) -> int:
     return expert_b + layer.router_weight.numel() * layer.router_weight.element_size() + T * K * (8 + 4) + T * H * 2 * 2
 
 
-# DRAM bytes (read + write) of the expert launches of one Qwen-shaped layer, per (T, activation
-# mode), from one ncu capture of bench's layer (profiles/). None where no capture was made.
-TRAFFIC_PER_LAYER: dict = {}
+# DRAM bytes (read + write) of one layer's expert launches (plan/quantise + GEMMs) at the
+# headline T, from the ncu launch list of `bench.py --workload layer` (profiles/, per mode)
+TRAFFIC_PER_LAYER: dict = {(4096, "hilo"): 1069.2e6, (4096, "block128"): 766.0e6}
 
 
 def expert_flops(layer, T: int) -> int:
