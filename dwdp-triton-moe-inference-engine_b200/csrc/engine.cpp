@@ -77,7 +77,9 @@ struct dwdp_engine {
   int next_slot = 0;
   unsigned long long bytes_copied = 0;
   unsigned long long copies_issued = 0;
-  int copy_mode = DWDP_COPY_ENGINE;  // DWDP_COPY_SM: one SM copy kernel per prefetch
+  // DWDP_COPY_SM: SM copy kernels instead of the copy engines (env DWDP_COPY_SM_CTAS=n at
+  // creation, or dwdp_engine_set_copy_mode)
+  int copy_mode = DWDP_COPY_ENGINE;
   int copy_ctas = 148;
   std::mutex mu;
 };
@@ -201,6 +203,13 @@ extern "C" int dwdp_engine_create(int device_id, size_t slot_bytes, int num_slot
   if (e != cudaSuccess) return set_error("cudaDeviceGetStreamPriorityRange", e);
   int n_streams = kCopyStreams;
   if (const char* v = std::getenv("DWDP_COPY_STREAMS")) n_streams = std::max(1, std::min(8, std::atoi(v)));  // tuning
+  if (const char* v = std::getenv("DWDP_COPY_SM_CTAS")) {  // tuning: SM copies with n CTAs
+    const int n = std::atoi(v);
+    if (n > 0) {
+      eng->copy_mode = DWDP_COPY_SM;
+      eng->copy_ctas = n;
+    }
+  }
   for (int i = 0; i < n_streams; ++i) {
     cudaStream_t cs;
     e = cudaStreamCreateWithPriority(&cs, cudaStreamNonBlocking, hi);  // greatest priority

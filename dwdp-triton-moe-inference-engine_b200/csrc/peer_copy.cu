@@ -2,6 +2,8 @@
 // engines, DWDP_COPY_SM): every CTA walks a grid-strided range of 16-byte vectors of each
 // listed copy, loading from the source (a peer GPU's memory through an IPC mapping or a
 // peer pointer: plain loads, no multicast) and storing into this GPU's staging buffer.
+// Loads and stores are streaming (evict-first): the staged slabs are read by the next layer,
+// long after the current layer's GEMMs, whose L2-resident weight tiles they must not evict.
 // Copy engines take no SMs from the persistent GEMMs, SM copies do; the engine measures
 // both (the reference's buffers.cu used cudaMemcpyPeerAsync, i.e. the copy engines).
 #include <cuda_runtime.h>
@@ -12,7 +14,8 @@
 
 namespace dwdp {
 
-constexpr int kCopyThreads = 512;
+// 128 threads: small enough to sit beside a persistent GEMM CTA on the same SM
+constexpr int kCopyThreads = 128;
 constexpr int kCopyUnroll = 4;  // 16-byte loads in flight per thread per step
 
 __global__ void __launch_bounds__(kCopyThreads) peer_copy_kernel(dwdp_copy_list list) {
@@ -29,9 +32,9 @@ __global__ void __launch_bounds__(kCopyThreads) peer_copy_kernel(dwdp_copy_list 
 #pragma unroll
       for (int u = 0; u < kCopyUnroll; ++u) v[u] = __ldcs(src + i + u * nthreads);
 #pragma unroll
-      for (int u = 0; u < kCopyUnroll; ++u) __stcg(dst + i + u * nthreads, v[u]);
+      for (int u = 0; u < kCopyUnroll; ++u) __stcs(dst + i + u * nthreads, v[u]);
     }
-    for (; i < nv; i += nthreads) __stcg(dst + i, __ldcs(src + i));
+    for (; i < nv; i += nthreads) __stcs(dst + i, __ldcs(src + i));
     // a ragged tail (sizes not a multiple of 16) byte by byte
     const size_t tail = list.bytes[c] - nv * 16;
     if (tid < tail)

@@ -127,6 +127,7 @@ class ExpertParallelMoE:
         self.shared_gate_weight = shared_gate_weight
         self.top_k, self.num_experts, self.hidden_size = top_k, E, H
         self.renormalize, self.eps = renormalize, eps
+        self.fused_routing = True  # as MoELayer: one-launch router + dispatch at the smallest sizes
         self.ex = exchange
         self.lo, self.hi = lo, hi
         self._routed_group = local_experts.group()
@@ -170,6 +171,13 @@ class ExpertParallelMoE:
             shared_ws=torch.empty(ops.moe_shared_workspace_bytes(T, H, Is), dtype=torch.uint8, device=dev)
             if parts else None,
             inv=torch.arange(T * K, dtype=torch.int64, device=dev),
+            # the one-launch router + dispatch of MoELayer at the smallest sizes (its dispatch
+            # outputs are not used here; the same routing kernel keeps EP bit-identical to it)
+            fdisp=ops.DispatchResult(*(torch.empty(n, dtype=torch.int64, device=dev)
+                                       for n in (E, E + 1, T * K, T * K, T * K, T * K)),
+                                     torch.empty(T * K, dtype=torch.float32, device=dev), None),
+            ticket=torch.zeros(1, dtype=torch.int32, device=dev),
+            gate_logit=torch.empty(max(T, 1), dtype=torch.float32, device=dev),
             status=torch.zeros(4, dtype=torch.int32, device=dev),
         )
         self._ws[T] = ws
@@ -194,8 +202,13 @@ class ExpertParallelMoE:
         lib, stream = _lib.load(), torch.cuda.current_stream().cuda_stream
         r = ws["router"]
         gate_w = self.shared_gate_weight if self.shared_expert is not None else None
-        ops.router_topk(x, self.router_weight, K, bias=self.router_bias, shared_gate_weight=gate_w,
-                        renormalize=self.renormalize, eps=self.eps, out=r)
+        if self.fused_routing and T > 0 and ops.use_fused_routing(T, K, self.num_experts, x, self.router_weight):
+            ops.route_dispatch_small(x, self.router_weight, K, r, ws["fdisp"], ws["ticket"], ws["gate_logit"],
+                                     bias=self.router_bias, shared_gate_weight=gate_w, renormalize=self.renormalize,
+                                     eps=self.eps, status=ws["status"])
+        else:
+            ops.router_topk(x, self.router_weight, K, bias=self.router_bias, shared_gate_weight=gate_w,
+                            renormalize=self.renormalize, eps=self.eps, out=r)
         st = ws["status"].data_ptr()
         rc = lib.dwdp_ep_dispatch(x.data_ptr(), r.topk_indices.data_ptr(), r.topk_weights.data_ptr(), T, K,
                                   self.num_experts, ex.world, ex.rank, H, ex.capacity, ex.peers.data_ptr(), st,

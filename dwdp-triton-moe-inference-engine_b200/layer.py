@@ -86,7 +86,7 @@ class MoELayer:
         # GEMMs each size their grid to every SM, so concurrent launches queue behind each
         # other, and the cross-stream join breaks the programmatic-launch chain): off by default.
         self.overlap_shared = False
-        # decode sizes (T * top_k <= 256, bf16 router): router and dispatch in one launch
+        # the smallest decode sizes (ops.use_fused_routing): router and dispatch in one launch
         self.fused_routing = True
         self.refresh_handles()
 
@@ -177,7 +177,7 @@ class MoELayer:
         if overlap:
             self._start_shared(x, ws)
         gate_w = self.shared_gate_weight if self.shared_expert is not None else None
-        if self.fused_routing and ops.route_dispatch_small_fits(T, K, self.num_experts, x, self.router_weight):
+        if self.fused_routing and ops.use_fused_routing(T, K, self.num_experts, x, self.router_weight):
             # decode sizes: router and dispatch in one launch
             ops.route_dispatch_small(x, self.router_weight, K, ws.router, ws.dispatch, ws.ticket, ws.gate_logit,
                                      bias=self.router_bias, shared_gate_weight=gate_w, score_scale=self.score_scale,
@@ -236,7 +236,7 @@ class MoELayer:
         router = 1 if self.router_weight.dtype == torch.bfloat16 and self.num_experts <= 256 else 2
         dispatch = 1 if num_tokens * self.top_k <= 256 else 2
         if (self.fused_routing and self.router_weight.dtype == torch.bfloat16 and self.num_experts <= 256
-                and 0 < num_tokens * self.top_k <= 256):
+                and 0 < num_tokens <= ops.FUSED_ROUTING_MAX_TOKENS and num_tokens * self.top_k <= 256):
             router, dispatch = 1, 0
         # e4m3 hi/lo: plan(+planes), gate/up, planes, down; e4m3 block128: the gate/up epilogue
         # writes the intermediate's e4m3 rows, so no launch between the GEMMs; bf16: row gather

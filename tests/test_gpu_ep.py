@@ -43,9 +43,6 @@ def _layers(pkg, ep, rank, world, dev, exchange):
     wr, gate = wr.to(dev), gate.to(dev)
     ref = pkg.MoELayer(wr, full, K, shared_expert=sh, shared_gate_weight=gate)
     ref.overlap_shared = True  # the shared expert in its own launches, gated by the merge
-    # the EP path routes with router_topk; the local layer's one-launch decode router sums the
-    # logits in another order (equal to 1e-5, not bit for bit), so it is off for this comparison
-    ref.fused_routing = False
     epl = ep.ExpertParallelMoE(wr, local, K, exchange, shared_expert=sh, shared_gate_weight=gate)
     return ref, epl
 
