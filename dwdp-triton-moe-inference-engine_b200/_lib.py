@@ -137,7 +137,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dwdp_moe_shared_workspace_bytes": (c_size_t, [c_int64, c_int, c_int]),
     "dwdp_moe_shared_expert": (
         c_int,
-        [ctypes.POINTER(ExpertGroup), c_void_p, c_int64, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p],
+        [ctypes.POINTER(ExpertGroup), c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p,
+         c_void_p],
     ),
     "dwdp_merge_gated": (
         c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int64, c_int, c_int, c_void_p, c_int, c_void_p]

@@ -366,8 +366,8 @@ extern "C" size_t dwdp_moe_shared_workspace_bytes(int64_t num_tokens, int hidden
 }
 
 extern "C" int dwdp_moe_shared_expert(const dwdp_expert_group* shared, const void* hidden, int64_t num_tokens,
-                                      void* shared_out, void* workspace, size_t workspace_bytes, int* status,
-                                      void* stream) {
+                                      const float* shared_gate, void* shared_out, void* workspace,
+                                      size_t workspace_bytes, int* status, void* stream) {
   g_last_error.clear();
   if (shared == nullptr || hidden == nullptr || shared_out == nullptr)
     return fail(DWDP_ERR_INVALID_ARGUMENT, "moe_shared_expert: shared group, hidden and shared_out are required");
@@ -379,7 +379,7 @@ extern "C" int dwdp_moe_shared_expert(const dwdp_expert_group* shared, const voi
   if (workspace == nullptr || workspace_bytes < need)
     return fail(DWDP_ERR_CAPACITY, "moe_shared_expert: workspace of %zu bytes < required %zu", workspace_bytes, need);
   return check(dwdp_moe_experts_launch(shared, shared, nullptr, nullptr, hidden, num_tokens, 1, nullptr, nullptr,
-                                       nullptr, nullptr, nullptr, shared_out, workspace, workspace_bytes, status, 1,
+                                       nullptr, shared_gate, nullptr, shared_out, workspace, workspace_bytes, status, 1,
                                        as_stream(stream)),
                "moe_shared_expert");
 }

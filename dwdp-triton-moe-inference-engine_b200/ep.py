@@ -228,19 +228,14 @@ class ExpertParallelMoE:
         if T == 0:
             return
         if self.shared_expert is not None:
-            # the shared expert over this rank's own tokens, ungated; the merge applies the gate
-            ops.moe_shared_expert(self._shared_group, x, ws["shared_out"], ws["shared_ws"], ws["status"])
-            gate = r.shared_gate if r.shared_gate is not None else self._ones(T)
+            # the shared expert over this rank's own tokens, gated in its down epilogue as in
+            # MoELayer's grouped launch (bit-identical partials), then the merge
+            ops.moe_shared_expert(self._shared_group, x, ws["shared_out"], ws["shared_ws"], ws["status"],
+                                  shared_gate=r.shared_gate)
             ops.merge(ex.returned_rows(T * K), ws["inv"], T, K, shared_out=ws["shared_out"],
-                      shared_parts=ws["parts"], out=out, shared_gate=gate)
+                      shared_parts=ws["parts"], out=out)
         else:
             ops.merge(ex.returned_rows(T * K), ws["inv"], T, K, out=out)
-
-    def _ones(self, T: int) -> torch.Tensor:
-        ws = self.workspace(T)
-        if "ones" not in ws:
-            ws["ones"] = torch.ones(T, dtype=torch.float32, device=self.ex.device)
-        return ws["ones"]
 
     def read_status(self, T: int) -> tuple[int, ...]:
         return tuple(self.workspace(T)["status"].cpu().tolist())

@@ -425,13 +425,18 @@ def moe_shared_workspace_bytes(num_tokens: int, hidden_size: int, shared_interme
 
 
 def moe_shared_expert(shared: _lib.ExpertGroup, hidden: torch.Tensor, shared_out: torch.Tensor,
-                      workspace: torch.Tensor, status: torch.Tensor | None = None) -> None:
-    """The shared expert alone, ungated: ``shared_out`` [parts, T, H] bf16 partials
-    (``moe_shared_parts(T, Is)`` of them); ``merge(..., shared_gate=g)`` applies the gate."""
-    _require_cuda(hidden, shared_out, workspace, status)
+                      workspace: torch.Tensor, status: torch.Tensor | None = None, *,
+                      shared_gate: torch.Tensor | None = None) -> None:
+    """The shared expert alone: ``shared_out`` [parts, T, H] bf16 partials
+    (``moe_shared_parts(T, Is)`` of them). Ungated by default (``merge(..., shared_gate=g)``
+    applies the gate); with ``shared_gate`` [T] fp32 the down epilogue applies it, as
+    :func:`moe_experts` does for its shared rows."""
+    _require_cuda(hidden, shared_out, workspace, status, shared_gate)
+    if shared_gate is not None and (shared_gate.dtype != torch.float32 or shared_gate.numel() < hidden.shape[0]):
+        raise ValueError("shared_gate must be fp32 with one value per token")
     rc = _lib.load().dwdp_moe_shared_expert(
-        ctypes.byref(shared), hidden.data_ptr(), hidden.shape[0], shared_out.data_ptr(), workspace.data_ptr(),
-        workspace.numel(), _ptr(status), _stream(),
+        ctypes.byref(shared), hidden.data_ptr(), hidden.shape[0], _ptr(shared_gate), shared_out.data_ptr(),
+        workspace.data_ptr(), workspace.numel(), _ptr(status), _stream(),
     )
     _lib.check(rc, "moe_shared_expert")
 

@@ -274,14 +274,16 @@ int dwdp_moe_experts_indexed(const dwdp_expert_group* routed, const dwdp_expert_
                              void* shared_out, void* workspace, size_t workspace_bytes, int* status,
                              void* stream);
 
-/* The shared expert alone, for running it concurrently with routing: for every
- * token t, sum_p shared_out[p][t] = down_s(silu(gate_s(x_t)) * up_s(x_t)) WITHOUT
- * the sigmoid gate (dwdp_merge_gated applies it), p < dwdp_moe_shared_parts(T, Is).
- * It depends only on `hidden`, so it can start before the router. */
+/* The shared expert alone: for every token t, sum_p shared_out[p][t] =
+ * g_t * down_s(silu(gate_s(x_t)) * up_s(x_t)), p < dwdp_moe_shared_parts(T, Is).
+ * shared_gate == NULL: g_t = 1 (ungated; dwdp_merge_gated applies the gate later),
+ * so it depends only on `hidden` and can start before the router. With the router's
+ * shared_gate [T] the gate is applied in the down epilogue exactly as
+ * dwdp_moe_experts does for its shared rows (bit-identical partials). */
 size_t dwdp_moe_shared_workspace_bytes(int64_t num_tokens, int hidden_size, int shared_intermediate_size);
 int dwdp_moe_shared_expert(const dwdp_expert_group* shared, const void* hidden, int64_t num_tokens,
-                           void* shared_out, void* workspace, size_t workspace_bytes, int* status,
-                           void* stream);
+                           const float* shared_gate, void* shared_out, void* workspace, size_t workspace_bytes,
+                           int* status, void* stream);
 
 /* ======================================================================== *
  * Merge (reference_merge, merger/kernels/reference.py:6-27): deterministic

@@ -42,7 +42,6 @@ def _layers(pkg, ep, rank, world, dev, exchange):
     sh.load_expert(0, *shared)
     wr, gate = wr.to(dev), gate.to(dev)
     ref = pkg.MoELayer(wr, full, K, shared_expert=sh, shared_gate_weight=gate)
-    ref.overlap_shared = True  # the shared expert in its own launches, gated by the merge
     epl = ep.ExpertParallelMoE(wr, local, K, exchange, shared_expert=sh, shared_gate_weight=gate)
     return ref, epl
 

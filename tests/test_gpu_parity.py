@@ -369,6 +369,12 @@ def test_shared_expert_side_stream(pkg, orc, T):
     torch.cuda.synchronize()
     ref = orc.swiglu_expert(x.float(), *(t.cpu() for t in layer.shared_expert.dequantized(0)))
     assert orc.rel_frobenius(sh_out.float().sum(0).cpu(), ref) < FP8_TOL
+    # gated in the down epilogue: each partial scaled by the token's gate before its bf16 rounding
+    g = torch.rand(T, generator=torch.Generator().manual_seed(5)).to(DEV)
+    sh_g = torch.empty_like(sh_out)
+    pkg.ops.moe_shared_expert(layer._shared_group, xd, sh_g, wsb, shared_gate=g)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(sh_g.float(), (sh_out.float() * g[None, :, None]), rtol=1e-2, atol=1e-5)
     layer.overlap_shared = True
     y1 = layer(xd)
     layer.overlap_shared = False
