@@ -8,5 +8,5 @@ from .weights import ExpertWeightStore  # noqa: F401
 from .layer import MoELayer, algorithmic_bytes, algorithmic_flops  # noqa: F401
 
 __all__ = ["_lib", "ops", "ExpertWeightStore", "MoELayer", "algorithmic_bytes", "algorithmic_flops"]
-from . import cost_model, decode, ep, hf_adapter, plans, reference_plugin, stages  # noqa: F401,E402
+from . import comms_metadata, cost_model, decode, ep, hf_adapter, plans, reference_plugin, stages, tensor_list  # noqa: F401,E402
 from .fused import fused_moe  # noqa: F401,E402

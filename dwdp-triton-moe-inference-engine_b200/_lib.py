@@ -60,6 +60,33 @@ class ExpertGroup(ctypes.Structure):
     ]
 
 
+TL_ROWS = 27  # DWDP_TL_ROWS: the reference's 26 TensorList fields + the down-scale row
+
+
+class TensorListBases(ctypes.Structure):
+    """Mirror of ``dwdp_tensor_list_bases``."""
+
+    _fields_ = [(n, c_void_p) for n in ("input", "token_index", "routing_weights", "intermediate", "output",
+                                        "weighted_output")] + [
+        (n, c_int64) for n in ("intermediate_row_bytes", "output_row_bytes", "weighted_row_bytes", "n", "k",
+                               "intermediate_n", "input_ld", "gate_ld", "up_ld", "down_ld", "output_ld",
+                               "dtype_code")]
+
+
+class TensorListHandle(ctypes.Structure):
+    """Mirror of ``dwdp_tensor_list``."""
+
+    _fields_ = [("capacity", c_int64), ("fields", c_void_p), ("hidden_size", c_int),
+                ("intermediate_size", c_int), ("weight_dtype", c_int), ("scale_mode", c_int),
+                ("act_quant", c_int)]
+
+
+class CopySlice(ctypes.Structure):
+    """Mirror of ``dwdp_copy_slice``."""
+
+    _fields_ = [("expert_id", c_int), ("reserved", c_int), ("start", ctypes.c_uint64), ("bytes", ctypes.c_uint64)]
+
+
 # name -> (restype, argtypes)
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dwdp_version": (c_int, []),
@@ -147,6 +174,17 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_void_p, c_int, c_void_p]
     ),
     "dwdp_moe_shared_parts": (c_int, [c_int64, c_int]),
+    "dwdp_tensor_list_build": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, ctypes.POINTER(ExpertGroup),
+         ctypes.POINTER(TensorListBases), ctypes.POINTER(TensorListHandle), c_void_p, c_void_p, c_void_p],
+    ),
+    "dwdp_grouped_moe": (
+        c_int,
+        [ctypes.POINTER(TensorListHandle), ctypes.POINTER(ExpertGroup), c_void_p, c_void_p, c_int64, c_int,
+         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p],
+    ),
+
     # communication engine
     "dwdp_engine_last_error": (ctypes.c_char_p, []),
     "dwdp_ipc_handle_bytes": (c_size_t, []),
@@ -159,6 +197,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dwdp_engine_register_peer": (c_int, [c_void_p, c_int, c_void_p, c_size_t, c_int]),
     "dwdp_engine_prefetch": (c_int, [c_void_p, ctypes.POINTER(c_int), c_int, c_int, c_void_p]),
     "dwdp_engine_wait": (c_int, [c_void_p, c_int, c_void_p]),
+    "dwdp_engine_prefetch_slices": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "dwdp_engine_resident_pointer": (c_int, [c_void_p, c_int, c_int, ctypes.POINTER(c_void_p)]),
     "dwdp_engine_is_remote": (c_int, [c_void_p, c_int, ctypes.POINTER(c_int)]),
     "dwdp_engine_release": (c_int, [c_void_p, c_int]),

@@ -249,6 +249,45 @@ class CommunicationEngine:
             if e not in self._local:
                 self._where[e] = buffer
 
+    def issue_order(self, plan) -> list:
+        """The plan's descriptors in the order the TransferScheduler releases their experts
+        (priority, then submission order; duplicates coalesced), each expert's slices kept in
+        the planner's rotated order. The reference's planner submits the same experts and
+        priorities to its scheduler (comms_planner/expert_parallel.py:266-272)."""
+        by_expert: dict[int, list] = {}
+        prio: dict[int, int] = {}
+        for d in plan.communication_descriptors:
+            by_expert.setdefault(int(d.source_expert_id), []).append(d)
+            prio.setdefault(int(d.source_expert_id), int(d.priority))
+        sched = TransferScheduler()
+        for e, p in prio.items():
+            sched.submit(e, p)
+        sched.close()
+        order = []
+        while (e := sched.take(0)) is not None:
+            order.extend(by_expert[e])
+            sched.complete(e)
+        return order
+
+    def execute_plan(self, plan, buffer: int | None = None, after_current_stream: bool = True) -> list:
+        """Run a communication plan's copies (``DWDPCommunicationPlanner``: 2 MiB slices with
+        rotated starts, priorities) into ``buffer`` (default: the next buffer) with ONE call
+        into the engine (``dwdp_engine_prefetch_slices``), in ``issue_order``. Returns the
+        descriptors in the order they were issued; ``wait_buffer(buffer)`` orders a stream
+        after them."""
+        buf = self.next_buffer if buffer is None else int(buffer)
+        order = self.issue_order(plan)
+        arr = (_lib.CopySlice * max(1, len(order)))()
+        for i, d in enumerate(order):
+            arr[i].expert_id, arr[i].start, arr[i].bytes = int(d.source_expert_id), int(d.start), int(d.count)
+        after = torch.cuda.current_stream(self.device_id).cuda_stream if after_current_stream else None
+        _chk(_lib.load().dwdp_engine_prefetch_slices(self._eng(), arr, len(order), buf, after), "prefetch_slices")
+        for d in order:
+            e = int(d.source_expert_id)
+            if e not in self._local:
+                self._where[e] = buf
+        return order
+
     def wait_buffer(self, buffer: int = 0, stream: torch.cuda.Stream | None = None) -> None:
         s = (stream or torch.cuda.current_stream(self.device_id)).cuda_stream
         _chk(_lib.load().dwdp_engine_wait(self._eng(), buffer, s), "wait")

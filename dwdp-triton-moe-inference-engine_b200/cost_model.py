@@ -119,6 +119,25 @@ def build_cost_model(remote_expert_ids: list[int], bytes_per_expert: int, link: 
                                   critical_path_us=exposed, estimated_bandwidth_gbps=link.aggregate_gbps)
 
 
+def build_descriptor_cost_model(descriptors, link: LinkProfile, *, prefetch_window_us: float = 0.0
+                                ) -> CommunicationCostModel:
+    """One estimate per communication descriptor (a slice or a whole expert) of a plan, the
+    copies issued in descriptor order round-robin over the engine's copy streams."""
+    sizes = [int(d.count) for d in descriptors]
+    total_us = link.batch_us(sizes)
+    overlap = min(total_us, max(0.0, prefetch_window_us))
+    exposed = total_us - overlap
+    est = tuple(
+        CommunicationCostEstimate(
+            descriptor_id=d.descriptor_id, estimated_bytes=int(d.count), estimated_latency_us=link.latency_us,
+            estimated_bandwidth_gbps=link.bandwidth_gbps, communication_priority=d.priority,
+            critical_path_us=exposed, transfer_duration_us=link.copy_us(int(d.count)),
+            prefetch_window_us=prefetch_window_us, overlap_estimate_us=overlap)
+        for d in descriptors)
+    return CommunicationCostModel(estimates=est, total_estimated_bytes=sum(sizes), total_estimated_latency_us=total_us,
+                                  critical_path_us=exposed, estimated_bandwidth_gbps=link.aggregate_gbps)
+
+
 @dataclass(frozen=True, slots=True)
 class DecodePathChoice:
     path: str  # "ep" | "dwdp"

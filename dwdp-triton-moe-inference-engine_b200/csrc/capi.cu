@@ -39,6 +39,10 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group*, const dwdp_expe
                                        const int64_t*, const float*, const float*, void*, void*,
                                        void*, size_t, int*, int, cudaStream_t);
 extern "C" size_t dwdp_moe_shared_workspace_bytes_impl(int64_t, int, int);
+extern "C" int dwdp_tensor_list_build_launch(const int64_t*, const int64_t*, const int64_t*, const int64_t*,
+                                             const int64_t*, int, const dwdp_expert_group*,
+                                             const dwdp_tensor_list_bases*, int64_t, int64_t*, int64_t*, int*,
+                                             cudaStream_t);
 extern "C" int dwdp_merge_launch(const void*, const int64_t*, const void*, int, const float*, int64_t, int, int,
                                  void*, int, int*, cudaStream_t);
 
@@ -382,6 +386,56 @@ extern "C" int dwdp_moe_shared_expert(const dwdp_expert_group* shared, const voi
                                        nullptr, shared_gate, nullptr, shared_out, workspace, workspace_bytes, status, 1,
                                        as_stream(stream)),
                "moe_shared_expert");
+}
+
+// --------------------------------------------------------------------------- TensorList
+extern "C" int dwdp_tensor_list_build(const int64_t* expert_queue, const int64_t* expert_starts,
+                                      const int64_t* expert_counts, const int64_t* priorities,
+                                      const int64_t* stream_ids, int plan_len, const dwdp_expert_group* experts,
+                                      const dwdp_tensor_list_bases* bases, const dwdp_tensor_list* tl,
+                                      int64_t* meta, int* status, void* stream) {
+  g_last_error.clear();
+  if (experts == nullptr || bases == nullptr || tl == nullptr || meta == nullptr || tl->fields == nullptr)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "tensor_list_build: null argument");
+  if (plan_len < 0 || (plan_len > 0 && (expert_queue == nullptr || expert_starts == nullptr ||
+                                        expert_counts == nullptr)))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "tensor_list_build: plan rows missing");
+  if (tl->capacity <= 0 || tl->capacity > 1024)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "tensor_list_build: capacity must be in [1, 1024]");
+  if (experts->w13 == nullptr || experts->w2 == nullptr || experts->num_experts <= 0)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "tensor_list_build: expert pointer arrays missing");
+  return check(dwdp_tensor_list_build_launch(expert_queue, expert_starts, expert_counts, priorities, stream_ids,
+                                             plan_len, experts, bases, tl->capacity, tl->fields, meta, status,
+                                             as_stream(stream)),
+               "tensor_list_build");
+}
+
+extern "C" int dwdp_grouped_moe(const dwdp_tensor_list* tl, const dwdp_expert_group* shared,
+                                const int64_t* packed_token_indices, const void* hidden, int64_t num_tokens,
+                                int top_k, const float* packed_weights, const float* shared_gate,
+                                void* weighted_out, void* shared_out, void* workspace, size_t workspace_bytes,
+                                int* status, void* stream) {
+  g_last_error.clear();
+  if (tl == nullptr || tl->fields == nullptr || tl->capacity <= 0 || tl->capacity > 1024)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "grouped_moe: TensorList with 1..1024 entries required");
+  // The TensorList's own rows are the expert group: entry i is "expert" i.
+  const int64_t cap = tl->capacity;
+  dwdp_expert_group g{};
+  g.num_experts = (int)cap;
+  g.hidden_size = tl->hidden_size;
+  g.intermediate_size = tl->intermediate_size;
+  g.weight_dtype = tl->weight_dtype;
+  g.scale_mode = tl->scale_mode;
+  g.act_quant = tl->act_quant;
+  g.w13 = reinterpret_cast<const void* const*>(tl->fields + DWDP_TL_GATE_WEIGHT_PTRS * cap);
+  g.w2 = reinterpret_cast<const void* const*>(tl->fields + DWDP_TL_DOWN_WEIGHT_PTRS * cap);
+  const bool scaled = tl->weight_dtype == DWDP_DTYPE_FP8_E4M3;
+  g.s13 = scaled ? reinterpret_cast<const float* const*>(tl->fields + DWDP_TL_QUANTIZATION_PTRS * cap) : nullptr;
+  g.s2 = scaled ? reinterpret_cast<const float* const*>(tl->fields + DWDP_TL_DOWN_QUANTIZATION_PTRS * cap) : nullptr;
+  return moe_experts_checked(&g, shared, nullptr, packed_token_indices, hidden, num_tokens, top_k,
+                             tl->fields + DWDP_TL_TOKEN_COUNTS * cap, tl->fields + DWDP_TL_TOKEN_OFFSETS * cap,
+                             packed_weights, shared_gate, weighted_out, shared_out, workspace, workspace_bytes,
+                             status, stream);
 }
 
 // --------------------------------------------------------------------------- decode-step attention pieces

@@ -329,13 +329,19 @@ extern "C" int dwdp_engine_register_peer(dwdp_engine* eng, int expert_id, const 
   return DWDP_OK;
 }
 
-extern "C" int dwdp_engine_prefetch(dwdp_engine* eng, const int* expert_ids, int n, int buffer,
-                                    void* after_stream) {
-  if (eng == nullptr || (n > 0 && expert_ids == nullptr))
-    return fail(DWDP_ERR_INVALID_ARGUMENT, "prefetch: bad argument");
-  if (buffer < 0 || buffer >= eng->num_buffers) return fail(DWDP_ERR_INVALID_ARGUMENT, "prefetch: bad buffer");
-  std::lock_guard<std::mutex> lock(eng->mu);
-  DeviceGuard guard(eng->device);
+namespace {
+
+struct PlannedCopy {
+  const char* src;
+  char* dst;
+  size_t bytes;
+};
+
+// Issue `copies` into staging `buffer` in list order, after the work already queued on
+// `after_stream`: copy k goes to copy stream k % streams (copy engines), or the list runs
+// as SM copy kernels of up to DWDP_COPY_LIST_MAX copies on stream 0. The copy streams then
+// join into stream 0 and one event marks the buffer ready. Caller holds eng->mu.
+int issue_copies(dwdp_engine* eng, const std::vector<PlannedCopy>& copies, int buffer, void* after_stream) {
   cudaError_t e;
   if (after_stream != nullptr) {
     // the buffer may still be read by earlier work on the caller's stream
@@ -346,6 +352,55 @@ extern "C" int dwdp_engine_prefetch(dwdp_engine* eng, const int* expert_ids, int
     for (auto cs : eng->copy_streams) cudaStreamWaitEvent(cs, dep, 0);
     cudaEventDestroy(dep);
   }
+  if (eng->copy_mode == DWDP_COPY_SM) {
+    dwdp_copy_list list;
+    list.n = 0;
+    for (size_t j = 0; j <= copies.size(); ++j) {
+      if (list.n == DWDP_COPY_LIST_MAX || (j == copies.size() && list.n > 0)) {
+        const int rc = dwdp_peer_copy_sm(&list, eng->copy_ctas, eng->copy_streams[0]);
+        if (rc != DWDP_OK) return fail(rc, "prefetch: SM copy launch failed");
+        eng->copies_issued += 1;
+        list.n = 0;
+      }
+      if (j == copies.size()) break;
+      list.src[list.n] = copies[j].src;
+      list.dst[list.n] = copies[j].dst;
+      list.bytes[list.n] = copies[j].bytes;
+      ++list.n;
+      eng->bytes_copied += copies[j].bytes;
+    }
+  } else {
+    for (size_t k = 0; k < copies.size(); ++k) {
+      e = cudaMemcpyAsync(copies[k].dst, copies[k].src, copies[k].bytes, cudaMemcpyDeviceToDevice,
+                          eng->copy_streams[k % eng->copy_streams.size()]);
+      if (e != cudaSuccess) return set_error("cudaMemcpyAsync(prefetch)", e);
+      eng->copies_issued += 1;
+      eng->bytes_copied += copies[k].bytes;
+    }
+  }
+  for (size_t i = 1; i < eng->copy_streams.size(); ++i) {
+    cudaEventRecord(eng->stream_done[i], eng->copy_streams[i]);
+    cudaStreamWaitEvent(eng->copy_streams[0], eng->stream_done[i], 0);
+  }
+  e = cudaEventRecord(eng->ready[buffer], eng->copy_streams[0]);
+  if (e != cudaSuccess) return set_error("cudaEventRecord", e);
+  eng->buffer_valid[buffer] = 1;
+  return DWDP_OK;
+}
+
+char* staging_slot(dwdp_engine* eng, const EngineExpert* x, int buffer) {
+  return static_cast<char*>(eng->buffers[buffer]) + (size_t)x->slot * eng->slot_bytes;
+}
+
+}  // namespace
+
+extern "C" int dwdp_engine_prefetch(dwdp_engine* eng, const int* expert_ids, int n, int buffer,
+                                    void* after_stream) {
+  if (eng == nullptr || (n > 0 && expert_ids == nullptr))
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "prefetch: bad argument");
+  if (buffer < 0 || buffer >= eng->num_buffers) return fail(DWDP_ERR_INVALID_ARGUMENT, "prefetch: bad buffer");
+  std::lock_guard<std::mutex> lock(eng->mu);
+  DeviceGuard guard(eng->device);
   std::vector<const EngineExpert*> todo;
   for (int i = 0; i < n; ++i) {
     auto it = eng->experts.find(expert_ids[i]);
@@ -355,57 +410,47 @@ extern "C" int dwdp_engine_prefetch(dwdp_engine* eng, const int* expert_ids, int
   // Copies start at a device-dependent expert so that ranks do not all read the same peer
   // first. With DWDP_PREFETCH_SLICE_MB = s > 0 every expert moves as s-MiB slices dealt
   // round-robin over the copy streams (the reference's 2 MiB slices, buffers.cu:94-134);
-  // by default each expert is one copy.
+  // by default each expert is one copy (SM copies always move whole experts).
   static const size_t slice = [] {
     const char* v = getenv("DWDP_PREFETCH_SLICE_MB");
     return v != nullptr ? (size_t)atoi(v) << 20 : (size_t)0;
   }();
   const size_t rot = todo.empty() ? 0 : (size_t)eng->device % todo.size();  // spread peer load across ranks
-  if (eng->copy_mode == DWDP_COPY_SM) {
-    // SM copies: the listed experts in kernels of up to DWDP_COPY_LIST_MAX copies on stream 0
-    dwdp_copy_list list;
-    list.n = 0;
-    for (size_t j = 0; j <= todo.size(); ++j) {
-      if (list.n == DWDP_COPY_LIST_MAX || (j == todo.size() && list.n > 0)) {
-        const int rc = dwdp_peer_copy_sm(&list, eng->copy_ctas, eng->copy_streams[0]);
-        if (rc != DWDP_OK) return fail(rc, "prefetch: SM copy launch failed");
-        eng->copies_issued += 1;
-        list.n = 0;
-      }
-      if (j == todo.size()) break;
-      const EngineExpert* x = todo[(j + rot) % todo.size()];
-      list.src[list.n] = x->src;
-      list.dst[list.n] = static_cast<char*>(eng->buffers[buffer]) + (size_t)x->slot * eng->slot_bytes;
-      list.bytes[list.n] = x->bytes;
-      ++list.n;
-      eng->bytes_copied += x->bytes;
-    }
-    todo.clear();
-  }
-  size_t k = 0;  // copy counter: picks the stream
+  std::vector<PlannedCopy> copies;
   for (size_t j = 0; j < todo.size(); ++j) {
     const EngineExpert* x = todo[(j + rot) % todo.size()];
-    char* dst = static_cast<char*>(eng->buffers[buffer]) + (size_t)x->slot * eng->slot_bytes;
+    char* dst = staging_slot(eng, x, buffer);
     const char* src = static_cast<const char*>(x->src);
-    const size_t step = slice > 0 ? slice : x->bytes;
-    for (size_t off = 0; off < x->bytes; off += step, ++k) {
-      const size_t n = std::min(step, x->bytes - off);
-      e = cudaMemcpyAsync(dst + off, src + off, n, cudaMemcpyDeviceToDevice,
-                          eng->copy_streams[k % eng->copy_streams.size()]);
-      if (e != cudaSuccess) return set_error("cudaMemcpyAsync(prefetch)", e);
-      eng->copies_issued += 1;
-    }
-    eng->bytes_copied += x->bytes;
+    const size_t step = (slice > 0 && eng->copy_mode != DWDP_COPY_SM) ? slice : x->bytes;
+    for (size_t off = 0; off < x->bytes; off += step)
+      copies.push_back(PlannedCopy{src + off, dst + off, std::min(step, x->bytes - off)});
   }
-  // join the copy streams into stream 0, then one event marks the buffer ready
-  for (size_t i = 1; i < eng->copy_streams.size(); ++i) {
-    cudaEventRecord(eng->stream_done[i], eng->copy_streams[i]);
-    cudaStreamWaitEvent(eng->copy_streams[0], eng->stream_done[i], 0);
+  return issue_copies(eng, copies, buffer, after_stream);
+}
+
+extern "C" int dwdp_engine_prefetch_slices(dwdp_engine* eng, const dwdp_copy_slice* slices, int n, int buffer,
+                                           void* after_stream) {
+  if (eng == nullptr || (n > 0 && slices == nullptr) || n < 0)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "prefetch_slices: bad argument");
+  if (buffer < 0 || buffer >= eng->num_buffers)
+    return fail(DWDP_ERR_INVALID_ARGUMENT, "prefetch_slices: bad buffer");
+  std::lock_guard<std::mutex> lock(eng->mu);
+  DeviceGuard guard(eng->device);
+  std::vector<PlannedCopy> copies;
+  copies.reserve((size_t)n);
+  for (int i = 0; i < n; ++i) {
+    const dwdp_copy_slice& sl = slices[i];
+    auto it = eng->experts.find(sl.expert_id);
+    if (it == eng->experts.end())
+      return fail(DWDP_ERR_NOT_FOUND, "prefetch_slices: unknown expert " + std::to_string(sl.expert_id));
+    const EngineExpert* x = &it->second;
+    if (sl.start > x->bytes || sl.bytes > x->bytes - sl.start)
+      return fail(DWDP_ERR_INVALID_ARGUMENT, "prefetch_slices: slice beyond expert " + std::to_string(sl.expert_id));
+    if (!x->remote || sl.bytes == 0) continue;  // local experts are read in place
+    copies.push_back(PlannedCopy{static_cast<const char*>(x->src) + sl.start, staging_slot(eng, x, buffer) + sl.start,
+                                 (size_t)sl.bytes});
   }
-  e = cudaEventRecord(eng->ready[buffer], eng->copy_streams[0]);
-  if (e != cudaSuccess) return set_error("cudaEventRecord", e);
-  eng->buffer_valid[buffer] = 1;
-  return DWDP_OK;
+  return issue_copies(eng, copies, buffer, after_stream);
 }
 
 extern "C" int dwdp_engine_set_copy_mode(dwdp_engine* eng, int mode, int ctas) {

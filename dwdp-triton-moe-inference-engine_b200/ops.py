@@ -572,3 +572,37 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     _lib.check(rc, "paged_attention")
     return out
 
+
+
+# ----------------------------------------------------------------------------- TensorList
+def tensor_list_build(plan_rows: tuple, plan_len: int, experts: _lib.ExpertGroup, bases: _lib.TensorListBases,
+                      handle: _lib.TensorListHandle, meta: torch.Tensor, status: torch.Tensor | None = None) -> None:
+    """Fill ``handle.fields`` on the device from the plan rows (queue, starts, counts,
+    priorities or None, streams or None); ``meta`` int64[2] receives (size, max_m)."""
+    _require_cuda(meta, *[t for t in plan_rows if t is not None])
+    for t in plan_rows:
+        if t is not None and (t.dtype != torch.int64 or not t.is_contiguous()):
+            raise ValueError("TensorList plan rows must be contiguous int64 tensors")
+    lib = _lib.load()
+    rc = lib.dwdp_tensor_list_build(*[_ptr(t) for t in plan_rows], plan_len, ctypes.byref(experts),
+                                    ctypes.byref(bases), ctypes.byref(handle), meta.data_ptr(), _ptr(status),
+                                    _stream())
+    _lib.check(rc, "tensor_list_build")
+
+
+def grouped_moe(handle: _lib.TensorListHandle, shared: _lib.ExpertGroup | None, packed_token_indices: torch.Tensor,
+                hidden: torch.Tensor, top_k: int, packed_weights: torch.Tensor, shared_gate: torch.Tensor | None,
+                weighted_out: torch.Tensor, shared_out: torch.Tensor | None, workspace: torch.Tensor,
+                status: torch.Tensor | None = None) -> None:
+    """Grouped expert GEMMs over the entries of a TensorList (``dwdp_grouped_moe``)."""
+    _require_cuda(packed_token_indices, hidden, packed_weights, weighted_out, workspace)
+    if packed_weights.dtype != torch.float32:
+        raise ValueError("packed routing weights must be fp32 for the grouped GEMM")
+    if packed_token_indices.dtype != torch.int64:
+        raise ValueError("packed_token_indices must be int64")
+    lib = _lib.load()
+    rc = lib.dwdp_grouped_moe(ctypes.byref(handle), ctypes.byref(shared) if shared is not None else None,
+                              packed_token_indices.data_ptr(), hidden.data_ptr(), hidden.shape[0], top_k,
+                              packed_weights.data_ptr(), _ptr(shared_gate), weighted_out.data_ptr(), _ptr(shared_out),
+                              workspace.data_ptr(), workspace.numel(), _ptr(status), _stream())
+    _lib.check(rc, "grouped_moe")

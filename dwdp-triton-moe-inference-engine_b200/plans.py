@@ -8,8 +8,8 @@ and meaning (the drop-in contract between stages):
                                            — DWDP/scheduler/execution.py:10-38, metadata.py:8-38 (the
   per-expert rows are padded to E with -1 and ``num_active`` is a device scalar,
   so building the plan needs no host synchronisation; statistics are read lazily)
-* ``CommunicationPlan``                    — DWDP/comms_planner/metadata.py:107-125 (the two
-  expert-id tensors and the policy name the executor reads)
+* ``CommunicationPlan``                    — DWDP/comms_planner/metadata.py:107-125, every field
+  (its parts in :mod:`comms_metadata`)
 * ``ExecutorOutput`` (+ ExpertOutput, OutputMetadata, ExecutionMetadata, timing and
   workspace metadata), ``MergerOutput`` (+ merge metadata and statistics)
                                            — DWDP/executor/outputs.py:10-82, executor/metadata.py,
@@ -168,13 +168,7 @@ class ExecutionPlan:
                              self.statistics, self.scheduling_policy, self.deterministic, self.num_active)
 
 
-@dataclass(slots=True)
-class CommunicationPlan:
-    local_expert_ids: torch.Tensor
-    remote_expert_ids: torch.Tensor
-    planner_policy: str = "static"
-    prefetch_buffer: int = 0
-    cost_model: object | None = None  # cost_model.CommunicationCostModel for remote transfers
+from .comms_metadata import CommunicationPlan  # noqa: E402  (DWDP/comms_planner/metadata.py:107-125)
 
 
 # ----------------------------------------------------------------------------- executor

@@ -142,9 +142,21 @@ class SchedulerConfig:
 
 @dataclass(frozen=True, slots=True)
 class CommunicationPlannerConfig:
+    """DWDP/comms_planner/config.py:15-60 (the fields the planners read)."""
+
     planner_policy: str = "static"
     world_size: int = 1
     local_rank: int = 0
+    local_gpu_id: int | None = None  # None: the local rank
+    deterministic: bool = True
+    default_link_bandwidth_gbps: float = 0.0
+    default_link_latency_us: float = 0.0
+
+    def __post_init__(self) -> None:
+        if self.world_size <= 0:
+            raise ValueError("world_size must be > 0")
+        if not 0 <= self.local_rank < self.world_size:
+            raise ValueError("local_rank must satisfy 0 <= local_rank < world_size")
 
 
 @dataclass(frozen=True, slots=True)
@@ -156,6 +168,9 @@ class ExecutorConfig:
     scale_mode: int = _lib.SCALE_CHANNEL
     deterministic: bool = True
     materialize_packed_outputs: bool = False
+    # drive the grouped GEMMs from a TensorList built from the plans (tensor_list.py)
+    # instead of the store's per-expert pointer arrays; same kernels, same results
+    use_tensor_list: bool = False
 
 
 @dataclass(frozen=True, slots=True)
@@ -299,8 +314,29 @@ class B200RoundRobinScheduler(nn.Module):
                              num_active=r.num_active)
 
 
+def _planner_gpu(config) -> int:
+    g = getattr(config, "local_gpu_id", None)
+    return getattr(config, "local_rank", 0) if g is None else g
+
+
+def _empty_plan_parts(dev, config, *, world_size: int, fabric: str, domains: tuple, locality: tuple,
+                      connectivity=None):
+    from . import comms_metadata as cmd
+
+    e64 = torch.empty(0, device=dev, dtype=torch.int64)
+    topo = cmd.TopologyMetadata(
+        local_gpu_id=_planner_gpu(config), world_size=world_size, local_rank=getattr(config, "local_rank", 0),
+        gpu_ids=torch.arange(world_size, device=dev, dtype=torch.int64),
+        numa_domains=torch.zeros(world_size, device=dev, dtype=torch.int64), nvlink_connectivity=connectivity,
+        nvswitch_domains=None, pcie_hierarchy=None, communication_domains=domains, locality_groups=locality,
+        fabric=fabric, default_link_bandwidth_gbps=getattr(config, "default_link_bandwidth_gbps", 0.0),
+        default_link_latency_us=getattr(config, "default_link_latency_us", 0.0))
+    return e64, topo
+
+
 class StaticCommunicationPlanner(nn.Module):
-    """Every expert local (DWDP/comms_planner/static.py:37-110)."""
+    """Every expert local (DWDP/comms_planner/static.py:37-110): the full plan schema with no
+    descriptors, an empty graph and a zero cost model."""
 
     def __init__(self, config: CommunicationPlannerConfig | None = None) -> None:
         super().__init__()
@@ -308,44 +344,149 @@ class StaticCommunicationPlanner(nn.Module):
 
     def forward(self, execution_plan: ExecutionPlan, workspace=None,
                 num_experts: int | None = None) -> CommunicationPlan:
+        from . import comms_metadata as cmd
+        from . import cost_model as cm
+
         dev = execution_plan.expert_queue.device
         E = num_experts if num_experts is not None else execution_plan.expert_queue.numel()
-        return CommunicationPlan(local_expert_ids=torch.arange(E, device=dev, dtype=torch.int64),
-                                 remote_expert_ids=torch.empty(0, device=dev, dtype=torch.int64),
-                                 planner_policy=self.config.planner_policy)
+        G = getattr(self.config, "world_size", 1)
+        gpu = _planner_gpu(self.config)
+        e64, topo = _empty_plan_parts(
+            dev, self.config, world_size=G, fabric="single_gpu" if G == 1 else "unspecified",
+            domains=(cmd.CommunicationDomain(0, "local", (gpu,), getattr(self.config, "default_link_bandwidth_gbps", 0.0),
+                                             getattr(self.config, "default_link_latency_us", 0.0)),),
+            locality=((gpu,),))
+        f32 = torch.empty(0, device=dev, dtype=torch.float32)
+        local = torch.arange(E, device=dev, dtype=torch.int64)
+        policy = self.config.planner_policy
+        return CommunicationPlan(
+            local_expert_ids=local, remote_expert_ids=e64,
+            graph=cmd.CommunicationGraph((), (), e64, e64, e64), topology=topo,
+            synchronization=cmd.SynchronizationMetadata(e64, e64, e64, e64),
+            dependencies=cmd.DependencyMetadata(e64, e64, e64), prefetch=cmd.PrefetchPlan(e64, e64, f32),
+            overlap=cmd.OverlapPlan(e64, e64, f32),
+            cost_model=cm.CommunicationCostModel((), 0, 0.0, 0.0, 0.0),
+            statistics=cmd.CommunicationStatistics(E, 0, 0, 0, 0, 0, 0, 0.0, policy),
+            planner_policy=policy, deterministic=getattr(self.config, "deterministic", True))
+
+
+SLICE_BYTES = 2 * 1024 * 1024  # the reference's NVLink slice (expert_parallel.py:60, buffers.cu kSliceSize)
 
 
 class DWDPCommunicationPlanner(nn.Module):
-    """Experts sharded over the ranks by owner(e) = e // ceil(E / G) (the reference's
-    expert-parallel planner, DWDP/comms_planner/expert_parallel.py:120-122): the local rank's
-    experts stay local, every other one is prefetched. The plan's cost model is built from a
+    """DWDP weight-streaming plan (DWDP/comms_planner/expert_parallel.py:182-359): experts
+    sharded over the ranks by owner(e) = e // ceil(E / G) (:120-122); the local rank's experts
+    stay local, every other one is planned as 2 MiB slice descriptors whose start slice is
+    rotated by the local rank (slice (rank + i) % n first, so ranks reading one peer enter its
+    memory at different offsets), priority E - position among the remote experts, one group
+    per source GPU, and the prefetch list with those priorities. ``op_type`` is
+    ``p2p_weight_copy`` where the owner is peer-reachable, else ``staged_weight_copy``.
+
+    Where the reference fills its cost model with constants, the estimates here come from a
     measured ``LinkProfile`` (``cost_model.measure_link``) and the prefetch window the caller
-    expects (the previous layer's compute time), where the reference fills constants."""
+    expects (the previous layer's compute time); without one they carry the config's default
+    link figures like the reference's. ``bytes_per_expert`` is an int or a callable e -> bytes
+    (the reference reads it from its GlobalExpertTable; 0 = unknown gives one empty
+    descriptor per expert, as there). ``peer_access(src, dst)`` defaults to the driver's
+    peer-access query. ``slice_bytes = 0`` plans one descriptor per expert. Issue order is
+    the engine's TransferScheduler's (``CommunicationEngine.execute_plan``)."""
 
     def __init__(self, config: CommunicationPlannerConfig | None = None, *, link=None,
-                 bytes_per_expert: int = 0, prefetch_window_us: float = 0.0) -> None:
+                 bytes_per_expert=0, prefetch_window_us: float = 0.0, peer_access=None,
+                 slice_bytes: int = SLICE_BYTES) -> None:
         super().__init__()
         self.config = config or CommunicationPlannerConfig(planner_policy="dwdp")
         self.link = link
         self.bytes_per_expert = bytes_per_expert
         self.prefetch_window_us = prefetch_window_us
+        self.peer_access = peer_access
+        self.slice_bytes = int(slice_bytes)
+
+    def _expert_bytes(self, e: int) -> int:
+        b = self.bytes_per_expert
+        return int(b(e) if callable(b) else b)
+
+    def _can_access(self, src: int, dst: int) -> bool:
+        if src == dst:
+            return True
+        if self.peer_access is not None:
+            return bool(self.peer_access(src, dst))
+        try:
+            from .communication import PeerTopology
+
+            return PeerTopology().can_access(src, dst)
+        except Exception:  # no driver here: treat the peer as unreachable (staged copy)
+            return False
 
     def forward(self, execution_plan: ExecutionPlan, workspace=None,
                 num_experts: int | None = None) -> CommunicationPlan:
+        from . import comms_metadata as cmd
         from . import cost_model as cm
         from .dwdp import owner_of
 
+        cfg = self.config
         dev = execution_plan.expert_queue.device
         E = num_experts if num_experts is not None else execution_plan.expert_queue.numel()
-        G, r = self.config.world_size, self.config.local_rank
-        local = [e for e in range(E) if owner_of(e, E, G) == r]
-        remote = [e for e in range(E) if owner_of(e, E, G) != r]
-        model = (cm.build_cost_model(remote, self.bytes_per_expert, self.link,
-                                     prefetch_window_us=self.prefetch_window_us)
-                 if self.link is not None and remote else None)
-        return CommunicationPlan(local_expert_ids=torch.tensor(local, device=dev, dtype=torch.int64),
-                                 remote_expert_ids=torch.tensor(remote, device=dev, dtype=torch.int64),
-                                 planner_policy=self.config.planner_policy, cost_model=model)
+        G, r = cfg.world_size, cfg.local_rank
+        gpu = _planner_gpu(cfg)
+        owners = [owner_of(e, E, G) for e in range(E)]
+        local = [e for e in range(E) if owners[e] == r]
+        remote = [e for e in range(E) if owners[e] != r]
+        bw = getattr(cfg, "default_link_bandwidth_gbps", 0.0)
+        lat = getattr(cfg, "default_link_latency_us", 0.0)
+        descs, transfers, pf_ids, pf_prio = [], [], [], []
+        for position, e in enumerate(remote):
+            owner, size = owners[e], self._expert_bytes(e)
+            step = self.slice_bytes if self.slice_bytes > 0 else max(size, 1)
+            n = max(1, -(-size // step))
+            op = "p2p_weight_copy" if self._can_access(owner, gpu) else "staged_weight_copy"
+            prio = E - position
+            for i in range(n):
+                off = ((r + i) % n) * step
+                nb = min(step, size - off) if size else 0
+                d = len(descs)
+                descs.append(cmd.CommunicationDescriptor(d, op, owner, gpu, e, e, off, off + nb, nb, prio, 1))
+                transfers.append(cmd.TransferDescriptor(d, d, owner, gpu, e, e, nb, prio))
+            pf_ids.append(e)
+            pf_prio.append(prio)
+        if self.link is not None:
+            model = cm.build_descriptor_cost_model(descs, self.link, prefetch_window_us=self.prefetch_window_us)
+        else:  # the reference's constant-filled model (expert_parallel.py:248-260, 298-304)
+            model = cm.CommunicationCostModel(
+                estimates=tuple(cm.CommunicationCostEstimate(d.descriptor_id, d.count, lat, bw, d.priority,
+                                                             0.0, 0.0, 0.0, 0.0) for d in descs),
+                total_estimated_bytes=sum(d.count for d in descs), total_estimated_latency_us=0.0,
+                critical_path_us=0.0, estimated_bandwidth_gbps=bw)
+        i64 = lambda v: torch.tensor(v, device=dev, dtype=torch.int64)  # noqa: E731
+        groups = tuple(cmd.CommunicationGroup(gi, i64([d.descriptor_id for d in descs if d.source_gpu == src]),
+                                              src, gpu, 0, 0)
+                       for gi, src in enumerate(sorted({d.source_gpu for d in descs})))
+        peers = tuple(g for g in range(G) if self._can_access(g, gpu))
+        conn = torch.zeros(G, G, device=dev, dtype=torch.int64)
+        for s_ in range(G):
+            for d_ in range(G):
+                if self._can_access(s_, d_):
+                    conn[d_, s_] = 1
+        e64, topo = _empty_plan_parts(
+            dev, cfg, world_size=G, fabric="nvlink" if G > 1 else "single_gpu",
+            domains=(cmd.CommunicationDomain(0, "nvlink" if len(peers) > 1 else "local", peers or (gpu,), bw, lat),),
+            locality=(peers or (gpu,),), connectivity=conn)
+        node_ids = i64([d.descriptor_id for d in descs])
+        f32 = torch.empty(0, device=dev, dtype=torch.float32)
+        policy = cfg.planner_policy
+        return CommunicationPlan(
+            local_expert_ids=i64(local), remote_expert_ids=i64(remote),
+            graph=cmd.CommunicationGraph((), (), node_ids, e64, e64),
+            communication_descriptors=tuple(descs), transfer_descriptors=tuple(transfers),
+            communication_groups=groups, topology=topo,
+            synchronization=cmd.SynchronizationMetadata(node_ids, e64, e64, e64),
+            dependencies=cmd.DependencyMetadata(e64, e64, e64),
+            prefetch=cmd.PrefetchPlan(i64(pf_ids), i64(pf_prio), f32),
+            overlap=cmd.OverlapPlan(node_ids, e64, f32), cost_model=model,
+            statistics=cmd.CommunicationStatistics(
+                len(local), len(remote), len(descs), 0, len(transfers), len(groups), model.total_estimated_bytes,
+                model.total_estimated_latency_us, policy),
+            planner_policy=policy, deterministic=getattr(cfg, "deterministic", True))
 
 
 # ----------------------------------------------------------------------------- executor
@@ -383,7 +524,8 @@ class B200Executor(nn.Module):
             for e, (g, u, d) in enumerate(ws):
                 self.store.load_expert(e, g, u, d)
         self._group = self.store.group()
-        self._ws: dict[tuple[int, int], torch.Tensor] = {}
+        self._ws: dict[tuple, torch.Tensor] = {}
+        self._tl_ws = None
 
     def forward(self, hidden_states: torch.Tensor, dispatch_plan: DispatchPlan, execution_plan: ExecutionPlan,
                 communication_plan: CommunicationPlan | None = None, workspace=None) -> ExecutorOutput:
@@ -405,9 +547,23 @@ class B200Executor(nn.Module):
         if w.dtype != torch.float32:
             w = w.float()
         weighted = torch.empty(md.num_assignments, H, dtype=torch.bfloat16, device=x.device)
-        ops.moe_experts(self._group, None, packed, x, K, md.expert_counts, md.expert_offsets, w, None,
-                        weighted, None, self._ws[key],
-                        packed_token_indices=dispatch_plan.assignments.packed_token_indices)
+        if getattr(self.config, "use_tensor_list", False):
+            from .tensor_list import TensorList, TensorListWorkspace, grouped_moe
+
+            if self._tl_ws is None:
+                self._tl_ws = TensorListWorkspace(x.device)
+            tl = TensorList.from_plans(x, dispatch_plan, execution_plan, self._tl_ws, self.store, None, weighted,
+                                       None, sync=False)
+            tkey = ("tl", T, K, tl.capacity)
+            if tkey not in self._ws:
+                self._ws[tkey] = torch.empty(ops.moe_workspace_bytes(T, K, tl.capacity,
+                                                                     self.store.intermediate_size, 0),
+                                             dtype=torch.uint8, device=x.device)
+            grouped_moe(tl, x, dispatch_plan, weighted, self._ws[tkey], top_k=K)
+        else:
+            ops.moe_experts(self._group, None, packed, x, K, md.expert_counts, md.expert_offsets, w, None,
+                            weighted, None, self._ws[key],
+                            packed_token_indices=dispatch_plan.assignments.packed_token_indices)
         asg = dispatch_plan.assignments
         counts, E = md.expert_counts, self.store.num_experts
 

@@ -286,6 +286,90 @@ int dwdp_moe_shared_expert(const dwdp_expert_group* shared, const void* hidden, 
                            int* status, void* stream);
 
 /* ======================================================================== *
+ * TensorList (DWDP/executor/tensor_list.py:29-228): the non-owning
+ * structure-of-arrays descriptor of the active experts. `fields` is one device
+ * int64 buffer of DWDP_TL_ROWS rows x `capacity` entries; rows 0..25 are the
+ * reference's fields in its order (tensor_list.py:201-228), row 26 holds the
+ * down-projection scale address (the reference has one quantization_ptrs row,
+ * left 0, tensor_list.py:160; here quantization_ptrs is the gate/up scale
+ * address). Entries past the active count are empty (count 0, null pointers,
+ * expert id -1), so a launch over all `capacity` entries needs no host count.
+ * gate_weight_ptrs and up_weight_ptrs name the same packed gate/up slab.
+ * ======================================================================== */
+#define DWDP_TL_INPUT_PTRS 0
+#define DWDP_TL_TOKEN_INDEX_PTRS 1
+#define DWDP_TL_ROUTING_WEIGHT_PTRS 2
+#define DWDP_TL_GATE_WEIGHT_PTRS 3
+#define DWDP_TL_UP_WEIGHT_PTRS 4
+#define DWDP_TL_DOWN_WEIGHT_PTRS 5
+#define DWDP_TL_INTERMEDIATE_PTRS 6
+#define DWDP_TL_OUTPUT_PTRS 7
+#define DWDP_TL_WEIGHTED_OUTPUT_PTRS 8
+#define DWDP_TL_QUANTIZATION_PTRS 9
+#define DWDP_TL_EXPERT_IDS 10
+#define DWDP_TL_TOKEN_OFFSETS 11
+#define DWDP_TL_TOKEN_COUNTS 12
+#define DWDP_TL_M 13
+#define DWDP_TL_N 14
+#define DWDP_TL_K 15
+#define DWDP_TL_INTERMEDIATE_N 16
+#define DWDP_TL_INPUT_LD 17
+#define DWDP_TL_GATE_LD 18
+#define DWDP_TL_UP_LD 19
+#define DWDP_TL_DOWN_LD 20
+#define DWDP_TL_OUTPUT_LD 21
+#define DWDP_TL_DTYPE_CODES 22
+#define DWDP_TL_WORKSPACE_INDICES 23
+#define DWDP_TL_EXECUTION_PRIORITIES 24
+#define DWDP_TL_STREAM_IDS 25
+#define DWDP_TL_DOWN_QUANTIZATION_PTRS 26
+#define DWDP_TL_ROWS 27
+
+/* Storage the pointer fields describe (the same for every entry, row-offset by
+ * the entry's token_offsets): what TensorList.from_plans reads off its tensors. */
+typedef struct dwdp_tensor_list_bases {
+  const void* input;            /* hidden_states [T, H]                       */
+  const void* token_index;      /* packed_token_indices [N] int64             */
+  const void* routing_weights;  /* packed_routing_weights [N]                 */
+  const void* intermediate;     /* [N, intermediate_n] or NULL                */
+  const void* output;           /* packed outputs [N, n] or NULL              */
+  const void* weighted_output;  /* weighted outputs [N, n] or NULL            */
+  int64_t intermediate_row_bytes, output_row_bytes, weighted_row_bytes;
+  int64_t n, k, intermediate_n, input_ld, gate_ld, up_ld, down_ld, output_ld, dtype_code;
+} dwdp_tensor_list_bases;
+
+typedef struct dwdp_tensor_list {
+  int64_t capacity;        /* entries per field row (<= 1024)                */
+  int64_t* fields;         /* device [DWDP_TL_ROWS][capacity] int64          */
+  int hidden_size, intermediate_size, weight_dtype, scale_mode, act_quant;
+} dwdp_tensor_list;
+
+/* Fill `tl->fields` from an execution plan (expert_queue / expert_starts /
+ * expert_counts / execution_priority / stream_assignments of plan_len rows;
+ * priorities and streams may be NULL) and the experts' pointer arrays
+ * (TensorList.from_plans, tensor_list.py:69-198): rows with expert id >= 0 and
+ * count > 0 are compacted in plan order. meta[0] = active entries, meta[1] =
+ * the largest token count (device int64[2]). One launch, no host sync. Plan
+ * rows beyond capacity: DWDP_ERR_CAPACITY in *status. */
+int dwdp_tensor_list_build(const int64_t* expert_queue, const int64_t* expert_starts,
+                           const int64_t* expert_counts, const int64_t* priorities, const int64_t* stream_ids,
+                           int plan_len, const dwdp_expert_group* experts, const dwdp_tensor_list_bases* bases,
+                           const dwdp_tensor_list* tl, int64_t* meta, int* status, void* stream);
+
+/* The grouped expert GEMMs driven by a TensorList (the dwdp_grouped_moe entry
+ * the reference's persistent Triton executors correspond to,
+ * executor/kernels/persistent.py:160-226): every entry i with token_counts[i] > 0
+ * computes weighted_out[r] = w[r] * down(silu(gate(x_r)) * up(x_r)) for its rows
+ * r in [token_offsets[i], token_offsets[i] + token_counts[i]), x_r =
+ * hidden[packed_token_indices[r]], reading its weights from the entry's pointer
+ * fields. `shared` and the rest as dwdp_moe_experts_indexed; the workspace is
+ * dwdp_moe_workspace_bytes(num_tokens, top_k, tl->capacity, I, Is). */
+int dwdp_grouped_moe(const dwdp_tensor_list* tl, const dwdp_expert_group* shared,
+                     const int64_t* packed_token_indices, const void* hidden, int64_t num_tokens, int top_k,
+                     const float* packed_weights, const float* shared_gate, void* weighted_out,
+                     void* shared_out, void* workspace, size_t workspace_bytes, int* status, void* stream);
+
+/* ======================================================================== *
  * Merge (reference_merge, merger/kernels/reference.py:6-27): deterministic
  * token-major reduction. out[t] = sum over the K rows inv[t*K+k] of
  * weighted[row] taken in ascending row order, plus shared_out[p][t] for
@@ -401,6 +485,23 @@ int dwdp_engine_register_peer(dwdp_engine* engine, int expert_id, const void* pe
  * after_stream is given the copies start after the work already queued on it. */
 int dwdp_engine_prefetch(dwdp_engine* engine, const int* expert_ids, int n, int buffer,
                          void* after_stream);
+/* One planned copy of a communication plan (the reference's CommunicationDescriptor,
+ * DWDP/comms_planner/metadata.py:12-26): bytes [start, start + bytes) of the expert's
+ * slab into the same offsets of its staging slot. */
+typedef struct dwdp_copy_slice {
+  int expert_id;
+  int reserved;
+  uint64_t start;
+  uint64_t bytes;
+} dwdp_copy_slice;
+/* Execute a plan's descriptors into `buffer` in the given order (the reference's sliced
+ * copyToNextAsync, communication/buffers.cu:94-134, with the slice order the planner and
+ * the TransferScheduler chose): copy k runs on copy stream k % streams, or all of them in
+ * SM copy kernels in DWDP_COPY_SM mode; slices of local experts are skipped; one event
+ * marks the buffer ready for dwdp_engine_wait. A slice beyond its expert's bytes:
+ * DWDP_ERR_INVALID_ARGUMENT, an unregistered expert: DWDP_ERR_NOT_FOUND (nothing issued). */
+int dwdp_engine_prefetch_slices(dwdp_engine* engine, const dwdp_copy_slice* slices, int n, int buffer,
+                                void* after_stream);
 int dwdp_engine_wait(dwdp_engine* engine, int buffer, void* stream);
 int dwdp_engine_resident_pointer(dwdp_engine* engine, int expert_id, int buffer, void** out);
 int dwdp_engine_is_remote(dwdp_engine* engine, int expert_id, int* out);

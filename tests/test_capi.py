@@ -87,6 +87,27 @@ def test_moe_and_merge_validation_errors(pkg):
     assert rc == pkg._lib.DWDP_ERR_INVALID_ARGUMENT and "multiples of 128" in pkg._lib.last_error()
 
 
+def test_tensor_list_validation_errors(pkg):
+    import ctypes
+
+    L = pkg._lib
+    lib = L.load()
+    g = L.ExpertGroup(num_experts=8, hidden_size=256, intermediate_size=256, weight_dtype=L.DTYPE_FP8_E4M3,
+                      scale_mode=L.SCALE_CHANNEL)
+    b = L.TensorListBases()
+    h = L.TensorListHandle(capacity=2048, fields=1)
+    rc = lib.dwdp_tensor_list_build(1, 1, 1, None, None, 8, ctypes.byref(g), ctypes.byref(b), ctypes.byref(h), 1,
+                                    None, None)
+    assert rc == L.DWDP_ERR_INVALID_ARGUMENT and "capacity" in L.last_error()
+    h.capacity = 8
+    rc = lib.dwdp_tensor_list_build(None, None, None, None, None, 8, ctypes.byref(g), ctypes.byref(b),
+                                    ctypes.byref(h), 1, None, None)
+    assert rc == L.DWDP_ERR_INVALID_ARGUMENT and "plan rows" in L.last_error()
+    h.capacity = 0
+    rc = lib.dwdp_grouped_moe(ctypes.byref(h), None, 1, 1, 4, 2, 1, None, 1, None, 1, 16, None, None)
+    assert rc == L.DWDP_ERR_INVALID_ARGUMENT and "TensorList" in L.last_error()
+
+
 def test_ops_refuse_cpu_tensors(pkg):
     import torch
     with pytest.raises(RuntimeError, match="no CPU fallback"):

@@ -4,6 +4,7 @@ import os
 import socket
 
 import pytest
+import torch
 import torch.multiprocessing as mp
 
 
@@ -157,3 +158,24 @@ def test_engine_reference_surface_bookkeeping(pkg):
         eng.register_peer_expert(4, 0x2000, 2 << 20, 1)
     with pytest.raises(RuntimeError):
         eng.wait(5)  # never prefetched
+
+
+def test_engine_issue_order_follows_the_scheduler(pkg):
+    """The engine issues a plan's slices expert by expert in the TransferScheduler's order
+    (priority, highest first), each expert's slices in the planner's rotated order."""
+    st = pkg.stages
+    E, G, rank = 16, 4, 2
+    sizes = [(3 << 20) + e for e in range(E)]
+    plan = st.DWDPCommunicationPlanner(st.CommunicationPlannerConfig("dwdp", G, rank),
+                                       bytes_per_expert=lambda e: sizes[e], peer_access=lambda s, d: True)(
+        type("EP", (), {"expert_queue": torch.zeros(E, dtype=torch.int64)})())
+    order = pkg.communication.CommunicationEngine(0).issue_order(plan)
+    assert sorted(d.descriptor_id for d in order) == list(range(len(plan.communication_descriptors)))
+    experts = []
+    for d in order:
+        if not experts or experts[-1] != d.source_expert_id:
+            experts.append(d.source_expert_id)
+    assert experts == plan.remote_expert_ids.tolist()  # priority E - position: ascending remote ids
+    first = [d for d in order if d.source_expert_id == experts[0]]
+    assert first[0].start == (rank % len(first)) * (2 << 20)  # rotated start slice
+    assert sum(d.count for d in first) == sizes[experts[0]]

@@ -145,3 +145,45 @@ def test_engine_sm_copy_mode_single_gpu(pkg):
         with pytest.raises(ValueError):
             eng.set_copy_mode("dma")
         eng.shutdown()
+
+
+@pytest.mark.parametrize("mode", ["engine", "sm"])
+def test_engine_executes_the_planners_slices_single_gpu(pkg, mode):
+    """The DWDP planner's plan (2 MiB slices, rotated start slice, priorities) executed by the
+    engine in the TransferScheduler's order stages every remote expert's bytes exactly; the
+    remote owners are same-device buffers standing in for peers."""
+    st = pkg.stages
+    dev = torch.device("cuda", 0)
+    E, G, rank = 12, 4, 1
+    sizes = [(5 << 20) + 4096 * e for e in range(E)]  # ragged: three slices, the last one short
+    srcs = [((torch.arange(n, dtype=torch.int64, device=dev) * (e + 3) + e) % 251).to(torch.uint8)
+            for e, n in enumerate(sizes)]
+    planner = st.DWDPCommunicationPlanner(st.CommunicationPlannerConfig("dwdp", G, rank),
+                                          bytes_per_expert=lambda e: sizes[e], peer_access=lambda s, d: True)
+    plan = planner(type("EP", (), {"expert_queue": torch.zeros(E, dtype=torch.int64, device=dev)})())
+    assert {d.count for d in plan.communication_descriptors} >= {2 << 20}
+    eng = pkg.communication.CommunicationEngine(0)
+    eng.initialize(max(sizes), len(plan.remote_expert_ids), 2)
+    owners = {e: min(e // -(-E // G), G - 1) for e in range(E)}
+    for e in range(E):
+        if owners[e] == rank:
+            eng.register_expert(e, srcs[e].data_ptr(), sizes[e])
+        else:
+            eng.register_peer_expert(e, srcs[e].data_ptr(), sizes[e], 0)
+    if mode == "sm":
+        eng.set_copy_mode("sm", 16)
+    import ctypes
+
+    order = eng.execute_plan(plan, buffer=1)
+    prios = [d.priority for d in order]
+    assert prios == sorted(prios, reverse=True)  # highest priority first
+    eng.wait_buffer(1)
+    torch.cuda.synchronize()
+    for e in plan.remote_expert_ids.tolist():
+        ptr = eng.get_resident_pointer(e, buffer=1)
+        got = torch.empty(sizes[e], dtype=torch.uint8, device=dev)
+        cudart = ctypes.CDLL("libcudart.so.12")
+        assert cudart.cudaMemcpy(ctypes.c_void_p(got.data_ptr()), ctypes.c_void_p(ptr), ctypes.c_size_t(sizes[e]),
+                                 3) == 0
+        assert torch.equal(got, srcs[e]), f"expert {e}"
+    eng.shutdown()
