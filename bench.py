@@ -432,6 +432,96 @@ def run_reference_cpu(T: int, L: int, steps: int, warmup: int, budget_s: float) 
             "seconds_per_step": med, "timed_steps": n}
 
 
+# ----------------------------------------------------------------------------- reference arm (GPU, same box)
+REF_GPU_BACKENDS = ("triton", "triton_fp8_tma")
+
+
+def run_reference_gpu(Ts: list[int], steps: int, warmup: int, device) -> dict:
+    """The reference's OWN Triton executors on this B200 (the same-box GPU comparison): one
+    Qwen-shaped layer through DWDPRuntime (router -> expert_major dispatcher with the
+    'triton_counting_scatter' algorithm -> round-robin -> static planner -> executor
+    'triton' (its persistent kernels, FP8-cast weights) or 'triton_fp8_tma' (block-scaled FP8
+    with TMA) -> PyTorch merger) plus the adapter's shared expert in bf16, JIT-compiled by
+    Triton for sm_100. CUDA-event time per layer after `warmup` untimed calls, median of
+    `steps`; L2 is not flushed (the layer's weights exceed it). Loads nothing of this
+    repository's package or library."""
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    from DWDP.dispatcher.config import DispatcherConfig
+    from DWDP.dispatcher.registry import build_dispatcher
+    from DWDP.router.config import MetadataLevel, RouterConfig
+    from DWDP.router.registry import build_router
+    from DWDP.runtime.config import RuntimeConfig
+    from DWDP.runtime.runtime import DWDPRuntime
+
+    H, E, I, K, Is = QWEN["H"], QWEN["E"], QWEN["I"], QWEN["K"], QWEN["Is"]
+    g = torch.Generator(device=device).manual_seed(1235)
+
+    def fp8_channel(shape):  # weights ~ N(0, 0.02) through per-output-channel e4m3, as bf16
+        w = torch.randn(shape, generator=g, device=device) * 0.02
+        s = w.abs().amax(dim=1, keepdim=True).clamp_min(1e-5) / 448.0
+        return ((w / s).to(torch.float8_e4m3fn).float() * s).bfloat16()
+
+    class QwenSwiGLUExpert(torch.nn.Module):
+        def __init__(self, hidden, inter):
+            super().__init__()
+            self.gate_proj = torch.nn.Linear(hidden, inter, bias=False, dtype=torch.bfloat16, device=device)
+            self.up_proj = torch.nn.Linear(hidden, inter, bias=False, dtype=torch.bfloat16, device=device)
+            self.down_proj = torch.nn.Linear(inter, hidden, bias=False, dtype=torch.bfloat16, device=device)
+            with torch.no_grad():
+                for lin in (self.gate_proj, self.up_proj, self.down_proj):
+                    lin.weight.copy_(fp8_channel(lin.weight.shape))
+
+        def forward(self, x):
+            return self.down_proj(torch.nn.functional.silu(self.gate_proj(x)) * self.up_proj(x))
+
+    out = {"workload": "reference_gpu", "model": "Qwen1.5-MoE-A2.7B (shape), one layer", "device": torch.cuda.get_device_name(device),
+           "timing": f"CUDA events, median of {steps} after {warmup} untimed", "results": {},
+           "versions": {"torch": torch.__version__, "triton": __import__("triton").__version__}}
+    for backend in REF_GPU_BACKENDS:
+        res = {}
+        try:
+            router = build_router(RouterConfig(hidden_size=H, num_experts=E, top_k=K,
+                                               metadata_level=MetadataLevel.COUNTS)).to(device)
+            with torch.no_grad():
+                router.weight.copy_(torch.randn(E, H, generator=g, device=device) / H**0.5)
+            router.to(torch.bfloat16)
+            experts = [QwenSwiGLUExpert(H, I) for _ in range(E)]
+            rt = DWDPRuntime.build_reference(hidden_size=H, num_experts=E, top_k=K, experts=experts, router=router,
+                                             config=RuntimeConfig(device=str(device), executor_backend=backend))
+            rt.dispatcher = build_dispatcher(DispatcherConfig(num_experts=E, algorithm="triton_counting_scatter",
+                                                              validate_inputs=False))
+            shared = QwenSwiGLUExpert(H, Is)
+            gate = (torch.randn(H, generator=g, device=device) * 0.02).bfloat16()
+
+            def layer(x):
+                routed = rt(x).hidden_states
+                return routed + torch.sigmoid(x @ gate.unsqueeze(-1)) * shared(x)
+
+            for T in Ts:
+                x = torch.randn(T, H, generator=g, device=device).bfloat16()
+                with torch.inference_mode():
+                    for _ in range(max(1, warmup)):
+                        layer(x)
+                    torch.cuda.synchronize(device)
+                    ts = []
+                    for _ in range(steps):
+                        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        a.record()
+                        layer(x)
+                        b.record()
+                        b.synchronize()
+                        ts.append(a.elapsed_time(b) * 1e3)
+                us = statistics.median(ts)
+                res[str(T)] = {"layer_us": us, "tokens_per_s": T / (us * 1e-6)}
+            del rt, experts, shared
+            torch.cuda.empty_cache()
+        except Exception as exc:  # noqa: BLE001 - report, do not hide, a reference backend that fails
+            res["error"] = f"{type(exc).__name__}: {str(exc)[:1500]}"
+        out["results"][backend] = res
+    return out
+
+
 # ----------------------------------------------------------------------------- layer stack (headline)
 class LayerStack:
     """L Qwen-shaped MoE layers with distinct weights, chained (layer l's output
@@ -841,7 +931,7 @@ def main() -> None:
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=256)
     ap.add_argument("--workload", default="moe_layers",
-                    choices=["moe_layers", "decode_step", "attention", "mixtral", "deepseek", "layer"])
+                    choices=["moe_layers", "decode_step", "attention", "mixtral", "deepseek", "layer", "reference_gpu"])
     ap.add_argument("--activation", default=None, choices=["hilo", "block128"],
                     help="activation mode of --workload layer (default: the headline's)")
     ap.add_argument("--batch", default="1,8,64", help="decode_step batch sizes")
@@ -886,6 +976,18 @@ def main() -> None:
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }), flush=True)
+        return
+
+    if args.workload == "reference_gpu":
+        # the reference's own Triton executors on this GPU, in a process that loads nothing of
+        # this repository's package (compare with `--workload layer` / the headline's per-layer time)
+        if rank == 0:
+            dev = torch.device("cuda", local)
+            torch.cuda.set_device(dev)
+            why = reference_available()
+            print(json.dumps({"workload": "reference_gpu", "unavailable": why} if why else
+                             run_reference_gpu([int(t) for t in args.batch.split(",")], args.steps, args.warmup, dev)),
+                  flush=True)
         return
 
     import __graft_entry__
