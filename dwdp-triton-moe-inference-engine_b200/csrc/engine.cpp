@@ -407,18 +407,30 @@ extern "C" int dwdp_engine_prefetch(dwdp_engine* eng, const int* expert_ids, int
     if (it == eng->experts.end()) return fail(DWDP_ERR_NOT_FOUND, "prefetch: unknown expert " + std::to_string(expert_ids[i]));
     if (it->second.remote) todo.push_back(&it->second);
   }
-  // Copies start at a device-dependent expert so that ranks do not all read the same peer
-  // first. With DWDP_PREFETCH_SLICE_MB = s > 0 every expert moves as s-MiB slices dealt
-  // round-robin over the copy streams (the reference's 2 MiB slices, buffers.cu:94-134);
-  // by default each expert is one copy (SM copies always move whole experts).
+  // Issue order: the owners are interleaved (one expert of each owner in turn) and every
+  // rank starts with the owner after itself, so consecutive copies (which run side by side
+  // on the copy streams) read different peers and the G ranks start on G different peers
+  // instead of all reading the first owner's memory at once. With DWDP_PREFETCH_SLICE_MB =
+  // s > 0 every expert moves as s-MiB slices dealt round-robin over the copy streams (the
+  // reference's 2 MiB slices, buffers.cu:94-134); by default each expert is one copy (SM
+  // copies always move whole experts).
   static const size_t slice = [] {
     const char* v = getenv("DWDP_PREFETCH_SLICE_MB");
     return v != nullptr ? (size_t)atoi(v) << 20 : (size_t)0;
   }();
-  const size_t rot = todo.empty() ? 0 : (size_t)eng->device % todo.size();  // spread peer load across ranks
+  std::map<int, std::vector<const EngineExpert*>> by_owner;  // ascending expert id per owner
+  for (const EngineExpert* x : todo) by_owner[x->owner_device].push_back(x);
+  std::vector<const std::vector<const EngineExpert*>*> owners;
+  for (auto it = by_owner.upper_bound(eng->device); it != by_owner.end(); ++it) owners.push_back(&it->second);
+  for (auto it = by_owner.begin(); it != by_owner.end() && it->first <= eng->device; ++it) owners.push_back(&it->second);
+  std::vector<const EngineExpert*> order;
+  order.reserve(todo.size());
+  for (size_t i = 0; order.size() < todo.size(); ++i)
+    for (const auto* lst : owners)
+      if (i < lst->size()) order.push_back((*lst)[i]);
   std::vector<PlannedCopy> copies;
-  for (size_t j = 0; j < todo.size(); ++j) {
-    const EngineExpert* x = todo[(j + rot) % todo.size()];
+  for (size_t j = 0; j < order.size(); ++j) {
+    const EngineExpert* x = order[j];
     char* dst = staging_slot(eng, x, buffer);
     const char* src = static_cast<const char*>(x->src);
     const size_t step = (slice > 0 && eng->copy_mode != DWDP_COPY_SM) ? slice : x->bytes;
