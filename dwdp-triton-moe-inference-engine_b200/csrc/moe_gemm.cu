@@ -552,6 +552,335 @@ moe_gemm_f8_kernel(const __grid_constant__ GemmParams p) {
 }
 
 // ---------------------------------------------------------------------------
+// CTA-pair (cta_group::2) primitives for moe_gemm_f8x2_kernel. Every tcgen05
+// instruction of that kernel uses cta_group::2; none issues a multicast load.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive on the mbarrier at the same shared-memory offset in CTA `cta` of the cluster. The
+// waiter polls with the usual CTA-scope acquire (as for any barrier): the data the phase
+// announces is read by the tensor core through the async proxy, not by the waiting thread.
+__device__ __forceinline__ void mbar_arrive_remote(uint64_t* bar, uint32_t cta) {
+  asm volatile(
+      "{\n\t.reg .b32 ra;\n\t"
+      "mapa.shared::cluster.u32 ra, %0, %1;\n\t"
+      "mbarrier.arrive.shared::cluster.b64 _, [ra];\n\t}" ::"r"(smem_u32(bar)),
+      "r"(cta)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc2(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish2() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem] (+)= A * B^T over the CTA pair: A = 128 rows in each CTA's shared memory
+// (M = 256), B = N / 2 rows in each CTA's shared memory, same offsets in both CTAs.
+__device__ __forceinline__ void mma2_e4m3_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+// Arrive once on the mbarrier at the same offset in every CTA of `mask` when the pair's
+// previously issued MMAs complete.
+__device__ __forceinline__ void mma2_commit_mc(uint64_t* bar, uint16_t mask) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                   smem_u32(bar)),
+               "h"(mask)
+               : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// e4m3 hi/lo GEMMs on a CTA pair (cta_group::2), for prefill-sized batches.
+//
+// A single CTA feeds 48 KB per 128-input stage (two 16 KB weight tiles + a 16 KB
+// hi/lo activation tile for 64 tokens); with the MMAs running, an SM's bulk-copy
+// fill rate caps that at ~840 cycles per stage against the MMAs' 512. Here two
+// SMs share one 256 x 256 MMA per 32 inputs, orientation tokens x features:
+//   A (M = 256): the activation planes of up to 128 tokens, 64 per CTA (rows
+//                2t = hi, 2t + 1 = lo of token t), 16 KB per CTA per stage;
+//   B (N = 256): MODE 0 gate rows (CTA 0) | up rows (CTA 1) of one 128-feature
+//                block; MODE 1 two consecutive 128-row down blocks; 16 KB per CTA.
+// So each SM moves 32 KB per stage for the same MMA work, and a 7-deep ring fits.
+// Each CTA's TMEM holds its 128 plane rows x 256 columns (double-buffered). The
+// leader (rank 0) issues the MMAs once both CTAs' stage is loaded (the peer's
+// MMA-issue thread relays its local barrier phases to the leader) and its
+// commits arrive on both CTAs' barriers. Epilogue: lane pairs (hi, lo) swap
+// halves so every lane forms 16 features of one token, then 32-byte stores.
+// ---------------------------------------------------------------------------
+#ifndef DWDP_X2_DIAG
+#define DWDP_X2_DIAG 0  // diagnostic builds only: 1 = no epilogue math (wrong results, timing only)
+#endif
+template <int MODE>
+struct CfgX2 {
+  static constexpr int A_TILE = 128 * BK8;  // 64 tokens x 2 planes x 128 inputs
+  static constexpr int B_TILE = kW8TileBytes;  // 128 weight rows x 128 inputs
+  static constexpr int STAGE = A_TILE + B_TILE;
+  static constexpr int S = 7;
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int EPI_THREADS = EPI_WARPS * 32;
+  static constexpr int THREADS = (2 + EPI_WARPS) * 32;
+  static constexpr int ACC_COLS = 256;
+  static constexpr int SMEM_BYTES = S * STAGE + 1024 + 512;
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(CfgX2<MODE>::THREADS, 1) moe_gemm_f8x2_kernel(const __grid_constant__ GemmParams p) {
+  using C = CfgX2<MODE>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::S * C::A_TILE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::S * C::STAGE);
+  uint64_t* full = bars;               // local loads of stage s landed
+  uint64_t* empty = full + C::S;       // the pair's MMAs read stage s (leader commit, both CTAs)
+  uint64_t* peer_full = empty + C::S;  // leader only: the peer's stage s landed
+  uint64_t* acc_full = peer_full + C::S;  // accumulator a ready (leader commit, both CTAs)
+  uint64_t* acc_empty = acc_full + 2;     // this CTA's epilogue drained accumulator a
+  uint64_t* peer_acc_empty = acc_empty + 2;  // leader only: the peer's epilogue drained a
+  __shared__ uint32_t s_tmem_base;
+  __shared__ volatile int s_abort;
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const uint32_t rank = cluster_rank();
+  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+  DeviceStatus* st = p.st;
+  griddep_launch();
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int i = 0; i < C::S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+      mbar_init(&peer_full[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], C::EPI_THREADS);
+      mbar_init(&peer_acc_empty[i], 1);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc2(&s_tmem_base, 2 * C::ACC_COLS);
+    tmem_relinquish2();
+  }
+  if (warp == 0 && lane == 0) {
+    if (p.g[0].enabled) prefetch_tmap(&p.g[0].tmap_b);
+    if (p.g[1].enabled) prefetch_tmap(&p.g[1].tmap_b);
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated in both
+  tc_fence_after();
+  const uint32_t tmem_base = s_tmem_base;
+  griddep_wait();
+  const int n_items = *p.n_items;
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (each CTA its halves)
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int item = cid; item < n_items && !s_abort; item += ncl) {
+        const WorkItem wi = p.items[item];
+        const GroupParams& g = p.g[wi.group];
+        const int h = min(64, (wi.nrows + 1) >> 1);  // tokens of CTA 0; CTA 1 takes the rest
+        const int tok0 = wi.row0 + (int)rank * h;
+        const uint8_t* wsrc = wi.wtiles + (size_t)rank * g.mstride;
+        for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
+          const int s = it % C::S;
+          if (!mbar_wait(&empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 61 + 8 * MODE)) break;
+          mbar_arrive_expect_tx(&full[s], (uint32_t)C::STAGE);
+          bulk_g2s(sB + s * C::B_TILE, wsrc + (size_t)kb * g.kstride, C::B_TILE, &full[s]);
+          tma_load_2d(sA + s * C::A_TILE, &g.tmap_b, kb * BK8, 2 * tok0, &full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ------------------------------------------------------------ MMA issuer (leader)
+      uint32_t it = 0;
+      int li = 0;
+      const uint32_t idesc = idesc_e4m3(256, 256);
+      for (int item = cid; item < n_items && !s_abort; item += ncl, ++li) {
+        const WorkItem wi = p.items[item];
+        const int a = li & 1;
+        const uint32_t par = ((li >> 1) & 1) ^ 1;
+        if (!mbar_wait(&acc_empty[a], par, &s_abort, st, 62 + 8 * MODE)) break;
+        if (!mbar_wait(&peer_acc_empty[a], par, &s_abort, st, 63 + 8 * MODE)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + a * C::ACC_COLS;
+        bool ok = true;
+        for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
+          const int s = it % C::S;
+          const uint32_t fp = (it / C::S) & 1;
+          if (!mbar_wait(&full[s], fp, &s_abort, st, 64 + 8 * MODE) ||
+              !mbar_wait(&peer_full[s], fp, &s_abort, st, 65 + 8 * MODE)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = smem_desc_sw128(smem_u32(sA + s * C::A_TILE));
+          const uint64_t bd = smem_desc_sw128(smem_u32(sB + s * C::B_TILE));
+#pragma unroll
+          for (int kk = 0; kk < BK8 / 32; ++kk)
+            mma2_e4m3_ss(d, ad + (uint64_t)(2 * kk), bd + (uint64_t)(2 * kk), idesc,
+                         (kk > 0 || kb > wi.kb_begin) ? 1u : 0u);
+          mma2_commit_mc(&empty[s], 0x3);
+        }
+        if (!ok) break;
+        mma2_commit_mc(&acc_full[a], 0x3);
+      }
+    } else if (lane == 0) {
+      // ------------------------------------------------------------ relay (peer): local phases -> leader
+      uint32_t it = 0;
+      int li = 0;
+      for (int item = cid; item < n_items && !s_abort; item += ncl, ++li) {
+        const WorkItem wi = p.items[item];
+        const int a = li & 1;
+        if (li >= 2) {
+          if (!mbar_wait(&acc_empty[a], ((li >> 1) & 1) ^ 1, &s_abort, st, 66 + 8 * MODE)) break;
+          mbar_arrive_remote(&peer_acc_empty[a], 0);
+        }
+        bool ok = true;
+        for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
+          const int s = it % C::S;
+          if (!mbar_wait(&full[s], (it / C::S) & 1, &s_abort, st, 67 + 8 * MODE)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_remote(&peer_full[s], 0);
+        }
+        if (!ok) break;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quad = warp & 3;              // TMEM lanes 32 quad .. 32 quad + 31
+    const int hw = (warp - 2) >> 2;         // column half of the item this warp drains
+    const int t_loc = quad * 16 + (lane >> 1);  // token of this lane inside the CTA's 64
+    const int odd = lane & 1;               // 0: hi row, keeps columns 0-15 of a chunk; 1: lo, 16-31
+    int li = 0;
+    for (int item = cid; item < n_items; item += ncl, ++li) {
+      if (__any_sync(0xffffffffu, s_abort != 0)) break;  // warp-uniform exit (the warp shuffles below)
+      const WorkItem wi = p.items[item];
+      const GroupParams& g = p.g[wi.group];
+      const int a = li & 1;
+      const int h = min(64, (wi.nrows + 1) >> 1);
+      const int n_my = rank == 0 ? h : wi.nrows - h;
+      const int tok = wi.row0 + (int)rank * h + t_loc;
+      const bool live = t_loc < n_my;
+      float fx = 0.f;
+      if (live) {
+        fx = g.x_scale[tok];
+        if (MODE == 1 && g.row_scale != nullptr) fx *= g.row_scale[tok];
+      }
+      const bool got = mbar_wait(&acc_full[a], (li >> 1) & 1, &s_abort, st, 68 + 8 * MODE);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      const uint32_t t_acc = tmem_base + a * C::ACC_COLS + ((uint32_t)(quad * 32) << 16);
+      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)wi.part * g.part_stride;
+      // MODE 0: this warp takes gate/up features [64 hw, 64 hw + 64) in two 32-column chunks;
+      // MODE 1: output columns [128 hw, 128 hw + 128) in four chunks.
+      constexpr int NCH = MODE == 0 ? 2 : 4;
+      uint4 res[NCH][2];
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        const int c0 = (MODE == 0 ? 64 : 128) * hw + 32 * c;  // first column of the chunk
+        float v[MODE == 0 ? 2 : 1][32];
+        tmem_ld32(t_acc + c0, v[0]);
+        if constexpr (MODE == 0) tmem_ld32(t_acc + 128 + c0, v[1]);
+        tmem_ld_wait();
+        // combine hi + lo / 16 for 16 columns per lane: hi lanes keep 0-15, lo lanes 16-31
+        float r[MODE == 0 ? 2 : 1][16];
+#pragma unroll
+        for (int m = 0; m < (MODE == 0 ? 2 : 1); ++m) {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const float send = odd ? v[m][k] : v[m][16 + k];
+            const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+            r[m][k] = odd ? recv + v[m][16 + k] * (1.0f / kLoPlaneGain) : v[m][k] + recv * (1.0f / kLoPlaneGain);
+          }
+        }
+        const int col = c0 + odd * 16;  // first item column of this lane's 16
+        uint32_t packed[8];
+        if (DWDP_X2_DIAG & 1) {  // diagnostic build: no epilogue math
+          res[c][0] = res[c][1] = make_uint4(__float_as_uint(r[0][0]), 0, 0, 0);
+          continue;
+        }
+        if constexpr (MODE == 0) {
+          const int f = wi.rb * BM + col;  // feature of the projection (16-float aligned)
+          float sg[16], su[16];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 a4 = __ldg(reinterpret_cast<const float4*>(wi.scales + f) + q);
+            const float4 b4 = __ldg(reinterpret_cast<const float4*>(wi.scales + g.R + f) + q);
+            sg[4 * q] = a4.x; sg[4 * q + 1] = a4.y; sg[4 * q + 2] = a4.z; sg[4 * q + 3] = a4.w;
+            su[4 * q] = b4.x; su[4 * q + 1] = b4.y; su[4 * q + 2] = b4.z; su[4 * q + 3] = b4.w;
+          }
+#pragma unroll
+          for (int k = 0; k < 16; k += 2) {
+            const float g0 = r[0][k] * (sg[k] * fx), g1 = r[0][k + 1] * (sg[k + 1] * fx);
+            const float u0 = r[1][k] * (su[k] * fx), u1 = r[1][k + 1] * (su[k + 1] * fx);
+            const __nv_bfloat162 hv = __floats2bfloat162_rn(silu_fast(g0) * u0, silu_fast(g1) * u1);
+            packed[k >> 1] = *reinterpret_cast<const uint32_t*>(&hv);
+          }
+        } else {
+          const int f = wi.rb * BM + col;  // output feature (two consecutive 128-row blocks)
+          float sw[16];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 a4 = __ldg(reinterpret_cast<const float4*>(wi.scales + f) + q);
+            sw[4 * q] = a4.x; sw[4 * q + 1] = a4.y; sw[4 * q + 2] = a4.z; sw[4 * q + 3] = a4.w;
+          }
+#pragma unroll
+          for (int k = 0; k < 16; k += 2) {
+            const __nv_bfloat162 yv =
+                __floats2bfloat162_rn(r[0][k] * (sw[k] * fx), r[0][k + 1] * (sw[k + 1] * fx));
+            packed[k >> 1] = *reinterpret_cast<const uint32_t*>(&yv);
+          }
+        }
+        res[c][0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        res[c][1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[a]);  // the accumulator is drained; stores follow
+      if (live && !(DWDP_X2_DIAG & 1)) {
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          const int col = (MODE == 0 ? 64 : 128) * hw + 32 * c + odd * 16;
+          uint4* dst = reinterpret_cast<uint4*>(out + (size_t)tok * g.R + wi.rb * BM + col);
+          dst[0] = res[c][0];
+          dst[1] = res[c][1];
+        }
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs done: the leader's MMAs and both epilogues
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc2(tmem_base, 2 * C::ACC_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // e4m3 tensor-core path with per-128-K-block promotion.
 //
 // Used when the product's scale changes along K every 128 inputs: activations
@@ -1693,6 +2022,35 @@ int launch_gemm_f8(const GemmParams& prm, int grid, cudaStream_t stream) {
              : DWDP_ERR_CUDA;
 }
 
+// CTA-pair kernels: clusters of two consecutive CTAs (grid must be even), programmatic launch.
+template <int MODE>
+int launch_gemm_f8x2(const GemmParams& prm, int grid, cudaStream_t stream) {
+  using C = CfgX2<MODE>;
+  auto kfn = moe_gemm_f8x2_kernel<MODE>;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
+    return DWDP_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid & ~1);
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  attr[n].id = cudaLaunchAttributeClusterDimension;
+  attr[n].val.clusterDim.x = 2;
+  attr[n].val.clusterDim.y = 1;
+  attr[n].val.clusterDim.z = 1;
+  ++n;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kfn, prm) == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;
+}
+
 // One warp per row once the rows fill every SM's warps; below that a CTA per
 // row (decode: a few long rows want more loads in flight than one warp has).
 constexpr int64_t kQuantWarpRows = 148 * 8;
@@ -1825,13 +2183,24 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   bool pair_dn = fp8 && !(act_blk && wide) && est_tiles * ((H / BM + 1) / 2) >= 4LL * std::max(1, sms_now);
   if (const char* v = getenv("DWDP_PAIR_DOWN"))  // tuning override
     pair_dn = fp8 && !(act_blk && wide) && v[0] == '1';
+  // Prefill-sized hi/lo batches run on CTA pairs (moe_gemm_f8x2_kernel: 128-token tiles, 64 per
+  // CTA, down items always two 128-row blocks). DWDP_PAIR_CTA=0|1 overrides the default.
+  bool use_pair = false;
+  {
+    static const int pair_env = [] {
+      const char* v = getenv("DWDP_PAIR_CTA");
+      return v != nullptr ? atoi(v) : 1;
+    }();
+    use_pair = pair_env == 1 && hilo_native && !wide && (H / BM) % 2 == 0 && N >= 148LL * 64;
+  }
+  if (use_pair) pair_dn = true;
   const int dn_items_per_tile = pair_dn ? (H / BM + 1) / 2 : H / BM;
   pp.rb_gu_r = I / BM; pp.rb_dn_r = dn_items_per_tile;
   pp.rb_gu_s = has_shared ? Is / BM : 0; pp.rb_dn_s = has_shared ? dn_items_per_tile : 0;
   pp.dn_pair = pair_dn ? 1 : 0; pp.blocks_dn = H / BM;
   pp.kb_gu = H / bk; pp.kb_dn_r = I / bk; pp.kb_dn_s = has_shared ? Is / bk : 0;
   pp.sdn_parts = has_shared ? parts : 0;
-  pp.bn_max = bn;
+  pp.bn_max = use_pair ? 128 : bn;
   const long long esz = fp8 ? 1 : 2;
   pp.w_gu[0] = routed->w13; pp.w_dn[0] = routed->w2; pp.s_gu[0] = routed->s13; pp.s_dn[0] = routed->s2;
   pp.rbb_gu[0] = 128LL * H * 2 * esz; pp.rbb_dn[0] = 128LL * I * esz;
@@ -1873,7 +2242,7 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   // The activation box must cover the largest tile: a routed tile holds at most
   // min(T * K, bn) rows (an expert may be picked more than once per token), a
   // shared tile at most min(T, bn).
-  const int box_r = box_rows_for(N, bn), box_s = box_rows_for(T, bn);
+  const int box_r = use_pair ? 64 : box_rows_for(N, bn), box_s = use_pair ? 64 : box_rows_for(T, bn);
   auto map = [&](CUtensorMap* m, const void* bf16, size_t planes_off, int64_t rows, int64_t cols, int box) {
     return fp8 ? make_tmap_planes(m, ws + planes_off, rows, cols, box, planes) : make_tmap(m, bf16, rows, cols, box);
   };
@@ -1927,7 +2296,12 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
                : DWDP_ERR_CUDA;
   };
   int rc;
-  if (hilo_native) {
+  if (use_pair) {
+    const int grid2 = std::max(2, (sms / 2) * 2);
+    rc = launch_gemm_f8x2<0>(gu, grid2, stream);
+    if (rc == DWDP_OK) rc = quant_h();
+    if (rc == DWDP_OK) rc = launch_gemm_f8x2<1>(dn, grid2, stream);
+  } else if (hilo_native) {
     rc = wide ? launch_gemm_f8<0, 2, 128>(gu, grid_gu, stream) : launch_gemm_f8<0, 2, 64>(gu, grid_gu, stream);
     if (rc == DWDP_OK) rc = quant_h();
     if (rc == DWDP_OK) {
