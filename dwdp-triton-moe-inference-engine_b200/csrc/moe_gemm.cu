@@ -694,6 +694,7 @@ __global__ void __launch_bounds__(CfgX2<MODE>::THREADS, 1) moe_gemm_f8x2_kernel(
   if (warp == 0) {
     // ------------------------------------------------------------ producer (each CTA its halves)
     if (lane == 0) {
+      PROF_DECL PROF_START
       uint32_t it = 0;
       for (int item = cid; item < n_items && !s_abort; item += ncl) {
         const WorkItem wi = p.items[item];
@@ -703,16 +704,18 @@ __global__ void __launch_bounds__(CfgX2<MODE>::THREADS, 1) moe_gemm_f8x2_kernel(
         const uint8_t* wsrc = wi.wtiles + (size_t)rank * g.mstride;
         for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
           const int s = it % C::S;
-          if (!mbar_wait(&empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 61 + 8 * MODE)) break;
+          if (!TW(0, mbar_wait(&empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 61 + 8 * MODE))) break;
           mbar_arrive_expect_tx(&full[s], (uint32_t)C::STAGE);
           bulk_g2s(sB + s * C::B_TILE, wsrc + (size_t)kb * g.kstride, C::B_TILE, &full[s]);
           tma_load_2d(sA + s * C::A_TILE, &g.tmap_b, kb * BK8, 2 * tok0, &full[s]);
         }
       }
+      PROF_END(7) PROF_STORE(0)
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       // ------------------------------------------------------------ MMA issuer (leader)
+      PROF_DECL PROF_START
       uint32_t it = 0;
       int li = 0;
       const uint32_t idesc = idesc_e4m3(256, 256);
@@ -720,16 +723,16 @@ __global__ void __launch_bounds__(CfgX2<MODE>::THREADS, 1) moe_gemm_f8x2_kernel(
         const WorkItem wi = p.items[item];
         const int a = li & 1;
         const uint32_t par = ((li >> 1) & 1) ^ 1;
-        if (!mbar_wait(&acc_empty[a], par, &s_abort, st, 62 + 8 * MODE)) break;
-        if (!mbar_wait(&peer_acc_empty[a], par, &s_abort, st, 63 + 8 * MODE)) break;
+        if (!TW(0, mbar_wait(&acc_empty[a], par, &s_abort, st, 62 + 8 * MODE))) break;
+        if (!TW(1, mbar_wait(&peer_acc_empty[a], par, &s_abort, st, 63 + 8 * MODE))) break;
         tc_fence_after();
         const uint32_t d = tmem_base + a * C::ACC_COLS;
         bool ok = true;
         for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
           const int s = it % C::S;
           const uint32_t fp = (it / C::S) & 1;
-          if (!mbar_wait(&full[s], fp, &s_abort, st, 64 + 8 * MODE) ||
-              !mbar_wait(&peer_full[s], fp, &s_abort, st, 65 + 8 * MODE)) {
+          if (!TW(2, mbar_wait(&full[s], fp, &s_abort, st, 64 + 8 * MODE)) ||
+              !TW(3, mbar_wait(&peer_full[s], fp, &s_abort, st, 65 + 8 * MODE))) {
             ok = false;
             break;
           }
@@ -745,21 +748,23 @@ __global__ void __launch_bounds__(CfgX2<MODE>::THREADS, 1) moe_gemm_f8x2_kernel(
         if (!ok) break;
         mma2_commit_mc(&acc_full[a], 0x3);
       }
+      PROF_END(7) PROF_STORE(4)
     } else if (lane == 0) {
       // ------------------------------------------------------------ relay (peer): local phases -> leader
+      PROF_DECL PROF_START
       uint32_t it = 0;
       int li = 0;
       for (int item = cid; item < n_items && !s_abort; item += ncl, ++li) {
         const WorkItem wi = p.items[item];
         const int a = li & 1;
         if (li >= 2) {
-          if (!mbar_wait(&acc_empty[a], ((li >> 1) & 1) ^ 1, &s_abort, st, 66 + 8 * MODE)) break;
+          if (!TW(0, mbar_wait(&acc_empty[a], ((li >> 1) & 1) ^ 1, &s_abort, st, 66 + 8 * MODE))) break;
           mbar_arrive_remote(&peer_acc_empty[a], 0);
         }
         bool ok = true;
         for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
           const int s = it % C::S;
-          if (!mbar_wait(&full[s], (it / C::S) & 1, &s_abort, st, 67 + 8 * MODE)) {
+          if (!TW(1, mbar_wait(&full[s], (it / C::S) & 1, &s_abort, st, 67 + 8 * MODE))) {
             ok = false;
             break;
           }
@@ -767,6 +772,7 @@ __global__ void __launch_bounds__(CfgX2<MODE>::THREADS, 1) moe_gemm_f8x2_kernel(
         }
         if (!ok) break;
       }
+      PROF_END(7) PROF_STORE(4)
     }
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
@@ -774,6 +780,7 @@ __global__ void __launch_bounds__(CfgX2<MODE>::THREADS, 1) moe_gemm_f8x2_kernel(
     const int hw = (warp - 2) >> 2;         // column half of the item this warp drains
     const int t_loc = quad * 16 + (lane >> 1);  // token of this lane inside the CTA's 64
     const int odd = lane & 1;               // 0: hi row, keeps columns 0-15 of a chunk; 1: lo, 16-31
+    PROF_DECL PROF_START
     int li = 0;
     for (int item = cid; item < n_items; item += ncl, ++li) {
       if (__any_sync(0xffffffffu, s_abort != 0)) break;  // warp-uniform exit (the warp shuffles below)
@@ -789,7 +796,7 @@ __global__ void __launch_bounds__(CfgX2<MODE>::THREADS, 1) moe_gemm_f8x2_kernel(
         fx = g.x_scale[tok];
         if (MODE == 1 && g.row_scale != nullptr) fx *= g.row_scale[tok];
       }
-      const bool got = mbar_wait(&acc_full[a], (li >> 1) & 1, &s_abort, st, 68 + 8 * MODE);
+      const bool got = TW(0, mbar_wait(&acc_full[a], (li >> 1) & 1, &s_abort, st, 68 + 8 * MODE));
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
       const uint32_t t_acc = tmem_base + a * C::ACC_COLS + ((uint32_t)(quad * 32) << 16);
@@ -869,6 +876,7 @@ __global__ void __launch_bounds__(CfgX2<MODE>::THREADS, 1) moe_gemm_f8x2_kernel(
         }
       }
     }
+    PROF_END(7) if (lane == 0 && warp == 2) PROF_STORE(8)
   }
 
   __syncwarp();
