@@ -2199,7 +2199,11 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
       const char* v = getenv("DWDP_PAIR_CTA");
       return v != nullptr ? atoi(v) : 1;
     }();
-    use_pair = pair_env == 1 && hilo_native && !wide && (H / BM) % 2 == 0 && N >= 148LL * 64;
+    static const long long pair_min = [] {  // tuning: routed rows from which the pairs run
+      const char* v = getenv("DWDP_PAIR_MIN_ROWS");
+      return v != nullptr ? atoll(v) : 148LL * 64;
+    }();
+    use_pair = pair_env == 1 && hilo_native && !wide && (H / BM) % 2 == 0 && N >= pair_min;
   }
   if (use_pair) pair_dn = true;
   const int dn_items_per_tile = pair_dn ? (H / BM + 1) / 2 : H / BM;
