@@ -627,12 +627,16 @@ __device__ __forceinline__ void mma2_commit_mc(uint64_t* bar, uint16_t mask) {
 #ifndef DWDP_X2_DIAG
 #define DWDP_X2_DIAG 0  // diagnostic builds only: 1 = no epilogue math (wrong results, timing only)
 #endif
-template <int MODE>
+// KPS = 128-input K blocks per pipeline stage: 2 halves the number of copies (one 3-D TMA box
+// for both activation tiles, one bulk copy for both weight tiles where they are contiguous).
+template <int MODE, int KPS>
 struct CfgX2 {
   static constexpr int A_TILE = 128 * BK8;  // 64 tokens x 2 planes x 128 inputs
   static constexpr int B_TILE = kW8TileBytes;  // 128 weight rows x 128 inputs
-  static constexpr int STAGE = A_TILE + B_TILE;
-  static constexpr int S = 7;
+  static constexpr int STAGE_A = KPS * A_TILE;
+  static constexpr int STAGE_B = KPS * B_TILE;
+  static constexpr int STAGE = STAGE_A + STAGE_B;
+  static constexpr int S = KPS == 1 ? 7 : 3;
   static constexpr int EPI_WARPS = 8;
   static constexpr int EPI_THREADS = EPI_WARPS * 32;
   static constexpr int THREADS = (2 + EPI_WARPS) * 32;
@@ -640,13 +644,13 @@ struct CfgX2 {
   static constexpr int SMEM_BYTES = S * STAGE + 1024 + 512;
 };
 
-template <int MODE>
-__global__ void __launch_bounds__(CfgX2<MODE>::THREADS, 1) moe_gemm_f8x2_kernel(const __grid_constant__ GemmParams p) {
-  using C = CfgX2<MODE>;
+template <int MODE, int KPS>
+__global__ void __launch_bounds__(CfgX2<MODE, KPS>::THREADS, 1) moe_gemm_f8x2_kernel(const __grid_constant__ GemmParams p) {
+  using C = CfgX2<MODE, KPS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + C::S * C::A_TILE;
+  uint8_t* sB = smem + C::S * C::STAGE_A;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::S * C::STAGE);
   uint64_t* full = bars;               // local loads of stage s landed
   uint64_t* empty = full + C::S;       // the pair's MMAs read stage s (leader commit, both CTAs)
@@ -702,12 +706,20 @@ __global__ void __launch_bounds__(CfgX2<MODE>::THREADS, 1) moe_gemm_f8x2_kernel(
         const int h = min(64, (wi.nrows + 1) >> 1);  // tokens of CTA 0; CTA 1 takes the rest
         const int tok0 = wi.row0 + (int)rank * h;
         const uint8_t* wsrc = wi.wtiles + (size_t)rank * g.mstride;
-        for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
+        for (int kb = wi.kb_begin; kb < wi.kb_end; kb += KPS, ++it) {
           const int s = it % C::S;
+          const int nkb = min(KPS, wi.kb_end - kb);
           if (!TW(0, mbar_wait(&empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 61 + 8 * MODE))) break;
-          mbar_arrive_expect_tx(&full[s], (uint32_t)C::STAGE);
-          bulk_g2s(sB + s * C::B_TILE, wsrc + (size_t)kb * g.kstride, C::B_TILE, &full[s]);
-          tma_load_2d(sA + s * C::A_TILE, &g.tmap_b, kb * BK8, 2 * tok0, &full[s]);
+          // the activation box always lands whole (K blocks past the end read as zeros)
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(C::STAGE_A + nkb * C::B_TILE));
+          if (g.kstride == C::B_TILE) {
+            bulk_g2s(sB + s * C::STAGE_B, wsrc + (size_t)kb * g.kstride, nkb * C::B_TILE, &full[s]);
+          } else {
+            for (int q = 0; q < nkb; ++q)
+              bulk_g2s(sB + s * C::STAGE_B + q * C::B_TILE, wsrc + (size_t)(kb + q) * g.kstride, C::B_TILE, &full[s]);
+          }
+          if constexpr (KPS == 1) tma_load_2d(sA + s * C::STAGE_A, &g.tmap_b, kb * BK8, 2 * tok0, &full[s]);
+          else tma_load_3d(sA + s * C::STAGE_A, &g.tmap_b, 0, 2 * tok0, kb, &full[s]);
         }
       }
       PROF_END(7) PROF_STORE(0)
@@ -728,8 +740,9 @@ __global__ void __launch_bounds__(CfgX2<MODE>::THREADS, 1) moe_gemm_f8x2_kernel(
         tc_fence_after();
         const uint32_t d = tmem_base + a * C::ACC_COLS;
         bool ok = true;
-        for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
+        for (int kb = wi.kb_begin; kb < wi.kb_end; kb += KPS, ++it) {
           const int s = it % C::S;
+          const int nkb = min(KPS, wi.kb_end - kb);
           const uint32_t fp = (it / C::S) & 1;
           if (!TW(2, mbar_wait(&full[s], fp, &s_abort, st, 64 + 8 * MODE)) ||
               !TW(3, mbar_wait(&peer_full[s], fp, &s_abort, st, 65 + 8 * MODE))) {
@@ -737,12 +750,14 @@ __global__ void __launch_bounds__(CfgX2<MODE>::THREADS, 1) moe_gemm_f8x2_kernel(
             break;
           }
           tc_fence_after();
-          const uint64_t ad = smem_desc_sw128(smem_u32(sA + s * C::A_TILE));
-          const uint64_t bd = smem_desc_sw128(smem_u32(sB + s * C::B_TILE));
+          for (int q = 0; q < nkb; ++q) {
+            const uint64_t ad = smem_desc_sw128(smem_u32(sA + s * C::STAGE_A + q * C::A_TILE));
+            const uint64_t bd = smem_desc_sw128(smem_u32(sB + s * C::STAGE_B + q * C::B_TILE));
 #pragma unroll
-          for (int kk = 0; kk < BK8 / 32; ++kk)
-            mma2_e4m3_ss(d, ad + (uint64_t)(2 * kk), bd + (uint64_t)(2 * kk), idesc,
-                         (kk > 0 || kb > wi.kb_begin) ? 1u : 0u);
+            for (int kk = 0; kk < BK8 / 32; ++kk)
+              mma2_e4m3_ss(d, ad + (uint64_t)(2 * kk), bd + (uint64_t)(2 * kk), idesc,
+                           (kk > 0 || q > 0 || kb > wi.kb_begin) ? 1u : 0u);
+          }
           mma2_commit_mc(&empty[s], 0x3);
         }
         if (!ok) break;
@@ -762,7 +777,7 @@ __global__ void __launch_bounds__(CfgX2<MODE>::THREADS, 1) moe_gemm_f8x2_kernel(
           mbar_arrive_remote(&peer_acc_empty[a], 0);
         }
         bool ok = true;
-        for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++it) {
+        for (int kb = wi.kb_begin; kb < wi.kb_end; kb += KPS, ++it) {
           const int s = it % C::S;
           if (!TW(1, mbar_wait(&full[s], (it / C::S) & 1, &s_abort, st, 67 + 8 * MODE))) {
             ok = false;
@@ -1946,6 +1961,22 @@ bool make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int
 
 // 2-D map over e4m3 activation rows: `planes` = 2 for the interleaved hi/lo planes
 // [2 * rows, cols] (box {128, 2 * box_rows}), 1 for one plane [rows, cols].
+// The same planes as a 3-D map {128 inputs, plane rows, K blocks}: one box brings two
+// consecutive 128-input tiles of box_rows tokens (two 16 KB tiles back to back in shared
+// memory), for the CTA-pair kernels with two K blocks per stage.
+bool make_tmap_planes3(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows, int planes) {
+  auto enc = get_encode_fn();
+  if (enc == nullptr || rows <= 0 || cols % BK8) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)BK8, (cuuint64_t)(planes * rows), (cuuint64_t)(cols / BK8)};
+  cuuint64_t strides[2] = {(cuuint64_t)cols, (cuuint64_t)BK8};
+  cuuint32_t box[3] = {(cuuint32_t)BK8, (cuuint32_t)(planes * box_rows), 2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool make_tmap_planes(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows, int planes) {
   auto enc = get_encode_fn();
   if (enc == nullptr || rows <= 0) return false;
@@ -2031,10 +2062,10 @@ int launch_gemm_f8(const GemmParams& prm, int grid, cudaStream_t stream) {
 }
 
 // CTA-pair kernels: clusters of two consecutive CTAs (grid must be even), programmatic launch.
-template <int MODE>
+template <int MODE, int KPS>
 int launch_gemm_f8x2(const GemmParams& prm, int grid, cudaStream_t stream) {
-  using C = CfgX2<MODE>;
-  auto kfn = moe_gemm_f8x2_kernel<MODE>;
+  using C = CfgX2<MODE, KPS>;
+  auto kfn = moe_gemm_f8x2_kernel<MODE, KPS>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return DWDP_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
@@ -2205,6 +2236,10 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
     }();
     use_pair = pair_env == 1 && hilo_native && !wide && (H / BM) % 2 == 0 && N >= pair_min;
   }
+  static const int pair_kps = [] {  // tuning: K blocks per stage of the pair kernels (1 or 2)
+    const char* v = getenv("DWDP_PAIR_KPS");
+    return v != nullptr && atoi(v) == 1 ? 1 : 2;
+  }();
   if (use_pair) pair_dn = true;
   const int dn_items_per_tile = pair_dn ? (H / BM + 1) / 2 : H / BM;
   pp.rb_gu_r = I / BM; pp.rb_dn_r = dn_items_per_tile;
@@ -2256,6 +2291,7 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   // shared tile at most min(T, bn).
   const int box_r = use_pair ? 64 : box_rows_for(N, bn), box_s = use_pair ? 64 : box_rows_for(T, bn);
   auto map = [&](CUtensorMap* m, const void* bf16, size_t planes_off, int64_t rows, int64_t cols, int box) {
+    if (fp8 && use_pair && pair_kps == 2) return make_tmap_planes3(m, ws + planes_off, rows, cols, box, planes);
     return fp8 ? make_tmap_planes(m, ws + planes_off, rows, cols, box, planes) : make_tmap(m, bf16, rows, cols, box);
   };
   GemmParams gu{}, dn{};
@@ -2310,9 +2346,10 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   int rc;
   if (use_pair) {
     const int grid2 = std::max(2, (sms / 2) * 2);
-    rc = launch_gemm_f8x2<0>(gu, grid2, stream);
+    rc = pair_kps == 2 ? launch_gemm_f8x2<0, 2>(gu, grid2, stream) : launch_gemm_f8x2<0, 1>(gu, grid2, stream);
     if (rc == DWDP_OK) rc = quant_h();
-    if (rc == DWDP_OK) rc = launch_gemm_f8x2<1>(dn, grid2, stream);
+    if (rc == DWDP_OK)
+      rc = pair_kps == 2 ? launch_gemm_f8x2<1, 2>(dn, grid2, stream) : launch_gemm_f8x2<1, 1>(dn, grid2, stream);
   } else if (hilo_native) {
     rc = wide ? launch_gemm_f8<0, 2, 128>(gu, grid_gu, stream) : launch_gemm_f8<0, 2, 64>(gu, grid_gu, stream);
     if (rc == DWDP_OK) rc = quant_h();
