@@ -2302,8 +2302,8 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   gu.g[0].out_scale = sh_r; gu.g[0].os_ld = N;
   gu.g[0].x_scale = sx_r; gu.g[0].xs_ld = N;
   gu.g[0].K = H; gu.g[0].R = I; gu.g[0].scale_mode = routed->scale_mode; gu.g[0].box_rows = box_r;
-  // e4m3 tiles: gate/up interleaved per 128-input stage; down row blocks are K/128 tiles apart
-  gu.g[0].mstride = kW8TileBytes; gu.g[0].kstride = 2 * kW8TileBytes;
+  // e4m3 tiles: a row block's gate tiles along K, then its up tiles; down row blocks are K/128 tiles apart
+  gu.g[0].mstride = (long long)(H / BK8) * kW8TileBytes; gu.g[0].kstride = kW8TileBytes;
   gu.g[1].enabled = has_shared;
   if (has_shared) {
     if (!map(&gu.g[1].tmap_b, hidden, L.x8_s, T, H, box_s)) return DWDP_ERR_CUDA;
@@ -2312,7 +2312,7 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
     gu.g[1].out_scale = sh_s; gu.g[1].os_ld = T;
     gu.g[1].x_scale = sx_s; gu.g[1].xs_ld = T;
     gu.g[1].K = H; gu.g[1].R = Is; gu.g[1].scale_mode = shared->scale_mode; gu.g[1].box_rows = box_s;
-    gu.g[1].mstride = kW8TileBytes; gu.g[1].kstride = 2 * kW8TileBytes;
+    gu.g[1].mstride = (long long)(H / BK8) * kW8TileBytes; gu.g[1].kstride = kW8TileBytes;
   }
   gu.items = items_gu; gu.n_items = n_items; gu.st = st; gu.cap = L.cap_gu;
 

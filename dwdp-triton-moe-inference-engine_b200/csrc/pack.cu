@@ -13,7 +13,12 @@
 // per output row like CHANNEL scales, every row of a matrix holding the same value,
 // so the GEMMs treat both modes alike.
 //
-// Tile layout: tile (rb, kb) of matrix p at index (rb * KB + kb) * P + p.
+// Tile layout (tile_slot):
+//   fp8 : tile (rb, kb) of matrix p at index (rb * P + p) * KB + kb: a row block's tiles of one
+//         matrix are contiguous along K, so a GEMM stage can bring two K blocks of a matrix
+//         with one bulk copy; the matrices of a row block follow each other.
+//   bf16: at index (rb * KB + kb) * P + p: both matrices of one K step side by side (the bf16
+//         kernel loads them with one copy).
 //   fp8 (all modes): 128 rows x 128 inputs, 128-byte rows in the 128B-swizzled
 //                 smem image (16-byte chunk c of row r stored at chunk c ^ (r & 7)):
 //                 the e4m3 operand the tcgen05 kind::f8f6f4 MMA reads directly.
@@ -24,6 +29,10 @@
 namespace dwdp {
 
 constexpr int kTileRows = 128;
+
+__host__ __device__ inline int64_t tile_slot(int rb, int kb, int p, int KB, int P, int dst_dtype) {
+  return dst_dtype == DWDP_DTYPE_FP8_E4M3 ? ((int64_t)rb * P + p) * KB + kb : ((int64_t)rb * KB + kb) * P + p;
+}
 
 // inputs per tile for a (dtype, scale mode) pair
 __host__ __device__ inline int tile_cols(int dst_dtype, int mode) {
@@ -110,7 +119,7 @@ tile_kernel(MatPtrs src, int R, int C, int P, int dst_dtype, int mode,
   const int r = threadIdx.x;
   const int grow = rb * kTileRows + r;
   const TS* w = reinterpret_cast<const TS*>(src.p[p]);
-  const int64_t tile_index = ((int64_t)rb * KB + kb) * P + p;
+  const int64_t tile_index = tile_slot(rb, kb, p, KB, P, dst_dtype);
   const int64_t row_base = (int64_t)grow * C + kb * kTileCols;
   if (dst_dtype == DWDP_DTYPE_FP8_E4M3) {
     float s;
@@ -142,7 +151,7 @@ untile_kernel(const uint8_t* __restrict__ tiles, const float* __restrict__ scale
   const int KB = C / kTileCols;
   const int r = threadIdx.x;
   const int grow = rb * kTileRows + r;
-  const int64_t tile_index = ((int64_t)rb * KB + kb) * P + p;
+  const int64_t tile_index = tile_slot(rb, kb, p, KB, P, dst_dtype);
   float* o = out + ((int64_t)p * R + grow) * C + kb * kTileCols;
   if (dst_dtype == DWDP_DTYPE_FP8_E4M3) {
     float s;

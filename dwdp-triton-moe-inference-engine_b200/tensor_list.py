@@ -18,7 +18,7 @@ skips them), so the fill can be captured in a CUDA graph.
 
 B200-specific meaning of a few fields:
 * ``gate_weight_ptrs`` and ``up_weight_ptrs`` both name the expert's packed
-  gate/up slab (the two projections are interleaved per 128-input stage);
+  gate/up slab (the row block's gate tiles, then its up tiles);
 * ``quantization_ptrs`` is the gate/up scale address (the reference leaves it 0,
   tensor_list.py:160) and the extra row ``down_quantization_ptrs`` the down
   scales; both 0 for bf16 weights;

@@ -118,8 +118,9 @@ def test_router_top1_weight_is_one(pkg):
 
 def _decode_fp8_tiles(tiles: torch.Tensor, R: int, C: int, P: int, channel: bool) -> torch.Tensor:
     """Undo the packed tiling: e4m3 tiles (every scale mode) are 128 x 128 in the
-    128-byte-swizzled image (16-byte chunk c of row r at c ^ (r % 8))."""
-    t = tiles.cpu().view(R // 128, C // 128, P, 128, 8, 16)
+    128-byte-swizzled image (16-byte chunk c of row r at c ^ (r % 8)), ordered
+    (row block, matrix, K block)."""
+    t = tiles.cpu().view(R // 128, P, C // 128, 128, 8, 16).permute(0, 2, 1, 3, 4, 5).contiguous()
     r = torch.arange(128).view(128, 1)
     src_chunk = torch.arange(8).view(1, 8) ^ (r % 8)  # logical chunk c sits at c ^ (r % 8)
     t = torch.gather(t, 4, src_chunk.view(1, 1, 1, 128, 8, 1).expand_as(t))
