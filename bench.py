@@ -251,7 +251,7 @@ def algo_layer_bytes(layer, expert_b: int, T: int) -> int:
 
 # DRAM bytes (read + write) of one layer's expert launches (plan/quantise + GEMMs) at the
 # headline T, from the ncu launch list of `bench.py --workload layer` (profiles/, per mode)
-TRAFFIC_PER_LAYER: dict = {(4096, "hilo"): 1075.1e6, (4096, "block128"): 766.0e6}
+TRAFFIC_PER_LAYER: dict = {(4096, "hilo"): 1067.5e6, (4096, "block128"): 766.0e6}
 
 
 def expert_flops(layer, T: int) -> int:
