@@ -529,11 +529,15 @@ class LayerStack:
     sharded over the ranks and the NEXT layer's remote experts are prefetched
     over NVLink while the current layer computes (DWDP)."""
 
-    def __init__(self, pkg, device, L: int, T: int, rank: int, world: int):
-        self.layers = [make_qwen_layer(pkg, device, seed=1235 + l, rank=rank, world=world) for l in range(L)]
+    def __init__(self, pkg, device, L: int, T: int, rank: int, world: int, shape: dict | None = None):
+        if shape is None:
+            self.layers = [make_qwen_layer(pkg, device, seed=1235 + l, rank=rank, world=world) for l in range(L)]
+        else:  # a BASELINE shape (Mixtral / DeepSeek), block-scaled weights
+            self.layers = [make_shape_layer(pkg, device, shape, seed=1240 + l, rank=rank, world=world)
+                           for l in range(L)]
         self.sharded = world > 1
         self.T = T
-        self.x0 = make_inputs(T, device, seed=4242 + 7919 * rank)
+        self.x0 = make_inputs(T, device, seed=4242 + 7919 * rank, H=None if shape is None else shape["H"])
         self.outs = [torch.empty_like(self.x0), torch.empty_like(self.x0)]
         self.ws = [lay.workspace(T) for lay in self.layers]
         if self.sharded:
@@ -822,33 +826,44 @@ SHAPES = {
 }
 
 
-def make_shape_layer(pkg, device, shape: dict, seed: int = 1240):
+def make_shape_layer(pkg, device, shape: dict, seed: int = 1240, *, rank: int = 0, world: int = 1):
     """Random-init layer of a BASELINE shape: router W ~ N(0, 1/H) (+ a Zipf(1.2) expert bias
     for Mixtral: bias_e = -1.2 ln(rank_e + 1)), experts ~ N(0, 0.02) in e4m3 with 128x128 block
     scales, bench's activation quantisation, shared expert with a sigmoid gate where the
-    shape has one. Weights are generated one expert at a time on the device."""
+    shape has one. Weights are generated one expert at a time on the device. With world > 1
+    the routed experts are sharded over the ranks (DWDP: every rank draws the same weights
+    and keeps its own experts' slabs) and the store is connected before it is returned."""
+    import importlib
+
     H, E, I, K, Is = shape["H"], shape["E"], shape["I"], shape["K"], shape["Is"]
     g = torch.Generator(device=device).manual_seed(seed)
 
-    def store(n, inter):
-        st = pkg.ExpertWeightStore(n, H, inter, weight_dtype=torch.float8_e4m3fn,
-                                   scale_mode=pkg._lib.SCALE_BLOCK128, device=device,
-                                   activation_quant=ACTIVATION_QUANT)
+    def store(n, inter, sharded=False):
+        if sharded:
+            dw = importlib.import_module("dwdp_b200.dwdp")
+            st = dw.ShardedExpertStore(n, H, inter, rank=rank, world_size=world, device=device,
+                                       scale_mode=pkg._lib.SCALE_BLOCK128, activation_quant=ACTIVATION_QUANT)
+        else:
+            st = pkg.ExpertWeightStore(n, H, inter, weight_dtype=torch.float8_e4m3fn,
+                                       scale_mode=pkg._lib.SCALE_BLOCK128, device=device,
+                                       activation_quant=ACTIVATION_QUANT)
         for e in range(n):
             st.load_expert(e, torch.randn(inter, H, generator=g, device=device) * 0.02,
                            torch.randn(inter, H, generator=g, device=device) * 0.02,
                            torch.randn(H, inter, generator=g, device=device) * 0.02)
+        if sharded:
+            st.connect()
         return st
 
     wr = (torch.randn(E, H, generator=g, device=device) / H**0.5).bfloat16()
     bias = None
     if shape["zipf"]:
-        rank = torch.randperm(E, generator=torch.Generator().manual_seed(seed))
-        bias = (-1.2 * torch.log(rank.float() + 1.0)).to(device)
+        order = torch.randperm(E, generator=torch.Generator().manual_seed(seed))
+        bias = (-1.2 * torch.log(order.float() + 1.0)).to(device)
     shared = store(1, Is) if Is else None
     gate = (torch.randn(H, generator=g, device=device) * 0.02).bfloat16() if Is else None
-    return pkg.MoELayer(wr, store(E, I), K, shared_expert=shared, shared_gate_weight=gate, router_bias=bias,
-                        activation_quant=ACTIVATION_QUANT)
+    return pkg.MoELayer(wr, store(E, I, sharded=world > 1), K, shared_expert=shared, shared_gate_weight=gate,
+                        router_bias=bias, activation_quant=ACTIVATION_QUANT)
 
 
 def shape_bench(pkg, device, name: str, steps: int, warmup: int, flush) -> dict:
@@ -886,6 +901,40 @@ def shape_bench(pkg, device, name: str, steps: int, warmup: int, flush) -> dict:
             "fp8_peak_tflops": peaks["fp8_tflops"], "hbm_peak_gbs": peaks["hbm_gbs"],
             "peak_source": peaks["fp8_source"],
             "l2": "flushed (256 MB write + 256 MB read) before every timed replay", **extra}
+
+
+def shape_dwdp_bench(pkg, device, name: str, L: int, steps: int, warmup: int, flush, rank: int, world: int,
+                     local: int) -> dict:
+    """A BASELINE shape on `world` GPUs under DWDP: L chained layers at the shape's prefill T per
+    GPU, each layer's routed experts sharded over the ranks, the next layer's remote experts
+    prefetched over NVLink while the current layer computes. Step time is the max over ranks
+    (CUDA events, L2 flushed); the step anatomy (copies alone, compute alone, overlapped)
+    gives the limiter."""
+    shape = SHAPES[name]
+    T = shape["prefill"]
+    stack = LayerStack(pkg, device, L, T, rank, world, shape=shape)
+    torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        step_ms = time_device(stack.step, steps, warmup, flush)
+    t = torch.tensor([sum(step_ms)], device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item()) / steps
+    st = stack.layers[0].read_status(T)
+    if st[0] != 0:
+        raise SystemExit(f"device status {st}")
+    rb = stack.remote_bytes_per_step()
+    return {"workload": f"{name}: {L} chained layers, prefill T={T} per GPU, DWDP over {world} GPUs",
+            "model": shape["model"], "value": world * T * L / (ms / 1e3), "ms_per_step": ms,
+            "config": {"workload": f"{L} chained {name}-shaped MoE layers, prefill T={T} per GPU",
+                       "hidden": shape["H"], "experts": shape["E"], "moe_intermediate": shape["I"],
+                       "top_k": shape["K"], "shared_intermediate": shape["Is"],
+                       "weights": "fp8 e4m3, 128x128 block scales", "activations": ACTIVATION_QUANT,
+                       "parallelism": f"dwdp{world}: tokens data-parallel, routed experts sharded over {world} "
+                                      "GPUs, next layer's remote experts prefetched over NVLink",
+                       "l2": "flushed (256 MB write + 256 MB read) before every timed step"},
+            "clocks": clocks.summary(),
+            "nvlink": {"remote_bytes_per_step_per_gpu": rb, "step_breakdown": step_breakdown(stack, steps, device)}}
 
 
 def attention_bench(pkg, device, batches: list[int], steps: int, warmup: int, flush) -> dict:
@@ -1020,6 +1069,16 @@ def main() -> None:
                           "status": list(st)}), flush=True)
         if st[0] != 0:
             raise SystemExit(f"device status {st}")
+        return
+    if args.workload in SHAPES and world > 1:
+        res = shape_dwdp_bench(pkg, device, args.workload, L, args.steps, args.warmup, flush, rank, world, local)
+        if rank == 0:
+            print(json.dumps({"metric": f"MoE-layer tokens/s ({res['model']})", "value": res["value"],
+                              "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                              "higher_is_better": True, "scaling": "weak", "dtype": "fp8_e4m3",
+                              "data": "synthetic", **res}), flush=True)
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
         return
     if args.workload in SHAPES:
         res = shape_bench(pkg, device, args.workload, args.steps, args.warmup, flush)

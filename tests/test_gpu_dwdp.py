@@ -22,7 +22,7 @@ def _port() -> int:
     return p
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, block_scales=False):
     import torch.distributed as dist
     import __graft_entry__
     pkg = __graft_entry__.load_package()
@@ -39,8 +39,10 @@ def _worker(rank, world, port, q):
         gates = [torch.randn(I, H, generator=g) * 0.02 for _ in range(E)]
         ups = [torch.randn(I, H, generator=g) * 0.02 for _ in range(E)]
         downs = [torch.randn(H, I, generator=g) * 0.02 for _ in range(E)]
-        full = pkg.ExpertWeightStore(E, H, I, device=dev)
-        shard = d.ShardedExpertStore(E, H, I, rank=rank, world_size=world, device=dev, num_buffers=2)
+        mode = pkg._lib.SCALE_BLOCK128 if block_scales else pkg._lib.SCALE_CHANNEL
+        full = pkg.ExpertWeightStore(E, H, I, device=dev, scale_mode=mode)
+        shard = d.ShardedExpertStore(E, H, I, rank=rank, world_size=world, device=dev, num_buffers=2,
+                                     scale_mode=mode)
         for e in range(E):
             full.load_expert(e, gates[e], ups[e], downs[e])
             shard.load_expert(e, gates[e], ups[e], downs[e])
@@ -67,12 +69,15 @@ def _worker(rank, world, port, q):
 
 
 @need2
-def test_dwdp_sharded_layer_matches_local():
+@pytest.mark.parametrize("block_scales", [False, True], ids=["channel_scales", "block128_scales"])
+def test_dwdp_sharded_layer_matches_local(block_scales):
+    """Per-channel weights (the Qwen shape's) and 128x128 block-scaled weights (the Mixtral /
+    DeepSeek shapes'): staged copies carry the slab's scales with its tiles."""
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, block_scales)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
