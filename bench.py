@@ -46,6 +46,10 @@ DECODE_SWEEP = [1, 8, 32, 64]
 # (`modes` in the JSON line).
 ACTIVATION_QUANT = "hilo"
 SIDE_MODES = ["block128"]
+# The block-scaled shapes (Mixtral, DeepSeek) run the reference's FP8 executor scheme: one
+# e4m3 activation plane per (token, 128 channels), which on these large experts is the faster
+# mode (CTA-pair kernels with per-K-block promotion); `--activation hilo` selects the other.
+SHAPE_ACTIVATION = "block128"
 
 
 def _peaks() -> dict:
@@ -842,11 +846,11 @@ def make_shape_layer(pkg, device, shape: dict, seed: int = 1240, *, rank: int = 
         if sharded:
             dw = importlib.import_module("dwdp_b200.dwdp")
             st = dw.ShardedExpertStore(n, H, inter, rank=rank, world_size=world, device=device,
-                                       scale_mode=pkg._lib.SCALE_BLOCK128, activation_quant=ACTIVATION_QUANT)
+                                       scale_mode=pkg._lib.SCALE_BLOCK128, activation_quant=SHAPE_ACTIVATION)
         else:
             st = pkg.ExpertWeightStore(n, H, inter, weight_dtype=torch.float8_e4m3fn,
                                        scale_mode=pkg._lib.SCALE_BLOCK128, device=device,
-                                       activation_quant=ACTIVATION_QUANT)
+                                       activation_quant=SHAPE_ACTIVATION)
         for e in range(n):
             st.load_expert(e, torch.randn(inter, H, generator=g, device=device) * 0.02,
                            torch.randn(inter, H, generator=g, device=device) * 0.02,
@@ -863,7 +867,7 @@ def make_shape_layer(pkg, device, shape: dict, seed: int = 1240, *, rank: int = 
     shared = store(1, Is) if Is else None
     gate = (torch.randn(H, generator=g, device=device) * 0.02).bfloat16() if Is else None
     return pkg.MoELayer(wr, store(E, I, sharded=world > 1), K, shared_expert=shared, shared_gate_weight=gate,
-                        router_bias=bias, activation_quant=ACTIVATION_QUANT)
+                        router_bias=bias, activation_quant=SHAPE_ACTIVATION)
 
 
 def shape_bench(pkg, device, name: str, steps: int, warmup: int, flush) -> dict:
@@ -897,7 +901,7 @@ def shape_bench(pkg, device, name: str, steps: int, warmup: int, flush) -> dict:
         extra["expert_load"] = load.tolist()
     return {"workload": name, "model": shape["model"], "hidden": shape["H"], "experts": shape["E"],
             "moe_intermediate": shape["I"], "top_k": shape["K"], "shared_intermediate": shape["Is"],
-            "weights": "fp8 e4m3, 128x128 block scales", "activations": ACTIVATION_QUANT, "points": points,
+            "weights": "fp8 e4m3, 128x128 block scales", "activations": SHAPE_ACTIVATION, "points": points,
             "fp8_peak_tflops": peaks["fp8_tflops"], "hbm_peak_gbs": peaks["hbm_gbs"],
             "peak_source": peaks["fp8_source"],
             "l2": "flushed (256 MB write + 256 MB read) before every timed replay", **extra}
@@ -929,7 +933,7 @@ def shape_dwdp_bench(pkg, device, name: str, L: int, steps: int, warmup: int, fl
             "config": {"workload": f"{L} chained {name}-shaped MoE layers, prefill T={T} per GPU",
                        "hidden": shape["H"], "experts": shape["E"], "moe_intermediate": shape["I"],
                        "top_k": shape["K"], "shared_intermediate": shape["Is"],
-                       "weights": "fp8 e4m3, 128x128 block scales", "activations": ACTIVATION_QUANT,
+                       "weights": "fp8 e4m3, 128x128 block scales", "activations": SHAPE_ACTIVATION,
                        "parallelism": f"dwdp{world}: tokens data-parallel, routed experts sharded over {world} "
                                       "GPUs, next layer's remote experts prefetched over NVLink",
                        "l2": "flushed (256 MB write + 256 MB read) before every timed step"},
@@ -982,10 +986,13 @@ def main() -> None:
     ap.add_argument("--workload", default="moe_layers",
                     choices=["moe_layers", "decode_step", "attention", "mixtral", "deepseek", "layer", "reference_gpu"])
     ap.add_argument("--activation", default=None, choices=["hilo", "block128"],
-                    help="activation mode of --workload layer (default: the headline's)")
+                    help="activation mode of --workload layer / mixtral / deepseek (default: the headline's)")
     ap.add_argument("--batch", default="1,8,64", help="decode_step batch sizes")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    global SHAPE_ACTIVATION
+    if args.activation is not None and args.workload in SHAPES:  # the shapes' activation mode
+        SHAPE_ACTIVATION = args.activation
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

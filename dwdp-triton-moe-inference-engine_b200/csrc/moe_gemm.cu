@@ -29,6 +29,11 @@
 //                        128x128 block-scaled weights): every 128-wide K block
 //                        accumulates into its own TMEM slot and the epilogue warps
 //                        promote it into fp32 registers with its scales.
+// and two CTA-pair kernels (tcgen05 cta_group::2, clusters of two CTAs sharing one
+// 256 x 256 MMA, orientation tokens x features) for prefill-sized batches:
+//   moe_gemm_f8x2_kernel   hi/lo activation planes, per-row weight scales.
+//   moe_gemm_f8x2p_kernel  one activation plane per (row, 128) (DWDP_ACT_BLOCK128),
+//                          any weight scale mode, per-K-block promotion.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -1451,6 +1456,445 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
 }
 
 // ---------------------------------------------------------------------------
+// One e4m3 activation plane scaled per (row, 128 inputs) (DWDP_ACT_BLOCK128, the
+// reference's FP8 executor scheme, DWDP/executor/fp8.py:86-115 and
+// kernels/fp8_tma.py:99-119) on a CTA pair, for prefill-sized batches.
+//
+// Same load structure as moe_gemm_f8x2_kernel (two 128-input K blocks per stage: one
+// 3-D TMA box of activation rows and one bulk copy of weight tiles per CTA, 32 KB per
+// K block per SM), but A holds 128 distinct tokens per CTA (items of up to 256
+// tokens), so one MMA column carries one token instead of a hi/lo pair: half the MMA
+// work of the hi/lo mode per token. The activation scale changes every 128 inputs,
+// so every K block is multiplied into its own TMEM slot (two slots of 256 columns,
+// the tensor core one block ahead of the epilogue) and the epilogue warps fold it
+// into fp32 registers:  acc += slot * (s_x[token][kb] * s_w[kb])  (s_w only for
+// 128x128 block-scaled weights; per-row weight scales are applied once at the end).
+// Epilogue warp (quadrant q = warp % 4, half hw): TMEM lanes 32q..32q+31 = tokens, and
+//   MODE 0: gate and up features [64 hw, 64 hw + 64) of the item's 128-feature block
+//           (TMEM columns 64 hw.. and 128 + 64 hw..). At the end: SwiGLU in the
+//           reference executor's bf16 arithmetic and re-quantisation per (token, 128
+//           features) into the down projection's e4m3 rows + scales; the two halves of a
+//           quadrant exchange their |h| maxima through shared memory behind a bounded
+//           flag wait (no CTA-wide barrier an aborting warp could leave waiting);
+//   MODE 1: output columns [128 hw, 128 hw + 128) = down row block rb + hw, times the
+//           routing weight, bf16.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+
+struct CfgX2P {
+  static constexpr int KPS = 2;                       // K blocks per stage
+  static constexpr int A_TILE = 128 * BK8;            // 128 tokens x 128 inputs
+  static constexpr int B_TILE = kW8TileBytes;         // 128 weight rows x 128 inputs
+  static constexpr int STAGE_A = KPS * A_TILE;
+  static constexpr int STAGE_B = KPS * B_TILE;
+  static constexpr int STAGE = STAGE_A + STAGE_B;
+  static constexpr int S = 3;
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int EPI_THREADS = EPI_WARPS * 32;
+  static constexpr int THREADS = (2 + EPI_WARPS) * 32;
+  static constexpr int SLOT_COLS = 256;               // one K block's 256 x 256 product per CTA pair
+  static constexpr int NSLOT = 2;
+  static constexpr int RED_BYTES = 2 * 2 * 128 * 4 + 2 * 2 * 4 * 4;  // |h| maxima + flags
+  // per-warp ring of K-block scales filled DIST blocks ahead by asynchronous copies:
+  // a slot holds [32 token scales | 2 weight-block scales | pad]
+  static constexpr int RING = 4, DIST = 3, RSTRIDE = 36;
+  static constexpr int SCL_BYTES = EPI_WARPS * RING * RSTRIDE * 4;
+  // per-warp copy of the item's per-row weight scales (its 128 accumulator columns)
+  static constexpr int ROW_BYTES = EPI_WARPS * 128 * 4;
+  static constexpr int SMEM_BYTES = S * STAGE + RED_BYTES + SCL_BYTES + ROW_BYTES + 1024 + 512;
+  static constexpr uint32_t kFlagPolls = 1u << 24;    // bound of the halves' exchange wait (polls)
+  // TMEM columns per load: 16 keeps the 128 accumulators + the loaded columns inside the
+  // 168 registers a thread of a 10-warp CTA gets (3 warps share the fullest sub-partition)
+#ifdef DWDP_X2P_CHUNK
+  static constexpr int CHUNK = DWDP_X2P_CHUNK;
+#else
+  static constexpr int CHUNK = 16;
+#endif
+};
+
+#ifdef DWDP_PROFILE_ROLES
+// Diagnostic build only: cycles per activity of moe_gemm_f8x2p_kernel's roles in
+// g_role_cycles[cta][32 * MODE + slot] (producer 0-1, leader / relay 2-5, epilogue warp 2: 6-10).
+#define XP_DECL unsigned long long xp_[12] = {}; long long xpt_ = clock64();
+#define XP_ACC(slot) { const long long n_ = clock64(); xp_[slot] += (unsigned long long)(n_ - xpt_); xpt_ = n_; }
+#define XP_STORE(lo, hi) { for (int q_ = lo; q_ <= hi; ++q_) g_role_cycles[blockIdx.x][32 * MODE + q_] = xp_[q_]; }
+#else
+#define XP_DECL
+#define XP_ACC(slot)
+#define XP_STORE(lo, hi)
+#endif
+
+template <int MODE>
+__global__ void __launch_bounds__(CfgX2P::THREADS, 1) moe_gemm_f8x2p_kernel(const __grid_constant__ GemmParams p) {
+  using C = CfgX2P;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::S * C::STAGE_A;
+  float* sRed = reinterpret_cast<float*>(smem + C::S * C::STAGE);                  // [2 buf][2 half][128 tok]
+  volatile int* sFlag = reinterpret_cast<volatile int*>(sRed + 2 * 2 * 128);       // [2 buf][2 half][4 quad]
+  float* sScl = reinterpret_cast<float*>(smem + C::S * C::STAGE + C::RED_BYTES);   // [EPI_WARPS][RING][RSTRIDE]
+  float* sRow = sScl + C::EPI_WARPS * C::RING * C::RSTRIDE;                         // [EPI_WARPS][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::S * C::STAGE + C::RED_BYTES + C::SCL_BYTES + C::ROW_BYTES);
+  uint64_t* full = bars;                       // local loads of stage s landed
+  uint64_t* empty = full + C::S;               // the pair's MMAs read stage s (leader commit, both CTAs)
+  uint64_t* peer_full = empty + C::S;          // leader only: the peer's stage s landed
+  uint64_t* acc_full = peer_full + C::S;       // TMEM slot holds a K block's product (leader commit, both)
+  uint64_t* acc_empty = acc_full + C::NSLOT;   // this CTA's epilogue read the slot
+  uint64_t* peer_acc_empty = acc_empty + C::NSLOT;  // leader only: the peer's epilogue read the slot
+  __shared__ uint32_t s_tmem_base;
+  __shared__ volatile int s_abort;
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const uint32_t rank = cluster_rank();
+  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+  DeviceStatus* st = p.st;
+  griddep_launch();
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int i = 0; i < C::S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+      mbar_init(&peer_full[i], 1);
+    }
+    for (int i = 0; i < C::NSLOT; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], C::EPI_WARPS);  // one arrival per epilogue warp
+      mbar_init(&peer_acc_empty[i], 1);
+    }
+    fence_barrier_init();
+  }
+  if (threadIdx.x < 16) sFlag[threadIdx.x] = 0;
+  if (warp == 1) {
+    tmem_alloc2(&s_tmem_base, C::NSLOT * C::SLOT_COLS);
+    tmem_relinquish2();
+  }
+  if (warp == 0 && lane == 0) {
+    if (p.g[0].enabled) prefetch_tmap(&p.g[0].tmap_b);
+    if (p.g[1].enabled) prefetch_tmap(&p.g[1].tmap_b);
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers and flags of both CTAs initialised, TMEM allocated in both
+  tc_fence_after();
+  const uint32_t tmem_base = s_tmem_base;
+  griddep_wait();
+  const int n_items = *p.n_items;
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (each CTA its halves)
+    if (lane == 0) {
+      XP_DECL
+      uint32_t it = 0;
+      for (int item = cid; item < n_items && !s_abort; item += ncl) {
+        const WorkItem wi = p.items[item];
+        const GroupParams& g = p.g[wi.group];
+        const int h = min(128, (wi.nrows + 1) >> 1);  // tokens of CTA 0; CTA 1 takes the rest
+        const int tok0 = wi.row0 + (int)rank * h;
+        const uint8_t* wsrc = wi.wtiles + (size_t)rank * g.mstride;
+        for (int kb = wi.kb_begin; kb < wi.kb_end; kb += C::KPS, ++it) {
+          const int s = it % C::S;
+          const int nkb = min(C::KPS, wi.kb_end - kb);
+          XP_ACC(1)
+          if (!mbar_wait(&empty[s], ((it / C::S) & 1) ^ 1, &s_abort, st, 121 + 8 * MODE)) break;
+          XP_ACC(0)
+          // the activation box always lands whole (K blocks past the end read as zeros)
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(C::STAGE_A + nkb * C::B_TILE));
+          if (g.kstride == C::B_TILE) {
+            bulk_g2s(sB + s * C::STAGE_B, wsrc + (size_t)kb * g.kstride, nkb * C::B_TILE, &full[s]);
+          } else {
+            for (int q = 0; q < nkb; ++q)
+              bulk_g2s(sB + s * C::STAGE_B + q * C::B_TILE, wsrc + (size_t)(kb + q) * g.kstride, C::B_TILE, &full[s]);
+          }
+          tma_load_3d(sA + s * C::STAGE_A, &g.tmap_b, 0, tok0, kb, &full[s]);
+        }
+      }
+      XP_ACC(1)
+      XP_STORE(0, 1)
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ------------------------------------------------------------ MMA issuer (leader)
+      XP_DECL
+      uint32_t it = 0, kc = 0;
+      const uint32_t idesc = idesc_e4m3(256, 256);
+      bool ok = true;
+      for (int item = cid; item < n_items && !s_abort && ok; item += ncl) {
+        const WorkItem wi = p.items[item];
+        for (int kb = wi.kb_begin; kb < wi.kb_end && ok; kb += C::KPS, ++it) {
+          const int s = it % C::S;
+          const int nkb = min(C::KPS, wi.kb_end - kb);
+          const uint32_t fp = (it / C::S) & 1;
+          XP_ACC(5)
+          if (!mbar_wait(&full[s], fp, &s_abort, st, 122 + 8 * MODE) ||
+              !mbar_wait(&peer_full[s], fp, &s_abort, st, 123 + 8 * MODE)) {
+            ok = false;
+            break;
+          }
+          XP_ACC(2)
+          for (int q = 0; q < nkb; ++q, ++kc) {
+            const int slot = kc & 1;
+            const uint32_t par = ((kc >> 1) & 1) ^ 1;
+            XP_ACC(5)
+            if (!mbar_wait(&acc_empty[slot], par, &s_abort, st, 124 + 8 * MODE)) {
+              ok = false;
+              break;
+            }
+            XP_ACC(3)
+            if (!mbar_wait(&peer_acc_empty[slot], par, &s_abort, st, 125 + 8 * MODE)) {
+              ok = false;
+              break;
+            }
+            XP_ACC(4)
+            tc_fence_after();
+            const uint32_t d = tmem_base + slot * C::SLOT_COLS;
+            const uint64_t ad = smem_desc_sw128(smem_u32(sA + s * C::STAGE_A + q * C::A_TILE));
+            const uint64_t bd = smem_desc_sw128(smem_u32(sB + s * C::STAGE_B + q * C::B_TILE));
+#pragma unroll
+            for (int kk = 0; kk < BK8 / 32; ++kk)
+              mma2_e4m3_ss(d, ad + (uint64_t)(2 * kk), bd + (uint64_t)(2 * kk), idesc, kk > 0 ? 1u : 0u);
+            mma2_commit_mc(&acc_full[slot], 0x3);
+          }
+          if (ok) mma2_commit_mc(&empty[s], 0x3);
+        }
+      }
+      XP_ACC(5)
+      XP_STORE(2, 5)
+    } else if (lane == 0) {
+      // ------------------------------------------------------------ relay (peer): local phases -> leader
+      XP_DECL
+      uint32_t it = 0, kc = 0;
+      bool ok = true;
+      for (int item = cid; item < n_items && !s_abort && ok; item += ncl) {
+        const WorkItem wi = p.items[item];
+        for (int kb = wi.kb_begin; kb < wi.kb_end && ok; kb += C::KPS, ++it) {
+          const int s = it % C::S;
+          const int nkb = min(C::KPS, wi.kb_end - kb);
+          XP_ACC(5)
+          if (!mbar_wait(&full[s], (it / C::S) & 1, &s_abort, st, 126 + 8 * MODE)) {
+            ok = false;
+            break;
+          }
+          XP_ACC(2)
+          mbar_arrive_remote(&peer_full[s], 0);
+          for (int q = 0; q < nkb; ++q, ++kc) {
+            if (kc < 2) continue;  // both slots start free
+            const int slot = kc & 1;
+            XP_ACC(5)
+            if (!mbar_wait(&acc_empty[slot], ((kc >> 1) & 1) ^ 1, &s_abort, st, 127 + 8 * MODE)) {
+              ok = false;
+              break;
+            }
+            XP_ACC(3)
+            mbar_arrive_remote(&peer_acc_empty[slot], 0);
+          }
+        }
+      }
+      XP_ACC(5)
+      XP_STORE(2, 5)
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quad = warp & 3;                 // TMEM lanes 32 quad .. 32 quad + 31
+    const int hw = (warp - 2) >> 2;            // column half of the item this warp folds
+    const int t_cta = quad * 32 + lane;        // token of this lane inside the CTA's 128
+    uint32_t kc = 0;
+    int li = 0;
+    XP_DECL
+    for (int item = cid; item < n_items; item += ncl, ++li) {
+      if (__any_sync(0xffffffffu, s_abort != 0)) break;  // warp-uniform exit
+      const WorkItem wi = p.items[item];
+      const GroupParams& g = p.g[wi.group];
+      const int h = min(128, (wi.nrows + 1) >> 1);
+      const int n_my = rank == 0 ? h : wi.nrows - h;
+      const bool live = t_cta < n_my;
+      const int tok = wi.row0 + (int)rank * h + t_cta;
+      const bool block_w = g.scale_mode == DWDP_SCALE_BLOCK128;
+      const int kbn = g.K / 128;
+      // K block kb's scales -> ring slot kb % RING: lane t the scale of its token (zero past the
+      // tile), lanes m < 2 the weight-block scale of matrix m (MODE 0: gate, up; MODE 1: block
+      // rb + hw in both) when the weights are block-scaled
+      float* ring = sScl + (warp - 2) * C::RING * C::RSTRIDE;
+      auto issue = [&](int kb) {
+        float* rs = ring + (kb % C::RING) * C::RSTRIDE;
+        cp_async4(rs + lane, g.x_scale + (size_t)kb * g.xs_ld + (live ? tok : wi.row0), live ? 4u : 0u);
+        if (block_w && lane < 2) {
+          const int blk = MODE == 0 ? (lane * (g.R / BM) + wi.rb) : (wi.rb + hw);
+          cp_async4(rs + 32 + lane, wi.scales + (size_t)blk * kbn + kb, 4u);
+        }
+        cp_async_commit();
+      };
+      // per-row weight scales of this warp's columns, in the first group: one 16-byte copy per lane
+      // (MODE 0: lanes 0-15 gate, 16-31 up of features fb..fb+63; MODE 1: features fb..fb+127)
+      const bool per_row = per_row_scales(g.scale_mode);
+      const int fb = MODE == 0 ? wi.rb * BM + 64 * hw : wi.rb * BM + 128 * hw;
+      float* row_s = sRow + (warp - 2) * 128;
+      if (per_row) {
+        const float* src = MODE == 0 ? wi.scales + (lane < 16 ? fb + 4 * lane : g.R + fb + 4 * (lane - 16))
+                                     : wi.scales + fb + 4 * lane;
+        cp_async16(row_s + 4 * lane, src);
+      }
+#pragma unroll
+      for (int d = 0; d < C::DIST; ++d) {
+        if (wi.kb_begin + d < wi.kb_end) issue(wi.kb_begin + d);
+        else cp_async_commit();
+      }
+      float acc[128];
+#pragma unroll
+      for (int j = 0; j < 128; ++j) acc[j] = 0.f;
+      bool ok = true;
+      XP_ACC(10)
+      for (int kb = wi.kb_begin; kb < wi.kb_end; ++kb, ++kc) {
+        const int slot = kc & 1;
+        // one lane per warp polls the barrier (256 pollers per K block would crowd shared memory)
+        int got = 1;
+        XP_ACC(6)
+        if (lane == 0) got = mbar_wait(&acc_full[slot], (kc >> 1) & 1, &s_abort, st, 128 + 8 * MODE) ? 1 : 0;
+        if (!__shfl_sync(0xffffffffu, got, 0)) {
+          ok = false;
+          break;
+        }
+        XP_ACC(7)
+        // the block's scales (their copies overlapped the wait above)
+        cp_async_wait<C::DIST - 1>();  // this lane's copies of block kb have landed
+        __syncwarp();                  // ... and every lane's are visible
+        const float* rs = ring + (kb % C::RING) * C::RSTRIDE;
+        const float sx = rs[lane];
+        const float f0 = block_w ? sx * rs[32] : sx;
+        const float f1 = block_w ? sx * rs[33] : sx;
+        tc_fence_after();
+        const uint32_t t_slot = tmem_base + slot * C::SLOT_COLS + ((uint32_t)(quad * 32) << 16);
+#pragma unroll
+        for (int c = 0; c < 128 / CfgX2P::CHUNK; ++c) {
+          constexpr int CH = CfgX2P::CHUNK;
+          const int a0 = CH * c;  // first accumulator of the chunk
+          const int col = MODE == 0 ? ((a0 >> 6) * 128 + 64 * hw + (a0 & 63)) : (128 * hw + a0);
+          const float f = (MODE == 0 && a0 >= 64) ? f1 : f0;
+          float v[CH];
+          tmem_ld<CH>(t_slot + col, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < CH; j += 2) fma_pair(acc[a0 + j], acc[a0 + j + 1], v[j], v[j + 1], f, f);
+        }
+        tc_fence_before();
+        __syncwarp();  // every lane is done with the TMEM slot and with ring slot kb % RING
+        if (lane == 0) mbar_arrive(&acc_empty[slot]);
+        XP_ACC(8)
+        if (kb + C::DIST < wi.kb_end) issue(kb + C::DIST);
+        else cp_async_commit();
+      }
+      cp_async_wait<0>();
+      __syncwarp();  // every lane's copies (ring, per-row scales) are visible
+      XP_ACC(6)
+      if (!ok) break;
+      if constexpr (MODE == 0) {
+        // h per the reference executor's bf16 arithmetic; acc[j] = gate, acc[64 + j] = up of
+        // feature fb + j
+        float amax = 0.f;
+#pragma unroll
+        for (int j = 0; j < 64; j += 4) {
+          float4 sg = make_float4(1.f, 1.f, 1.f, 1.f), su = sg;
+          if (per_row) {
+            sg = *reinterpret_cast<const float4*>(row_s + j);
+            su = *reinterpret_cast<const float4*>(row_s + 64 + j);
+          }
+          const float gs[4] = {sg.x, sg.y, sg.z, sg.w}, us[4] = {su.x, su.y, su.z, su.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float gb = bf16_round(acc[j + e] * gs[e]);
+            const float ub = bf16_round(acc[64 + j + e] * us[e]);
+            const float sgm = bf16_round(__fdividef(1.0f, 1.0f + __expf(-gb)));
+            const float hv = bf16_round(bf16_round(gb * sgm) * ub);
+            acc[j + e] = hv;  // h replaces the gate accumulator
+            amax = fmaxf(amax, fabsf(hv));
+          }
+        }
+        // (token, 128-feature) amax: exchange with the other half of this quadrant
+        const int b = li & 1;
+        sRed[(b * 2 + hw) * 128 + t_cta] = live ? amax : 0.f;
+        __syncwarp();
+        __threadfence_block();
+        if (lane == 0) sFlag[(b * 2 + hw) * 4 + quad] = li + 1;
+        int seen = 1;
+        if (lane == 0) {
+          uint32_t n = 0;
+          while (sFlag[(b * 2 + (hw ^ 1)) * 4 + quad] != li + 1) {
+            if (++n >= C::kFlagPolls || s_abort) {
+              seen = 0;
+              break;
+            }
+          }
+        }
+        seen = __shfl_sync(0xffffffffu, seen, 0);
+        if (!seen) {
+          if (lane == 0 && !s_abort) {
+            s_abort = 1;
+            record_error(st, DWDP_ERR_DEVICE_TIMEOUT, 129 + 8 * MODE, li);
+          }
+          break;
+        }
+        __threadfence_block();
+        const float tmax = fmaxf(amax, sRed[(b * 2 + (hw ^ 1)) * 128 + t_cta]);
+        const float tsc = __fdiv_rn(fmaxf(tmax, 1e-5f), 448.0f);
+        const float rcp = __frcp_rn(tsc);  // quantise by multiplying with the reciprocal
+        if (live) {
+          if (hw == 0) g.out_scale[(size_t)wi.rb * g.os_ld + tok] = tsc;
+          uint8_t* dst = reinterpret_cast<uint8_t*>(g.out) + (size_t)tok * g.R + fb;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int j = 16 * q + 4 * e;
+              const uint32_t lo = (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(acc[j] * rcp, acc[j + 1] * rcp),
+                                                                      __NV_SATFINITE, __NV_E4M3);
+              const uint32_t hi = (uint32_t)__nv_cvt_float2_to_fp8x2(
+                  make_float2(acc[j + 2] * rcp, acc[j + 3] * rcp), __NV_SATFINITE, __NV_E4M3);
+              w[e] = lo | (hi << 16);
+            }
+            reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      } else {
+        if (live) {
+          const float rw = g.row_scale != nullptr ? g.row_scale[tok] : 1.0f;
+          __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)wi.part * g.part_stride +
+                               (size_t)tok * g.R + fb;
+#pragma unroll
+          for (int j = 0; j < 128; j += 8) {
+            float4 s0 = make_float4(1.f, 1.f, 1.f, 1.f), s1 = s0;
+            if (per_row) {
+              s0 = *reinterpret_cast<const float4*>(row_s + j);
+              s1 = *reinterpret_cast<const float4*>(row_s + j + 4);
+            }
+            const float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const __nv_bfloat162 yv = __floats2bfloat162_rn(acc[j + 2 * e] * (sc[2 * e] * rw),
+                                                              acc[j + 2 * e + 1] * (sc[2 * e + 1] * rw));
+              w[e] = *reinterpret_cast<const uint32_t*>(&yv);
+            }
+            reinterpret_cast<uint4*>(out)[j / 8] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+      XP_ACC(9)
+    }
+    if (warp == 2 && lane == 0) { XP_STORE(6, 10) }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs done: the leader's MMAs and both epilogues
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc2(tmem_base, C::NSLOT * C::SLOT_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Device tile planner (the scheduler's job, DWDP/scheduler/ops/round_robin.py:
 // active experts in ascending id), run on device so no counts reach the host.
 // Shared-expert tiles go first (longest-running work first); routed tiles are
@@ -2062,16 +2506,14 @@ int launch_gemm_f8(const GemmParams& prm, int grid, cudaStream_t stream) {
 }
 
 // CTA-pair kernels: clusters of two consecutive CTAs (grid must be even), programmatic launch.
-template <int MODE, int KPS>
-int launch_gemm_f8x2(const GemmParams& prm, int grid, cudaStream_t stream) {
-  using C = CfgX2<MODE, KPS>;
-  auto kfn = moe_gemm_f8x2_kernel<MODE, KPS>;
-  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
+template <typename Kfn>
+int launch_pair(Kfn kfn, int threads, int smem_bytes, const GemmParams& prm, int grid, cudaStream_t stream) {
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
     return DWDP_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid & ~1);
-  cfg.blockDim = dim3(C::THREADS);
-  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   unsigned n = 0;
@@ -2088,6 +2530,17 @@ int launch_gemm_f8x2(const GemmParams& prm, int grid, cudaStream_t stream) {
   cfg.attrs = attr;
   cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kfn, prm) == cudaSuccess ? DWDP_OK : DWDP_ERR_CUDA;
+}
+
+template <int MODE, int KPS>
+int launch_gemm_f8x2(const GemmParams& prm, int grid, cudaStream_t stream) {
+  using C = CfgX2<MODE, KPS>;
+  return launch_pair(moe_gemm_f8x2_kernel<MODE, KPS>, C::THREADS, C::SMEM_BYTES, prm, grid, stream);
+}
+
+template <int MODE>
+int launch_gemm_f8x2p(const GemmParams& prm, int grid, cudaStream_t stream) {
+  return launch_pair(moe_gemm_f8x2p_kernel<MODE>, CfgX2P::THREADS, CfgX2P::SMEM_BYTES, prm, grid, stream);
 }
 
 // One warp per row once the rows fill every SM's warps; below that a CTA per
@@ -2224,30 +2677,36 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
     pair_dn = fp8 && !(act_blk && wide) && v[0] == '1';
   // Prefill-sized hi/lo batches run on CTA pairs (moe_gemm_f8x2_kernel: 128-token tiles, 64 per
   // CTA, down items always two 128-row blocks). DWDP_PAIR_CTA=0|1 overrides the default.
-  bool use_pair = false;
+  bool use_pair = false, use_pair_blk = false;
   {
     static const int pair_env = [] {
       const char* v = getenv("DWDP_PAIR_CTA");
       return v != nullptr ? atoi(v) : 1;
     }();
-    static const long long pair_min = [] {  // tuning: routed rows from which the pairs run
-      const char* v = getenv("DWDP_PAIR_MIN_ROWS");
-      return v != nullptr ? atoll(v) : 148LL * 64;
-    }();
+    // tuning: routed rows from which the pairs run (read every call, so tests can move it)
+    const char* pmin = getenv("DWDP_PAIR_MIN_ROWS");
+    const long long pair_min = pmin != nullptr ? atoll(pmin) : 148LL * 64;
     use_pair = pair_env == 1 && hilo_native && !wide && (H / BM) % 2 == 0 && N >= pair_min;
+    // the reference's single-plane scheme on CTA pairs (moe_gemm_f8x2p_kernel: 256-token
+    // tiles, 128 per CTA, per-K-block promotion); DWDP_PAIR_BLK=0 keeps the one-CTA kernels
+    static const int pair_blk_env = [] {
+      const char* v = getenv("DWDP_PAIR_BLK");
+      return v != nullptr ? atoi(v) : 1;
+    }();
+    use_pair_blk = pair_env == 1 && pair_blk_env == 1 && act_blk && !wide && (H / BM) % 2 == 0 && N >= pair_min;
   }
   static const int pair_kps = [] {  // tuning: K blocks per stage of the pair kernels (1 or 2)
     const char* v = getenv("DWDP_PAIR_KPS");
     return v != nullptr && atoi(v) == 1 ? 1 : 2;
   }();
-  if (use_pair) pair_dn = true;
+  if (use_pair || use_pair_blk) pair_dn = true;
   const int dn_items_per_tile = pair_dn ? (H / BM + 1) / 2 : H / BM;
   pp.rb_gu_r = I / BM; pp.rb_dn_r = dn_items_per_tile;
   pp.rb_gu_s = has_shared ? Is / BM : 0; pp.rb_dn_s = has_shared ? dn_items_per_tile : 0;
   pp.dn_pair = pair_dn ? 1 : 0; pp.blocks_dn = H / BM;
   pp.kb_gu = H / bk; pp.kb_dn_r = I / bk; pp.kb_dn_s = has_shared ? Is / bk : 0;
   pp.sdn_parts = has_shared ? parts : 0;
-  pp.bn_max = use_pair ? 128 : bn;
+  pp.bn_max = use_pair ? 128 : use_pair_blk ? 256 : bn;
   const long long esz = fp8 ? 1 : 2;
   pp.w_gu[0] = routed->w13; pp.w_dn[0] = routed->w2; pp.s_gu[0] = routed->s13; pp.s_dn[0] = routed->s2;
   pp.rbb_gu[0] = 128LL * H * 2 * esz; pp.rbb_dn[0] = 128LL * I * esz;
@@ -2289,9 +2748,11 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
   // The activation box must cover the largest tile: a routed tile holds at most
   // min(T * K, bn) rows (an expert may be picked more than once per token), a
   // shared tile at most min(T, bn).
-  const int box_r = use_pair ? 64 : box_rows_for(N, bn), box_s = use_pair ? 64 : box_rows_for(T, bn);
+  const int box_r = use_pair ? 64 : use_pair_blk ? 128 : box_rows_for(N, bn);
+  const int box_s = use_pair ? 64 : use_pair_blk ? 128 : box_rows_for(T, bn);
   auto map = [&](CUtensorMap* m, const void* bf16, size_t planes_off, int64_t rows, int64_t cols, int box) {
-    if (fp8 && use_pair && pair_kps == 2) return make_tmap_planes3(m, ws + planes_off, rows, cols, box, planes);
+    if (fp8 && ((use_pair && pair_kps == 2) || use_pair_blk))
+      return make_tmap_planes3(m, ws + planes_off, rows, cols, box, planes);
     return fp8 ? make_tmap_planes(m, ws + planes_off, rows, cols, box, planes) : make_tmap(m, bf16, rows, cols, box);
   };
   GemmParams gu{}, dn{};
@@ -2344,7 +2805,12 @@ extern "C" int dwdp_moe_experts_launch(const dwdp_expert_group* routed, const dw
                : DWDP_ERR_CUDA;
   };
   int rc;
-  if (use_pair) {
+  if (use_pair_blk) {
+    // the gate/up epilogue writes the e4m3 intermediate and its scales: no launch between
+    const int grid2 = std::max(2, (sms / 2) * 2);
+    rc = launch_gemm_f8x2p<0>(gu, grid2, stream);
+    if (rc == DWDP_OK) rc = launch_gemm_f8x2p<1>(dn, grid2, stream);
+  } else if (use_pair) {
     const int grid2 = std::max(2, (sms / 2) * 2);
     rc = pair_kps == 2 ? launch_gemm_f8x2<0, 2>(gu, grid2, stream) : launch_gemm_f8x2<0, 1>(gu, grid2, stream);
     if (rc == DWDP_OK) rc = quant_h();

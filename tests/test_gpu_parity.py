@@ -530,3 +530,17 @@ def test_route_dispatch_small(pkg, orc, T, E, K, H, gate, renorm):
         assert np.array_equal(d.packed_token_indices.cpu().numpy(), plan["tok"])
         assert np.array_equal(d.packed_routing_weights.cpu().numpy().view(np.uint32),
                               plan["weights"].astype(np.float32).view(np.uint32))
+
+
+@pytest.mark.parametrize("T", [7, 300, 1024])
+@pytest.mark.parametrize("wcfg,I,Is", [("channel", 256, 2048), ("block", 384, 512), ("tensor", 384, 0)])
+def test_moe_layer_block128_cta_pairs(pkg, orc, monkeypatch, T, wcfg, I, Is):
+    """The single-plane CTA-pair kernels (256-token tiles, per-K-block promotion) forced at
+    small sizes: partial tiles, an odd number of K blocks in the down projection (I = 384),
+    the shared expert's K-split down projection (Is = 2048 at T = 7), every weight-scale mode."""
+    monkeypatch.setenv("DWDP_PAIR_MIN_ROWS", "1")
+    mode = {"channel": pkg._lib.SCALE_CHANNEL, "block": pkg._lib.SCALE_BLOCK128,
+            "tensor": pkg._lib.SCALE_TENSOR}[wcfg]
+    layer = _make_layer(pkg, 8, 512, I, 2, Is, torch.float8_e4m3fn, mode, seed=T + 17, act="block128")
+    err = _check_layer(pkg, orc, layer, T, FP8_TOL)
+    assert err < 1e-2, err
