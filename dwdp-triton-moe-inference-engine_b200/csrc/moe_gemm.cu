@@ -1483,6 +1483,14 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
 }
 
+// logistic function from the hardware tanh: 1 / (1 + e^-x) = 0.5 + 0.5 tanh(x / 2), one MUFU
+// operation instead of an exponential and a reciprocal (max abs error ~2^-11, below bf16's step)
+__device__ __forceinline__ float sigmoid_tanh(float x) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
+  return fmaf(0.5f, t, 0.5f);
+}
+
 struct CfgX2P {
   static constexpr int KPS = 2;                       // K blocks per stage
   static constexpr int A_TILE = 128 * BK8;            // 128 tokens x 128 inputs
@@ -1804,7 +1812,7 @@ __global__ void __launch_bounds__(CfgX2P::THREADS, 1) moe_gemm_f8x2p_kernel(cons
           for (int e = 0; e < 4; ++e) {
             const float gb = bf16_round(acc[j + e] * gs[e]);
             const float ub = bf16_round(acc[64 + j + e] * us[e]);
-            const float sgm = bf16_round(__fdividef(1.0f, 1.0f + __expf(-gb)));
+            const float sgm = bf16_round(sigmoid_tanh(gb));
             const float hv = bf16_round(bf16_round(gb * sgm) * ub);
             acc[j + e] = hv;  // h replaces the gate accumulator
             amax = fmaxf(amax, fabsf(hv));
