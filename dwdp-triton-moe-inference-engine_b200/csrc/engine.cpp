@@ -428,6 +428,51 @@ extern "C" int dwdp_engine_prefetch(dwdp_engine* eng, const int* expert_ids, int
   for (size_t i = 0; order.size() < todo.size(); ++i)
     for (const auto* lst : owners)
       if (i < lst->size()) order.push_back((*lst)[i]);
+  // Coalesced copies (the default: DWDP_PREFETCH_COALESCE_MB = c, 64 unless set, 0 = one copy per
+  // expert; copy engines, no slicing): an owner's
+  // experts sit back to back in its slab tensor and in staging (ascending ids both sides), so
+  // each run contiguous on both sides moves as c-MiB pieces instead of one copy per expert;
+  // the owners' pieces are interleaved as above. Fewer, larger copies keep the copy engines
+  // streaming (per-copy rates measured on B200: 8.65 MB 492 GB/s, 44 MB 670, 176 MB 721).
+  static const size_t coalesce = [] {
+    const char* v = getenv("DWDP_PREFETCH_COALESCE_MB");
+    return v != nullptr ? (size_t)atoi(v) << 20 : (size_t)64 << 20;
+  }();
+  if (coalesce > 0 && slice == 0 && eng->copy_mode != DWDP_COPY_SM) {
+    std::vector<std::vector<PlannedCopy>> per_owner;
+    for (const auto* lst : owners) {
+      std::vector<PlannedCopy> pieces;
+      for (size_t i = 0; i < lst->size();) {
+        const EngineExpert* a = (*lst)[i];
+        const char* src = static_cast<const char*>(a->src);
+        char* dst = staging_slot(eng, a, buffer);
+        size_t bytes = a->bytes;
+        size_t j = i + 1;
+        for (; j < lst->size(); ++j) {
+          const EngineExpert* b = (*lst)[j];
+          if (static_cast<const char*>(b->src) != src + bytes || staging_slot(eng, b, buffer) != dst + bytes) break;
+          bytes += b->bytes;
+        }
+        const size_t npieces = (bytes + coalesce - 1) / coalesce;  // equal pieces, none tiny
+        const size_t step = ((bytes + npieces - 1) / npieces + 255) & ~(size_t)255;
+        for (size_t off = 0; off < bytes; off += step)
+          pieces.push_back(PlannedCopy{src + off, dst + off, std::min(step, bytes - off)});
+        i = j;
+      }
+      per_owner.push_back(std::move(pieces));
+    }
+    std::vector<PlannedCopy> copies;
+    for (size_t k = 0;; ++k) {
+      bool any = false;
+      for (const auto& pc : per_owner)
+        if (k < pc.size()) {
+          copies.push_back(pc[k]);
+          any = true;
+        }
+      if (!any) break;
+    }
+    return issue_copies(eng, copies, buffer, after_stream);
+  }
   std::vector<PlannedCopy> copies;
   for (size_t j = 0; j < order.size(); ++j) {
     const EngineExpert* x = order[j];
