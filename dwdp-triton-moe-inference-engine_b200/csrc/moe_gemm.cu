@@ -1808,14 +1808,19 @@ __global__ void __launch_bounds__(CfgX2P::THREADS, 1) moe_gemm_f8x2p_kernel(cons
             su = *reinterpret_cast<const float4*>(row_s + 64 + j);
           }
           const float gs[4] = {sg.x, sg.y, sg.z, sg.w}, us[4] = {su.x, su.y, su.z, su.w};
+          // pairs of features in bf16x2: a product of two bf16 values is exact in fp32, so the
+          // packed bf16 multiply rounds exactly as bf16(fp32 product) does
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float gb = bf16_round(acc[j + e] * gs[e]);
-            const float ub = bf16_round(acc[64 + j + e] * us[e]);
-            const float sgm = bf16_round(sigmoid_tanh(gb));
-            const float hv = bf16_round(bf16_round(gb * sgm) * ub);
-            acc[j + e] = hv;  // h replaces the gate accumulator
-            amax = fmaxf(amax, fabsf(hv));
+          for (int e = 0; e < 4; e += 2) {
+            const __nv_bfloat162 g2 = __floats2bfloat162_rn(acc[j + e] * gs[e], acc[j + e + 1] * gs[e + 1]);
+            const __nv_bfloat162 u2 =
+                __floats2bfloat162_rn(acc[64 + j + e] * us[e], acc[64 + j + e + 1] * us[e + 1]);
+            const float2 gf = __bfloat1622float2(g2);
+            const __nv_bfloat162 s2 = __floats2bfloat162_rn(sigmoid_tanh(gf.x), sigmoid_tanh(gf.y));
+            const float2 hf = __bfloat1622float2(__hmul2(__hmul2(g2, s2), u2));
+            acc[j + e] = hf.x;  // h replaces the gate accumulators
+            acc[j + e + 1] = hf.y;
+            amax = fmaxf(amax, fmaxf(fabsf(hf.x), fabsf(hf.y)));
           }
         }
         // (token, 128-feature) amax: exchange with the other half of this quadrant
