@@ -2879,6 +2879,28 @@ extern "C" int dwdp_quantize_activations_launch(const void* src, int64_t src_row
 }
 
 #ifdef DWDP_PROFILE_ROLES
+// Diagnostic build only: how many two-CTA clusters of the pair kernels can be resident at once.
+extern "C" int dwdp_debug_max_pair_clusters(int* hilo, int* blk) {
+  auto query = [](auto kfn, int threads, int smem, int* out) {
+    if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -3;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 148);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaOccupancyMaxActiveClusters(out, kfn, &cfg) == cudaSuccess ? 0 : -3;
+  };
+  using C = dwdp::CfgX2<0, 2>;
+  if (query(dwdp::moe_gemm_f8x2_kernel<0, 2>, C::THREADS, C::SMEM_BYTES, hilo) != 0) return -3;
+  return query(dwdp::moe_gemm_f8x2p_kernel<0>, dwdp::CfgX2P::THREADS, dwdp::CfgX2P::SMEM_BYTES, blk);
+}
+
 extern "C" int dwdp_debug_role_cycles(unsigned long long* out) {
   return cudaMemcpyFromSymbol(out, dwdp::g_role_cycles, sizeof(dwdp::g_role_cycles)) == cudaSuccess ? 0 : -3;
 }
