@@ -38,6 +38,7 @@
 #include <vector>
 
 #include "dwdp_b200.h"
+#include "prefetch_plan.h"
 
 namespace {
 
@@ -407,81 +408,29 @@ extern "C" int dwdp_engine_prefetch(dwdp_engine* eng, const int* expert_ids, int
     if (it == eng->experts.end()) return fail(DWDP_ERR_NOT_FOUND, "prefetch: unknown expert " + std::to_string(expert_ids[i]));
     if (it->second.remote) todo.push_back(&it->second);
   }
-  // Issue order: the owners are interleaved (one expert of each owner in turn) and every
-  // rank starts with the owner after itself, so consecutive copies (which run side by side
-  // on the copy streams) read different peers and the G ranks start on G different peers
-  // instead of all reading the first owner's memory at once. With DWDP_PREFETCH_SLICE_MB =
-  // s > 0 every expert moves as s-MiB slices dealt round-robin over the copy streams (the
-  // reference's 2 MiB slices, buffers.cu:94-134); by default each expert is one copy (SM
-  // copies always move whole experts).
+  // Order and granularity: dwdp_plan::plan_prefetch (prefetch_plan.h). With DWDP_PREFETCH_SLICE_MB
+  // = s > 0 every expert moves as s-MiB slices (the reference's 2 MiB scheme); otherwise each
+  // owner's contiguous experts move as ~DWDP_PREFETCH_COALESCE_MB-MiB pieces (default 64; 0 = one
+  // copy per expert): per-copy rates on B200 grow with the copy (8.65 MB 492 GB/s, 44 MB 670,
+  // 176 MB 721). SM copies always move whole experts.
   static const size_t slice = [] {
     const char* v = getenv("DWDP_PREFETCH_SLICE_MB");
     return v != nullptr ? (size_t)atoi(v) << 20 : (size_t)0;
   }();
-  std::map<int, std::vector<const EngineExpert*>> by_owner;  // ascending expert id per owner
-  for (const EngineExpert* x : todo) by_owner[x->owner_device].push_back(x);
-  std::vector<const std::vector<const EngineExpert*>*> owners;
-  for (auto it = by_owner.upper_bound(eng->device); it != by_owner.end(); ++it) owners.push_back(&it->second);
-  for (auto it = by_owner.begin(); it != by_owner.end() && it->first <= eng->device; ++it) owners.push_back(&it->second);
-  std::vector<const EngineExpert*> order;
-  order.reserve(todo.size());
-  for (size_t i = 0; order.size() < todo.size(); ++i)
-    for (const auto* lst : owners)
-      if (i < lst->size()) order.push_back((*lst)[i]);
-  // Coalesced copies (the default: DWDP_PREFETCH_COALESCE_MB = c, 64 unless set, 0 = one copy per
-  // expert; copy engines, no slicing): an owner's
-  // experts sit back to back in its slab tensor and in staging (ascending ids both sides), so
-  // each run contiguous on both sides moves as c-MiB pieces instead of one copy per expert;
-  // the owners' pieces are interleaved as above. Fewer, larger copies keep the copy engines
-  // streaming (per-copy rates measured on B200: 8.65 MB 492 GB/s, 44 MB 670, 176 MB 721).
   static const size_t coalesce = [] {
     const char* v = getenv("DWDP_PREFETCH_COALESCE_MB");
     return v != nullptr ? (size_t)atoi(v) << 20 : (size_t)64 << 20;
   }();
-  if (coalesce > 0 && slice == 0 && eng->copy_mode != DWDP_COPY_SM) {
-    std::vector<std::vector<PlannedCopy>> per_owner;
-    for (const auto* lst : owners) {
-      std::vector<PlannedCopy> pieces;
-      for (size_t i = 0; i < lst->size();) {
-        const EngineExpert* a = (*lst)[i];
-        const char* src = static_cast<const char*>(a->src);
-        char* dst = staging_slot(eng, a, buffer);
-        size_t bytes = a->bytes;
-        size_t j = i + 1;
-        for (; j < lst->size(); ++j) {
-          const EngineExpert* b = (*lst)[j];
-          if (static_cast<const char*>(b->src) != src + bytes || staging_slot(eng, b, buffer) != dst + bytes) break;
-          bytes += b->bytes;
-        }
-        const size_t npieces = (bytes + coalesce - 1) / coalesce;  // equal pieces, none tiny
-        const size_t step = ((bytes + npieces - 1) / npieces + 255) & ~(size_t)255;
-        for (size_t off = 0; off < bytes; off += step)
-          pieces.push_back(PlannedCopy{src + off, dst + off, std::min(step, bytes - off)});
-        i = j;
-      }
-      per_owner.push_back(std::move(pieces));
-    }
-    std::vector<PlannedCopy> copies;
-    for (size_t k = 0;; ++k) {
-      bool any = false;
-      for (const auto& pc : per_owner)
-        if (k < pc.size()) {
-          copies.push_back(pc[k]);
-          any = true;
-        }
-      if (!any) break;
-    }
-    return issue_copies(eng, copies, buffer, after_stream);
-  }
+  const bool sm = eng->copy_mode == DWDP_COPY_SM;
+  std::vector<dwdp_plan::Expert> remote;
+  remote.reserve(todo.size());
+  for (const EngineExpert* x : todo)
+    remote.push_back(dwdp_plan::Expert{x->owner_device, static_cast<const char*>(x->src), staging_slot(eng, x, buffer),
+                                       x->bytes});
+  const auto plan = dwdp_plan::plan_prefetch(remote, eng->device, sm ? 0 : slice, sm ? 0 : coalesce);
   std::vector<PlannedCopy> copies;
-  for (size_t j = 0; j < order.size(); ++j) {
-    const EngineExpert* x = order[j];
-    char* dst = staging_slot(eng, x, buffer);
-    const char* src = static_cast<const char*>(x->src);
-    const size_t step = (slice > 0 && eng->copy_mode != DWDP_COPY_SM) ? slice : x->bytes;
-    for (size_t off = 0; off < x->bytes; off += step)
-      copies.push_back(PlannedCopy{src + off, dst + off, std::min(step, x->bytes - off)});
-  }
+  copies.reserve(plan.size());
+  for (const auto& c : plan) copies.push_back(PlannedCopy{c.src, c.dst, c.bytes});
   return issue_copies(eng, copies, buffer, after_stream);
 }
 
