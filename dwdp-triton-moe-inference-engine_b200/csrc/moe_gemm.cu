@@ -1270,7 +1270,6 @@ moe_gemm_f8p_kernel(const __grid_constant__ GemmParams p) {
               if (m < nm) tmem_ld<C::TCOL>(t_acc + m * C::NCOL, v[m]);
 #endif
             tmem_ld_wait();
-#pragma unroll
             if constexpr (PLANES == 1) {
               // each float4 of token scales serves every matrix
               const float4* f4 = reinterpret_cast<const float4*>(rs);
